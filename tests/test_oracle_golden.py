@@ -1,0 +1,154 @@
+"""The numpy oracle against golden vectors produced by the unmodified reference.
+
+Fixtures come from ``tests/golden/make_golden.py`` (run once where the
+reference is importable); these tests need neither the reference nor a GPU.
+"""
+
+import numpy as np
+import pytest
+
+import oracle as O
+from longspark_b200.config import DraftShape
+
+
+def _load(golden_dir, name):
+    return np.load(golden_dir / f"{name}.npz")
+
+
+@pytest.mark.parametrize("name", ["refresh_gqa4_ref", "refresh_gqa5_ref", "refresh_gqa4_s64_v16"])
+def test_refresh_chain_matches_reference(golden_dir, name):
+    z = _load(golden_dir, name)
+    hq, hkv, s, v, steps, *batches = [int(x) for x in z["meta"]]
+    for b in batches:
+        p = f"b{b}_"
+        q = O.from_bf16_bits(z[p + "query"])
+        out, lse = z[p + "output0"].copy(), z[p + "lse0"].copy()
+        for step in range(steps):
+            keys = O.from_bf16_bits(z[p + "keys"][step])
+            vals = O.from_bf16_bits(z[p + "values"][step])
+            sc = O.position_scores(np.broadcast_to(q[None], (b,) + q.shape), keys, 128 ** -0.5)
+            if step == 0:
+                np.testing.assert_allclose(sc, z[p + "scores0"], rtol=1e-5, atol=1e-5)
+            out, lse = O.merge_accepted(out, lse, sc, vals, z[p + "lens"][step])
+        np.testing.assert_allclose(out, z[p + "final_output"], rtol=2e-5, atol=2e-5)
+        np.testing.assert_allclose(lse, z[p + "final_lse"], rtol=2e-5, atol=2e-5)
+
+
+def _shape_from(arr):
+    h, hq, hkv, inter, vocab, tap, drf, slots, window, block, rank, mask = [int(x) for x in arr]
+    return DraftShape(hidden=h, q_heads=hq, kv_heads=hkv, inter=inter, vocab=vocab, tap_layers=tap,
+                      draft_layers=drf, slots=slots, window=window, block=block,
+                      max_commit=block + 1, markov_rank=rank, mask_token_id=mask)
+
+
+def _inv_freq(shape):
+    d = shape.head_dim
+    return (1.0 / (np.float32(shape.rope_theta) ** (np.arange(0, d, 2, dtype=np.float32) / d))).astype(np.float32)
+
+
+def _run_oracle(shape, W, inp, prec):
+    views = O.build_views(inp["kv_k"], inp["kv_v"], inp["table"], inp["seq_lens"], inp["summary_out"],
+                          W["global16_raw256_reference.global_query_generator.learned_query"],
+                          shape.window, shape.draft_layers, prec=prec)
+    hidden = inp["hidden"]
+    if prec == "fp32":
+        views = [dict(v, qg=v["qg"]) for v in views]
+    osh = O.DraftShapeOracle(shape.hidden, shape.q_heads, shape.kv_heads, 128, shape.block,
+                             shape.mask_token_id)
+    base, _ = O.draft_pass(W, osh, inp["anchors"], inp["seq_lens"].astype(np.int64), hidden, views,
+                           _inv_freq(shape), prec)
+    return base
+
+
+def _small_inputs(golden_dir, stem):
+    z = _load(golden_dir, f"{stem}_inputs")
+    W = {k[3:]: O.from_bf16_bits(z[k]) for k in z.files if k.startswith("w::")}
+    inp = dict(kv_k=O.from_bf16_bits(z["kv_k"]), kv_v=O.from_bf16_bits(z["kv_v"]), table=z["table"],
+               seq_lens=z["seq_lens"], hidden=O.from_bf16_bits(z["hidden"]), anchors=z["anchors"],
+               summary_out=z["summary_out"])
+    return W, inp
+
+
+@pytest.mark.parametrize("stem", ["draft_small_ref", "draft_small_gqa5_s64_w512"])
+def test_draft_pass_fp32_matches_reference(golden_dir, stem):
+    W, inp = _small_inputs(golden_dir, stem)
+    gold = _load(golden_dir, f"{stem}_fp32")
+    shape = _shape_from(gold["shape"])
+    base = _run_oracle(shape, W, inp, "fp32")
+    np.testing.assert_allclose(base, gold["base_logits"], rtol=1e-4, atol=2e-5)
+    toks, corrected = O.markov_sample(base, inp["anchors"], W, "fp32")
+    np.testing.assert_allclose(corrected, gold["corrected"], rtol=1e-4, atol=2e-5)
+    np.testing.assert_array_equal(toks, gold["tokens"])
+
+
+@pytest.mark.parametrize("stem", ["draft_small_ref", "draft_small_gqa5_s64_w512"])
+def test_draft_pass_bf16_matches_reference(golden_dir, stem):
+    """bf16 mode: identical rounding points; only the fp32 accumulation order
+    differs, so an intermediate may land one bf16 step away and the difference
+    propagates.  Bound: one bf16 step at the largest logit magnitude."""
+    W, inp = _small_inputs(golden_dir, stem)
+    gold = _load(golden_dir, f"{stem}_bf16")
+    shape = _shape_from(gold["shape"])
+    base = _run_oracle(shape, W, inp, "bf16")
+    ref = O.from_bf16_bits(gold["base_logits"])
+    step = 2.0 ** (np.floor(np.log2(np.abs(ref).max())) - 7)
+    assert np.abs(base - ref).max() <= step
+    assert (base == ref).mean() > 0.5
+    toks, _ = O.markov_sample(base, inp["anchors"], W, "bf16")
+    np.testing.assert_array_equal(toks, gold["tokens"])
+
+
+@pytest.mark.parametrize("tag", ["fp32", "bf16"])
+def test_draft_pass_cfg1_shape_matches_reference(golden_dir, tag):
+    """Config-1 dimensions (H=2560, Hq/Hkv=32/8, I=9728, V=151936, S=64, W=512)
+    with the reference's 7 drafter rows; inputs regenerated from the seeds."""
+    import torch
+    from longspark_b200.synthetic import make_views, make_weights
+
+    gold = _load(golden_dir, f"draft_cfg1_p7_{tag}")
+    shape = _shape_from(gold["shape"])
+    Wt = make_weights(shape, seed=int(gold["seed"]), norm_jitter=float(gold["norm_jitter"]))
+    W = {k: v.float().numpy() for k, v in Wt.items()}
+    del Wt
+    v = make_views(shape, 1, [int(c) for c in gold["contexts"]], seed=int(gold["seed"]) + 1)
+    inp = dict(kv_k=v["kv_k"].float().numpy(), kv_v=v["kv_v"].float().numpy(),
+               table=v["page_table"].numpy(), seq_lens=v["seq_lens"].numpy(),
+               hidden=v["hidden"].float().numpy(), anchors=v["anchors"].numpy(),
+               summary_out=v["summary_out"].numpy())
+    base = _run_oracle(shape, W, inp, tag)
+    ids = gold["base_top_ids"]
+    vals = np.take_along_axis(base, ids, axis=-1)
+    tol = 2e-4 if tag == "fp32" else 0.07
+    np.testing.assert_allclose(vals, gold["base_top_values"], rtol=0, atol=tol)
+    toks, _ = O.markov_sample(base, inp["anchors"], W, tag)
+    np.testing.assert_array_equal(toks, gold["tokens"])
+
+
+def test_accept_lengths():
+    t = np.array([[5, 6, 7, 8], [1, 2, 3, 4], [9, 9, 9, 9]])
+    d = np.array([[5, 6, 0], [0, 2, 3], [9, 9, 9]])
+    acc, bonus = O.accept_lengths(t, d)
+    np.testing.assert_array_equal(acc, [2, 0, 3])
+    np.testing.assert_array_equal(bonus, [7, 1, 9])
+
+
+def test_prefill_plus_increments_equals_full_prefix():
+    """Folding rows one round at a time equals scanning the whole prefix."""
+    rng = np.random.default_rng(3)
+    hq, hkv, s, d, T = 8, 2, 16, 128, 200
+    q = O.bf16_round(rng.standard_normal((hq, s, d)).astype(np.float32) * 0.3)
+    K = O.bf16_round(rng.standard_normal((T, hkv, d)).astype(np.float32))
+    V = O.bf16_round(rng.standard_normal((T, hkv, d)).astype(np.float32))
+    out, lse = O.full_prefix_state(q, K, V, 120, chunk=32)
+    pos = 120
+    for c in (1, 16, 7, 16, 16, 4):
+        keys = np.zeros((1, 16, hkv, d), np.float32)
+        vals = np.zeros_like(keys)
+        keys[0, :c], vals[0, :c] = K[pos:pos + c], V[pos:pos + c]
+        sc = O.position_scores(q[None], keys, d ** -0.5)
+        o, l = O.merge_accepted(out[None], lse[None], sc, vals, np.array([c]))
+        out, lse = o[0], l[0]
+        pos += c
+    ref_out, ref_lse = O.full_prefix_state(q, K, V, pos)
+    np.testing.assert_allclose(out, ref_out, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(lse, ref_lse, rtol=1e-5, atol=1e-5)
