@@ -1,0 +1,276 @@
+/*
+ * longspark_b200 — C ABI of the B200 (sm_100a) drafting hot path of LongSpark.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*), launches asynchronously on that stream, and
+ * returns an LS_* status.  Nothing here allocates device memory: scratch space
+ * is a caller-provided workspace whose size the *_workspace_bytes queries
+ * report, and whose counter region must be zeroed once after allocation (the
+ * kernels leave it zeroed again).  Errors that can only be seen on the device
+ * (bounded waits that gave up, out-of-range indices) are written to an
+ * optional device status word (int, 0 = ok) the caller reads after a sync.
+ *
+ * Reference interfaces replaced (paths relative to the LongSpark project):
+ *   SP = vendor/sglang/python/sglang/srt/speculative/
+ *   SF = vendor/specforge/modeling/draft/
+ *   LS = src/longspark/
+ */
+#ifndef LONGSPARK_B200_H
+#define LONGSPARK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LS_API __attribute__((visibility("default")))
+#else
+#define LS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LS_OK 0
+#define LS_ERR_INVALID 1     /* bad shape / pointer / alignment argument      */
+#define LS_ERR_CUDA 2        /* a CUDA runtime or driver call failed          */
+#define LS_ERR_UNSUPPORTED 3 /* shape outside what the kernels implement      */
+#define LS_ERR_WORKSPACE 4   /* workspace too small                           */
+
+/* GEMM epilogues (what is written for out[token, feature]). */
+#define LS_EPI_STORE 0      /* bf16(acc)                                            */
+#define LS_EPI_SILU 1       /* bf16(silu(bf16(acc)))    (Linear -> SiLU)            */
+#define LS_EPI_RESIDUAL 2   /* bf16(residual + bf16(acc))                           */
+#define LS_EPI_QKV 3        /* per-head q/k RMSNorm + RoPE, v stored as is          */
+#define LS_EPI_GATEUP 4     /* bf16(bf16(silu(gate)) * up), gate/up rows interleaved */
+#define LS_EPI_LMHEAD 5     /* bf16 logits + per-128-row tile (max, argmax)         */
+#define LS_EPI_MARKOV_ADD 6 /* bf16(base + bf16(acc))                               */
+
+/* Library version (major*10000 + minor*100 + patch). */
+LS_API int ls_version(void);
+
+/* Human-readable text of the last host-side error on this thread. */
+LS_API const char* ls_last_error(void);
+
+/* Number of SMs of the current device (grid sizing of the persistent kernels). */
+LS_API int ls_device_sm_count(void);
+
+/* ------------------------------------------------------------------------- */
+/* Dense projections: out = epilogue(x[rows, k] . w[n_out, k]^T)             */
+/* Replaces the cuBLAS GEMMs behind nn.Linear / SGLang QKVParallelLinear,     */
+/* MergedColumnParallelLinear, RowParallelLinear of the drafter              */
+/* (SP global16_native_draft_executor.py:141-165,435-457), the state-encoder  */
+/* and shifted-input FeedForwards (SF draftfreekv.py:1498-1516), the bf16     */
+/* vocabulary projection (SP global16_markov_precision.py:79-130) and the     */
+/* Markov bias projection (SF draftfreekv.py:2346-2356).                      */
+/* tcgen05/TMEM tensor cores, TMA loads, stream-K over (tile, k-block).       */
+/* ------------------------------------------------------------------------- */
+typedef struct ls_gemm_args {
+  const void* x;        /* [rows, x_ld] bf16, K contiguous (activations)       */
+  const void* w;        /* [n_out, k] bf16, K contiguous (weights)             */
+  int rows;             /* tokens                                              */
+  int k;                /* reduction length, multiple of 64                    */
+  int n_out;            /* output features, multiple of 128                    */
+  int x_ld;             /* row pitch of x in elements (multiple of 8, >= k)    */
+  int epilogue;         /* LS_EPI_*                                            */
+  void* out;            /* bf16 output                                         */
+  int out_ld;           /* row pitch of out in elements                        */
+  const void* residual; /* LS_EPI_RESIDUAL: bf16 [rows, res_ld]; may alias out */
+  int res_ld;
+  int q_heads;          /* LS_EPI_QKV: tiles [0,q) are q heads, [q,q+kv) k heads */
+  int kv_heads;
+  const void* q_norm_w; /* [128] bf16                                          */
+  const void* k_norm_w; /* [128] bf16                                          */
+  float norm_eps;
+  const int* positions; /* [rows] int32 RoPE positions                          */
+  const float* inv_freq;/* [64] fp32 RoPE inverse frequencies                  */
+  float* tile_max;      /* LS_EPI_LMHEAD: [rows, n_out/128] fp32                */
+  int* tile_arg;        /* LS_EPI_LMHEAD: [rows, n_out/128] int32 (vocab index) */
+  const void* base;     /* LS_EPI_MARKOV_ADD: bf16 [rows, base_ld]              */
+  int base_ld;
+  int* status;          /* optional device status word                          */
+} ls_gemm_args;
+
+LS_API size_t ls_gemm_workspace_bytes(int rows, int k, int n_out);
+LS_API int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------------------- */
+/* (a) View refresh                                                          */
+/* ------------------------------------------------------------------------- */
+
+/* Scores of the S learned summary queries against new target K rows.
+ * Replaces cache_position_scores / reference_position_scores
+ * (SP global16_raw256_incremental.py:50-87, 400-456) and the GQA-5 variant
+ * (LS patches/gqa5_attention.py:17-63); S, V and the GQA group are parameters.
+ * query [batch, q_heads, slots, 128] bf16 (strides in elements, the batch
+ * stride may be 0 for a shared query); new_keys [batch, rows, kv_heads, 128]
+ * bf16 contiguous; out [batch, q_heads, slots, rows] fp32 contiguous. */
+LS_API int ls_position_scores(void* stream, const void* query, long long q_stride_b, long long q_stride_h,
+                       const void* new_keys, float* out, int batch, int q_heads, int kv_heads,
+                       int slots, int rows, float softmax_scale);
+
+/* Online-softmax merge of the first accept_lens[b] value rows into the fp32
+ * (output, lse) state, in place on the slot pool.  Replaces
+ * merge_accepted_positions_ / reference_merge_accepted_positions
+ * (SP global16_raw256_incremental.py:90-166, 459-584).
+ * state_out [capacity, q_heads, slots, 128] fp32 with row pitch state_stride
+ * elements between pool entries; state_lse [capacity, q_heads, slots] fp32
+ * with pitch lse_stride; scores [batch, q_heads, slots, rows] fp32;
+ * values: value rows addressed as value_rows + (locs[b*rows + r] * kv_heads + h) * 128
+ * (bf16); accept_lens [batch] int32 in [1, rows]; state_slots [batch] int32
+ * (NULL = identity). */
+LS_API int ls_merge_accepted(void* stream, float* state_out, long long state_stride, float* state_lse,
+                      long long lse_stride, const float* scores, const void* value_rows,
+                      const long long* locs, const int* accept_lens, const int* state_slots,
+                      int batch, int q_heads, int kv_heads, int slots, int rows, int* status);
+
+/* Fused view refresh over all tapped layers: for each request b it reads the
+ * commit_lens[b] newly committed K/V rows at positions
+ * [seq_lens[b]-commit_lens[b], seq_lens[b]) straight from the paged KV pool,
+ * scores them against the learned summary queries and folds them into the
+ * fp32 (output, lse) summary state of pool slot slots[b].  Replaces the
+ * per-tapped-layer loop of LongSparkDraft._update_delta (LS engine/draft.py:215-260).
+ * kv_k/kv_v: [tap_layers, pages, 16, kv_heads, 128] bf16; page_table
+ * [batch, table_stride] int32 (logical page p of request b at
+ * page_table[b*table_stride + (ring_pages ? p % ring_pages : p)]);
+ * learned_query [tap_layers, q_heads, slots, 128] bf16;
+ * state_out [capacity, tap_layers, q_heads, slots, 128] fp32;
+ * state_lse [capacity, tap_layers, q_heads, slots] fp32. */
+typedef struct ls_refresh_args {
+  const void* kv_k;
+  const void* kv_v;
+  long long pool_pages;  /* pages per tapped layer in the pool */
+  const int* page_table;
+  int table_stride;
+  int ring_pages;
+  const int* seq_lens;    /* committed length after this commit */
+  const int* commit_lens; /* rows committed this round, in [1, max_commit] */
+  const int* slots;
+  const void* learned_query;
+  float* state_out;
+  float* state_lse;
+  int capacity;           /* entries in the state pools (slots are checked against it) */
+  int batch, tap_layers, q_heads, kv_heads, slots_per_head, max_commit;
+  float softmax_scale;
+  int* status;
+} ls_refresh_args;
+
+LS_API int ls_refresh_views(void* stream, const ls_refresh_args* a);
+
+/* Copy packet K/V rows ([tap_layers, total_rows, kv_heads, 128] bf16, request b
+ * owning rows [row_offsets[b], row_offsets[b] + counts[b])) into the paged pool
+ * at positions [seq_lens[b]-counts[b], seq_lens[b]) through the page table, and
+ * the boundary hidden state last_hidden [batch, tap_layers*hidden] into
+ * hidden_pool[slots[b]].  Replaces the ring scatter of LongSparkDraft.update /
+ * _update_delta (LS engine/draft.py:207-212, 257-260). */
+LS_API int ls_window_scatter(void* stream, const void* keys, const void* values, long long total_rows,
+                      const int* row_offsets, const int* counts, const int* seq_lens, void* kv_k,
+                      void* kv_v, long long pool_pages, const int* page_table, int table_stride,
+                      int ring_pages, const void* last_hidden, void* hidden_pool, int capacity, const int* slots,
+                      int batch, int tap_layers, int kv_heads, int hidden, int* status);
+
+/* ------------------------------------------------------------------------- */
+/* (b) Drafter attention over [summary | window | local rows]                */
+/* Replaces Global16Raw256PagedDraftContext.attend (SP global16_raw256.py:   */
+/* 1431-1647) and fused_global_local_raw_attention                           */
+/* (SP global16_raw256_draft_all_attention.py:51-410).                       */
+/* ------------------------------------------------------------------------- */
+typedef struct ls_attention_args {
+  const void* qkv;      /* [batch*block, (q_heads + 2*kv_heads)*128] bf16: rotated q | rotated k | v */
+  int block;            /* P, drafter rows per request (<= 16)                    */
+  const void* kv_k;     /* one tapped layer: [pages, 16, kv_heads, 128] bf16      */
+  const void* kv_v;
+  long long pool_pages; /* page ids are checked against it                        */
+  const int* page_table;
+  int table_stride;
+  int ring_pages;
+  const int* seq_lens;  /* committed length; the window is the last min(len, W) rows */
+  int window;           /* W */
+  const void* learned_query; /* one tapped layer: [q_heads, slots, 128] bf16       */
+  const float* state_out;    /* [capacity, ...]: entry of request b at state_out + slots[b]*state_stride */
+  long long state_stride;
+  const int* slots;
+  int capacity;         /* entries in the state pool                              */
+  int slots_per_head;   /* S */
+  int batch, q_heads, kv_heads;
+  float softmax_scale;
+  void* out;            /* [batch*block, q_heads*128] bf16 */
+  int* status;
+} ls_attention_args;
+
+LS_API size_t ls_attention_workspace_bytes(int batch, int q_heads, int kv_heads, int window, int slots_per_head);
+LS_API int ls_draft_attention(void* stream, const ls_attention_args* a, void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------------------- */
+/* Elementwise pieces of the drafter pass                                     */
+/* ------------------------------------------------------------------------- */
+
+/* RMSNorm over rows of length n.  mode 0: SpecForge/HF rounding
+ * bf16(w * bf16(x*rstd)) (SF draftfreekv.py:1518-1530); mode 1: F.rms_norm
+ * rounding bf16(x*rstd*w) (target final norm, SF draftfreekv.py:3607-3647). */
+LS_API int ls_rmsnorm(void* stream, const void* x, int x_ld, const void* w, void* out, int out_ld, int rows,
+               int n, float eps, int mode);
+
+/* ParallelShiftedInput input rows (SF draftfreekv.py:1692-1739):
+ * out[b*block + i] = [bf16(embed[tok_i] + pos_emb[i]) | latest[b]],
+ * tok_0 = anchors[b], tok_i = mask_token_id for i > 0.  out is [batch*block, 2*hidden].
+ * When positions != NULL also writes the RoPE positions of the block rows,
+ * positions[b*block + i] = seq_lens[b] + i (SF draftfreekv.py:3259-3263). */
+LS_API int ls_shifted_input(void* stream, const long long* anchors, const int* seq_lens, int* positions,
+                            const void* embed, const void* pos_emb, const void* latest, void* out, int batch,
+                            int block, int hidden, int vocab, int mask_token_id, int* status);
+
+/* Gather rows: out[b] = src[idx[b]] (row_bytes each, 16-byte multiples);
+ * indices outside [0, src_rows) are recorded in *status and the row is zeroed. */
+LS_API int ls_gather_rows(void* stream, const void* src, long long src_rows, const int* idx, void* out, int rows,
+                          long long row_bytes, int* status);
+
+/* ------------------------------------------------------------------------- */
+/* Greedy proposal tokens and the accept check                               */
+/* ------------------------------------------------------------------------- */
+
+/* Greedy Markov chain over bf16 base logits (DSparkVanillaMarkovHead.
+ * sample_block_tokens at temperature 0, SF draftfreekv.py:2366-2407; without a
+ * Markov head base_logits.argmax(-1), :3545-3578): for t in [0, block):
+ * tok_t = argmax_v bf16(base[t, v] + bf16(w2[v] . w1[prev])), prev = tok_{t-1}
+ * (anchors for t = 0), lowest index on ties.  Candidates are restricted to
+ * tokens whose base logit is within a rigorous bound of the row maximum
+ * (Cauchy-Schwarz on w2_row_bound * |w1[prev]|); the result is identical to
+ * the full-vocabulary scan.  w1 == NULL: no Markov head.
+ * base: [batch*block, vocab] bf16; tile_max/tile_arg: [batch*block, vocab/128]
+ * from the LS_EPI_LMHEAD epilogue.  tokens [batch, block] int64.  When
+ * target != NULL ([batch, target_ld] int64) also writes accept_out [batch]
+ * (greedy accepted-prefix length, LS engine/target.py:472-477). */
+typedef struct ls_markov_args {
+  const void* base;
+  const float* tile_max;
+  const int* tile_arg;
+  const void* w1;            /* [vocab, rank] bf16 or NULL */
+  const void* w2;            /* [vocab, rank] bf16 */
+  const float* w2_row_bound; /* device fp32, >= max_v ||w2[v]||_2 (ls_row_norm_bound) */
+  int rank;
+  const long long* anchors;  /* [batch] */
+  long long* tokens;         /* [batch, block] */
+  const long long* target;   /* optional [batch, target_ld] */
+  int target_ld;
+  long long* accept_out;     /* optional [batch] */
+  int batch, block, vocab;
+  int* status;
+} ls_markov_args;
+
+LS_API int ls_markov_argmax(void* stream, const ls_markov_args* a);
+
+/* Greedy accept check: accept[b] = number of leading i < block with
+ * target[b, i] == draft[b, i] (LS engine/target.py:472-477). */
+LS_API int ls_accept(void* stream, const long long* target, int target_ld, const long long* draft, long long* accept,
+              int batch, int block);
+
+/* Row-norm bound of a [vocab, rank] bf16 matrix: writes max_v ||m[v]||_2 * (1 + 1e-6)
+ * to *out (device fp32). */
+LS_API int ls_row_norm_bound(void* stream, const void* m, int vocab, int rank, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LONGSPARK_B200_H */

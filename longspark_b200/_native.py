@@ -1,0 +1,110 @@
+"""ctypes binding of the C ABI declared in ``include/longspark_b200.h``.
+
+The shared library is built in-tree by ``longspark_b200.build``.  Loading is
+strict: if the library is missing or a symbol is absent, ``lib()`` raises —
+there is no CPU or PyTorch fallback behind any entry point of this package.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_native" / "liblongspark_b200.so"
+
+LS_OK = 0
+EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_QKV, EPI_GATEUP, EPI_LMHEAD, EPI_MARKOV_ADD = range(7)
+
+vp = C.c_void_p
+i32 = C.c_int
+i64 = C.c_longlong
+f32 = C.c_float
+sz = C.c_size_t
+
+
+class GemmArgs(C.Structure):
+    _fields_ = [("x", vp), ("w", vp), ("rows", i32), ("k", i32), ("n_out", i32), ("x_ld", i32),
+                ("epilogue", i32), ("out", vp), ("out_ld", i32), ("residual", vp), ("res_ld", i32),
+                ("q_heads", i32), ("kv_heads", i32), ("q_norm_w", vp), ("k_norm_w", vp), ("norm_eps", f32),
+                ("positions", vp), ("inv_freq", vp), ("tile_max", vp), ("tile_arg", vp), ("base", vp),
+                ("base_ld", i32), ("status", vp)]
+
+
+class RefreshArgs(C.Structure):
+    _fields_ = [("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("page_table", vp), ("table_stride", i32),
+                ("ring_pages", i32), ("seq_lens", vp), ("commit_lens", vp), ("slots", vp),
+                ("learned_query", vp), ("state_out", vp), ("state_lse", vp), ("capacity", i32), ("batch", i32),
+                ("tap_layers", i32), ("q_heads", i32), ("kv_heads", i32), ("slots_per_head", i32),
+                ("max_commit", i32), ("softmax_scale", f32), ("status", vp)]
+
+
+class AttentionArgs(C.Structure):
+    _fields_ = [("qkv", vp), ("block", i32), ("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("page_table", vp),
+                ("table_stride", i32), ("ring_pages", i32), ("seq_lens", vp), ("window", i32),
+                ("learned_query", vp), ("state_out", vp), ("state_stride", i64), ("slots", vp),
+                ("capacity", i32), ("slots_per_head", i32), ("batch", i32), ("q_heads", i32), ("kv_heads", i32),
+                ("softmax_scale", f32), ("out", vp), ("status", vp)]
+
+
+class MarkovArgs(C.Structure):
+    _fields_ = [("base", vp), ("tile_max", vp), ("tile_arg", vp), ("w1", vp), ("w2", vp),
+                ("w2_row_bound", vp), ("rank", i32), ("anchors", vp), ("tokens", vp), ("target", vp),
+                ("target_ld", i32), ("accept_out", vp), ("batch", i32), ("block", i32), ("vocab", i32),
+                ("status", vp)]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "ls_version": (i32, []),
+    "ls_last_error": (C.c_char_p, []),
+    "ls_device_sm_count": (i32, []),
+    "ls_gemm_workspace_bytes": (sz, [i32, i32, i32]),
+    "ls_gemm": (i32, [vp, C.POINTER(GemmArgs), vp, sz]),
+    "ls_position_scores": (i32, [vp, vp, i64, i64, vp, vp, i32, i32, i32, i32, i32, f32]),
+    "ls_merge_accepted": (i32, [vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "ls_refresh_views": (i32, [vp, C.POINTER(RefreshArgs)]),
+    "ls_window_scatter": (i32, [vp, vp, vp, i64, vp, vp, vp, vp, vp, i64, vp, i32, i32, vp, vp, i32, vp, i32,
+                                i32, i32, i32, vp]),
+    "ls_attention_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+    "ls_draft_attention": (i32, [vp, C.POINTER(AttentionArgs), vp, sz]),
+    "ls_rmsnorm": (i32, [vp, vp, i32, vp, vp, i32, i32, i32, f32, i32]),
+    "ls_shifted_input": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "ls_gather_rows": (i32, [vp, vp, i64, vp, vp, i32, i64, vp]),
+    "ls_markov_argmax": (i32, [vp, C.POINTER(MarkovArgs)]),
+    "ls_accept": (i32, [vp, vp, i32, vp, vp, i32, i32]),
+    "ls_row_norm_bound": (i32, [vp, vp, i32, i32, vp]),
+}
+
+_lib = None
+
+
+class NativeError(RuntimeError):
+    pass
+
+
+def lib():
+    """The loaded native library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        path = Path(os.environ.get("LONGSPARK_B200_LIB", LIB_PATH))
+        if not path.exists():
+            raise NativeError(f"native library not found at {path}; build it with "
+                              "`python -m longspark_b200.build` (there is no fallback path)")
+        handle = C.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)  # AttributeError if a declared symbol is missing
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(rc, what=""):
+    if rc != LS_OK:
+        msg = lib().ls_last_error().decode(errors="replace")
+        raise NativeError(f"{what or 'native call'} failed (status {rc}): {msg}")
+
+
+def call(name, *args):
+    check(getattr(lib(), name)(*args), name)

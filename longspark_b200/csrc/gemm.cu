@@ -1,0 +1,580 @@
+// Dense projections of the drafting round on the 5th-generation tensor cores.
+//
+//   out[token, feature] = epilogue( sum_k x[token, k] * w[feature, k] )
+//
+// Swap-AB: the weight matrix is the 128-row MMA "A" operand and the few tokens
+// of a draft block (16 at batch 1) are the N dimension, so a batch-1 round
+// streams every weight byte exactly once through TMA at full HBM rate while
+// tcgen05.mma (M=128, N=16..256, K=16) accumulates in TMEM.
+//
+// Work split: stream-K over the linear space of (tile, 64-wide k-block)
+// units.  Each persistent CTA takes a contiguous, equal share of units, so all
+// SMs stream the same number of weight bytes whatever the matrix shape.  A
+// tile covered by several CTAs is reduced by the last CTA to finish it
+// (per-tile arrival counter), which sums the fp32 partials in a fixed order —
+// results do not depend on timing.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
+// TMEM owner, warps 2-5 = epilogue (TMEM -> registers -> fused epilogue).
+#include "common.cuh"
+#include "host_common.h"
+
+#include <algorithm>
+
+namespace ls {
+
+constexpr int GEMM_THREADS = 192;
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
+constexpr int EPI_SCRATCH_BYTES = 128 * 17 * 4 + 2 * 4 * 16 * 4 + 64;
+
+struct GemmKernelParams {
+  ls_gemm_args a;
+  int bn;            // token tile (multiple of 16, <= 256)
+  int n_tiles;       // token tiles
+  int m_tiles;       // feature tiles (n_out / 128)
+  int kb;            // k-blocks per tile
+  long long units;   // tiles * kb
+  int grid;          // CTAs
+  int stages;
+  uint32_t tmem_cols;
+  float* partials;   // [grid * 2][bn][128]
+  int* counters;     // [tiles]
+};
+
+__device__ __forceinline__ long long unit_begin(long long c, long long units, long long grid) {
+  return (c * units) / grid;
+}
+__device__ __forceinline__ int cta_of_unit(long long u, long long units, long long grid) {
+  return static_cast<int>(((u + 1) * grid - 1) / units);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Final epilogue on a 16-token chunk: thread `r` owns feature row r of the
+// 128-row tile and v[j] = fp32 accumulator for token n0 + j.
+// ---------------------------------------------------------------------------
+struct EpiScratch {
+  float xch[128][17];
+  float red_v[4][16];
+  int red_i[4][16];
+  int flag;
+};
+
+__device__ void final_epilogue(const GemmKernelParams& P, int m_tile, int n0, const float* v, int r, int ew,
+                               EpiScratch* sc) {
+  const ls_gemm_args& a = P.a;
+  const int rows = a.rows;
+  bf16* out = reinterpret_cast<bf16*>(a.out);
+  switch (a.epilogue) {
+    case LS_EPI_STORE:
+    case LS_EPI_SILU:
+    case LS_EPI_RESIDUAL:
+    case LS_EPI_MARKOV_ADD: {
+      const int f = m_tile * BM + r;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int tok = n0 + j;
+        if (tok >= rows) break;
+        float y = bf16_round(v[j]);
+        if (a.epilogue == LS_EPI_SILU) {
+          y = silu_f(y);
+        } else if (a.epilogue == LS_EPI_RESIDUAL) {
+          y = y + __bfloat162float(reinterpret_cast<const bf16*>(a.residual)[(long long)tok * a.res_ld + f]);
+        } else if (a.epilogue == LS_EPI_MARKOV_ADD) {
+          y = y + __bfloat162float(reinterpret_cast<const bf16*>(a.base)[(long long)tok * a.base_ld + f]);
+        }
+        out[(long long)tok * a.out_ld + f] = __float2bfloat16_rn(y);
+      }
+      break;
+    }
+    case LS_EPI_QKV: {
+      const int head = m_tile;
+      const bool is_v = head >= a.q_heads + a.kv_heads;
+      float y[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) y[j] = bf16_round(v[j]);
+      if (!is_v) {
+        // Per-head RMSNorm over the 128 features of this tile (HF rounding),
+        // then RoPE with the rotate-half partner exchanged through shared memory.
+        float ss[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ss[j] = warp_sum(y[j] * y[j]);
+        const int lane = threadIdx.x & 31;
+        if (lane == 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) sc->red_v[ew][j] = ss[j];
+        }
+        epi_bar();
+        const bf16* nw = reinterpret_cast<const bf16*>(head < a.q_heads ? a.q_norm_w : a.k_norm_w);
+        const float wr = __bfloat162float(nw[r]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float tot = sc->red_v[0][j] + sc->red_v[1][j] + sc->red_v[2][j] + sc->red_v[3][j];
+          const float rstd = 1.0f / sqrtf(tot / 128.0f + a.norm_eps);
+          y[j] = bf16_round(bf16_round(y[j] * rstd) * wr);
+          sc->xch[r][j] = y[j];
+        }
+        epi_bar();
+        const int partner = r < 64 ? r + 64 : r - 64;
+        const float fr = a.inv_freq[r & 63];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int tok = n0 + j;
+          const float other = sc->xch[partner][j];
+          const float rot = r < 64 ? -other : other;
+          const int pos = tok < rows ? a.positions[tok] : 0;
+          const float ang = static_cast<float>(pos) * fr;
+          const float cs = bf16_round(cosf(ang));
+          const float sn = bf16_round(sinf(ang));
+          y[j] = bf16_round(bf16_round(y[j] * cs) + bf16_round(rot * sn));
+        }
+        epi_bar();  // xch/red reused by the next chunk
+      }
+      const int f = head * BM + r;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int tok = n0 + j;
+        if (tok >= rows) break;
+        out[(long long)tok * a.out_ld + f] = __float2bfloat16_rn(y[j]);
+      }
+      break;
+    }
+    case LS_EPI_GATEUP: {
+      // Rows [0, 64) of the tile are gate features, rows [64, 128) the up
+      // features of the same 64 output columns.
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sc->xch[r][j] = bf16_round(v[j]);
+      epi_bar();
+      if (r < 64) {
+        const int f = m_tile * 64 + r;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int tok = n0 + j;
+          if (tok >= rows) break;
+          const float g = bf16_round(silu_f(sc->xch[r][j]));
+          const float u = sc->xch[r + 64][j];
+          out[(long long)tok * a.out_ld + f] = __float2bfloat16_rn(g * u);
+        }
+      }
+      epi_bar();
+      break;
+    }
+    case LS_EPI_LMHEAD: {
+      const int f = m_tile * BM + r;
+      const int lane = threadIdx.x & 31;
+      float y[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        y[j] = bf16_round(v[j]);
+        const int tok = n0 + j;
+        if (tok < rows) out[(long long)tok * a.out_ld + f] = __float2bfloat16_rn(y[j]);
+      }
+      // (max, lowest index) over the 128 rows of the tile for every token.
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float bv = y[j];
+        int bi = f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0) {
+          sc->red_v[ew][j] = bv;
+          sc->red_i[ew][j] = bi;
+        }
+      }
+      epi_bar();
+      if (r < 16) {
+        const int j = r;
+        const int tok = n0 + j;
+        float bv = sc->red_v[0][j];
+        int bi = sc->red_i[0][j];
+        for (int w = 1; w < 4; ++w) {
+          const float ov = sc->red_v[w][j];
+          const int oi = sc->red_i[w][j];
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (tok < rows) {
+          a.tile_max[(long long)tok * P.m_tiles + m_tile] = bv;
+          a.tile_arg[(long long)tok * P.m_tiles + m_tile] = bi;
+        }
+      }
+      epi_bar();
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                   const __grid_constant__ GemmKernelParams P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = P.stages;
+  const int bn = P.bn;
+  const int b_stage_bytes = bn * BK * 2;
+  uint8_t* a_buf = smem;
+  uint8_t* b_buf = a_buf + S * A_STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(b_buf + S * b_stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* done_bar = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  EpiScratch* sc = reinterpret_cast<EpiScratch*>(reinterpret_cast<uint8_t*>(tmem_holder) + 64);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long G = P.grid;
+  const long long U = P.units;
+  const long long u0 = unit_begin(blockIdx.x, U, G);
+  const long long u1 = unit_begin(blockIdx.x + 1, U, G);
+  const int KB = P.kb;
+  int* status = P.a.status;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, P.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      for (long long u = u0; u < u1; ++u) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
+        const int t = static_cast<int>(u / KB);
+        const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
+        const int m_tile = t / P.n_tiles;
+        const int n_tile = t - m_tile * P.n_tiles;
+        mbar_arrive_expect_tx(&full[stage], A_STAGE_BYTES + b_stage_bytes);
+        tma_load_2d(a_buf + stage * A_STAGE_BYTES, &map_w, &full[stage], kb * BK, m_tile * BM, pol_w);
+        tma_load_2d(b_buf + stage * b_stage_bytes, &map_x, &full[stage], kb * BK, n_tile * bn, pol_x);
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (*abort_flag) {
+        // Let the copies already in flight land before the CTA exits.
+        long long n = issued < S ? issued : S;
+        int st = stage;
+        uint32_t ph = phase;
+        for (long long i = 0; i < n; ++i) {
+          if (--st < 0) {
+            st = S - 1;
+            ph ^= 1u;
+          }
+          mbar_wait(&full[st], ph, nullptr, status, LS_DEV_TIMEOUT_PRODUCER);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_bf16_f32(BM, bn);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase[2] = {0u, 0u};
+      bool ok = true;
+      long long u = u0;
+      while (u < u1 && ok) {
+        const int t = static_cast<int>(u / KB);
+        const int k0 = static_cast<int>(u - static_cast<long long>(t) * KB);
+        const int k1 = static_cast<int>((u1 - u) < (long long)(KB - k0) ? k0 + (u1 - u) : KB);
+        if (!mbar_wait(&acc_empty[acc], acc_phase[acc] ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * bn);
+        for (int kb = k0; kb < k1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status, LS_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(a_buf + stage * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(b_buf + stage * b_stage_bytes);
+          const uint64_t a_desc = sdesc_kmajor_sw128(a_addr);
+          const uint64_t b_desc = sdesc_kmajor_sw128(b_addr);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // +32 bytes along K inside the 128-byte swizzled row (encoded >> 4).
+            tc_mma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb > k0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+        acc_phase[acc] ^= 1u;
+        acc ^= 1;
+        u += k1 - k0;
+      }
+      // Drain: wait until every MMA issued by this thread has completed.
+      tc_commit(done_bar);
+      mbar_wait(done_bar, 0, nullptr, status, LS_DEV_TIMEOUT_MMA);
+    }
+  } else {
+    // ---------------- Epilogue (warps 2..5) ----------------
+    const int ew = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = ew * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase[2] = {0u, 0u};
+    long long u = u0;
+    const int t_first = static_cast<int>(u0 / KB);
+    while (u < u1) {
+      const int t = static_cast<int>(u / KB);
+      const int k0 = static_cast<int>(u - static_cast<long long>(t) * KB);
+      const int k1 = static_cast<int>((u1 - u) < (long long)(KB - k0) ? k0 + (u1 - u) : KB);
+      const bool ok_wait = mbar_wait(&acc_full[acc], acc_phase[acc], abort_flag, status, LS_DEV_TIMEOUT_EPILOGUE);
+      // All four warps agree on whether to continue.
+      if (r == 0) sc->flag = 1;
+      epi_bar();
+      if (!ok_wait) sc->flag = 0;
+      epi_bar();
+      const bool go = sc->flag != 0;
+      epi_bar();
+      if (!go) break;
+      tc_fence_after();
+      const int m_tile = t / P.n_tiles;
+      const int n_tile = t - m_tile * P.n_tiles;
+      const int n0 = n_tile * P.bn;
+      const bool full_tile = (k0 == 0 && k1 == KB);
+      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * bn);
+      if (full_tile) {
+        for (int c = 0; c < bn; c += 16) {
+          float v[16];
+          tmem_ld16(t_addr + c, v);
+          if (n0 + c < P.a.rows) final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+      } else {
+        // Partial tile: park the fp32 partial, the last contributor reduces.
+        const int slot = (t == t_first) ? 0 : 1;
+        float* part = P.partials + (static_cast<long long>(blockIdx.x) * 2 + slot) * (static_cast<long long>(bn) * BM);
+        for (int c = 0; c < bn; c += 16) {
+          float v[16];
+          tmem_ld16(t_addr + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(&part[(c + j) * BM + r], v[j]);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        __threadfence();
+        epi_bar();
+        const long long tu0 = static_cast<long long>(t) * KB;
+        const int first = cta_of_unit(tu0, U, G);
+        const int last = cta_of_unit(tu0 + KB - 1, U, G);
+        if (r == 0) {
+          const int prev = atomicAdd(&P.counters[t], 1);
+          sc->flag = (prev == last - first) ? 1 : 0;
+        }
+        epi_bar();
+        const bool reducer = sc->flag != 0;
+        epi_bar();
+        if (reducer) {
+          __threadfence();
+          for (int c = 0; c < bn; c += 16) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+            for (int q = first; q <= last; ++q) {
+              const int q_t_first = static_cast<int>(unit_begin(q, U, G) / KB);
+              const int q_slot = (q_t_first == t) ? 0 : 1;
+              const float* qp =
+                  P.partials + (static_cast<long long>(q) * 2 + q_slot) * (static_cast<long long>(bn) * BM);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += __ldcg(&qp[(c + j) * BM + r]);
+            }
+            if (n0 + c < P.a.rows) final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
+          }
+          if (r == 0) atomicExch(&P.counters[t], 0);
+        }
+      }
+      acc_phase[acc] ^= 1u;
+      acc ^= 1;
+      u += k1 - k0;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, P.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static int pick_bn(int rows) {
+  int r16 = (rows + 15) / 16 * 16;
+  return r16 > 256 ? 256 : r16;
+}
+
+static int pick_stages(int bn) {
+  const int budget = 227 * 1024 - 1024 - 256 - EPI_SCRATCH_BYTES - 512;
+  int s = budget / (A_STAGE_BYTES + bn * BK * 2);
+  return s > 12 ? 12 : s;
+}
+
+static size_t gemm_smem_bytes(int bn, int stages) {
+  return 1024 + static_cast<size_t>(stages) * (A_STAGE_BYTES + bn * BK * 2) + (2 * stages + 5) * 8 + 64 +
+         EPI_SCRATCH_BYTES;
+}
+
+struct GemmPlan {
+  int bn, n_tiles, m_tiles, kb, grid, stages;
+  long long units;
+  size_t partial_bytes, counter_bytes;
+};
+
+static GemmPlan plan_gemm(int rows, int k, int n_out) {
+  GemmPlan p{};
+  p.bn = pick_bn(rows);
+  p.n_tiles = (rows + p.bn - 1) / p.bn;
+  p.m_tiles = n_out / BM;
+  p.kb = k / BK;
+  p.units = static_cast<long long>(p.m_tiles) * p.n_tiles * p.kb;
+  const int sms = host_sm_count();
+  p.grid = static_cast<int>(std::min<long long>(sms, p.units));
+  p.stages = pick_stages(p.bn);
+  p.partial_bytes = static_cast<size_t>(p.grid) * 2 * p.bn * BM * sizeof(float);
+  p.counter_bytes = (static_cast<size_t>(p.m_tiles) * p.n_tiles * sizeof(int) + 255) / 256 * 256;
+  return p;
+}
+
+}  // namespace ls
+
+using namespace ls;
+
+extern "C" size_t ls_gemm_workspace_bytes(int rows, int k, int n_out) {
+  if (rows <= 0 || k <= 0 || n_out <= 0) return 0;
+  GemmPlan p = plan_gemm(rows, k, n_out);
+  return p.counter_bytes + p.partial_bytes;
+}
+
+extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes) {
+  if (a == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm: null args");
+  if (a->x == nullptr || a->w == nullptr || a->out == nullptr)
+    return set_error(LS_ERR_INVALID, "ls_gemm: null x/w/out");
+  if (a->rows <= 0 || a->k <= 0 || a->k % BK || a->n_out <= 0 || a->n_out % BM)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_gemm: rows>0, k%%64==0, n_out%%128==0 required (rows=%d k=%d n=%d)",
+                     a->rows, a->k, a->n_out);
+  if (a->x_ld < a->k || a->x_ld % 8)
+    return set_error(LS_ERR_INVALID, "ls_gemm: x_ld must be >= k and a multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(a->x) | reinterpret_cast<uintptr_t>(a->w)) & 15)
+    return set_error(LS_ERR_INVALID, "ls_gemm: x and w must be 16-byte aligned");
+  switch (a->epilogue) {
+    case LS_EPI_STORE:
+    case LS_EPI_SILU:
+      break;
+    case LS_EPI_RESIDUAL:
+      if (a->residual == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm: residual epilogue needs residual");
+      break;
+    case LS_EPI_QKV:
+      if (a->q_norm_w == nullptr || a->k_norm_w == nullptr || a->positions == nullptr || a->inv_freq == nullptr ||
+          a->q_heads <= 0 || a->kv_heads <= 0 || a->n_out != (a->q_heads + 2 * a->kv_heads) * BM)
+        return set_error(LS_ERR_INVALID, "ls_gemm: QKV epilogue needs norms, positions, inv_freq, matching heads");
+      break;
+    case LS_EPI_GATEUP:
+      break;
+    case LS_EPI_LMHEAD:
+      if (a->tile_max == nullptr || a->tile_arg == nullptr)
+        return set_error(LS_ERR_INVALID, "ls_gemm: LM-head epilogue needs tile_max/tile_arg");
+      break;
+    case LS_EPI_MARKOV_ADD:
+      if (a->base == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm: Markov-add epilogue needs base");
+      break;
+    default:
+      return set_error(LS_ERR_INVALID, "ls_gemm: unknown epilogue %d", a->epilogue);
+  }
+  GemmPlan p = plan_gemm(a->rows, a->k, a->n_out);
+  if (workspace == nullptr || workspace_bytes < p.counter_bytes + p.partial_bytes)
+    return set_error(LS_ERR_WORKSPACE, "ls_gemm: workspace %zu < %zu bytes", workspace_bytes,
+                     p.counter_bytes + p.partial_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return set_error(LS_ERR_INVALID, "ls_gemm: workspace must be 256-byte aligned");
+
+  CUtensorMap map_w, map_x;
+  int rc = encode_tma_2d_bf16(&map_w, a->w, a->k, a->n_out, a->k, BK, BM);
+  if (rc) return rc;
+  rc = encode_tma_2d_bf16(&map_x, a->x, a->k, a->rows, a->x_ld, BK, p.bn);
+  if (rc) return rc;
+
+  GemmKernelParams kp{};
+  kp.a = *a;
+  kp.bn = p.bn;
+  kp.n_tiles = p.n_tiles;
+  kp.m_tiles = p.m_tiles;
+  kp.kb = p.kb;
+  kp.units = p.units;
+  kp.grid = p.grid;
+  kp.stages = p.stages;
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(2 * p.bn)) cols <<= 1;
+  kp.tmem_cols = cols;
+  kp.counters = reinterpret_cast<int*>(workspace);
+  kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + p.counter_bytes);
+
+  const size_t smem = gemm_smem_bytes(p.bn, p.stages);
+  static int configured_smem = 0;
+  if (configured_smem < static_cast<int>(smem)) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(227 * 1024));
+    if (e != cudaSuccess) return set_cuda_error("ls_gemm: cudaFuncSetAttribute", e);
+    configured_smem = 227 * 1024;
+  }
+  gemm_tc_kernel<<<p.grid, GEMM_THREADS, smem, reinterpret_cast<cudaStream_t>(stream)>>>(map_w, map_x, kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("ls_gemm: launch", e);
+  return LS_OK;
+}

@@ -1,0 +1,199 @@
+"""View refresh, drafter attention and greedy sampling kernels against the oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from gpu_util import assert_bf16_close, to_np, tokens_exact_or_tied
+from longspark_b200 import _native as N
+from longspark_b200 import ops
+from longspark_b200.config import DraftShape
+from longspark_b200.synthetic import make_views
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+# --------------------------------------------------------------------------
+# (a) refresh
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("q_heads,kv_heads,slots,max_commit", [(32, 8, 16, 8), (40, 8, 16, 8), (32, 8, 256, 16),
+                                                                  (40, 8, 64, 16)])
+def test_refresh_chain_matches_oracle(q_heads, kv_heads, slots, max_commit):
+    """The reference's own protocol (tests/gpu/test_gqa5_attention.py:20-50):
+    random bf16 queries and rows, random initial state, permuted pool slots,
+    accept lengths ((arange(B) + step) % V) + 1, chained steps, tolerance 3e-5."""
+    g = torch.Generator().manual_seed(980426)
+    L, batch, steps = 2, 3, 12
+    shape = DraftShape(hidden=512, q_heads=q_heads, kv_heads=kv_heads, inter=512, vocab=1024, tap_layers=L,
+                       draft_layers=1, slots=slots, window=256, block=7, max_commit=max_commit, markov_rank=0,
+                       mask_token_id=0)
+    capacity = batch + 3
+    ctx0 = [37, 300, 1000]
+    v = make_views(shape, batch, ctx0, seed=5, extra_rows=steps * max_commit, gen=g)
+    q = torch.randn(L, q_heads, slots, 128, generator=g).to(torch.bfloat16)
+    out0 = torch.randn(capacity, L, q_heads, slots, 128, generator=g)
+    lse0 = torch.randn(capacity, L, q_heads, slots, generator=g)
+    slot_ids = torch.randperm(capacity, generator=g)[:batch].to(torch.int32)
+    dev = "cuda"
+    kv_k, kv_v, table = v["kv_k"].to(dev), v["kv_v"].to(dev), v["page_table"].to(dev)
+    st_out, st_lse, qd = out0.to(dev), lse0.to(dev), q.to(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ref_out, ref_lse = out0.numpy().copy(), lse0.numpy().copy()
+    kk, vv = O.from_bf16_bits(v["kv_k"].view(torch.int16).numpy()), O.from_bf16_bits(v["kv_v"].view(torch.int16).numpy())
+    lens = np.array(ctx0)
+    for step in range(steps):
+        commit = (np.arange(batch) + step) % max_commit + 1
+        lens = lens + commit
+        ops.refresh_views(kv_k=kv_k, kv_v=kv_v, page_table=table,
+                          seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev),
+                          commit_lens=torch.tensor(commit, dtype=torch.int32, device=dev),
+                          slots=slot_ids.to(dev), learned_query=qd, state_out=st_out, state_lse=st_lse,
+                          max_commit=max_commit, status=status)
+        # oracle: the same rows gathered from the pool
+        nk = np.zeros((L, batch, max_commit, kv_heads, 128), np.float32)
+        nv = np.zeros_like(nk)
+        for b in range(batch):
+            for r in range(commit[b]):
+                pos = lens[b] - commit[b] + r
+                page = int(v["page_table"][b, pos // 16])
+                nk[:, b, r] = kk[:, page, pos % 16]
+                nv[:, b, r] = vv[:, page, pos % 16]
+        ref_out, ref_lse = O.refresh_views(ref_out, ref_lse, slot_ids.numpy(), to_np(q), nk, nv, commit,
+                                           128 ** -0.5)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    np.testing.assert_allclose(to_np(st_out), ref_out, rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(to_np(st_lse), ref_lse, rtol=3e-5, atol=3e-5)
+
+
+def test_reference_api_scores_and_merge():
+    """cache_position_scores + merge_accepted_positions_ with the reference's
+    argument conventions (fixed [B, 8] locations, page-size-one value cache)."""
+    g = torch.Generator().manual_seed(7)
+    batch, hq, hkv, s, rows = 3, 40, 8, 16, 8
+    dev = "cuda"
+    query = torch.randn(1, hq, s, 128, generator=g).to(torch.bfloat16).to(dev).expand(batch, -1, -1, -1)
+    capacity = batch + 2
+    out = torch.randn(capacity, hq, s, 128, generator=g).to(dev)
+    lse = torch.randn(capacity, hq, s, generator=g).to(dev)
+    slots = torch.tensor([4, 0, 2], dtype=torch.int32, device=dev)
+    exp_out, exp_lse = to_np(out)[[4, 0, 2]], to_np(lse)[[4, 0, 2]]
+    for step in range(4):
+        keys = torch.randn(batch, rows, hkv, 128, generator=g).to(torch.bfloat16).to(dev)
+        values = torch.randn(batch, rows, hkv, 128, generator=g).to(torch.bfloat16).to(dev)
+        sc = torch.empty(batch, hq, s, rows, device=dev)
+        ops.cache_position_scores(layer_id=0, global_query=query, new_keys=keys, output=sc,
+                                  softmax_scale=128 ** -0.5)
+        ref_sc = O.position_scores(np.broadcast_to(to_np(query[:1]), (batch, hq, s, 128)), to_np(keys), 128 ** -0.5)
+        np.testing.assert_allclose(to_np(sc), ref_sc, rtol=2e-5, atol=2e-5)
+        lens = ((torch.arange(batch) + step) % rows + 1).to(torch.int32).to(dev)
+        locs = torch.arange(batch * rows, device=dev).reshape(batch, rows)
+        ops.merge_accepted_positions_(state_output=out, state_lse=lse, position_scores=sc,
+                                      value_cache=values.reshape(batch * rows, 1, hkv, 128),
+                                      accepted_cache_locs=locs, accept_lens=lens, accept_offsets=None,
+                                      state_slots=slots)
+        exp_out, exp_lse = O.merge_accepted(exp_out, exp_lse, ref_sc, to_np(values), lens.cpu().numpy())
+    np.testing.assert_allclose(to_np(out)[[4, 0, 2]], exp_out, rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(to_np(lse)[[4, 0, 2]], exp_lse, rtol=3e-5, atol=3e-5)
+
+
+# --------------------------------------------------------------------------
+# (b) attention
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("q_heads,kv_heads,slots,window,block,contexts", [
+    (8, 2, 16, 256, 7, (300, 100)),
+    (32, 8, 64, 512, 15, (4096,)),
+    (40, 8, 256, 2048, 15, (5000, 1999)),
+    (32, 8, 256, 1024, 15, (1024, 17, 3000)),
+])
+def test_attention_matches_oracle(q_heads, kv_heads, slots, window, block, contexts):
+    g = torch.Generator().manual_seed(11)
+    batch = len(contexts)
+    shape = DraftShape(hidden=512, q_heads=q_heads, kv_heads=kv_heads, inter=512, vocab=1024, tap_layers=1,
+                       draft_layers=1, slots=slots, window=window, block=block, max_commit=block + 1,
+                       markov_rank=0, mask_token_id=0)
+    v = make_views(shape, batch, list(contexts), seed=3, gen=g)
+    qkv = torch.randn(batch * block, (q_heads + 2 * kv_heads) * 128, generator=g).to(torch.bfloat16)
+    qg = (0.3 * torch.randn(q_heads, slots, 128, generator=g)).to(torch.bfloat16)
+    dev = "cuda"
+    out = torch.empty(batch * block, q_heads * 128, dtype=torch.bfloat16, device=dev)
+    ws = torch.zeros(ops.attention_workspace_bytes(batch, q_heads, kv_heads, window, slots), dtype=torch.uint8,
+                     device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    slots_t = torch.arange(batch, dtype=torch.int32, device=dev)
+    ops.draft_attention(qkv=qkv.to(dev), block=block, kv_k=v["kv_k"][0].to(dev), kv_v=v["kv_v"][0].to(dev),
+                        page_table=v["page_table"].to(dev), seq_lens=v["seq_lens"].to(dev), window=window,
+                        learned_query=qg.to(dev), state_out=v["summary_out"][:, 0].to(dev), slots=slots_t, out=out,
+                        workspace=ws, q_heads=q_heads, kv_heads=kv_heads, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    x = to_np(qkv).reshape(batch, block, -1, 128)
+    q = x[:, :, :q_heads].transpose(0, 2, 1, 3)
+    k = x[:, :, q_heads:q_heads + kv_heads].transpose(0, 2, 1, 3)
+    vl = x[:, :, q_heads + kv_heads:].transpose(0, 2, 1, 3)
+    views = O.build_views(to_np(v["kv_k"]), to_np(v["kv_v"]), v["page_table"].numpy(), v["seq_lens"].numpy(),
+                          v["summary_out"].numpy(), to_np(qg)[None], window, 1)
+    w0 = views[0]
+    ref = O.attend(q, k, vl, w0["qg"], w0["summary_out"], w0["win_k"], w0["win_v"], w0["win_len"], "bf16")
+    ref = ref.transpose(0, 2, 1, 3).reshape(batch * block, q_heads * 128)
+    assert_bf16_close(to_np(out), ref, steps=2.0, exact_frac=0.80, what="attention")
+
+
+# --------------------------------------------------------------------------
+# greedy chain + accept
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("rank", [0, 64, 256])
+def test_markov_chain_matches_oracle(rank):
+    g = torch.Generator().manual_seed(21 + rank)
+    batch, block, vocab = 3, 15, 151936
+    dev = "cuda"
+    base = (1.3 * torch.randn(batch * block, vocab, generator=g)).to(torch.bfloat16)
+    # plant exact ties and near-ties in a few rows
+    base[0, 77] = base[0].max()
+    base[1, 5] = base[1].max()
+    base[1, 90000] = base[1].max()
+    bl = base.to(dev)
+    tmax = torch.empty(batch * block, vocab // 128, device=dev)
+    targ = torch.empty(batch * block, vocab // 128, dtype=torch.int32, device=dev)
+    lv = to_np(bl).reshape(batch * block, vocab // 128, 128)
+    tmax.copy_(torch.from_numpy(lv.max(-1)))
+    targ.copy_(torch.from_numpy((lv.argmax(-1) + np.arange(vocab // 128)[None] * 128).astype(np.int32)))
+    anchors = torch.randint(0, vocab, (batch,), generator=g)
+    W = {}
+    w1 = w2 = bound = None
+    if rank:
+        w1 = (0.02 * torch.randn(vocab, rank, generator=g)).to(torch.bfloat16).to(dev)
+        w2 = (0.02 * torch.randn(vocab, rank, generator=g)).to(torch.bfloat16).to(dev)
+        bound = torch.zeros(1, device=dev)
+        ops.row_norm_bound(w2, bound)
+        W = {"parallel_markov_head.markov_w1.weight": to_np(w1), "parallel_markov_head.markov_w2.weight": to_np(w2)}
+    tokens = torch.empty(batch, block, dtype=torch.int64, device=dev)
+    target = torch.randint(0, vocab, (batch, block + 1), generator=g)
+    acc = torch.empty(batch, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.markov_argmax(base=bl, tile_max=tmax, tile_arg=targ, anchors=anchors.to(dev), tokens=tokens, block=block,
+                      w1=w1, w2=w2, w2_bound=bound, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    gt = tokens.cpu().numpy()
+    # oracle, teacher-forced on the GPU's own chain so a flipped near-tie does not cascade
+    toks, corrected = O.markov_sample(to_np(bl).reshape(batch, block, vocab), anchors.numpy(), W, "bf16", forced=gt)
+    ties = tokens_exact_or_tied(gt, corrected, what=f"markov rank {rank}")
+    assert ties <= 2
+    # accept check against a target that agrees on a known prefix
+    k = torch.tensor([0, 4, block])
+    tgt = torch.where(torch.arange(block + 1)[None] < k[:, None], torch.cat([tokens.cpu(), tokens.cpu()[:, -1:]], 1),
+                      (torch.cat([tokens.cpu(), tokens.cpu()[:, -1:]], 1) + 1) % vocab)
+    ops.accept_lengths(tgt.to(dev), tokens, acc)
+    assert acc.cpu().tolist() == k.tolist()
+    np.testing.assert_array_equal(O.accept_lengths(tgt.numpy(), gt)[0], k.numpy())

@@ -1,0 +1,75 @@
+"""CPU checks of the C-ABI boundary: the shared library loads without a GPU and
+exports every entry point ``include/longspark_b200.h`` declares; the ctypes
+layer agrees with the header; host-side argument validation raises."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "longspark_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^LS_API\s+[\w\s\*]+?\b(ls_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from longspark_b200 import build
+    build.build()
+    from longspark_b200 import _native
+    return _native.lib()
+
+
+def test_header_declares_the_boundary():
+    syms = declared_symbols()
+    for name in ("ls_gemm", "ls_refresh_views", "ls_draft_attention", "ls_markov_argmax", "ls_accept",
+                 "ls_position_scores", "ls_merge_accepted", "ls_window_scatter"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(str(ROOT / "longspark_b200" / "_native" / "liblongspark_b200.so"))
+    missing = [s for s in declared_symbols() if not hasattr(raw, s)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_ctypes_signatures_cover_the_header(lib):
+    from longspark_b200 import _native
+    assert set(_native.SIGNATURES) == set(declared_symbols())
+
+
+def test_struct_layouts_match_the_header(lib):
+    """Field order of the ctypes structs follows the C structs."""
+    from longspark_b200 import _native as N
+    text = HEADER.read_text()
+    for cname, py in (("ls_gemm_args", N.GemmArgs), ("ls_refresh_args", N.RefreshArgs),
+                      ("ls_attention_args", N.AttentionArgs), ("ls_markov_args", N.MarkovArgs)):
+        body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
+        body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+        names = []
+        for decl in body.split(";"):
+            decl = decl.strip()
+            if not decl:
+                continue
+            head, *rest = [p.strip() for p in decl.split(",")]
+            names.append(re.findall(r"(\w+)\s*$", head)[0])
+            names += [re.findall(r"(\w+)\s*$", r)[0] for r in rest]
+        assert names == [f[0] for f in py._fields_], cname
+
+
+def test_version_and_errors_without_gpu(lib):
+    assert lib.ls_version() >= 100
+    from longspark_b200 import _native as N
+    # argument validation happens on the host, before any CUDA call
+    rc = lib.ls_gemm(None, None, None, 0)
+    assert rc == 1
+    assert b"null args" in lib.ls_last_error()
+    a = N.GemmArgs(x=16, w=16, out=16, rows=4, k=100, n_out=128, x_ld=100)
+    rc = lib.ls_gemm(None, ctypes.byref(a), None, 0)
+    assert rc == 3 and b"k%64" in lib.ls_last_error()
+    assert lib.ls_accept(None, None, 0, None, None, 1, 1) == 1
