@@ -1,0 +1,524 @@
+"""Benchmark of the LongSpark drafting round on B200 (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Workload: Qwen3-8B-shaped drafter (H=4096, 32/8 heads,
+I=12288, V=151936, 1 drafter layer, 5 tapped layers, Markov rank 256), batch 1,
+paged KV cache (page 16, shuffled page table) at 1K/8K/32K/64K/128K context,
+W=1024, S=256, 16-token verify block (anchor + 15 proposals).  A step is one
+full round: view refresh of a 16-row commit over the 5 tapped layers, the
+parallel drafter pass, the Markov greedy chain and the accept check, replayed
+as one CUDA graph.  Weights and inputs are synthetic (seeded N(0, 0.02) weights,
+N(0, 1) K/V); the 2.1 GB of weights streamed per round exceed the 126 MB L2, so
+no flush is needed between steps.  ``value`` is the headline context (128K).
+
+Multi-GPU (``torchrun --nproc-per-node N``): requests shard across GPUs with
+no cross-GPU traffic (each rank runs its own batch), so scaling is weak and
+``value`` sums the ranks' tokens over the max-over-ranks time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "draft-round latency (µs) + HBM GB/s vs ctx 1K–128K; tokens/s at 1/2/4/8 B200"
+CONTEXTS = (1024, 8192, 32768, 65536, 131072)
+HEADLINE_CTX = 131072
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sweep-steps", type=int, default=300)
+    ap.add_argument("--load-seconds", type=float, default=0.5,
+                    help="untimed load before the timed steps, so clock samples see the GPU busy")
+    ap.add_argument("--contexts", type=str, default=",".join(str(c) for c in CONTEXTS),
+                    help="comma-separated context lengths of the sweep (the headline is the largest)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend=backend, timeout=__import__("datetime").timedelta(seconds=300))
+    return rank, world, local
+
+
+def dist_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle baseline (bounded sample of the same workload)
+# ---------------------------------------------------------------------------
+
+def cpu_round_sample(shape, ctx, rounds, seed=0):
+    """Time the numpy oracle (fp32, the reference drafter's CPU path restated)
+    on ``rounds`` drafting rounds of the workload.  Returns (seconds per round,
+    threads)."""
+    import numpy as np
+    import oracle as O
+
+    rng = np.random.default_rng(seed)
+    H, Hq, Hkv, I, V, L, S, Wn = (shape.hidden, shape.q_heads, shape.kv_heads, shape.inter, shape.vocab,
+                                  shape.tap_layers, shape.slots, shape.window)
+
+    def nrm(*s, std=0.02):
+        return (rng.standard_normal(s, dtype=np.float32) * std).astype(np.float32)
+
+    W = {"draft_state_encoder.proj.net.0.weight": nrm(H, L * H), "draft_state_encoder.proj.net.2.weight": nrm(H, H),
+         "draft_state_encoder.norm.weight": np.ones(H, np.float32),
+         "parallel_shifted_input.position_embedding.weight": nrm(shape.block, H),
+         "parallel_shifted_input.proj.net.0.weight": nrm(H, 2 * H), "parallel_shifted_input.proj.net.2.weight": nrm(H, H),
+         "parallel_shifted_input.norm.weight": np.ones(H, np.float32),
+         "model.embed_tokens.weight": nrm(V, H), "lm_head.weight": nrm(V, H), "model.norm.weight": np.ones(H, np.float32),
+         "parallel_markov_head.markov_w1.weight": nrm(V, shape.markov_rank),
+         "parallel_markov_head.markov_w2.weight": nrm(V, shape.markov_rank)}
+    for j in range(shape.draft_layers):
+        p = f"parallel_qwen_layers.{j}."
+        W.update({p + "self_attn.q_proj.weight": nrm(Hq * 128, H), p + "self_attn.k_proj.weight": nrm(Hkv * 128, H),
+                  p + "self_attn.v_proj.weight": nrm(Hkv * 128, H), p + "self_attn.o_proj.weight": nrm(H, Hq * 128),
+                  p + "self_attn.q_norm.weight": np.ones(128, np.float32),
+                  p + "self_attn.k_norm.weight": np.ones(128, np.float32),
+                  p + "mlp.gate_proj.weight": nrm(I, H), p + "mlp.up_proj.weight": nrm(I, H),
+                  p + "mlp.down_proj.weight": nrm(H, I), p + "input_layernorm.weight": np.ones(H, np.float32),
+                  p + "post_attention_layernorm.weight": np.ones(H, np.float32)})
+    qg = nrm(L, Hq, S, 128)
+    win_k = rng.standard_normal((1, Hkv, Wn, 128), dtype=np.float32)
+    win_v = rng.standard_normal((1, Hkv, Wn, 128), dtype=np.float32)
+    out = nrm(1, L, Hq, S, 128, std=0.1)
+    lse = np.full((1, L, Hq, S), 10.0, np.float32)
+    new_k = rng.standard_normal((L, 1, shape.max_commit, Hkv, 128), dtype=np.float32)
+    new_v = rng.standard_normal((L, 1, shape.max_commit, Hkv, 128), dtype=np.float32)
+    hidden = rng.standard_normal((1, L, H), dtype=np.float32)
+    inv = (1.0 / (np.float32(shape.rope_theta) ** (np.arange(0, 128, 2, dtype=np.float32) / 128))).astype(np.float32)
+    osh = O.DraftShapeOracle(H, Hq, Hkv, 128, shape.block, shape.mask_token_id)
+    target = rng.integers(0, V, (1, shape.block + 1))
+    times = []
+    for _ in range(rounds):
+        t0 = time.perf_counter()
+        out, lse = O.refresh_views(out, lse, np.array([0]), qg, new_k, new_v, np.array([shape.max_commit]),
+                                   128 ** -0.5)
+        views = [dict(qg=qg[j], summary_out=out[:, j], win_k=win_k, win_v=win_v, win_len=np.array([Wn]))
+                 for j in range(shape.draft_layers)]
+        base, _ = O.draft_pass(W, osh, np.array([7]), np.array([ctx]), hidden, views, inv, "fp32")
+        toks, _ = O.markov_sample(base, np.array([7]), W, "fp32")
+        O.accept_lengths(target, toks)
+        times.append(time.perf_counter() - t0)
+    threads = os.cpu_count() or 1
+    return statistics.median(times), threads
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def build_round(shape, ctx, batch, dev, seed):
+    import torch
+    from longspark_b200.engine import DraftEngine, DraftWeights, GraphedDraft, ViewPools
+    from longspark_b200.synthetic import make_views, make_weights
+
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    W = make_weights(shape, device=dev, gen=gen)
+    v = make_views(shape, batch, ctx, device=dev, gen=gen, extra_rows=shape.max_commit)
+    pools = ViewPools(kv_k=v["kv_k"], kv_v=v["kv_v"], page_table=v["page_table"], summary_out=v["summary_out"],
+                      summary_lse=v["summary_lse"], hidden=v["hidden"])
+    eng = DraftEngine(shape, DraftWeights(shape, W, dev), pools, max_batch=batch, device=dev)
+    del W
+    g = GraphedDraft(eng, batch, with_refresh=True, with_target=True)
+    commit = torch.full((batch,), shape.max_commit, dtype=torch.int32, device=dev)
+    target = torch.randint(0, shape.vocab, (batch, shape.block + 1), device=dev, generator=gen)
+    g.load(slots=torch.arange(batch, dtype=torch.int32, device=dev), seq_lens=v["seq_lens"], anchors=v["anchors"],
+           page_table=v["page_table"], commit_lens=commit, target=target)
+    return eng, g, v
+
+
+def algorithmic_bytes(shape, eng, batch):
+    """HBM bytes a round must move (one pass over every streamed weight, the
+    summary state read+write, learned queries, window K/V, new rows)."""
+    s = shape
+    w = eng.w.nbytes()
+    refresh = s.tap_layers * (2 * s.max_commit * s.kv_heads * 128 * 2 + s.q_heads * s.slots * 128 * 2
+                              + 2 * s.q_heads * s.slots * 129 * 4)
+    attn = s.draft_layers * (2 * s.window * s.kv_heads * 128 * 2 + s.q_heads * s.slots * 128 * (4 + 2))
+    return w + batch * (refresh + attn)
+
+
+def time_graph(g, steps, warmup, world, load_seconds=0.0):
+    """Mean ms per replay over exactly ``steps`` replays (CUDA events on the
+    launching stream), after ``warmup`` replays plus, when ``load_seconds`` > 0,
+    enough extra untimed replays to keep the GPU busy that long (so clock
+    samples taken around the timed region see it under load)."""
+    import torch
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if load_seconds > 0:
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < load_seconds:
+            for _ in range(50):
+                g.replay()
+            torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    return e0.elapsed_time(e1) / steps  # ms
+
+
+def time_dominant_kernel(eng, reps=20):
+    """CUDA-event duration of the vocabulary-projection GEMM (the largest single
+    weight stream of the round) launched on the current stream with the round's
+    live buffers; returns ms per launch."""
+    import torch
+    from longspark_b200 import _native as N
+    from longspark_b200 import ops
+    b, w, s = eng.buf, eng.w, eng.shape
+    M = eng.max_batch * s.block
+
+    def launch():
+        ops.gemm(b["xn"], w.lm_head, b["logits"], workspace=eng.gemm_ws, epilogue=N.EPI_LMHEAD, rows=M,
+                 tile_max=b["tile_max"], tile_arg=b["tile_arg"])
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        launch()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def count_launches(eng, g):
+    """Kernels of one round, counted from the native calls of an eager run."""
+    from longspark_b200 import _native as N
+    counts = {"ls_draft_attention": 2, "ls_row_norm_bound": 1}
+    seen = []
+    orig = N.call
+
+    def counting(name, *args):
+        seen.append(name)
+        return orig(name, *args)
+
+    N.call = counting
+    try:
+        g._run()
+    finally:
+        N.call = orig
+    return sum(counts.get(n, 1) for n in seen)
+
+
+def e2e_api(shape, batch, steps, warmup, dev, world):
+    """Through the drop-in API: per step, the committed K/V rows, boundary hidden
+    state and metadata go host->device (pinned), ``update`` folds them,
+    ``propose`` drafts, and the tokens come back device->host."""
+    import torch
+    from longspark_b200.draft import LongSparkDraft
+    from longspark_b200.synthetic import make_weights
+
+    gen = torch.Generator(device=dev).manual_seed(7)
+    W = make_weights(shape, device=dev, gen=gen)
+    cfg = dict(draft_device=dev.index or 0, max_running_requests=batch, draft_state_gib=16.0, cuda_graph=True,
+               graph_batch_sizes=(batch,))
+    d = LongSparkDraft(cfg, weights=W, shape=shape, materialize_logits=False)
+    del W
+    L, Hkv, Hq, S, Wn = shape.tap_layers, shape.kv_heads, shape.q_heads, shape.slots, shape.window
+    ids = [f"r{i}" for i in range(batch)]
+    length = HEADLINE_CTX
+    pk = torch.randn(L, batch * Wn, Hkv, 128).to(torch.bfloat16)
+    d.update(dict(format="longspark_state_batch_v1", ids=ids, lengths=[length] * batch, commit_lens=[Wn] * batch,
+                  export_counts=[Wn] * batch, keys=pk, values=pk.clone(),
+                  last_hidden=torch.randn(batch, L, shape.hidden).to(torch.bfloat16),
+                  global_output=0.1 * torch.randn(batch, L, Hq, S, 128), global_lse=torch.full((batch, L, Hq, S), 11.0)),
+             prefill=True)
+    c = shape.max_commit
+    keys = torch.randn(L, batch * c, Hkv, 128).to(torch.bfloat16).pin_memory()
+    vals = torch.randn(L, batch * c, Hkv, 128).to(torch.bfloat16).pin_memory()
+    hid = torch.randn(batch, L, shape.hidden).to(torch.bfloat16).pin_memory()
+    anchors = torch.randint(0, shape.vocab, (batch,)).pin_memory()
+    h2d = keys.numel() * 2 + vals.numel() * 2 + hid.numel() * 2 + anchors.numel() * 8 + batch * 4 * 5
+    d2h = batch * shape.block * 8
+
+    def step():
+        nonlocal length
+        length += c
+        d.update(dict(format="longspark_state_batch_v1", ids=ids, lengths=[length] * batch, commit_lens=[c] * batch,
+                      export_counts=[c] * batch, keys=keys, values=vals, last_hidden=hid))
+        toks, _, _ = d.propose(ids, anchors, 0.0)
+        return toks.cpu()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1) / steps
+    wall = (time.perf_counter() - t0) / steps * 1e3
+    status = d.device_status()
+    return max(ms, wall), h2d, d2h, status
+
+
+def run_b200(args):
+    import torch
+    from longspark_b200.config import CFG2
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shape = CFG2.shape
+    batch = args.batch
+    peaks = {}
+    pp = ROOT / "MEASURED_PEAKS.json"
+    if pp.exists():
+        peaks = json.loads(pp.read_text())
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    # context sweep (each context its own synthetic cache; same weights seed)
+    sweep = []
+    headline = None
+    contexts = sorted(int(c) for c in args.contexts.split(","))
+    head_ctx = contexts[-1]
+    for ctx in contexts:
+        eng, g, v = build_round(shape, ctx, batch, dev, seed=1000 + rank)
+        g.capture()
+        steps = args.steps if ctx == head_ctx else args.sweep_steps
+        if ctx == head_ctx:
+            with ClockSampler(local) as clk:
+                ms = time_graph(g, steps, max(3, args.warmup), world, load_seconds=args.load_seconds)
+            ms_max = dist_max(ms, world)
+            launches = count_launches(eng, g)
+            status = eng.device_status()
+            dom_ms = time_dominant_kernel(eng)
+            abytes = algorithmic_bytes(shape, eng, batch)
+            headline = dict(ms=ms_max, clocks=clk.summary(), launches=launches, status=status, dom_ms=dom_ms,
+                            abytes=abytes, eng=eng)
+        else:
+            ms_max = dist_max(time_graph(g, steps, 3, world), world)
+            abytes = algorithmic_bytes(shape, eng, batch)
+        sweep.append({"ctx": ctx, "round_us": round(ms_max * 1e3, 1),
+                      "hbm_gbs": round(abytes / (ms_max * 1e-3) / 1e9, 1)})
+        if ctx != head_ctx:
+            del eng, g, v
+            torch.cuda.empty_cache()
+
+    ms = headline["ms"]
+    tokens_per_round = batch * shape.block
+    value = tokens_per_round * world / (ms * 1e-3)
+    eng = headline["eng"]
+    lm_bytes = eng.w.lm_head.numel() * 2 + batch * shape.block * shape.hidden * 2 + \
+        batch * shape.block * shape.vocab * 2
+    dom_gbs = lm_bytes / (headline["dom_ms"] * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "lm_head_gemm_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+
+    e2e = None
+    if not args.no_e2e:
+        del headline["eng"], eng
+        torch.cuda.empty_cache()
+        e_ms, h2d, d2h, e_status = e2e_api(shape, batch, max(5, args.steps // 2), 3, dev, world)
+        e_ms = dist_max(e_ms, world)
+        e2e = {"value": round(tokens_per_round * world / (e_ms * 1e-3), 1), "unit": "draft tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 4),
+               "path": "LongSparkDraft.update(batch packet from pinned host) + propose(T=0) + tokens.cpu()",
+               "device_status": e_status}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, threads = cpu_round_sample(shape, HEADLINE_CTX, rounds=3)
+        cpu = {"value": round(tokens_per_round / sec, 2), "unit": "draft tokens/s", "cores": threads, "kind": "port",
+               "sample": f"3 fp32 rounds of the numpy oracle at the cfg2 shapes (median {sec:.2f} s/round)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "draft tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) paged K/V, shuffled 16-row pages)",
+            "config": {"workload": "cfg2-qwen3-8b drafter round (BASELINE configs[1])", "batch_per_gpu": batch,
+                       "hidden": shape.hidden, "q_heads": shape.q_heads, "kv_heads": shape.kv_heads,
+                       "inter": shape.inter, "vocab": shape.vocab, "tap_layers": shape.tap_layers,
+                       "draft_layers": shape.draft_layers, "window": shape.window, "slots": shape.slots,
+                       "verify_block": shape.block + 1, "draft_rows": shape.block, "markov_rank": shape.markov_rank,
+                       "headline_ctx": head_ctx, "parallelism": f"request-sharded x{world}",
+                       "l2": "inputs larger than L2 (2.1 GB of weights streamed per round)",
+                       "graph": "refresh + drafter pass + Markov chain + accept in one CUDA graph"},
+            "round_latency_us": round(ms * 1e3, 1),
+            "ctx_sweep": sweep,
+            "round_hbm_gbs": round(headline["abytes"] / (ms * 1e-3) / 1e9, 1),
+            "round_algorithmic_bytes": headline["abytes"],
+            "roofline": {"bound": "hbm", "kernel": "vocabulary projection GEMM (tcgen05, LS_EPI_LMHEAD)",
+                         "achieved": round(dom_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(dom_gbs / hbm_peak, 3), "peak_source": peak_src,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": lm_bytes,
+                         "launch_ms": round(headline["dom_ms"], 4)},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": headline["launches"] * args.steps,
+            "gpu_launches_per_step": headline["launches"],
+            "device_status": headline["status"],
+            "clocks": headline["clocks"],
+            "clocks_note": "nvidia-smi every 100 ms from 0.5 s of untimed load before the timed steps to their end",
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference arm: the reference drafter's CPU path (numpy restatement,
+    fp32) on the host cores, same metric/unit/config; rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from longspark_b200.config import CFG2
+    shape = CFG2.shape
+    for _ in range(min(args.warmup, 1)):
+        cpu_round_sample(shape, HEADLINE_CTX, rounds=1)
+    sec, threads = cpu_round_sample(shape, HEADLINE_CTX, rounds=max(1, min(args.steps, 5)))
+    value = shape.block / sec
+    line = {"metric": METRIC, "value": round(value, 2), "unit": "draft tokens/s", "impl": "reference",
+            "n_gpus": world, "steps": max(1, min(args.steps, 5)), "warmup": min(args.warmup, 1),
+            "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "cfg2-qwen3-8b drafter round (BASELINE configs[1])", "batch_per_gpu": 1,
+                       "headline_ctx": HEADLINE_CTX},
+            "cpu_baseline": {"value": round(value, 2), "unit": "draft tokens/s", "cores": threads, "kind": "port",
+                             "sample": "fp32 rounds of the numpy restatement of the reference drafter "
+                                       "(refresh + pass + Markov chain + accept) at the cfg2 shapes"},
+            "e2e": {"value": round(value, 2), "unit": "draft tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -91,6 +91,10 @@ typedef struct ls_gemm_args {
   int* status;          /* optional device status word                          */
 } ls_gemm_args;
 
+/* Workspace layout: a 64 KiB region of per-tile arrival counters (zero it once
+ * after allocation; every launch leaves it zeroed) followed by the fp32
+ * partial tiles.  One workspace sized for the largest GEMM can be shared by
+ * all GEMMs issued on the same stream. */
 LS_API size_t ls_gemm_workspace_bytes(int rows, int k, int n_out);
 LS_API int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes);
 

