@@ -223,7 +223,7 @@ def build_round(shape, ctx, batch, dev, seed):
                       summary_lse=v["summary_lse"], hidden=v["hidden"])
     eng = DraftEngine(shape, DraftWeights(shape, W, dev), pools, max_batch=batch, device=dev)
     del W
-    g = GraphedDraft(eng, batch, with_refresh=True, with_target=True)
+    g = GraphedDraft(eng, batch, with_refresh=True, with_target=True, slots_are_rows=True)
     commit = torch.full((batch,), shape.max_commit, dtype=torch.int32, device=dev)
     target = torch.randint(0, shape.vocab, (batch, shape.block + 1), device=dev, generator=gen)
     g.load(slots=torch.arange(batch, dtype=torch.int32, device=dev), seq_lens=v["seq_lens"], anchors=v["anchors"],

@@ -46,6 +46,10 @@ extern "C" {
 #define LS_EPI_LMHEAD 5     /* bf16 logits + per-128-row tile (max, argmax)         */
 #define LS_EPI_MARKOV_ADD 6 /* bf16(base + bf16(acc))                               */
 
+/* Weight layouts of ls_gemm. */
+#define LS_W_ROWMAJOR 0
+#define LS_W_TILED 1
+
 /* Library version (major*10000 + minor*100 + patch). */
 LS_API int ls_version(void);
 
@@ -67,7 +71,10 @@ LS_API int ls_device_sm_count(void);
 /* ------------------------------------------------------------------------- */
 typedef struct ls_gemm_args {
   const void* x;        /* [rows, x_ld] bf16, K contiguous (activations)       */
-  const void* w;        /* [n_out, k] bf16, K contiguous (weights)             */
+  const void* w;        /* weights, layout per w_layout                        */
+  int w_layout;         /* LS_W_ROWMAJOR: [n_out, k] bf16, K contiguous;
+                           LS_W_TILED: ls_tile_weight() layout (16 KiB tiles streamed
+                           as contiguous bulk copies)                           */
   int rows;             /* tokens                                              */
   int k;                /* reduction length, multiple of 64                    */
   int n_out;            /* output features, multiple of 128                    */
@@ -84,6 +91,8 @@ typedef struct ls_gemm_args {
   float norm_eps;
   const int* positions; /* [rows] int32 RoPE positions                          */
   const float* inv_freq;/* [64] fp32 RoPE inverse frequencies                  */
+  const float* rope_table; /* optional [rows, 128] fp32: bf16-rounded cos (0..63) and sin (64..127);
+                              when NULL the epilogue evaluates them from positions and inv_freq */
   float* tile_max;      /* LS_EPI_LMHEAD: [rows, n_out/128] fp32                */
   int* tile_arg;        /* LS_EPI_LMHEAD: [rows, n_out/128] int32 (vocab index) */
   const void* base;     /* LS_EPI_MARKOV_ADD: bf16 [rows, base_ld]              */
@@ -96,6 +105,14 @@ typedef struct ls_gemm_args {
  * partial tiles.  One workspace sized for the largest GEMM can be shared by
  * all GEMMs issued on the same stream. */
 LS_API size_t ls_gemm_workspace_bytes(int rows, int k, int n_out);
+
+/* Re-lay a row-major [n_out, k] bf16 weight matrix (n_out % 128 == 0,
+ * k % 64 == 0) into the LS_W_TILED layout: 128 x 64 tiles stored
+ * contiguously in (row tile, k tile) order, each already in the 128-byte
+ * swizzled order the tensor cores read from shared memory (the 16-byte chunk
+ * c of tile row r is stored at chunk c ^ (r % 8)).  out has n_out * k elements
+ * and must not alias w. */
+LS_API int ls_tile_weight(void* stream, const void* w, void* out, int n_out, int k);
 LS_API int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes);
 
 /* ------------------------------------------------------------------------- */
@@ -153,6 +170,9 @@ typedef struct ls_refresh_args {
   const void* learned_query;
   float* state_out;
   float* state_lse;
+  void* state_bf16;       /* optional [capacity, bf16_layers, q_heads, slots, 128] bf16 copy of
+                             state_out for the tapped layers the drafter attends to */
+  int bf16_layers;        /* tapped layers [0, bf16_layers) get the bf16 copy */
   int capacity;           /* entries in the state pools (slots are checked against it) */
   int batch, tap_layers, q_heads, kv_heads, slots_per_head, max_commit;
   float softmax_scale;
@@ -193,6 +213,8 @@ typedef struct ls_attention_args {
   const void* learned_query; /* one tapped layer: [q_heads, slots, 128] bf16       */
   const float* state_out;    /* [capacity, ...]: entry of request b at state_out + slots[b]*state_stride */
   long long state_stride;
+  const void* state_bf16;    /* optional bf16 copy of the same entries (read instead of state_out) */
+  long long state_bf16_stride;
   const int* slots;
   int capacity;         /* entries in the state pool                              */
   int slots_per_head;   /* S */
@@ -219,10 +241,14 @@ LS_API int ls_rmsnorm(void* stream, const void* x, int x_ld, const void* w, void
  * out[b*block + i] = [bf16(embed[tok_i] + pos_emb[i]) | latest[b]],
  * tok_0 = anchors[b], tok_i = mask_token_id for i > 0.  out is [batch*block, 2*hidden].
  * When positions != NULL also writes the RoPE positions of the block rows,
- * positions[b*block + i] = seq_lens[b] + i (SF draftfreekv.py:3259-3263). */
+ * positions[b*block + i] = seq_lens[b] + i (SF draftfreekv.py:3259-3263), and
+ * when rope_table != NULL the table the QKV epilogue reads: per row,
+ * bf16(cos(pos * inv_freq[j])) at j and bf16(sin(...)) at 64 + j, j < 64
+ * (SF draftfreekv.py:1996-2007). */
 LS_API int ls_shifted_input(void* stream, const long long* anchors, const int* seq_lens, int* positions,
-                            const void* embed, const void* pos_emb, const void* latest, void* out, int batch,
-                            int block, int hidden, int vocab, int mask_token_id, int* status);
+                            const float* inv_freq, float* rope_table, const void* embed, const void* pos_emb,
+                            const void* latest, void* out, int batch, int block, int hidden, int vocab,
+                            int mask_token_id, int* status);
 
 /* Gather rows: out[b] = src[idx[b]] (row_bytes each, 16-byte multiples);
  * indices outside [0, src_rows) are recorded in *status and the row is zeroed. */
@@ -237,21 +263,26 @@ LS_API int ls_gather_rows(void* stream, const void* src, long long src_rows, con
  * sample_block_tokens at temperature 0, SF draftfreekv.py:2366-2407; without a
  * Markov head base_logits.argmax(-1), :3545-3578): for t in [0, block):
  * tok_t = argmax_v bf16(base[t, v] + bf16(w2[v] . w1[prev])), prev = tok_{t-1}
- * (anchors for t = 0), lowest index on ties.  Candidates are restricted to
- * tokens whose base logit is within a rigorous bound of the row maximum
- * (Cauchy-Schwarz on w2_row_bound * |w1[prev]|); the result is identical to
- * the full-vocabulary scan.  w1 == NULL: no Markov head.
- * base: [batch*block, vocab] bf16; tile_max/tile_arg: [batch*block, vocab/128]
- * from the LS_EPI_LMHEAD epilogue.  tokens [batch, block] int64.  When
- * target != NULL ([batch, target_ld] int64) also writes accept_out [batch]
- * (greedy accepted-prefix length, LS engine/target.py:472-477). */
+ * (anchors for t = 0), lowest index on ties.  Only tokens whose base logit lies
+ * within a rigorous bound of the row maximum can win (Cauchy-Schwarz:
+ * |bias| <= w1_row_bound * w2_row_bound); those candidates are listed per row
+ * in parallel, every (previous candidate, candidate) bias is evaluated at once
+ * and the serial chain is a table walk.  The tokens equal the full-vocabulary
+ * scan's; a request whose band overflows the candidate buffers is evaluated
+ * step by step over the band, and over the whole vocabulary if needed.
+ * w1 == NULL: no Markov head.  base: [batch*block, vocab] bf16;
+ * tile_max/tile_arg: [batch*block, vocab/128] from the LS_EPI_LMHEAD epilogue.
+ * tokens [batch, block] int64.  When target != NULL ([batch, target_ld] int64)
+ * also writes accept_out [batch] (greedy accepted-prefix length,
+ * LS engine/target.py:472-477). */
 typedef struct ls_markov_args {
   const void* base;
   const float* tile_max;
   const int* tile_arg;
   const void* w1;            /* [vocab, rank] bf16 or NULL */
   const void* w2;            /* [vocab, rank] bf16 */
-  const float* w2_row_bound; /* device fp32, >= max_v ||w2[v]||_2 (ls_row_norm_bound) */
+  const float* w1_row_bound; /* device fp32, >= max_v ||w1[v]||_2 (ls_row_norm_bound) */
+  const float* w2_row_bound; /* device fp32, >= max_v ||w2[v]||_2 */
   int rank;
   const long long* anchors;  /* [batch] */
   long long* tokens;         /* [batch, block] */
@@ -262,7 +293,8 @@ typedef struct ls_markov_args {
   int* status;
 } ls_markov_args;
 
-LS_API int ls_markov_argmax(void* stream, const ls_markov_args* a);
+LS_API size_t ls_markov_workspace_bytes(int batch, int block);
+LS_API int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes);
 
 /* Greedy accept check: accept[b] = number of leading i < block with
  * target[b, i] == draft[b, i] (LS engine/target.py:472-477). */

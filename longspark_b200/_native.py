@@ -14,6 +14,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_native" / "liblongspark_b200.so"
 
 LS_OK = 0
+W_ROWMAJOR, W_TILED = 0, 1
 EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_QKV, EPI_GATEUP, EPI_LMHEAD, EPI_MARKOV_ADD = range(7)
 
 vp = C.c_void_p
@@ -24,17 +25,18 @@ sz = C.c_size_t
 
 
 class GemmArgs(C.Structure):
-    _fields_ = [("x", vp), ("w", vp), ("rows", i32), ("k", i32), ("n_out", i32), ("x_ld", i32),
+    _fields_ = [("x", vp), ("w", vp), ("w_layout", i32), ("rows", i32), ("k", i32), ("n_out", i32), ("x_ld", i32),
                 ("epilogue", i32), ("out", vp), ("out_ld", i32), ("residual", vp), ("res_ld", i32),
                 ("q_heads", i32), ("kv_heads", i32), ("q_norm_w", vp), ("k_norm_w", vp), ("norm_eps", f32),
-                ("positions", vp), ("inv_freq", vp), ("tile_max", vp), ("tile_arg", vp), ("base", vp),
+                ("positions", vp), ("inv_freq", vp), ("rope_table", vp), ("tile_max", vp), ("tile_arg", vp), ("base", vp),
                 ("base_ld", i32), ("status", vp)]
 
 
 class RefreshArgs(C.Structure):
     _fields_ = [("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("page_table", vp), ("table_stride", i32),
                 ("ring_pages", i32), ("seq_lens", vp), ("commit_lens", vp), ("slots", vp),
-                ("learned_query", vp), ("state_out", vp), ("state_lse", vp), ("capacity", i32), ("batch", i32),
+                ("learned_query", vp), ("state_out", vp), ("state_lse", vp), ("state_bf16", vp), ("bf16_layers", i32),
+                ("capacity", i32), ("batch", i32),
                 ("tap_layers", i32), ("q_heads", i32), ("kv_heads", i32), ("slots_per_head", i32),
                 ("max_commit", i32), ("softmax_scale", f32), ("status", vp)]
 
@@ -42,14 +44,14 @@ class RefreshArgs(C.Structure):
 class AttentionArgs(C.Structure):
     _fields_ = [("qkv", vp), ("block", i32), ("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("page_table", vp),
                 ("table_stride", i32), ("ring_pages", i32), ("seq_lens", vp), ("window", i32),
-                ("learned_query", vp), ("state_out", vp), ("state_stride", i64), ("slots", vp),
-                ("capacity", i32), ("slots_per_head", i32), ("batch", i32), ("q_heads", i32), ("kv_heads", i32),
+                ("learned_query", vp), ("state_out", vp), ("state_stride", i64), ("state_bf16", vp),
+                ("state_bf16_stride", i64), ("slots", vp), ("capacity", i32), ("slots_per_head", i32), ("batch", i32), ("q_heads", i32), ("kv_heads", i32),
                 ("softmax_scale", f32), ("out", vp), ("status", vp)]
 
 
 class MarkovArgs(C.Structure):
     _fields_ = [("base", vp), ("tile_max", vp), ("tile_arg", vp), ("w1", vp), ("w2", vp),
-                ("w2_row_bound", vp), ("rank", i32), ("anchors", vp), ("tokens", vp), ("target", vp),
+                ("w1_row_bound", vp), ("w2_row_bound", vp), ("rank", i32), ("anchors", vp), ("tokens", vp), ("target", vp),
                 ("target_ld", i32), ("accept_out", vp), ("batch", i32), ("block", i32), ("vocab", i32),
                 ("status", vp)]
 
@@ -61,6 +63,7 @@ SIGNATURES = {
     "ls_device_sm_count": (i32, []),
     "ls_gemm_workspace_bytes": (sz, [i32, i32, i32]),
     "ls_gemm": (i32, [vp, C.POINTER(GemmArgs), vp, sz]),
+    "ls_tile_weight": (i32, [vp, vp, vp, i32, i32]),
     "ls_position_scores": (i32, [vp, vp, i64, i64, vp, vp, i32, i32, i32, i32, i32, f32]),
     "ls_merge_accepted": (i32, [vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "ls_refresh_views": (i32, [vp, C.POINTER(RefreshArgs)]),
@@ -69,9 +72,10 @@ SIGNATURES = {
     "ls_attention_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
     "ls_draft_attention": (i32, [vp, C.POINTER(AttentionArgs), vp, sz]),
     "ls_rmsnorm": (i32, [vp, vp, i32, vp, vp, i32, i32, i32, f32, i32]),
-    "ls_shifted_input": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "ls_shifted_input": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "ls_gather_rows": (i32, [vp, vp, i64, vp, vp, i32, i64, vp]),
-    "ls_markov_argmax": (i32, [vp, C.POINTER(MarkovArgs)]),
+    "ls_markov_workspace_bytes": (sz, [i32, i32]),
+    "ls_markov_argmax": (i32, [vp, C.POINTER(MarkovArgs), vp, sz]),
     "ls_accept": (i32, [vp, vp, i32, vp, vp, i32, i32]),
     "ls_row_norm_bound": (i32, [vp, vp, i32, i32, vp]),
 }

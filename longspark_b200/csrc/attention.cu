@@ -175,6 +175,7 @@ __device__ __forceinline__ void store_partial(const AttnParams& p, const WarpSta
 
 __global__ void __launch_bounds__(256) attention_split_kernel(const AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  asm volatile("griddepcontrol.launch_dependents;");
   const ls_attention_args& a = p.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.G;
@@ -257,21 +258,40 @@ __global__ void __launch_bounds__(256) attention_split_kernel(const AttnParams p
       if (lane == 0) record_status(a.status, LS_DEV_BAD_INDEX);
       slot = 0;  // read a valid entry; the status word reports the bad index
     }
-    const float* vq = a.state_out + (long long)slot * a.state_stride + ((long long)h * a.slots_per_head + s0) * 128;
-    for (int i = lane; i < AT_GSLOTS * 16; i += 32) {
-      const int r = i >> 4, col = (i & 15) << 3;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (r < ns) {
-        kv = *reinterpret_cast<const uint4*>(kq + (long long)r * 128 + col);
-        const float4 v0 = __ldcs(reinterpret_cast<const float4*>(vq + (long long)r * 128 + col));
-        const float4 v1 = __ldcs(reinterpret_cast<const float4*>(vq + (long long)r * 128 + col + 4));
-        vv.x = pack_bf16(v0.x, v0.y);
-        vv.y = pack_bf16(v0.z, v0.w);
-        vv.z = pack_bf16(v1.x, v1.y);
-        vv.w = pack_bf16(v1.z, v1.w);
+    if (a.state_bf16 != nullptr) {
+      // bf16 copy of the summary kept by the refresh: straight async copies
+      const bf16* vb = reinterpret_cast<const bf16*>(a.state_bf16) + (long long)slot * a.state_bf16_stride +
+                       ((long long)h * a.slots_per_head + s0) * 128;
+      for (int i = lane; i < AT_GSLOTS * 16; i += 32) {
+        const int r = i >> 4, col = (i & 15) << 3;
+        if (r < ns) {
+          cp_async16(&ks[r][col], kq + (long long)r * 128 + col);
+          cp_async16(&vs[r][col], vb + (long long)r * 128 + col);
+        } else {
+          *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
+        }
       }
-      *reinterpret_cast<uint4*>(&ks[r][col]) = kv;
-      *reinterpret_cast<uint4*>(&vs[r][col]) = vv;
+      cp_async_commit();
+      cp_async_wait_all();
+    } else {
+      const float* vq =
+          a.state_out + (long long)slot * a.state_stride + ((long long)h * a.slots_per_head + s0) * 128;
+      for (int i = lane; i < AT_GSLOTS * 16; i += 32) {
+        const int r = i >> 4, col = (i & 15) << 3;
+        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+        if (r < ns) {
+          kv = *reinterpret_cast<const uint4*>(kq + (long long)r * 128 + col);
+          const float4 v0 = __ldcs(reinterpret_cast<const float4*>(vq + (long long)r * 128 + col));
+          const float4 v1 = __ldcs(reinterpret_cast<const float4*>(vq + (long long)r * 128 + col + 4));
+          vv.x = pack_bf16(v0.x, v0.y);
+          vv.y = pack_bf16(v0.z, v0.w);
+          vv.z = pack_bf16(v1.x, v1.y);
+          vv.w = pack_bf16(v1.z, v1.w);
+        }
+        *reinterpret_cast<uint4*>(&ks[r][col]) = kv;
+        *reinterpret_cast<uint4*>(&vs[r][col]) = vv;
+      }
     }
     __syncwarp();
     uint32_t qf[8][4];
@@ -314,6 +334,7 @@ __global__ void __launch_bounds__(256) attention_split_kernel(const AttnParams p
 // source maximum, round the weighted sum to bf16, normalise; then merge the
 // sources by log-sum-exp in the reference's order (summary, window, local).
 __global__ void __launch_bounds__(512) attention_combine_kernel(const AttnParams p) {
+  asm volatile("griddepcontrol.launch_dependents;");
   const ls_attention_args& a = p.a;
   const int bh = blockIdx.x;
   const int b = bh / a.q_heads, h = bh % a.q_heads;
@@ -322,27 +343,29 @@ __global__ void __launch_bounds__(512) attention_combine_kernel(const AttnParams
   const long long base = (long long)bh * p.np * 16;
   float out_src[3][4];
   float lse_src[3];
-  const int ranges[4] = {p.nsw, p.nsw + p.ngc, p.np, 0};
   // source order in the part array: window [0, nsw), summary [nsw, nsw+ngc), local
   for (int src = 0; src < 3; ++src) {
-    const int lo = src == 0 ? 0 : ranges[src - 1];
-    const int hi = ranges[src];
-    float M = -INFINITY;
-    for (int pi = lo; pi < hi; ++pi) M = fmaxf(M, p.part_ml[(base + pi * 16 + row) * 2]);
-    float L = 0.0f;
+    const int lo = src == 0 ? 0 : (src == 1 ? p.nsw : p.nsw + p.ngc);
+    const int n = src == 0 ? p.nsw : (src == 1 ? p.ngc : 1);  // <= 32 partials per source
+    float m_i = -INFINITY, l_i = 0.0f;
+    if (lane < n) {
+      const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + (base + (lo + lane) * 16 + row) * 2);
+      m_i = ml.x;
+      l_i = ml.y;
+    }
+    const float M = warp_max(m_i);
+    const float f_i = (m_i == -INFINITY) ? 0.0f : expf(m_i - M);
+    const float L = warp_sum(l_i * f_i);
     float wv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (M != -INFINITY) {
-      for (int pi = lo; pi < hi; ++pi) {
-        const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + (base + pi * 16 + row) * 2);
-        if (ml.x == -INFINITY) continue;
-        const float f = expf(ml.x - M);
-        L += ml.y * f;
-        const float4 acc = reinterpret_cast<const float4*>(p.part_acc + (base + pi * 16 + row) * 128)[lane];
-        wv[0] += acc.x * f;
-        wv[1] += acc.y * f;
-        wv[2] += acc.z * f;
-        wv[3] += acc.w * f;
-      }
+    const float4* accp = reinterpret_cast<const float4*>(p.part_acc + (base + lo * 16 + row) * 128) + lane;
+#pragma unroll 4
+    for (int i = 0; i < n; ++i) {
+      const float f = __shfl_sync(0xffffffffu, f_i, i);
+      const float4 acc = accp[(long long)i * 16 * 32];
+      wv[0] += acc.x * f;
+      wv[1] += acc.y * f;
+      wv[2] += acc.z * f;
+      wv[3] += acc.w * f;
     }
     const float safe = fmaxf(L, 1.17549435e-38f);
 #pragma unroll
@@ -394,7 +417,7 @@ static AttnPlan plan_attention(int batch, int q_heads, int kv_heads, int window,
   if (nsw > max_chunks) nsw = max_chunks;
   pl.wc = ((window + nsw - 1) / nsw + AT_WROWS - 1) / AT_WROWS * AT_WROWS;
   pl.nsw = (window + pl.wc - 1) / pl.wc;
-  pl.np = pl.nsw + pl.ngc + 1;
+  pl.np = pl.nsw + pl.ngc + 1;  // the combine reduces <= 32 partials per source (one per lane)
   pl.n_win = (long long)batch * kv_heads * pl.nsw;
   pl.n_glob = (long long)batch * kv_heads * pl.ngc;
   pl.n_loc = (long long)batch * kv_heads;
@@ -426,7 +449,8 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
     return set_error(LS_ERR_INVALID, "ls_draft_attention: null pointer argument");
   if (a->batch <= 0) return LS_OK;
   if (a->kv_heads <= 0 || a->q_heads % a->kv_heads || a->q_heads / a->kv_heads > 8 || a->block < 1 ||
-      a->block > 16 || a->window < 1 || a->slots_per_head < 1)
+      a->block > 16 || a->window < 1 || a->window > 32 * 128 || a->slots_per_head < 1 ||
+      a->slots_per_head > 32 * 32)
     return set_error(LS_ERR_UNSUPPORTED, "ls_draft_attention: need GQA group <= 8, 1 <= block <= 16");
   AttnPlan pl = plan_attention(a->batch, a->q_heads, a->kv_heads, a->window, a->slots_per_head);
   if (workspace == nullptr || workspace_bytes < pl.ml_bytes + pl.acc_bytes)

@@ -15,6 +15,7 @@ constexpr int EW_THREADS = 256;
 // rstd = 1 / sqrt(mean(x^2) + eps), mean accumulated in fp32.
 __global__ void __launch_bounds__(EW_THREADS) rmsnorm_kernel(const bf16* x, int x_ld, const bf16* w, bf16* out,
                                                              int out_ld, int n, float eps, int mode) {
+  asm volatile("griddepcontrol.launch_dependents;");
   __shared__ float red[EW_THREADS / 32];
   const int row = blockIdx.x;
   const bf16* xr = x + (long long)row * x_ld;
@@ -56,12 +57,21 @@ __global__ void __launch_bounds__(EW_THREADS) rmsnorm_kernel(const bf16* x, int 
 
 // out[b*block + i] = [ bf16(embed[tok_i] + pos_emb[i]) | latest[b] ]
 __global__ void __launch_bounds__(EW_THREADS)
-    shifted_input_kernel(const long long* anchors, const int* seq_lens, int* positions, const bf16* embed,
-                         const bf16* pos_emb, const bf16* latest, bf16* out, int block, int hidden, int vocab,
-                         int mask_token_id, int* status) {
+    shifted_input_kernel(const long long* anchors, const int* seq_lens, int* positions, const float* inv_freq,
+                         float* rope_table, const bf16* embed, const bf16* pos_emb, const bf16* latest, bf16* out,
+                         int block, int hidden, int vocab, int mask_token_id, int* status) {
+  asm volatile("griddepcontrol.launch_dependents;");
   const int row = blockIdx.x;
   const int b = row / block, i = row % block;
-  if (positions != nullptr && threadIdx.x == 0) positions[row] = seq_lens[b] + i;
+  if (positions != nullptr) {
+    const int pos = seq_lens[b] + i;
+    if (threadIdx.x == 0) positions[row] = pos;
+    if (rope_table != nullptr && threadIdx.x < 64) {
+      const float ang = static_cast<float>(pos) * inv_freq[threadIdx.x];
+      rope_table[(long long)row * 128 + threadIdx.x] = bf16_round(cosf(ang));
+      rope_table[(long long)row * 128 + 64 + threadIdx.x] = bf16_round(sinf(ang));
+    }
+  }
   long long tok = i == 0 ? anchors[b] : mask_token_id;
   if (tok < 0 || tok >= vocab) {
     if (threadIdx.x == 0) record_status(status, LS_DEV_BAD_TOKEN);
@@ -103,14 +113,16 @@ extern "C" int ls_rmsnorm(void* stream, const void* x, int x_ld, const void* w, 
 }
 
 extern "C" int ls_shifted_input(void* stream, const long long* anchors, const int* seq_lens, int* positions,
-                                const void* embed, const void* pos_emb, const void* latest, void* out, int batch,
-                                int block, int hidden, int vocab, int mask_token_id, int* status) {
+                                const float* inv_freq, float* rope_table, const void* embed, const void* pos_emb,
+                                const void* latest, void* out, int batch, int block, int hidden, int vocab,
+                                int mask_token_id, int* status) {
   if (batch <= 0) return LS_OK;
   if (anchors == nullptr || embed == nullptr || pos_emb == nullptr || latest == nullptr || out == nullptr ||
-      hidden % 8 || block < 1 || (positions != nullptr && seq_lens == nullptr))
+      hidden % 8 || block < 1 || (positions != nullptr && seq_lens == nullptr) ||
+      (rope_table != nullptr && (positions == nullptr || inv_freq == nullptr)))
     return set_error(LS_ERR_INVALID, "ls_shifted_input: bad arguments");
   shifted_input_kernel<<<batch * block, EW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      anchors, seq_lens, positions, reinterpret_cast<const bf16*>(embed), reinterpret_cast<const bf16*>(pos_emb),
+      anchors, seq_lens, positions, inv_freq, rope_table, reinterpret_cast<const bf16*>(embed), reinterpret_cast<const bf16*>(pos_emb),
       reinterpret_cast<const bf16*>(latest), reinterpret_cast<bf16*>(out), block, hidden, vocab, mask_token_id, status);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_shifted_input: launch", e);

@@ -20,6 +20,8 @@
 #include "host_common.h"
 
 #include <algorithm>
+#include <stdlib.h>
+#include <string.h>
 
 namespace ls {
 
@@ -68,8 +70,8 @@ struct EpiScratch {
   int flag;
 };
 
-__device__ void final_epilogue(const GemmKernelParams& P, int m_tile, int n0, const float* v, int r, int ew,
-                               EpiScratch* sc) {
+__device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_tile, int n0, const float (&v)[16],
+                                               int r, int ew, EpiScratch* sc) {
   const ls_gemm_args& a = P.a;
   const int rows = a.rows;
   bf16* out = reinterpret_cast<bf16*>(a.out);
@@ -130,10 +132,17 @@ __device__ void final_epilogue(const GemmKernelParams& P, int m_tile, int n0, co
           const int tok = n0 + j;
           const float other = sc->xch[partner][j];
           const float rot = r < 64 ? -other : other;
-          const int pos = tok < rows ? a.positions[tok] : 0;
-          const float ang = static_cast<float>(pos) * fr;
-          const float cs = bf16_round(cosf(ang));
-          const float sn = bf16_round(sinf(ang));
+          float cs, sn;
+          if (a.rope_table != nullptr) {
+            const int tr = tok < rows ? tok : 0;
+            cs = a.rope_table[(long long)tr * 128 + (r & 63)];
+            sn = a.rope_table[(long long)tr * 128 + 64 + (r & 63)];
+          } else {
+            const int pos = tok < rows ? a.positions[tok] : 0;
+            const float ang = static_cast<float>(pos) * fr;
+            cs = bf16_round(cosf(ang));
+            sn = bf16_round(sinf(ang));
+          }
           y[j] = bf16_round(bf16_round(y[j] * cs) + bf16_round(rot * sn));
         }
         epi_bar();  // xch/red reused by the next chunk
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     mbar_fence_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&map_w);
+    if (P.a.w_layout != LS_W_TILED) tma_prefetch_desc(&map_w);
     tma_prefetch_desc(&map_x);
   }
   if (warp == 1) {
@@ -277,22 +286,55 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
+  // Let the next kernel of the stream launch (a dependent GEMM only starts
+  // streaming its own weights; it waits for this grid before touching data).
+  asm volatile("griddepcontrol.launch_dependents;");
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      long long issued = 0;
-      for (long long u = u0; u < u1; ++u) {
+      const bool tiled_w = P.a.w_layout == LS_W_TILED;
+      const bf16* w_tiles = reinterpret_cast<const bf16*>(P.a.w);
+      // Weights do not depend on the previous kernel: fill the first stages with
+      // weight tiles before waiting for it, then add the activation tiles.
+      const int pre = static_cast<int>((u1 - u0) < S ? (u1 - u0) : S);
+      for (int i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        const int t = static_cast<int>(u / KB);
+        const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
+        const int m_tile = t / P.n_tiles;
+        mbar_arrive_expect_tx(&full[i], A_STAGE_BYTES + b_stage_bytes);
+        if (tiled_w)
+          bulk_load(a_buf + i * A_STAGE_BYTES, w_tiles + (static_cast<long long>(m_tile) * KB + kb) * (BM * BK),
+                    A_STAGE_BYTES, &full[i], pol_w);
+        else
+          tma_load_2d(a_buf + i * A_STAGE_BYTES, &map_w, &full[i], kb * BK, m_tile * BM, pol_w);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        const int t = static_cast<int>(u / KB);
+        const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
+        const int n_tile = t % P.n_tiles;
+        tma_load_2d(b_buf + i * b_stage_bytes, &map_x, &full[i], kb * BK, n_tile * bn, pol_x);
+      }
+      int stage = pre % S;
+      uint32_t phase = pre == S ? 1u : 0u;
+      long long issued = pre;
+      for (long long u = u0 + pre; u < u1; ++u) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
         const int t = static_cast<int>(u / KB);
         const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
         const int m_tile = t / P.n_tiles;
         const int n_tile = t - m_tile * P.n_tiles;
         mbar_arrive_expect_tx(&full[stage], A_STAGE_BYTES + b_stage_bytes);
-        tma_load_2d(a_buf + stage * A_STAGE_BYTES, &map_w, &full[stage], kb * BK, m_tile * BM, pol_w);
+        if (tiled_w)
+          bulk_load(a_buf + stage * A_STAGE_BYTES, w_tiles + (static_cast<long long>(m_tile) * KB + kb) * (BM * BK),
+                    A_STAGE_BYTES, &full[stage], pol_w);
+        else
+          tma_load_2d(a_buf + stage * A_STAGE_BYTES, &map_w, &full[stage], kb * BK, m_tile * BM, pol_w);
         tma_load_2d(b_buf + stage * b_stage_bytes, &map_x, &full[stage], kb * BK, n_tile * bn, pol_x);
         ++issued;
         if (++stage == S) {
@@ -367,6 +409,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------
+    // Residual/base reads and all writes wait for the previous kernel.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int ew = warp & 3;  // TMEM lane quarter this warp may access
     const int r = ew * 32 + lane;
     int acc = 0;
@@ -412,24 +456,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
-        __threadfence();
-        epi_bar();
+        epi_bar();  // every thread's partial is stored; thread 0 publishes them (release)
         const long long tu0 = static_cast<long long>(t) * KB;
         const int first = cta_of_unit(tu0, U, G);
         const int last = cta_of_unit(tu0 + KB - 1, U, G);
         if (r == 0) {
-          const int prev = atomicAdd(&P.counters[t], 1);
+          const int prev = atomic_add_acq_rel_gpu(&P.counters[t], 1);
           sc->flag = (prev == last - first) ? 1 : 0;
         }
         epi_bar();
         const bool reducer = sc->flag != 0;
         epi_bar();
         if (reducer) {
-          __threadfence();
           for (int c = 0; c < bn; c += 16) {
             float v[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+#pragma unroll 2
             for (int q = first; q <= last; ++q) {
               const int q_t_first = static_cast<int>(unit_begin(q, U, G) / KB);
               const int q_slot = (q_t_first == t) ? 0 : 1;
@@ -526,7 +569,8 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
       if (a->residual == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm: residual epilogue needs residual");
       break;
     case LS_EPI_QKV:
-      if (a->q_norm_w == nullptr || a->k_norm_w == nullptr || a->positions == nullptr || a->inv_freq == nullptr ||
+      if (a->q_norm_w == nullptr || a->k_norm_w == nullptr ||
+          (a->rope_table == nullptr && (a->positions == nullptr || a->inv_freq == nullptr)) ||
           a->q_heads <= 0 || a->kv_heads <= 0 || a->n_out != (a->q_heads + 2 * a->kv_heads) * BM)
         return set_error(LS_ERR_INVALID, "ls_gemm: QKV epilogue needs norms, positions, inv_freq, matching heads");
       break;
@@ -553,8 +597,14 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
     return set_error(LS_ERR_INVALID, "ls_gemm: workspace must be 256-byte aligned");
 
   CUtensorMap map_w, map_x;
-  int rc = encode_tma_2d_bf16(&map_w, a->w, a->k, a->n_out, a->k, BK, BM);
-  if (rc) return rc;
+  memset(&map_w, 0, sizeof(map_w));
+  int rc = LS_OK;
+  if (a->w_layout == LS_W_ROWMAJOR) {
+    rc = encode_tma_2d_bf16(&map_w, a->w, a->k, a->n_out, a->k, BK, BM);
+    if (rc) return rc;
+  } else if (a->w_layout != LS_W_TILED) {
+    return set_error(LS_ERR_INVALID, "ls_gemm: unknown weight layout %d", a->w_layout);
+  }
   rc = encode_tma_2d_bf16(&map_x, a->x, a->k, a->rows, a->x_ld, BK, p.bn);
   if (rc) return rc;
 
@@ -579,10 +629,57 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(227 * 1024));
     if (e != cudaSuccess) return set_cuda_error("ls_gemm: cudaFuncSetAttribute", e);
+    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return set_cuda_error("ls_gemm: carveout", e);
     configured_smem = 227 * 1024;
   }
-  gemm_tc_kernel<<<p.grid, GEMM_THREADS, smem, reinterpret_cast<cudaStream_t>(stream)>>>(map_w, map_x, kp);
-  cudaError_t e = cudaGetLastError();
+  // Programmatic dependent launch: the GEMM may start while the previous
+  // kernel of the stream finishes; it prefetches weights, then waits for it.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  // LONGSPARK_B200_PDL=0 launches with plain stream ordering (for A/B timing).
+  static const bool pdl = [] {
+    const char* e = getenv("LONGSPARK_B200_PDL");
+    return e == nullptr || e[0] != '0';
+  }();
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map_w, map_x, kp);
   if (e != cudaSuccess) return set_cuda_error("ls_gemm: launch", e);
   return LS_OK;
+}
+
+// Row-major [n_out, k] -> (row tile, k tile) tiles of 128 x 64, rows of each
+// tile in the 128-byte swizzled chunk order.  One thread per 16-byte chunk.
+__global__ void tile_weight_kernel(const uint4* w, uint4* out, int n_out, int k) {
+  const long long chunks_per_row = k / 8;
+  const long long total = static_cast<long long>(n_out) * chunks_per_row;
+  const int kb_count = k / BK;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / chunks_per_row;
+    const int cc = static_cast<int>(i - row * chunks_per_row);  // chunk along k
+    const int m_tile = static_cast<int>(row / BM), r = static_cast<int>(row % BM);
+    const int kb = cc / 8, c = cc % 8;
+    const long long tile = static_cast<long long>(m_tile) * kb_count + kb;
+    out[tile * (BM * 8) + r * 8 + (c ^ (r & 7))] = w[i];
+  }
+}
+
+extern "C" int ls_tile_weight(void* stream, const void* w, void* out, int n_out, int k) {
+  if (w == nullptr || out == nullptr || n_out <= 0 || k <= 0 || n_out % BM || k % BK)
+    return set_error(LS_ERR_INVALID, "ls_tile_weight: n_out %% 128 == 0 and k %% 64 == 0 required");
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return set_error(LS_ERR_INVALID, "ls_tile_weight: 16-byte aligned buffers required");
+  tile_weight_kernel<<<1184, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(w), reinterpret_cast<uint4*>(out), n_out, k);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_cuda_error("ls_tile_weight: launch", e);
 }

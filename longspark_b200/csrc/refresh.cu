@@ -30,10 +30,11 @@ constexpr int RF_QPITCH = 136; // bf16 row pitch in smem (272 B: ldmatrix rows h
 struct RefreshSmem {
   bf16 q[RF_SLOTS][RF_QPITCH];
   bf16 k[RF_MAXROWS][RF_QPITCH];
-  float v[RF_MAXROWS][128];
-  float w[RF_SLOTS][RF_MAXROWS + 1];
+  bf16 v[RF_MAXROWS][128];
+  float w[RF_SLOTS][RF_MAXROWS + 4];  // row pitch 36 floats: float4 reads stay 16-byte aligned
   float prior_w[RF_SLOTS];
   float merged[RF_SLOTS];
+  float prior[RF_SLOTS];
 };
 
 __device__ __forceinline__ long long paged_row(const int* table, int table_stride, int ring_pages, int b, int pos,
@@ -81,6 +82,7 @@ __device__ __forceinline__ void warp_slot_scores(const bf16 (*q)[RF_QPITCH], con
 
 __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_args a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  asm volatile("griddepcontrol.launch_dependents;");
   RefreshSmem& sm = *reinterpret_cast<RefreshSmem*>(smem_raw);
   const int chunks = (a.slots_per_head + RF_SLOTS - 1) / RF_SLOTS;
   int bid = blockIdx.x;
@@ -105,6 +107,18 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
   if (slot < 0 || slot >= a.capacity) {
     if (tid == 0) record_status(a.status, LS_DEV_BAD_INDEX);
     return;
+  }
+  // Issue the state reads first: each warp's 16 slots (512 B each, float4 per
+  // lane) stay in flight while the queries and new rows load and the scores run.
+  const long long st_base = ((long long)slot * a.tap_layers + layer) * a.q_heads + h;
+  float* out = a.state_out + (st_base * a.slots_per_head + s0) * 128;
+  float* lse = a.state_lse + st_base * a.slots_per_head + s0;
+  const bool warp_active = warp * 16 < nslots;
+  float4 o[16];
+  if (warp_active) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = __ldcs(reinterpret_cast<const float4*>(out + (long long)(warp * 16 + i) * 128) + lane);
+    if (lane < 16) sm.prior[warp * 16 + lane] = lse[warp * 16 + lane];
   }
 
   // Queries of this head/chunk -> smem (cp.async 16 B pieces).
@@ -136,20 +150,14 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
       }
     }
     *reinterpret_cast<uint4*>(&sm.k[r][col]) = kq;
-    const bf16* vh = reinterpret_cast<const bf16*>(&vq);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sm.v[r][col + e] = __bfloat162float(vh[e]);
+    *reinterpret_cast<uint4*>(&sm.v[r][col]) = vq;
   }
   if (!ok) bad_page = 1;
   cp_async_wait_all();
   __syncthreads();
   if (bad_page) return;  // a bad page id was recorded; leave the state untouched
 
-  const long long st_base = ((long long)slot * a.tap_layers + layer) * a.q_heads + h;
-  float* out = a.state_out + (st_base * a.slots_per_head + s0) * 128;
-  float* lse = a.state_lse + st_base * a.slots_per_head + s0;
-
-  if (warp * 16 < nslots) {
+  if (warp_active) {
     float acc[4][4];
     const int n_tiles = (c + 7) >> 3;
     warp_slot_scores(sm.q, sm.k, warp * 16, n_tiles, acc);
@@ -181,7 +189,7 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
       const float delta = mx + logf(sum);
-      const float prior = lse[sl];
+      const float prior = sm.prior[sl];
       const float m2 = fmaxf(prior, delta);
       const float merged = m2 + logf(expf(prior - m2) + expf(delta - m2));
 #pragma unroll
@@ -189,7 +197,7 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int r = nt * 8 + t2 + e;
-          if (r < c) sm.w[sl][r] = expf(sv[nt * 2 + e] - merged);
+          sm.w[sl][r] = r < c ? expf(sv[nt * 2 + e] - merged) : 0.0f;
         }
       if ((lane & 3) == 0) {
         sm.prior_w[sl] = expf(prior - merged);
@@ -197,26 +205,60 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
       }
     }
     __syncwarp();
-    // State update: lanes cover the 128 dims as float4.
-    for (int i = 0; i < 16; ++i) {
-      const int sl = warp * 16 + i;
-      float4 o = __ldcs(reinterpret_cast<const float4*>(out + (long long)sl * 128) + lane);
-      const float pw = sm.prior_w[sl];
-      o.x *= pw;
-      o.y *= pw;
-      o.z *= pw;
-      o.w *= pw;
-      for (int r = 0; r < c; ++r) {
-        const float w = sm.w[sl][r];
-        const float4 vv = *reinterpret_cast<const float4*>(&sm.v[r][lane * 4]);
-        o.x += w * vv.x;
-        o.y += w * vv.y;
-        o.z += w * vv.z;
-        o.w += w * vv.w;
+    // State update: lanes cover the 128 dims as float4; the lane's 4 dims of
+    // every new V row stay in registers (packed bf16), the weights of a slot
+    // come as float4 broadcasts.  Rows are folded in order r = 0, 1, ...
+    const int c4 = (c + 3) & ~3;  // weights beyond c are zero (masked above)
+    for (int r0 = 0; r0 < c; r0 += 16) {
+      uint2 vr[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) vr[r] = *reinterpret_cast<const uint2*>(&sm.v[r0 + r][lane * 4]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int sl = warp * 16 + i;
+        float4 oi = o[i];
+        if (r0 == 0) {
+          const float pw = sm.prior_w[sl];
+          oi.x *= pw;
+          oi.y *= pw;
+          oi.z *= pw;
+          oi.w *= pw;
+        }
+#pragma unroll
+        for (int rq = 0; rq < 16; rq += 4) {
+          if (r0 + rq < c4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(&sm.w[sl][r0 + rq]);
+            const float ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr[rq + e].x));
+              const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr[rq + e].y));
+              oi.x += ws[e] * v01.x;
+              oi.y += ws[e] * v01.y;
+              oi.z += ws[e] * v23.x;
+              oi.w += ws[e] * v23.y;
+            }
+          }
+        }
+        o[i] = oi;
       }
-      __stcs(reinterpret_cast<float4*>(out + (long long)sl * 128) + lane, o);
-      if (lane == 0) lse[sl] = sm.merged[sl];
     }
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      __stcs(reinterpret_cast<float4*>(out + (long long)(warp * 16 + i) * 128) + lane, o[i]);
+    if (a.state_bf16 != nullptr && layer < a.bf16_layers) {
+      // bf16 copy read by the drafter attention (same rounding it would apply)
+      bf16* ob = reinterpret_cast<bf16*>(a.state_bf16) +
+                 ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * a.slots_per_head + s0) * 128;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        uint2 pk;
+        pk.x = pack_bf16(o[i].x, o[i].y);
+        pk.y = pack_bf16(o[i].z, o[i].w);
+        *reinterpret_cast<uint2*>(ob + (long long)(warp * 16 + i) * 128 + lane * 4) = pk;
+      }
+    }
+    if (lane < 16) lse[warp * 16 + lane] = sm.merged[warp * 16 + lane];
   }
 }
 
@@ -368,6 +410,7 @@ __global__ void scatter_rows_kernel(const uint4* src, const int* idx, uint4* out
 
 __global__ void gather_rows_kernel(const uint4* src, long long src_rows, const int* idx, uint4* out, long long row_vec,
                                    int* status) {
+  asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x;
   const long long s = idx[b];
   const bool ok = s >= 0 && s < src_rows;

@@ -25,10 +25,13 @@
 
 namespace ls {
 
-constexpr int MK_THREADS = 512;
+constexpr int MK_THREADS = 256;
 constexpr int MK_MAXCAND = 4096;
 constexpr int MK_MAXRANK = 512;
 constexpr int MK_MAXTILES = 1024;
+constexpr int MK_ROWCAND = 256;    // candidate tokens kept per row by phase 1
+constexpr int MK_MAXPAIRS = 2048;  // (previous, current) candidate pairs per request
+constexpr int MK_STAGEROWS = 64;   // candidate rows staged in shared memory per request
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
@@ -91,15 +94,44 @@ __device__ float block_sum(float v, float* sv) {
   return v;
 }
 
-__global__ void __launch_bounds__(MK_THREADS) markov_argmax_kernel(const ls_markov_args a) {
-  __shared__ float latent[MK_MAXRANK];
-  __shared__ int cand[MK_MAXCAND];
-  __shared__ int n_cand;
-  __shared__ int tile_list[MK_MAXTILES];
-  __shared__ int n_tl;
-  __shared__ float red_v[32];
-  __shared__ int red_i[32];
-  const int b = blockIdx.x;
+// Band threshold: every token whose bf16 base logit is below it loses to the
+// row's maximising token for any previous token and any rounding of the bias.
+__device__ __forceinline__ float band_threshold(float m, float beta_exact) {
+  // fp32 dot-product error and norm rounding (1e-4), bf16 rounding of the bias (2^-7)
+  const float beta = beta_exact * (1.0f + 1e-4f) * (1.0f + 0.0079f);
+  const float mag = fabsf(m) + 2.0f * beta + 1.0f;
+  const float margin = exp2f(floorf(log2f(mag)) - 6.0f);  // two bf16 steps at that magnitude
+  return m - 2.0f * beta - margin;
+}
+
+__device__ __forceinline__ void row_max(const float* tmax, const int* targ, int n_tiles, float* red_v, int* red_i,
+                                        float& bv, int& bi) {
+  bv = -INFINITY;
+  bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n_tiles; i += blockDim.x) {
+    if (better(tmax[i], targ[i], bv, bi)) {
+      bv = tmax[i];
+      bi = targ[i];
+    }
+  }
+  block_argmax(bv, bi, red_v, red_i);
+}
+
+// Dynamic shared memory of the Markov kernel.  The table path and the
+// step-by-step fallback never run in the same CTA, so they share the region.
+struct MarkovTable {
+  int tok[MK_STAGEROWS];
+};
+__host__ __device__ constexpr size_t mk_table_bytes(int rank) {
+  return MK_STAGEROWS * 4 + static_cast<size_t>(2 * MK_STAGEROWS + 1) * rank * 2 + MK_MAXPAIRS * 4;
+}
+__host__ __device__ constexpr size_t mk_stepwise_bytes() { return MK_MAXCAND * 4 + MK_MAXRANK * 4; }
+
+// Exact step-by-step chain over the per-previous-token band (and over the
+// whole vocabulary when that band does not fit); used when the candidate
+// lists overflowed.
+__device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, int* cand, int* n_cand, int* tile_list,
+                               int* n_tl, float* red_v, int* red_i) {
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int n_tiles = a.vocab / 128;
@@ -110,98 +142,259 @@ __global__ void __launch_bounds__(MK_THREADS) markov_argmax_kernel(const ls_mark
     const bf16* base = base_all + row * a.vocab;
     const float* tmax = a.tile_max + row * n_tiles;
     const int* targ = a.tile_arg + row * n_tiles;
-    // Row maximum of the base logits and its first index.
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
+    float bv;
+    int bi;
+    row_max(tmax, targ, n_tiles, red_v, red_i, bv, bi);
+    if (prev < 0 || prev >= a.vocab) {
+      if (tid == 0) record_status(a.status, LS_DEV_BAD_TOKEN);
+      prev = 0;
+    }
+    const bf16* w1r = reinterpret_cast<const bf16*>(a.w1) + prev * a.rank;
+    float sq = 0.0f;
+    for (int k = tid; k < a.rank; k += blockDim.x) {
+      const float x = __bfloat162float(w1r[k]);
+      latent[k] = x;
+      sq += x * x;
+    }
+    const float norm_l = sqrtf(block_sum(sq, red_v));
+    const float thr = band_threshold(bv, (*a.w2_row_bound) * norm_l);
+    if (tid == 0) {
+      *n_cand = 0;
+      *n_tl = 0;
+    }
+    __syncthreads();
     for (int i = tid; i < n_tiles; i += blockDim.x) {
-      if (better(tmax[i], targ[i], bv, bi)) {
-        bv = tmax[i];
-        bi = targ[i];
+      if (tmax[i] >= thr) {
+        const int slot = atomicAdd(n_tl, 1);
+        if (slot < MK_MAXTILES) tile_list[slot] = i;
       }
     }
-    block_argmax(bv, bi, red_v, red_i);
-    long long tok = bi;
-    if (a.w1 != nullptr) {
-      if (prev < 0 || prev >= a.vocab) {
-        if (tid == 0) record_status(a.status, LS_DEV_BAD_TOKEN);
-        prev = 0;
-      }
-      const bf16* w1r = reinterpret_cast<const bf16*>(a.w1) + prev * a.rank;
-      float sq = 0.0f;
-      for (int k = tid; k < a.rank; k += blockDim.x) {
-        const float x = __bfloat162float(w1r[k]);
-        latent[k] = x;
-        sq += x * x;
-      }
-      const float norm_l = sqrtf(block_sum(sq, red_v));
-      const float m = bv;
-      // |bias| bound incl. fp32 dot rounding, widened for the bf16 rounding of the bias.
-      const float beta = (*a.w2_row_bound) * norm_l * (1.0f + 1e-4f) * (1.0f + 0.0079f);
-      const float mag = fabsf(m) + 2.0f * beta + 1.0f;
-      const float margin = exp2f(floorf(log2f(mag)) - 6.0f);  // two bf16 steps at that magnitude
-      const float thr = m - 2.0f * beta - margin;
-      if (tid == 0) {
-        n_cand = 0;
-        n_tl = 0;
-      }
-      __syncthreads();
-      // tiles whose maximum reaches the band
-      for (int i = tid; i < n_tiles; i += blockDim.x) {
-        if (tmax[i] >= thr) {
-          const int slot = atomicAdd(&n_tl, 1);
-          if (slot < MK_MAXTILES) tile_list[slot] = i;
-        }
-      }
-      __syncthreads();
-      const int ntl = n_tl;
-      if (ntl > MK_MAXTILES) {
-        if (tid == 0) n_cand = MK_MAXCAND + 1;  // force the full scan
-      } else {
-        // one warp per listed tile, 4 logits per lane
-        for (int ti = warp; ti < ntl; ti += nwarps) {
-          const int v0 = tile_list[ti] * 128 + lane * 4;
-          const uint2 raw = *reinterpret_cast<const uint2*>(base + v0);
-          const bf16* e4 = reinterpret_cast<const bf16*>(&raw);
+    __syncthreads();
+    const int ntl = *n_tl;
+    if (ntl > MK_MAXTILES) {
+      if (tid == 0) *n_cand = MK_MAXCAND + 1;
+    } else {
+      for (int ti = warp; ti < ntl; ti += nwarps) {
+        const int v0 = tile_list[ti] * 128 + lane * 4;
+        const uint2 raw = *reinterpret_cast<const uint2*>(base + v0);
+        const bf16* e4 = reinterpret_cast<const bf16*>(&raw);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (__bfloat162float(e4[j]) >= thr) {
-              const int slot = atomicAdd(&n_cand, 1);
-              if (slot < MK_MAXCAND) cand[slot] = v0 + j;
-            }
+        for (int j = 0; j < 4; ++j) {
+          if (__bfloat162float(e4[j]) >= thr) {
+            const int slot = atomicAdd(n_cand, 1);
+            if (slot < MK_MAXCAND) cand[slot] = v0 + j;
           }
         }
       }
-      __syncthreads();
-      const int nc = n_cand;
-      const bool full_scan = nc > MK_MAXCAND;
-      const int count = full_scan ? a.vocab : nc;
-      const bf16* w2 = reinterpret_cast<const bf16*>(a.w2);
-      float best = -INFINITY;
-      int best_i = 0x7fffffff;
-      // one warp per candidate: dot(latent, w2[v]) over the rank
-      for (int ci = warp; ci < count; ci += nwarps) {
-        const int v = full_scan ? ci : cand[ci];
-        const bf16* w2r = w2 + (long long)v * a.rank;
-        float acc = 0.0f;
-        for (int k = lane; k < a.rank; k += 32) acc += latent[k] * __bfloat162float(w2r[k]);
-        acc = warp_sum(acc);
-        const float s = bf16_round(__bfloat162float(base[v]) + bf16_round(acc));
-        if (better(s, v, best, best_i)) {
-          best = s;
-          best_i = v;
-        }
-      }
-      block_argmax(best, best_i, red_v, red_i);
-      tok = best_i;
     }
-    if (tid == 0) a.tokens[row] = tok;
-    prev = tok;
+    __syncthreads();
+    const int nc = *n_cand;
+    const bool full_scan = nc > MK_MAXCAND;
+    const int count = full_scan ? a.vocab : nc;
+    const bf16* w2 = reinterpret_cast<const bf16*>(a.w2);
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int ci = warp; ci < count; ci += nwarps) {
+      const int v = full_scan ? ci : cand[ci];
+      const bf16* w2r = w2 + (long long)v * a.rank;
+      float acc = 0.0f;
+      for (int k = lane; k < a.rank; k += 32) acc += latent[k] * __bfloat162float(w2r[k]);
+      acc = warp_sum(acc);
+      const float sv = bf16_round(__bfloat162float(base[v]) + bf16_round(acc));
+      if (better(sv, v, best, best_i)) {
+        best = sv;
+        best_i = v;
+      }
+    }
+    block_argmax(best, best_i, red_v, red_i);
+    if (tid == 0) a.tokens[row] = best_i;
+    prev = best_i;
     __syncthreads();
   }
+}
+
+// One launch.  Every CTA handles one (request, step) row: the row maximum
+// (the token itself when there is no Markov head) and the band's candidate
+// tokens.  The last row of a request to finish then runs the chain for that
+// request: the w1 rows of every possible previous token and the w2 rows of
+// every candidate are staged in shared memory with one burst of loads, the
+// bias of every (previous candidate, candidate) pair is evaluated in parallel,
+// and a single thread walks the table.  Then the accept check.
+__global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args a, int* cand_count, int* cand_all,
+                                                            int* done) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  __shared__ float red_v[32];
+  __shared__ int red_i[32];
+  __shared__ int tile_list[MK_MAXTILES];
+  __shared__ int n_tl, n_c;
+  __shared__ int cnt[17], off[18], roff[18];
+  __shared__ int last_row, use_table;
+  asm volatile("griddepcontrol.launch_dependents;");
+  const long long row = blockIdx.x;
+  const int P = a.block;
+  const int b = static_cast<int>(row / P);
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int n_tiles = a.vocab / 128;
+  const float* tmax = a.tile_max + row * n_tiles;
+  const int* targ = a.tile_arg + row * n_tiles;
+  float m;
+  int arg;
+  row_max(tmax, targ, n_tiles, red_v, red_i, m, arg);
+  if (a.w1 == nullptr) {
+    if (tid == 0) a.tokens[row] = arg;
+  } else {
+    const float thr = band_threshold(m, (*a.w1_row_bound) * (*a.w2_row_bound));
+    if (tid == 0) {
+      n_tl = 0;
+      n_c = 0;
+    }
+    __syncthreads();
+    for (int i = tid; i < n_tiles; i += blockDim.x) {
+      if (tmax[i] >= thr) {
+        const int slot = atomicAdd(&n_tl, 1);
+        if (slot < MK_MAXTILES) tile_list[slot] = i;
+      }
+    }
+    __syncthreads();
+    const int ntl = n_tl;
+    int* my = cand_all + row * MK_ROWCAND;
+    if (ntl <= MK_MAXTILES) {
+      const bf16* base = reinterpret_cast<const bf16*>(a.base) + row * a.vocab;
+      for (int ti = warp; ti < ntl; ti += nwarps) {
+        const int v0 = tile_list[ti] * 128 + lane * 4;
+        const uint2 raw = *reinterpret_cast<const uint2*>(base + v0);
+        const bf16* e4 = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (__bfloat162float(e4[j]) >= thr) {
+            const int slot = atomicAdd(&n_c, 1);
+            if (slot < MK_ROWCAND) my[slot] = v0 + j;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (tid == 0) cand_count[row] = (ntl > MK_MAXTILES || n_c > MK_ROWCAND) ? -1 : n_c;
+  }
+  // publish this row; the request's last row to finish continues with the chain
+  __syncthreads();
+  if (tid == 0) {
+    const int prev_done = atomic_add_acq_rel_gpu(&done[b], 1);
+    last_row = prev_done == P - 1;
+    if (last_row) done[b] = 0;  // leave the counter zeroed for the next launch
+  }
+  __syncthreads();
+  if (!last_row) return;
+
+  if (a.w1 != nullptr) {
+    const int R = a.rank;
+    if (tid < P) cnt[tid] = __ldcg(&cand_count[(long long)b * P + tid]);
+    __syncthreads();
+    if (tid == 0) {
+      int ok = 1, total = 0, rows = 0;
+      off[0] = 0;
+      roff[0] = 0;
+      for (int t = 0; t < P; ++t) {
+        const int c = cnt[t];
+        if (c < 1) ok = 0;
+        const int prev_n = t == 0 ? 1 : cnt[t - 1];
+        total += prev_n * (c < 1 ? 0 : c);
+        off[t + 1] = total;
+        rows += c < 1 ? 0 : c;
+        roff[t + 1] = rows;
+      }
+      use_table = ok && total <= MK_MAXPAIRS && rows <= MK_STAGEROWS;
+    }
+    __syncthreads();
+    if (!use_table) {
+      float* latent = reinterpret_cast<float*>(dsm);
+      int* cand = reinterpret_cast<int*>(dsm + MK_MAXRANK * 4);
+      stepwise_chain(a, b, latent, cand, &n_c, tile_list, &n_tl, red_v, red_i);
+    } else {
+      const int rows = roff[P];
+      int* tok = reinterpret_cast<int*>(dsm);
+      bf16* w1s = reinterpret_cast<bf16*>(dsm + MK_STAGEROWS * 4);
+      bf16* w2s = w1s + (size_t)(MK_STAGEROWS + 1) * R;
+      float* pair_val = reinterpret_cast<float*>(w2s + (size_t)MK_STAGEROWS * R);
+      for (int i = tid; i < rows; i += blockDim.x) {
+        int t = 0;
+        while (roff[t + 1] <= i) ++t;
+        tok[i] = __ldcg(&cand_all[((long long)b * P + t) * MK_ROWCAND + (i - roff[t])]);
+      }
+      __syncthreads();
+      const bf16* w1 = reinterpret_cast<const bf16*>(a.w1);
+      const bf16* w2 = reinterpret_cast<const bf16*>(a.w2);
+      const int vec_per_row = R / 8;
+      // w1 row 0 = anchor, w1 row 1 + i = candidate i (a possible previous token)
+      for (int e = tid; e < (rows + 1) * vec_per_row; e += blockDim.x) {
+        const int r = e / vec_per_row, k = (e - r * vec_per_row) * 8;
+        long long v = r == 0 ? a.anchors[b] : tok[r - 1];
+        if (v < 0 || v >= a.vocab) {
+          record_status(a.status, LS_DEV_BAD_TOKEN);
+          v = 0;
+        }
+        *reinterpret_cast<uint4*>(w1s + (size_t)r * R + k) = *reinterpret_cast<const uint4*>(w1 + v * R + k);
+      }
+      for (int e = tid; e < rows * vec_per_row; e += blockDim.x) {
+        const int r = e / vec_per_row, k = (e - r * vec_per_row) * 8;
+        *reinterpret_cast<uint4*>(w2s + (size_t)r * R + k) =
+            *reinterpret_cast<const uint4*>(w2 + (long long)tok[r] * R + k);
+      }
+      __syncthreads();
+      const int total = off[P];
+      const bf16* base_all = reinterpret_cast<const bf16*>(a.base);
+      for (int q = warp; q < total; q += nwarps) {
+        int t = 0;
+        while (off[t + 1] <= q) ++t;
+        const int n_t = cnt[t];
+        const int pi = (q - off[t]) / n_t, ci = (q - off[t]) % n_t;
+        const int prow = t == 0 ? 0 : 1 + roff[t - 1] + pi;  // w1s row of the previous token
+        const int crow = roff[t] + ci;                           // w2s row of the candidate
+        float acc = 0.0f;
+        for (int k = lane * 8; k < R; k += 256) {
+          const uint4 x = *reinterpret_cast<const uint4*>(w1s + (size_t)prow * R + k);
+          const uint4 y = *reinterpret_cast<const uint4*>(w2s + (size_t)crow * R + k);
+          const bf16* xe = reinterpret_cast<const bf16*>(&x);
+          const bf16* ye = reinterpret_cast<const bf16*>(&y);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc += __bfloat162float(xe[e]) * __bfloat162float(ye[e]);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) {
+          const float bv = __bfloat162float(base_all[((long long)b * P + t) * a.vocab + tok[crow]]);
+          pair_val[q] = bf16_round(bv + bf16_round(acc));
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int pos = 0;  // position of the previous token in the previous step's list (anchor: 0)
+        for (int t = 0; t < P; ++t) {
+          const int n_t = cnt[t];
+          float best = -INFINITY;
+          int best_tok = 0x7fffffff, best_j = 0;
+          for (int j = 0; j < n_t; ++j) {
+            const float v = pair_val[off[t] + pos * n_t + j];
+            const int tk = tok[roff[t] + j];
+            if (better(v, tk, best, best_tok)) {
+              best = v;
+              best_tok = tk;
+              best_j = j;
+            }
+          }
+          red_i[t] = best_tok;
+          pos = best_j;
+        }
+      }
+      __syncthreads();
+      if (tid < P) a.tokens[(long long)b * P + tid] = red_i[tid];
+    }
+  }
+  __syncthreads();
   if (a.target != nullptr && a.accept_out != nullptr && tid == 0) {
     long long acc = 0;
-    for (int t = 0; t < a.block; ++t) {
-      if (a.target[(long long)b * a.target_ld + t] != a.tokens[(long long)b * a.block + t]) break;
+    for (int t = 0; t < P; ++t) {
+      if (a.target[(long long)b * a.target_ld + t] != __ldcg(&a.tokens[(long long)b * P + t])) break;
       ++acc;
     }
     a.accept_out[b] = acc;
@@ -247,16 +440,50 @@ __global__ void row_norm_bound_kernel(const bf16* m, int vocab, int rank, float*
 
 using namespace ls;
 
-extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a) {
+extern "C" size_t ls_markov_workspace_bytes(int batch, int block) {
+  if (batch <= 0 || block <= 0) return 0;
+  const size_t rows = static_cast<size_t>(batch) * block;
+  // [done counters (batch)] [candidate counts (rows)] [candidates (rows x MK_ROWCAND)]
+  return 256 + (static_cast<size_t>(batch) * 4 + 255) / 256 * 256 + (rows * 4 + 255) / 256 * 256 +
+         rows * MK_ROWCAND * 4;
+}
+
+extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes) {
   if (a == nullptr || a->base == nullptr || a->tile_max == nullptr || a->tile_arg == nullptr || a->anchors == nullptr ||
       a->tokens == nullptr)
     return set_error(LS_ERR_INVALID, "ls_markov_argmax: null pointer argument");
   if (a->batch <= 0) return LS_OK;
-  if (a->vocab <= 0 || a->vocab % 128 || a->block < 1)
-    return set_error(LS_ERR_UNSUPPORTED, "ls_markov_argmax: vocab must be a positive multiple of 128");
-  if (a->w1 != nullptr && (a->w2 == nullptr || a->w2_row_bound == nullptr || a->rank < 1 || a->rank > MK_MAXRANK))
-    return set_error(LS_ERR_INVALID, "ls_markov_argmax: Markov head needs w2, its row bound and 1 <= rank <= 512");
-  markov_argmax_kernel<<<a->batch, MK_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*a);
+  if (a->vocab <= 0 || a->vocab % 128 || a->block < 1 || a->block > 16)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_markov_argmax: vocab must be a positive multiple of 128, block <= 16");
+  if (a->w1 != nullptr && (a->w2 == nullptr || a->w1_row_bound == nullptr || a->w2_row_bound == nullptr ||
+                           a->rank < 64 || a->rank > MK_MAXRANK || a->rank % 64))
+    return set_error(LS_ERR_INVALID,
+                     "ls_markov_argmax: Markov head needs w2, both row bounds and a rank in [64, 512], multiple of 64");
+  const size_t need = ls_markov_workspace_bytes(a->batch, a->block);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(LS_ERR_WORKSPACE, "ls_markov_argmax: workspace %zu < %zu", workspace_bytes, need);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return set_error(LS_ERR_INVALID, "ls_markov_argmax: workspace must be 256-byte aligned");
+  const size_t rows = static_cast<size_t>(a->batch) * a->block;
+  uint8_t* w = reinterpret_cast<uint8_t*>(workspace) + 256;
+  int* done = reinterpret_cast<int*>(w);
+  w += (static_cast<size_t>(a->batch) * 4 + 255) / 256 * 256;
+  int* counts = reinterpret_cast<int*>(w);
+  w += (rows * 4 + 255) / 256 * 256;
+  int* cand = reinterpret_cast<int*>(w);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  size_t dsmem = 0;
+  if (a->w1 != nullptr) {
+    dsmem = mk_table_bytes(a->rank);
+    if (mk_stepwise_bytes() > dsmem) dsmem = mk_stepwise_bytes();
+  }
+  static size_t configured = 0;
+  if (dsmem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(markov_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dsmem));
+    if (e != cudaSuccess) return set_cuda_error("ls_markov_argmax: cudaFuncSetAttribute", e);
+    configured = dsmem;
+  }
+  markov_kernel<<<static_cast<unsigned>(rows), MK_THREADS, dsmem, st>>>(*a, counts, cand, done);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_markov_argmax: launch", e);
 }

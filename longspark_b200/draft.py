@@ -179,6 +179,7 @@ class LongSparkDraft:
         if prefill:
             self.pools.summary_out.index_copy_(0, slot_t.long(), extra["global_output"].to(dev, torch.float32))
             self.pools.summary_lse.index_copy_(0, slot_t.long(), extra["global_lse"].to(dev, torch.float32))
+            self.pools.sync_summary_bf16(slot_t)
         else:
             self.engine.refresh(slots=slot_t, seq_lens=lens_t, commit_lens=cnt_t, page_table=table, batch=B)
 

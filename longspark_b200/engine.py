@@ -43,35 +43,43 @@ class DraftWeights:
         def t(name):
             return W[name].to(device=dev, dtype=torch.bfloat16).contiguous()
 
-        self.enc_w1 = t("draft_state_encoder.proj.net.0.weight")
-        self.enc_w2 = t("draft_state_encoder.proj.net.2.weight")
+        def tiled(w):
+            # GEMM weights live in the tensor-core tile order (ls_tile_weight)
+            out = ops.TiledWeight(w)
+            del w
+            return out
+
+        self.enc_w1 = tiled(t("draft_state_encoder.proj.net.0.weight"))
+        self.enc_w2 = tiled(t("draft_state_encoder.proj.net.2.weight"))
         self.enc_norm = t("draft_state_encoder.norm.weight")
         self.pos_emb = t("parallel_shifted_input.position_embedding.weight")
-        self.sh_w1 = t("parallel_shifted_input.proj.net.0.weight")
-        self.sh_w2 = t("parallel_shifted_input.proj.net.2.weight")
+        self.sh_w1 = tiled(t("parallel_shifted_input.proj.net.0.weight"))
+        self.sh_w2 = tiled(t("parallel_shifted_input.proj.net.2.weight"))
         self.sh_norm = t("parallel_shifted_input.norm.weight")
         self.layers = []
         for j in range(shape.draft_layers):
             p = f"parallel_qwen_layers.{j}."
             self.layers.append(dict(
-                qkv=torch.cat([t(p + "self_attn.q_proj.weight"), t(p + "self_attn.k_proj.weight"),
-                               t(p + "self_attn.v_proj.weight")], dim=0).contiguous(),
-                o=t(p + "self_attn.o_proj.weight"),
+                qkv=tiled(torch.cat([t(p + "self_attn.q_proj.weight"), t(p + "self_attn.k_proj.weight"),
+                                     t(p + "self_attn.v_proj.weight")], dim=0)),
+                o=tiled(t(p + "self_attn.o_proj.weight")),
                 q_norm=t(p + "self_attn.q_norm.weight"), k_norm=t(p + "self_attn.k_norm.weight"),
                 in_norm=t(p + "input_layernorm.weight"), post_norm=t(p + "post_attention_layernorm.weight"),
-                gate_up=_interleave_gate_up(t(p + "mlp.gate_proj.weight"), t(p + "mlp.up_proj.weight")),
-                down=t(p + "mlp.down_proj.weight")))
+                gate_up=tiled(_interleave_gate_up(t(p + "mlp.gate_proj.weight"), t(p + "mlp.up_proj.weight"))),
+                down=tiled(t(p + "mlp.down_proj.weight"))))
         self.learned_query = t("global16_raw256_reference.global_query_generator.learned_query")
         self.embed = t("model.embed_tokens.weight")
-        self.lm_head = t("lm_head.weight")
+        self.lm_head = tiled(t("lm_head.weight"))
         self.final_norm = t("model.norm.weight")
         if shape.markov_rank:
             self.w1 = t("parallel_markov_head.markov_w1.weight")
             self.w2 = t("parallel_markov_head.markov_w2.weight")
+            self.w1_bound = torch.zeros(1, dtype=torch.float32, device=dev)
             self.w2_bound = torch.zeros(1, dtype=torch.float32, device=dev)
+            ops.row_norm_bound(self.w1, self.w1_bound)
             ops.row_norm_bound(self.w2, self.w2_bound)
         else:
-            self.w1 = self.w2 = self.w2_bound = None
+            self.w1 = self.w2 = self.w1_bound = self.w2_bound = None
         if inv_freq is None:
             d = shape.head_dim
             inv_freq = 1.0 / (float(shape.rope_theta) ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
@@ -99,6 +107,19 @@ class ViewPools:
     summary_lse: torch.Tensor   # [capacity, L_tap, Hq, S] fp32
     hidden: torch.Tensor        # [capacity, L_tap, H] bf16
     ring_pages: int = 0         # > 0: page_table rows are rings of this many pages
+    summary_bf16: torch.Tensor = None  # [capacity, L_draft, Hq, S, 128] bf16 copy the attention reads
+
+    def sync_summary_bf16(self, slots=None):
+        """Refresh the bf16 copy from the fp32 state (after the state was set by
+        other means than the refresh kernel, e.g. a prefill)."""
+        if self.summary_bf16 is None:
+            return
+        n = self.summary_bf16.shape[1]
+        if slots is None:
+            self.summary_bf16.copy_(self.summary_out[:, :n])
+        else:
+            idx = slots.long()
+            self.summary_bf16.index_copy_(0, idx, self.summary_out.index_select(0, idx)[:, :n].to(torch.bfloat16))
 
 
 class DraftEngine:
@@ -131,6 +152,7 @@ class DraftEngine:
             tile_max=torch.zeros(M, V // 128, dtype=torch.float32, device=dev),
             tile_arg=torch.zeros(M, V // 128, dtype=torch.int32, device=dev),
             positions=torch.zeros(M, dtype=torch.int32, device=dev),
+            rope=torch.zeros(M, 128, dtype=torch.float32, device=dev),
             tokens=torch.zeros(B, P, dtype=torch.int64, device=dev),
             accept=torch.zeros(B, dtype=torch.int64, device=dev),
             status=torch.zeros(1, dtype=torch.int32, device=dev),
@@ -145,6 +167,11 @@ class DraftEngine:
         self.gemm_ws = torch.zeros(ws, dtype=torch.uint8, device=dev)
         self.attn_ws = torch.zeros(max(1, ops.attention_workspace_bytes(B, Hq, Hkv, s.window, s.slots)),
                                    dtype=torch.uint8, device=dev)
+        self.markov_ws = torch.zeros(max(1, ops.markov_workspace_bytes(B, P)), dtype=torch.uint8, device=dev)
+        if pools.summary_bf16 is None:
+            pools.summary_bf16 = torch.empty(pools.summary_out.shape[0], s.draft_layers, Hq, s.slots, 128,
+                                             dtype=torch.bfloat16, device=dev)
+            pools.sync_summary_bf16()
         self.graphs = {}
         self.graph_replays = 0
 
@@ -156,12 +183,14 @@ class DraftEngine:
                           commit_lens=commit_lens, slots=slots, learned_query=self.w.learned_query,
                           state_out=p.summary_out, state_lse=p.summary_lse, max_commit=self.shape.max_commit,
                           ring_pages=p.ring_pages, softmax_scale=self.shape.head_dim ** -0.5,
-                          status=self.buf["status"], batch=batch)
+                          status=self.buf["status"], batch=batch, state_bf16=p.summary_bf16)
 
     # ------------------------------------------------------------------ drafter
-    def draft(self, *, slots, seq_lens, anchors, page_table, target=None, batch=None):
+    def draft(self, *, slots, seq_lens, anchors, page_table, target=None, batch=None, slots_are_rows=False):
         """One parallel drafter pass: writes ``buf['tokens']`` [B, P] (and
-        ``buf['accept']`` [B] when ``target`` is given) and bf16 base logits."""
+        ``buf['accept']`` [B] when ``target`` is given) and bf16 base logits.
+        ``slots_are_rows``: the caller guarantees ``slots == arange(B)``, so the
+        boundary hidden states are read in place instead of gathered."""
         s, w, p, b = self.shape, self.w, self.pools, self.buf
         B = anchors.shape[0] if batch is None else batch
         P = s.block
@@ -170,13 +199,18 @@ class DraftEngine:
         ws = self.gemm_ws
         st = b["status"]
         # state encoder
-        ops.gather_rows(p.hidden.view(p.hidden.shape[0], -1), slots, b["enc_in"], rows=B, status=st)
-        ops.gemm(b["enc_in"], w.enc_w1, b["t"], workspace=ws, epilogue=N.EPI_SILU, rows=B, status=st)
+        if slots_are_rows:
+            enc_in = p.hidden.view(p.hidden.shape[0], -1)
+        else:
+            enc_in = b["enc_in"]
+            ops.gather_rows(p.hidden.view(p.hidden.shape[0], -1), slots, enc_in, rows=B, status=st)
+        ops.gemm(enc_in, w.enc_w1, b["t"], workspace=ws, epilogue=N.EPI_SILU, rows=B, status=st)
         ops.gemm(b["t"], w.enc_w2, b["u"], workspace=ws, rows=B, status=st)
         ops.rmsnorm(b["u"], w.enc_norm, b["latest"], s.rms_eps, mode=0, rows=B)
         # shifted input
         ops.shifted_input(anchors, seq_lens, b["positions"], w.embed, w.pos_emb, b["latest"], b["xsh"],
-                          block=P, mask_token_id=s.mask_token_id, status=st)
+                          block=P, mask_token_id=s.mask_token_id, status=st, inv_freq=w.inv_freq,
+                          rope_table=b["rope"], batch=B)
         ops.gemm(b["xsh"], w.sh_w1, b["f1"], workspace=ws, epilogue=N.EPI_SILU, rows=M, status=st)
         ops.gemm(b["f1"], w.sh_w2, b["g"], workspace=ws, rows=M, status=st)
         ops.rmsnorm(b["g"], w.sh_norm, b["h"], s.rms_eps, mode=0, rows=M)
@@ -185,12 +219,13 @@ class DraftEngine:
             ops.rmsnorm(b["h"], L["in_norm"], b["xn"], s.rms_eps, mode=0, rows=M)
             ops.gemm(b["xn"], L["qkv"], b["qkv"], workspace=ws, epilogue=N.EPI_QKV, rows=M, q_heads=Hq,
                      kv_heads=Hkv, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"], norm_eps=s.rms_eps,
-                     positions=b["positions"], inv_freq=w.inv_freq, status=st)
+                     positions=b["positions"], inv_freq=w.inv_freq, rope_table=b["rope"], status=st)
             ops.draft_attention(qkv=b["qkv"], block=P, kv_k=p.kv_k[v], kv_v=p.kv_v[v], page_table=page_table,
                                 seq_lens=seq_lens, window=s.window, learned_query=w.learned_query[v],
                                 state_out=p.summary_out[:, v], slots=slots, out=b["attn"], workspace=self.attn_ws,
                                 q_heads=Hq, kv_heads=Hkv, ring_pages=p.ring_pages,
-                                softmax_scale=s.head_dim ** -0.5, status=st, batch=B)
+                                softmax_scale=s.head_dim ** -0.5, status=st, batch=B,
+                                state_bf16=p.summary_bf16[:, v] if p.summary_bf16 is not None else None)
             ops.gemm(b["attn"], L["o"], b["h"], workspace=ws, epilogue=N.EPI_RESIDUAL, rows=M, residual=b["h"],
                      status=st)
             ops.rmsnorm(b["h"], L["post_norm"], b["xn"], s.rms_eps, mode=0, rows=M)
@@ -201,7 +236,8 @@ class DraftEngine:
         ops.gemm(b["xn"], w.lm_head, b["logits"], workspace=ws, epilogue=N.EPI_LMHEAD, rows=M,
                  tile_max=b["tile_max"], tile_arg=b["tile_arg"], status=st)
         ops.markov_argmax(base=b["logits"], tile_max=b["tile_max"], tile_arg=b["tile_arg"], anchors=anchors,
-                          tokens=b["tokens"], block=P, w1=w.w1, w2=w.w2, w2_bound=w.w2_bound, target=target,
+                          tokens=b["tokens"], block=P, workspace=self.markov_ws, w1=w.w1, w2=w.w2,
+                          w1_bound=w.w1_bound, w2_bound=w.w2_bound, target=target,
                           accept_out=b["accept"] if target is not None else None, status=st, batch=B)
 
     def corrected_logits(self, anchors, out, batch=None):
@@ -219,11 +255,12 @@ class DraftEngine:
                  status=b["status"])
         return out
 
-    def round(self, *, slots, seq_lens, commit_lens, anchors, page_table, target=None, batch=None):
+    def round(self, *, slots, seq_lens, commit_lens, anchors, page_table, target=None, batch=None,
+              slots_are_rows=False):
         """Refresh then draft (one full drafting round)."""
         self.refresh(slots=slots, seq_lens=seq_lens, commit_lens=commit_lens, page_table=page_table, batch=batch)
         self.draft(slots=slots, seq_lens=seq_lens, anchors=anchors, page_table=page_table, target=target,
-                   batch=batch)
+                   batch=batch, slots_are_rows=slots_are_rows)
 
     # ------------------------------------------------------------------ status
     def device_status(self):
@@ -240,8 +277,10 @@ class GraphedDraft:
     whole round — every kernel of the pass, including the greedy Markov chain
     the reference runs eagerly — replays as one graph."""
 
-    def __init__(self, engine: DraftEngine, batch: int, *, with_refresh: bool, with_target: bool):
+    def __init__(self, engine: DraftEngine, batch: int, *, with_refresh: bool, with_target: bool,
+                 slots_are_rows: bool = False):
         self.engine = engine
+        self.slots_are_rows = slots_are_rows
         self.batch = batch
         dev = engine.device
         tstride = engine.pools.page_table.shape[1]
@@ -261,7 +300,7 @@ class GraphedDraft:
             e.refresh(slots=self.slots, seq_lens=self.seq_lens, commit_lens=self.commit_lens,
                       page_table=self.page_table, batch=self.batch)
         e.draft(slots=self.slots, seq_lens=self.seq_lens, anchors=self.anchors, page_table=self.page_table,
-                target=self.target, batch=self.batch)
+                target=self.target, batch=self.batch, slots_are_rows=self.slots_are_rows)
 
     def load(self, *, slots, seq_lens, anchors, page_table, commit_lens=None, target=None):
         self.slots.copy_(slots, non_blocking=True)

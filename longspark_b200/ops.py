@@ -38,21 +38,48 @@ def _require_cuda(*ts):
             raise ValueError("longspark_b200 kernels require CUDA tensors")
 
 
+class TiledWeight:
+    """A [n_out, k] bf16 weight re-laid into the tensor-core tile order
+    (``ls_tile_weight``): 128 x 64 tiles, contiguous per tile, pre-swizzled, so
+    the GEMM streams each tile with one contiguous bulk copy."""
+
+    def __init__(self, w):
+        if w.dtype != torch.bfloat16 or w.ndim != 2 or w.shape[0] % 128 or w.shape[1] % 64:
+            raise ValueError("tiled weights must be bf16 [n_out % 128 == 0, k % 64 == 0]")
+        self.n_out, self.k = w.shape
+        w = w.contiguous()
+        self.data = torch.empty_like(w)
+        N.call("ls_tile_weight", _stream(w.device), _p(w), _p(self.data), self.n_out, self.k)
+        self.shape = (self.n_out, self.k)
+        self.device = w.device
+
+    def numel(self):
+        return self.data.numel()
+
+    def element_size(self):
+        return 2
+
+
 def gemm(x, w, out, *, workspace, epilogue=N.EPI_STORE, rows=None, residual=None, q_heads=0, kv_heads=0,
-         q_norm_w=None, k_norm_w=None, norm_eps=1e-6, positions=None, inv_freq=None, tile_max=None,
-         tile_arg=None, base=None, status=None):
-    """out = epilogue(x[:rows] @ w.T) on the tcgen05 tensor cores (see ``ls_gemm``)."""
-    _require_cuda(x, w, out, workspace)
-    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+         q_norm_w=None, k_norm_w=None, norm_eps=1e-6, positions=None, inv_freq=None, rope_table=None,
+         tile_max=None, tile_arg=None, base=None, status=None):
+    """out = epilogue(x[:rows] @ w.T) on the tcgen05 tensor cores (see ``ls_gemm``).
+    ``w`` is a row-major [n_out, k] bf16 tensor or a ``TiledWeight``."""
+    tiled = isinstance(w, TiledWeight)
+    wt = w.data if tiled else w
+    _require_cuda(x, wt, out, workspace)
+    if x.dtype != torch.bfloat16 or wt.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
         raise ValueError("gemm operands must be bf16")
-    if x.stride(-1) != 1 or w.stride(-1) != 1 or out.stride(-1) != 1 or not w.is_contiguous():
+    if x.stride(-1) != 1 or out.stride(-1) != 1 or not wt.is_contiguous():
         raise ValueError("gemm operands must be contiguous along K")
     rows = x.shape[0] if rows is None else rows
-    a = N.GemmArgs(x=_p(x), w=_p(w), rows=rows, k=w.shape[1], n_out=w.shape[0], x_ld=x.stride(0),
+    n_out, k = w.shape
+    a = N.GemmArgs(x=_p(x), w=_p(wt), w_layout=N.W_TILED if tiled else N.W_ROWMAJOR, rows=rows, k=k, n_out=n_out,
+                   x_ld=x.stride(0),
                    epilogue=epilogue, out=_p(out), out_ld=out.stride(0), residual=_p(residual),
                    res_ld=0 if residual is None else residual.stride(0), q_heads=q_heads, kv_heads=kv_heads,
                    q_norm_w=_p(q_norm_w), k_norm_w=_p(k_norm_w), norm_eps=norm_eps, positions=_p(positions),
-                   inv_freq=_p(inv_freq), tile_max=_p(tile_max), tile_arg=_p(tile_arg), base=_p(base),
+                   inv_freq=_p(inv_freq), rope_table=_p(rope_table), tile_max=_p(tile_max), tile_arg=_p(tile_arg), base=_p(base),
                    base_ld=0 if base is None else base.stride(0), status=_p(status))
     N.call("ls_gemm", _stream(x.device), C.byref(a), _p(workspace), workspace.numel() * workspace.element_size())
     return out
@@ -71,12 +98,13 @@ def rmsnorm(x, w, out, eps, *, mode=0, rows=None):
     return out
 
 
-def shifted_input(anchors, seq_lens, positions, embed, pos_emb, latest, out, *, block, mask_token_id, status=None):
+def shifted_input(anchors, seq_lens, positions, embed, pos_emb, latest, out, *, block, mask_token_id, status=None,
+                  inv_freq=None, rope_table=None, batch=None):
     _require_cuda(anchors, embed, pos_emb, latest, out)
-    batch = anchors.shape[0]
-    N.call("ls_shifted_input", _stream(out.device), _p(anchors), _p(seq_lens), _p(positions), _p(embed),
-           _p(pos_emb), _p(latest), _p(out), batch, block, embed.shape[1], embed.shape[0], mask_token_id,
-           _p(status))
+    batch = anchors.shape[0] if batch is None else batch
+    N.call("ls_shifted_input", _stream(out.device), _p(anchors), _p(seq_lens), _p(positions), _p(inv_freq),
+           _p(rope_table), _p(embed), _p(pos_emb), _p(latest), _p(out), batch, block, embed.shape[1],
+           embed.shape[0], mask_token_id, _p(status))
     return out
 
 
@@ -170,7 +198,7 @@ def merge_accepted_positions_(*, state_output, state_lse, position_scores, value
 
 
 def refresh_views(*, kv_k, kv_v, page_table, seq_lens, commit_lens, slots, learned_query, state_out, state_lse,
-                  max_commit, ring_pages=0, softmax_scale=128 ** -0.5, status=None, batch=None):
+                  max_commit, ring_pages=0, softmax_scale=128 ** -0.5, status=None, batch=None, state_bf16=None):
     """Fused paged view refresh over all tapped layers (see ``ls_refresh_views``).
 
     kv_k/kv_v [L_tap, pages, 16, Hkv, 128] bf16; page_table [B, max_pages]
@@ -192,7 +220,8 @@ def refresh_views(*, kv_k, kv_v, page_table, seq_lens, commit_lens, slots, learn
     a = N.RefreshArgs(kv_k=_p(kv_k), kv_v=_p(kv_v), pool_pages=pages, page_table=_p(page_table),
                       table_stride=page_table.stride(0), ring_pages=ring_pages, seq_lens=_p(seq_lens),
                       commit_lens=_p(commit_lens), slots=_p(slots), learned_query=_p(learned_query),
-                      state_out=_p(state_out), state_lse=_p(state_lse), capacity=state_out.shape[0],
+                      state_out=_p(state_out), state_lse=_p(state_lse), state_bf16=_p(state_bf16),
+                      bf16_layers=0 if state_bf16 is None else state_bf16.shape[1], capacity=state_out.shape[0],
                       batch=batch, tap_layers=L,
                       q_heads=hq, kv_heads=hkv, slots_per_head=s, max_commit=max_commit,
                       softmax_scale=float(softmax_scale), status=_p(status))
@@ -221,7 +250,7 @@ def attention_workspace_bytes(batch, q_heads, kv_heads, window, slots):
 
 def draft_attention(*, qkv, block, kv_k, kv_v, page_table, seq_lens, window, learned_query, state_out, slots, out,
                     workspace, q_heads, kv_heads, ring_pages=0, softmax_scale=128 ** -0.5, status=None,
-                    batch=None):
+                    batch=None, state_bf16=None):
     """Block queries over [summary | window | local].  qkv [B*P, (Hq+2Hkv)*128]
     (rotated q, rotated k, v); kv_k/kv_v one tapped layer [pages, 16, Hkv, 128];
     learned_query [Hq, S, 128]; state_out [cap, ..., Hq, S, 128] fp32 (entry of
@@ -232,7 +261,9 @@ def draft_attention(*, qkv, block, kv_k, kv_v, page_table, seq_lens, window, lea
                         page_table=_p(page_table),
                         table_stride=page_table.stride(0), ring_pages=ring_pages, seq_lens=_p(seq_lens),
                         window=window, learned_query=_p(learned_query), state_out=_p(state_out),
-                        state_stride=state_out.stride(0), slots=_p(slots), capacity=state_out.shape[0],
+                        state_stride=state_out.stride(0), state_bf16=_p(state_bf16),
+                        state_bf16_stride=0 if state_bf16 is None else state_bf16.stride(0),
+                        slots=_p(slots), capacity=state_out.shape[0],
                         slots_per_head=learned_query.shape[1],
                         batch=batch, q_heads=q_heads, kv_heads=kv_heads, softmax_scale=float(softmax_scale),
                         out=_p(out), status=_p(status))
@@ -241,15 +272,22 @@ def draft_attention(*, qkv, block, kv_k, kv_v, page_table, seq_lens, window, lea
     return out
 
 
-def markov_argmax(*, base, tile_max, tile_arg, anchors, tokens, block, w1=None, w2=None, w2_bound=None,
-                  target=None, accept_out=None, status=None, batch=None):
-    _require_cuda(base, tile_max, tile_arg, anchors, tokens)
+def markov_workspace_bytes(batch, block):
+    return int(N.lib().ls_markov_workspace_bytes(batch, block))
+
+
+def markov_argmax(*, base, tile_max, tile_arg, anchors, tokens, block, workspace, w1=None, w2=None, w1_bound=None,
+                  w2_bound=None, target=None, accept_out=None, status=None, batch=None):
+    """Greedy Markov chain (or plain argmax without a head) over bf16 base logits."""
+    _require_cuda(base, tile_max, tile_arg, anchors, tokens, workspace)
     batch = anchors.shape[0] if batch is None else batch
     a = N.MarkovArgs(base=_p(base), tile_max=_p(tile_max), tile_arg=_p(tile_arg), w1=_p(w1), w2=_p(w2),
-                     w2_row_bound=_p(w2_bound), rank=0 if w1 is None else w1.shape[1], anchors=_p(anchors),
-                     tokens=_p(tokens), target=_p(target), target_ld=0 if target is None else target.stride(0),
-                     accept_out=_p(accept_out), batch=batch, block=block, vocab=base.shape[-1], status=_p(status))
-    N.call("ls_markov_argmax", _stream(tokens.device), C.byref(a))
+                     w1_row_bound=_p(w1_bound), w2_row_bound=_p(w2_bound), rank=0 if w1 is None else w1.shape[1],
+                     anchors=_p(anchors), tokens=_p(tokens), target=_p(target),
+                     target_ld=0 if target is None else target.stride(0), accept_out=_p(accept_out), batch=batch,
+                     block=block, vocab=base.shape[-1], status=_p(status))
+    N.call("ls_markov_argmax", _stream(tokens.device), C.byref(a), _p(workspace),
+           workspace.numel() * workspace.element_size())
     return tokens
 
 

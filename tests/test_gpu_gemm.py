@@ -155,3 +155,18 @@ def test_gemms_of_different_shapes_share_one_workspace():
         ops.gemm(x, w, out, workspace=ws)
         ref = (x.float() @ w.float().T).to(torch.bfloat16)
         assert_bf16_close(to_np(out), to_np(ref), steps=1.0, exact_frac=0.97, what=f"shared ws {rows}x{k}x{n}")
+
+
+@pytest.mark.parametrize("rows,k,n", [(15, 4096, 4096), (1, 20480, 4096), (16, 4096, 151936), (300, 256, 384)])
+def test_tiled_weights_match_row_major(rows, k, n):
+    """The tensor-core tile layout streams the same weights: results are bit-identical."""
+    x = _rand(rows, k)
+    w = _rand(n, k, std=0.02)
+    wt = ops.TiledWeight(w)
+    a = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+    b = torch.empty_like(a)
+    ws = gemm_ws(rows, k, n)
+    ops.gemm(x, w, a, workspace=ws)
+    ops.gemm(x, wt, b, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)

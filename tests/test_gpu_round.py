@@ -131,15 +131,18 @@ def test_round_with_refresh_and_graph_replay():
     g = GraphedDraft(e2, batch, with_refresh=True, with_target=True)
     g.load(slots=slots, seq_lens=lens, anchors=anchors, page_table=table, commit_lens=commit, target=target)
     # the warm-up run inside capture() performs one real refresh: restore the state first
-    state = (e2.pools.summary_out.clone(), e2.pools.summary_lse.clone())
+    state = (e2.pools.summary_out.clone(), e2.pools.summary_lse.clone(), e2.pools.summary_bf16.clone())
     g.capture()
     e2.pools.summary_out.copy_(state[0])
     e2.pools.summary_lse.copy_(state[1])
+    e2.pools.summary_bf16.copy_(state[2])
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(e1.buf["tokens"][:batch], e2.buf["tokens"][:batch])
     assert torch.equal(e1.buf["logits"][:batch * shape.block], e2.buf["logits"][:batch * shape.block])
     assert torch.equal(e1.pools.summary_out, e2.pools.summary_out)
+    # the bf16 copy the attention reads is the rounded fp32 state
+    assert torch.equal(e1.pools.summary_bf16, e1.pools.summary_out[:, :shape.draft_layers].to(torch.bfloat16))
     assert e1.device_status() == 0 and e2.device_status() == 0
     # summary vs oracle
     kk, vv = to_np(v["kv_k"]), to_np(v["kv_v"])

@@ -152,8 +152,10 @@ def test_attention_matches_oracle(q_heads, kv_heads, slots, window, block, conte
 # greedy chain + accept
 # --------------------------------------------------------------------------
 
-@pytest.mark.parametrize("rank", [0, 64, 256])
-def test_markov_chain_matches_oracle(rank):
+@pytest.mark.parametrize("rank,wstd", [(0, 0.02), (64, 0.02), (256, 0.02), (64, 0.3)])
+def test_markov_chain_matches_oracle(rank, wstd):
+    """wstd 0.3 makes the bias bound cover most of the vocabulary, so the
+    candidate lists overflow and the exact step-by-step path runs."""
     g = torch.Generator().manual_seed(21 + rank)
     batch, block, vocab = 3, 15, 151936
     dev = "cuda"
@@ -170,19 +172,21 @@ def test_markov_chain_matches_oracle(rank):
     targ.copy_(torch.from_numpy((lv.argmax(-1) + np.arange(vocab // 128)[None] * 128).astype(np.int32)))
     anchors = torch.randint(0, vocab, (batch,), generator=g)
     W = {}
-    w1 = w2 = bound = None
+    w1 = w2 = b1 = b2 = None
     if rank:
-        w1 = (0.02 * torch.randn(vocab, rank, generator=g)).to(torch.bfloat16).to(dev)
-        w2 = (0.02 * torch.randn(vocab, rank, generator=g)).to(torch.bfloat16).to(dev)
-        bound = torch.zeros(1, device=dev)
-        ops.row_norm_bound(w2, bound)
+        w1 = (wstd * torch.randn(vocab, rank, generator=g)).to(torch.bfloat16).to(dev)
+        w2 = (wstd * torch.randn(vocab, rank, generator=g)).to(torch.bfloat16).to(dev)
+        b1, b2 = torch.zeros(1, device=dev), torch.zeros(1, device=dev)
+        ops.row_norm_bound(w1, b1)
+        ops.row_norm_bound(w2, b2)
         W = {"parallel_markov_head.markov_w1.weight": to_np(w1), "parallel_markov_head.markov_w2.weight": to_np(w2)}
     tokens = torch.empty(batch, block, dtype=torch.int64, device=dev)
     target = torch.randint(0, vocab, (batch, block + 1), generator=g)
     acc = torch.empty(batch, dtype=torch.int64, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(ops.markov_workspace_bytes(batch, block), dtype=torch.uint8, device=dev)
     ops.markov_argmax(base=bl, tile_max=tmax, tile_arg=targ, anchors=anchors.to(dev), tokens=tokens, block=block,
-                      w1=w1, w2=w2, w2_bound=bound, status=status)
+                      workspace=ws, w1=w1, w2=w2, w1_bound=b1, w2_bound=b2, status=status)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     gt = tokens.cpu().numpy()
