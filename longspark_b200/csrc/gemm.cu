@@ -41,7 +41,8 @@ struct GemmKernelParams {
   int bn;            // token tile (multiple of 16, <= 256)
   int n_tiles;       // token tiles
   int m_tiles;       // feature tiles (n_out / 128)
-  int kb;            // k-blocks per tile
+  int kb;            // stream-K units per tile (each unit = kg k-blocks of 64)
+  int kg;            // k-blocks per unit and per pipeline stage (1, 2 or 4)
   long long units;   // tiles * kb
   int grid;          // CTAs
   int stages;
@@ -232,6 +233,35 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
   }
 }
 
+// Producer helpers: stage `st` receives unit u's KG k-blocks of weights (one
+// contiguous bulk copy from the tiled layout, or KG tensor-map boxes) and of
+// activations (KG tensor-map boxes).  The tensor maps stay in parameter space.
+__device__ __forceinline__ void gemm_load_a(const GemmKernelParams& P, const CUtensorMap* map_w, const bf16* w_tiles,
+                                            bool tiled_w, uint8_t* a_buf, int a_stage_bytes, uint64_t* full, int st,
+                                            long long u, uint64_t pol) {
+  const int t = static_cast<int>(u / P.kb);
+  const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
+  const int m_tile = t / P.n_tiles;
+  if (tiled_w) {
+    // KG consecutive tiles of one row block are contiguous in the tiled layout
+    bulk_load(a_buf + st * a_stage_bytes,
+              w_tiles + (static_cast<long long>(m_tile) * P.kb * P.kg + kb0) * (BM * BK), a_stage_bytes, &full[st], pol);
+  } else {
+    for (int j = 0; j < P.kg; ++j)
+      tma_load_2d(a_buf + st * a_stage_bytes + j * A_STAGE_BYTES, map_w, &full[st], (kb0 + j) * BK, m_tile * BM, pol);
+  }
+}
+
+__device__ __forceinline__ void gemm_load_b(const GemmKernelParams& P, const CUtensorMap* map_x, uint8_t* b_buf,
+                                            int b_stage_bytes, int b_blk_bytes, uint64_t* full, int st, long long u,
+                                            uint64_t pol) {
+  const int t = static_cast<int>(u / P.kb);
+  const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
+  const int n_tile = t % P.n_tiles;
+  for (int j = 0; j < P.kg; ++j)
+    tma_load_2d(b_buf + st * b_stage_bytes + j * b_blk_bytes, map_x, &full[st], (kb0 + j) * BK, n_tile * P.bn, pol);
+}
+
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ GemmKernelParams P) {
@@ -239,9 +269,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = P.stages;
   const int bn = P.bn;
-  const int b_stage_bytes = bn * BK * 2;
+  const int KG = P.kg;
+  const int b_blk_bytes = bn * BK * 2;          // one k-block of activations
+  const int a_stage_bytes = KG * A_STAGE_BYTES;  // one stage = KG k-blocks
+  const int b_stage_bytes = KG * b_blk_bytes;
   uint8_t* a_buf = smem;
-  uint8_t* b_buf = a_buf + S * A_STAGE_BYTES;
+  uint8_t* b_buf = a_buf + S * a_stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(b_buf + S * b_stage_bytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
@@ -301,41 +334,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // weight tiles before waiting for it, then add the activation tiles.
       const int pre = static_cast<int>((u1 - u0) < S ? (u1 - u0) : S);
       for (int i = 0; i < pre; ++i) {
-        const long long u = u0 + i;
-        const int t = static_cast<int>(u / KB);
-        const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
-        const int m_tile = t / P.n_tiles;
-        mbar_arrive_expect_tx(&full[i], A_STAGE_BYTES + b_stage_bytes);
-        if (tiled_w)
-          bulk_load(a_buf + i * A_STAGE_BYTES, w_tiles + (static_cast<long long>(m_tile) * KB + kb) * (BM * BK),
-                    A_STAGE_BYTES, &full[i], pol_w);
-        else
-          tma_load_2d(a_buf + i * A_STAGE_BYTES, &map_w, &full[i], kb * BK, m_tile * BM, pol_w);
+        mbar_arrive_expect_tx(&full[i], a_stage_bytes + b_stage_bytes);
+        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, i, u0 + i, pol_w);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int i = 0; i < pre; ++i) {
-        const long long u = u0 + i;
-        const int t = static_cast<int>(u / KB);
-        const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
-        const int n_tile = t % P.n_tiles;
-        tma_load_2d(b_buf + i * b_stage_bytes, &map_x, &full[i], kb * BK, n_tile * bn, pol_x);
-      }
+      for (int i = 0; i < pre; ++i) gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, i, u0 + i, pol_x);
       int stage = pre % S;
       uint32_t phase = pre == S ? 1u : 0u;
       long long issued = pre;
       for (long long u = u0 + pre; u < u1; ++u) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
-        const int t = static_cast<int>(u / KB);
-        const int kb = static_cast<int>(u - static_cast<long long>(t) * KB);
-        const int m_tile = t / P.n_tiles;
-        const int n_tile = t - m_tile * P.n_tiles;
-        mbar_arrive_expect_tx(&full[stage], A_STAGE_BYTES + b_stage_bytes);
-        if (tiled_w)
-          bulk_load(a_buf + stage * A_STAGE_BYTES, w_tiles + (static_cast<long long>(m_tile) * KB + kb) * (BM * BK),
-                    A_STAGE_BYTES, &full[stage], pol_w);
-        else
-          tma_load_2d(a_buf + stage * A_STAGE_BYTES, &map_w, &full[stage], kb * BK, m_tile * BM, pol_w);
-        tma_load_2d(b_buf + stage * b_stage_bytes, &map_x, &full[stage], kb * BK, n_tile * bn, pol_x);
+        mbar_arrive_expect_tx(&full[stage], a_stage_bytes + b_stage_bytes);
+        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, stage, u, pol_w);
+        gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, u, pol_x);
         ++issued;
         if (++stage == S) {
           stage = 0;
@@ -363,14 +374,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
-      uint32_t acc_phase[2] = {0u, 0u};
+      uint32_t acc_phase = 0u;  // bit i: phase parity of accumulator buffer i
       bool ok = true;
       long long u = u0;
       while (u < u1 && ok) {
         const int t = static_cast<int>(u / KB);
         const int k0 = static_cast<int>(u - static_cast<long long>(t) * KB);
         const int k1 = static_cast<int>((u1 - u) < (long long)(KB - k0) ? k0 + (u1 - u) : KB);
-        if (!mbar_wait(&acc_empty[acc], acc_phase[acc] ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_MMA)) {
+        if (!mbar_wait(&acc_empty[acc], ((acc_phase >> acc) & 1u) ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
@@ -382,14 +393,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(a_buf + stage * A_STAGE_BYTES);
-          const uint32_t b_addr = smem_u32(b_buf + stage * b_stage_bytes);
-          const uint64_t a_desc = sdesc_kmajor_sw128(a_addr);
-          const uint64_t b_desc = sdesc_kmajor_sw128(b_addr);
+          for (int j = 0; j < KG; ++j) {
+            const uint32_t a_addr = smem_u32(a_buf + stage * a_stage_bytes + j * A_STAGE_BYTES);
+            const uint32_t b_addr = smem_u32(b_buf + stage * b_stage_bytes + j * b_blk_bytes);
+            const uint64_t a_desc = sdesc_kmajor_sw128(a_addr);
+            const uint64_t b_desc = sdesc_kmajor_sw128(b_addr);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            // +32 bytes along K inside the 128-byte swizzled row (encoded >> 4).
-            tc_mma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb > k0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              // +32 bytes along K inside the 128-byte swizzled row (encoded >> 4).
+              tc_mma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb > k0 || j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           tc_commit(&empty[stage]);
           if (++stage == S) {
@@ -399,7 +412,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (!ok) break;
         tc_commit(&acc_full[acc]);
-        acc_phase[acc] ^= 1u;
+        acc_phase ^= 1u << acc;
         acc ^= 1;
         u += k1 - k0;
       }
@@ -414,14 +427,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int ew = warp & 3;  // TMEM lane quarter this warp may access
     const int r = ew * 32 + lane;
     int acc = 0;
-    uint32_t acc_phase[2] = {0u, 0u};
+    uint32_t acc_phase = 0u;  // bit i: phase parity of accumulator buffer i
     long long u = u0;
     const int t_first = static_cast<int>(u0 / KB);
     while (u < u1) {
       const int t = static_cast<int>(u / KB);
       const int k0 = static_cast<int>(u - static_cast<long long>(t) * KB);
       const int k1 = static_cast<int>((u1 - u) < (long long)(KB - k0) ? k0 + (u1 - u) : KB);
-      const bool ok_wait = mbar_wait(&acc_full[acc], acc_phase[acc], abort_flag, status, LS_DEV_TIMEOUT_EPILOGUE);
+      const bool ok_wait =
+          mbar_wait(&acc_full[acc], (acc_phase >> acc) & 1u, abort_flag, status, LS_DEV_TIMEOUT_EPILOGUE);
       // All four warps agree on whether to continue.
       if (r == 0) sc->flag = 1;
       epi_bar();
@@ -486,7 +500,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (r == 0) atomicExch(&P.counters[t], 0);
         }
       }
-      acc_phase[acc] ^= 1u;
+      acc_phase ^= 1u << acc;
       acc ^= 1;
       u += k1 - k0;
     }
@@ -508,19 +522,19 @@ static int pick_bn(int rows) {
   return r16 > 256 ? 256 : r16;
 }
 
-static int pick_stages(int bn) {
+static int pick_stages(int bn, int kg) {
   const int budget = 227 * 1024 - 1024 - 256 - EPI_SCRATCH_BYTES - 512;
-  int s = budget / (A_STAGE_BYTES + bn * BK * 2);
+  int s = budget / (kg * (A_STAGE_BYTES + bn * BK * 2));
   return s > 12 ? 12 : s;
 }
 
-static size_t gemm_smem_bytes(int bn, int stages) {
-  return 1024 + static_cast<size_t>(stages) * (A_STAGE_BYTES + bn * BK * 2) + (2 * stages + 5) * 8 + 64 +
+static size_t gemm_smem_bytes(int bn, int kg, int stages) {
+  return 1024 + static_cast<size_t>(stages) * kg * (A_STAGE_BYTES + bn * BK * 2) + (2 * stages + 5) * 8 + 64 +
          EPI_SCRATCH_BYTES;
 }
 
 struct GemmPlan {
-  int bn, n_tiles, m_tiles, kb, grid, stages;
+  int bn, n_tiles, m_tiles, kb, kg, grid, stages;
   long long units;
   size_t partial_bytes, counter_bytes;
 };
@@ -530,11 +544,23 @@ static GemmPlan plan_gemm(int rows, int k, int n_out) {
   p.bn = pick_bn(rows);
   p.n_tiles = (rows + p.bn - 1) / p.bn;
   p.m_tiles = n_out / BM;
-  p.kb = k / BK;
-  p.units = static_cast<long long>(p.m_tiles) * p.n_tiles * p.kb;
   const int sms = host_sm_count();
+  // Pipeline stages of up to 4 k-blocks (64 KiB of weights): HBM streams best
+  // with a few large requests in flight per SM.  Smaller stages when the tile
+  // count is low (stream-K balance) or the token tile is wide (shared memory).
+  const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  p.kg = 1;
+  for (int kg = 4; kg > 1; kg >>= 1) {
+    if (k % (BK * kg)) continue;
+    if (pick_stages(p.bn, kg) < 3) continue;
+    if (tiles * (k / (BK * kg)) < 4LL * sms) continue;
+    p.kg = kg;
+    break;
+  }
+  p.kb = k / (BK * p.kg);
+  p.units = tiles * p.kb;
   p.grid = static_cast<int>(std::min<long long>(sms, p.units));
-  p.stages = pick_stages(p.bn);
+  p.stages = pick_stages(p.bn, p.kg);
   p.partial_bytes = static_cast<size_t>(p.grid) * 2 * p.bn * BM * sizeof(float);
   p.counter_bytes = COUNTER_BYTES;
   return p;
@@ -614,6 +640,7 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
   kp.n_tiles = p.n_tiles;
   kp.m_tiles = p.m_tiles;
   kp.kb = p.kb;
+  kp.kg = p.kg;
   kp.units = p.units;
   kp.grid = p.grid;
   kp.stages = p.stages;
@@ -623,7 +650,7 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
   kp.counters = reinterpret_cast<int*>(workspace);
   kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + p.counter_bytes);
 
-  const size_t smem = gemm_smem_bytes(p.bn, p.stages);
+  const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.stages);
   static int configured_smem = 0;
   if (configured_smem < static_cast<int>(smem)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
