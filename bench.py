@@ -285,17 +285,22 @@ def time_dominant_kernel(eng, reps=20):
         ops.gemm(b["xn"], w.lm_head, b["logits"], workspace=eng.gemm_ws, epilogue=N.EPI_LMHEAD, rows=M,
                  tile_max=b["tile_max"], tile_arg=b["tile_arg"])
 
+    # Each launch is bracketed by its own events, with a 256 MiB write (twice the
+    # L2) before it, so no launch starts on L2-resident weights or overlaps the
+    # tail of the previous one.
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for _ in range(3):
         launch()
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(reps):
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for e0, e1 in ev:
+        flush.fill_(1)
+        e0.record(st)
         launch()
-    e1.record(st)
+        e1.record(st)
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / reps
+    return sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps
 
 
 def count_launches(eng, g):
