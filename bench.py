@@ -9,7 +9,7 @@ W=1024, S=256, 16-token verify block (anchor + 15 proposals).  A step is one
 full round: view refresh of a 16-row commit over the 5 tapped layers, the
 parallel drafter pass, the Markov greedy chain and the accept check, replayed
 as one CUDA graph.  Weights and inputs are synthetic (seeded N(0, 0.02) weights,
-N(0, 1) K/V); the 2.1 GB of weights streamed per round exceed the 126 MB L2, so
+N(0, 1) K/V); the 1.9 GB of weights streamed per round exceed the 126 MB L2, so
 no flush is needed between steps.  ``value`` is the headline context (128K).
 
 Multi-GPU (``torchrun --nproc-per-node N``): requests shard across GPUs with
@@ -465,7 +465,7 @@ def run_b200(args):
                        "draft_layers": shape.draft_layers, "window": shape.window, "slots": shape.slots,
                        "verify_block": shape.block + 1, "draft_rows": shape.block, "markov_rank": shape.markov_rank,
                        "headline_ctx": head_ctx, "parallelism": f"request-sharded x{world}",
-                       "l2": "inputs larger than L2 (2.1 GB of weights streamed per round)",
+                       "l2": "inputs larger than L2 (1.9 GB of weights streamed per round)",
                        "graph": "refresh + drafter pass + Markov chain + accept in one CUDA graph"},
             "round_latency_us": round(ms * 1e3, 1),
             "ctx_sweep": sweep,

@@ -86,12 +86,12 @@ class DraftWeights:
         self.inv_freq = inv_freq.to(device=dev, dtype=torch.float32).contiguous()
 
     def nbytes(self):
-        """Weight bytes streamed by one round (each matrix once)."""
+        """Weight bytes streamed by one round (each GEMM matrix once).  The
+        Markov w1/w2 are not streamed: the chain gathers only the rows of its
+        band candidates (a few KiB)."""
         mats = [self.enc_w1, self.enc_w2, self.sh_w1, self.sh_w2, self.lm_head]
         for L in self.layers:
             mats += [L["qkv"], L["o"], L["gate_up"], L["down"]]
-        if self.w2 is not None:
-            mats.append(self.w2)
         return sum(m.numel() * m.element_size() for m in mats)
 
 
