@@ -296,6 +296,28 @@ typedef struct ls_markov_args {
 LS_API size_t ls_markov_workspace_bytes(int batch, int block);
 LS_API int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes);
 
+/* ls_markov_argmax with its scratch in a fixed device array inside this
+ * library (1 MiB + 8.25 KiB per device) instead of a caller workspace.  No
+ * counterpart in the reference, which allocates its step tensors through
+ * PyTorch; this exists for callers that cannot allocate device memory when
+ * they propose tokens: a serving process that handed all free HBM to its paged
+ * KV-cache pool at start-up (a cudaMalloc in the middle of serving fails or
+ * must evict cache pages), or a host binding over this C ABI that owns no
+ * device allocator to carve a workspace from.  It calls no cudaMalloc,
+ * cudaFree or allocating library routine.
+ * Limit: batch x block <= LS_MARKOV_STATIC_MAX_ROWS; larger calls fail with
+ * LS_ERR_WORKSPACE and launch nothing.
+ * The first call on each device, made with that device current, looks up the
+ * array's address (cudaGetSymbolAddress); make that first call before any
+ * stream capture on the device.  Every call on a device shares the one array,
+ * which keeps the last call's contents: each call clears the counters that must
+ * start at zero with a memset on its own stream.  Calls that overlap on the
+ * GPU (on different streams, or from threads without ordering between them)
+ * race on the array and give undefined tokens; calls on one stream are
+ * ordered and safe. */
+#define LS_MARKOV_STATIC_MAX_ROWS 1024
+LS_API int ls_markov_argmax_static(void* stream, const ls_markov_args* a);
+
 /* Greedy accept check: accept[b] = number of leading i < block with
  * target[b, i] == draft[b, i] (LS engine/target.py:472-477). */
 LS_API int ls_accept(void* stream, const long long* target, int target_ld, const long long* draft, long long* accept,

@@ -76,6 +76,7 @@ SIGNATURES = {
     "ls_gather_rows": (i32, [vp, vp, i64, vp, vp, i32, i64, vp]),
     "ls_markov_workspace_bytes": (sz, [i32, i32]),
     "ls_markov_argmax": (i32, [vp, C.POINTER(MarkovArgs), vp, sz]),
+    "ls_markov_argmax_static": (i32, [vp, C.POINTER(MarkovArgs)]),
     "ls_accept": (i32, [vp, vp, i32, vp, vp, i32, i32]),
     "ls_row_norm_bound": (i32, [vp, vp, i32, i32, vp]),
 }

@@ -20,6 +20,8 @@
 // LM-head epilogue find the band without rescanning the row).  The tokens are
 // identical to the full scan's.  If the band holds more than the candidate
 // buffer, the step falls back to scoring every token.
+#include <mutex>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -486,6 +488,66 @@ extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* wor
   markov_kernel<<<static_cast<unsigned>(rows), MK_THREADS, dsmem, st>>>(*a, counts, cand, done);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_markov_argmax: launch", e);
+}
+
+// ---------------------------------------------------------------------------
+// ls_markov_argmax_static: the same kernel with its scratch in a fixed device
+// array inside this library, for callers that cannot allocate device memory
+// when they propose tokens: a serving process that handed all free HBM to its
+// paged KV-cache pool at start-up (a cudaMalloc in the middle of serving fails
+// or has to evict cache pages), or a host binding over the C ABI that owns no
+// device allocator to carve a workspace from.  The array holds the scratch of
+// LS_MARKOV_STATIC_MAX_ROWS (request, step) rows in the ls_markov_argmax
+// workspace layout: [256 pad][done counters][candidate counts][candidates].
+// ---------------------------------------------------------------------------
+namespace ls {
+
+constexpr int MK_STATIC_MAX_DEVICES = 64;
+constexpr size_t MK_STATIC_BYTES =
+    256 + 2 * ((static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * 4 + 255) / 256 * 256) +
+    static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * MK_ROWCAND * 4;  // 1 MiB + 8.25 KiB
+
+static __device__ __align__(256) uint8_t mk_static_scratch[MK_STATIC_BYTES];
+
+static std::mutex mk_static_mutex;
+static void* mk_static_ptr[MK_STATIC_MAX_DEVICES];  // device address of the array, per device ordinal
+
+}  // namespace ls
+
+extern "C" int ls_markov_argmax_static(void* stream, const ls_markov_args* a) {
+  if (a == nullptr) return set_error(LS_ERR_INVALID, "ls_markov_argmax_static: null argument struct");
+  // empty batches and bad block sizes get the workspace entry point's own checks and errors
+  if (a->batch <= 0 || a->block < 1) return ls_markov_argmax(stream, a, nullptr, 0);
+  const long long rows = static_cast<long long>(a->batch) * a->block;
+  if (rows > LS_MARKOV_STATIC_MAX_ROWS)
+    return set_error(LS_ERR_WORKSPACE,
+                     "ls_markov_argmax_static: batch x block = %lld rows exceeds the static scratch maximum of %d "
+                     "rows; use ls_markov_argmax with a caller workspace",
+                     rows, LS_MARKOV_STATIC_MAX_ROWS);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error("ls_markov_argmax_static: cudaGetDevice", e);
+  if (dev < 0 || dev >= MK_STATIC_MAX_DEVICES)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_markov_argmax_static: device ordinal %d >= %d", dev,
+                     MK_STATIC_MAX_DEVICES);
+  void* scratch = nullptr;
+  {
+    // set-up, once per device, on the first call made with that device current
+    std::lock_guard<std::mutex> lock(mk_static_mutex);
+    scratch = mk_static_ptr[dev];
+    if (scratch == nullptr) {
+      e = cudaGetSymbolAddress(&scratch, mk_static_scratch);
+      if (e != cudaSuccess) return set_cuda_error("ls_markov_argmax_static: cudaGetSymbolAddress", e);
+      mk_static_ptr[dev] = scratch;
+    }
+  }
+  // The per-request done counters must start at zero; a previous call that
+  // stopped early may have left them set.  Everything else is written before
+  // it is read.
+  e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + 256, 0, static_cast<size_t>(a->batch) * sizeof(int),
+                      reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_cuda_error("ls_markov_argmax_static: clearing the done counters", e);
+  return ls_markov_argmax(stream, a, scratch, MK_STATIC_BYTES);
 }
 
 extern "C" int ls_accept(void* stream, const long long* target, int target_ld, const long long* draft, long long* accept,
