@@ -11,15 +11,17 @@
 // tokens are base.argmax(-1).
 //
 // The reference streams the whole [vocab, rank] w2 matrix once per step (P
-// serial full-vocabulary GEMVs).  Here one CTA per request runs the P steps
-// and evaluates the bias only where it can change the argmax: with
-// |bias_v| <= B2 * |w1[prev]| (Cauchy-Schwarz, B2 = max_v |w2[v]|) every token
-// whose base logit is more than 2*bound + 2 bf16 steps below the row maximum
-// loses to the maximising token however the biases round, so only tokens
-// inside that band are scored (the per-128-token tile maxima written by the
-// LM-head epilogue find the band without rescanning the row).  The tokens are
-// identical to the full scan's.  If the band holds more than the candidate
-// buffer, the step falls back to scoring every token.
+// serial full-vocabulary GEMVs).  Here the bias is evaluated only where it can
+// change the argmax: with |bias_v| <= B1 * B2 (Cauchy-Schwarz, B1 and B2 the
+// largest w1 and w2 row norms) every token whose base logit is more than
+// 2*B1*B2 + 2 bf16 steps below the row maximum loses to the maximising token
+// for any previous token and however the biases round, so only the tokens
+// inside that band are candidates (the per-128-token tile maxima written by
+// the LM-head epilogue find the band without rescanning the row).  The serial
+// chain then only picks among precomputed (previous candidate, candidate)
+// values.  The tokens are identical to the full scan's.  A request whose band
+// overflows the candidate buffers is evaluated step by step, over the whole
+// vocabulary if needed.
 #include <mutex>
 
 #include "common.cuh"
@@ -31,9 +33,8 @@ constexpr int MK_THREADS = 256;
 constexpr int MK_MAXCAND = 4096;
 constexpr int MK_MAXRANK = 512;
 constexpr int MK_MAXTILES = 1024;
-constexpr int MK_ROWCAND = 256;    // candidate tokens kept per row by phase 1
-constexpr int MK_MAXPAIRS = 2048;  // (previous, current) candidate pairs per request
-constexpr int MK_STAGEROWS = 64;   // candidate rows staged in shared memory per request
+constexpr int MK_ROWCAND = 128;   // band candidates kept per row
+constexpr int MK_ROWPAIRS = 256;  // (previous candidate, candidate) pair values kept per row
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
@@ -119,13 +120,11 @@ __device__ __forceinline__ void row_max(const float* tmax, const int* targ, int 
   block_argmax(bv, bi, red_v, red_i);
 }
 
-// Dynamic shared memory of the Markov kernel.  The table path and the
-// step-by-step fallback never run in the same CTA, so they share the region.
-struct MarkovTable {
-  int tok[MK_STAGEROWS];
-};
-__host__ __device__ constexpr size_t mk_table_bytes(int rank) {
-  return MK_STAGEROWS * 4 + static_cast<size_t>(2 * MK_STAGEROWS + 1) * rank * 2 + MK_MAXPAIRS * 4;
+// Dynamic shared memory of the Markov kernel's last CTA per request.  The
+// table walk and the step-by-step fallback never run in the same CTA, so they
+// share the region.
+__host__ __device__ constexpr size_t mk_table_bytes() {
+  return static_cast<size_t>(16) * (MK_ROWCAND + MK_ROWPAIRS) * 4;  // candidates + pair values of <= 16 rows
 }
 __host__ __device__ constexpr size_t mk_stepwise_bytes() { return MK_MAXCAND * 4 + MK_MAXRANK * 4; }
 
@@ -215,29 +214,87 @@ __device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, in
   }
 }
 
-// One launch.  Every CTA handles one (request, step) row: the row maximum
-// (the token itself when there is no Markov head) and the band's candidate
-// tokens.  The last row of a request to finish then runs the chain for that
-// request: the w1 rows of every possible previous token and the w2 rows of
-// every candidate are staged in shared memory with one burst of loads, the
-// bias of every (previous candidate, candidate) pair is evaluated in parallel,
-// and a single thread walks the table.  Then the accept check.
+// Band candidates of one row: every token whose bf16 base logit is >= thr,
+// found through the per-128-token tile maxima, sorted by token id (so two CTAs
+// that scan the same row list its candidates in the same order).  Returns the
+// count, or -1 when the band holds more than MK_ROWCAND tokens or MK_MAXTILES
+// tiles.  Block-wide; ends with a barrier.
+__device__ int band_candidates(const bf16* base, const float* tmax, int n_tiles, float thr, int* tile_list,
+                               int* raw, int* out, int* n_tl, int* n_c) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  if (tid == 0) {
+    *n_tl = 0;
+    *n_c = 0;
+  }
+  __syncthreads();
+  for (int i = tid; i < n_tiles; i += blockDim.x) {
+    if (tmax[i] >= thr) {
+      const int slot = atomicAdd(n_tl, 1);
+      if (slot < MK_MAXTILES) tile_list[slot] = i;
+    }
+  }
+  __syncthreads();
+  const int ntl = *n_tl;
+  if (ntl <= MK_MAXTILES) {
+    for (int ti = warp; ti < ntl; ti += nwarps) {
+      const int v0 = tile_list[ti] * 128 + lane * 4;
+      const uint2 rw = *reinterpret_cast<const uint2*>(base + v0);
+      const bf16* e4 = reinterpret_cast<const bf16*>(&rw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (__bfloat162float(e4[j]) >= thr) {
+          const int slot = atomicAdd(n_c, 1);
+          if (slot < MK_ROWCAND) raw[slot] = v0 + j;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int n = (ntl > MK_MAXTILES || *n_c > MK_ROWCAND) ? -1 : *n_c;
+  // rank sort (token ids of one row are distinct)
+  for (int i = tid; i < n; i += blockDim.x) {
+    const int v = raw[i];
+    int r = 0;
+    for (int j = 0; j < n; ++j) r += raw[j] < v;
+    out[r] = v;
+  }
+  __syncthreads();
+  return n;
+}
+
+// One launch, one CTA per (request, step) row t.
+//
+// Row phase (every CTA): the row maximum (the token itself when there is no
+// Markov head); the band candidates C_t of row t and, recomputed from row
+// t-1's logits, C_{t-1} (the anchor for t = 0); then the value
+// bf16(base[t][c] + bf16(w2[c] . w1[p])) of every pair (p in C_{t-1}, c in C_t),
+// one warp per pair, written to the workspace.  Every CTA of a request does its
+// own pairs in parallel, so the w1/w2 row loads overlap across the request.
+//
+// Chain (the request's last row to finish): with every row's candidates and
+// pair values staged in shared memory, one thread walks the steps: at step t
+// the token is the best candidate of C_t given the previous step's choice
+// (first maximum by token id, as torch.argmax).  A row whose band overflowed
+// sends the request to the exact step-by-step fallback.  Then the accept check.
 __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args a, int* cand_count, int* cand_all,
-                                                            int* done) {
+                                                            float* pair_all, int* done) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ float red_v[32];
   __shared__ int red_i[32];
   __shared__ int tile_list[MK_MAXTILES];
+  __shared__ int raw[MK_ROWCAND], cur[MK_ROWCAND], prv[MK_ROWCAND];
   __shared__ int n_tl, n_c;
-  __shared__ int cnt[17], off[18], roff[18];
+  __shared__ int cnt[16];
   __shared__ int last_row, use_table;
   asm volatile("griddepcontrol.launch_dependents;");
   const long long row = blockIdx.x;
   const int P = a.block;
   const int b = static_cast<int>(row / P);
+  const int t = static_cast<int>(row - static_cast<long long>(b) * P);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int n_tiles = a.vocab / 128;
+  const bf16* base_all = reinterpret_cast<const bf16*>(a.base);
   const float* tmax = a.tile_max + row * n_tiles;
   const int* targ = a.tile_arg + row * n_tiles;
   float m;
@@ -246,39 +303,55 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
   if (a.w1 == nullptr) {
     if (tid == 0) a.tokens[row] = arg;
   } else {
-    const float thr = band_threshold(m, (*a.w1_row_bound) * (*a.w2_row_bound));
-    if (tid == 0) {
-      n_tl = 0;
-      n_c = 0;
-    }
-    __syncthreads();
-    for (int i = tid; i < n_tiles; i += blockDim.x) {
-      if (tmax[i] >= thr) {
-        const int slot = atomicAdd(&n_tl, 1);
-        if (slot < MK_MAXTILES) tile_list[slot] = i;
-      }
-    }
-    __syncthreads();
-    const int ntl = n_tl;
-    int* my = cand_all + row * MK_ROWCAND;
-    if (ntl <= MK_MAXTILES) {
-      const bf16* base = reinterpret_cast<const bf16*>(a.base) + row * a.vocab;
-      for (int ti = warp; ti < ntl; ti += nwarps) {
-        const int v0 = tile_list[ti] * 128 + lane * 4;
-        const uint2 raw = *reinterpret_cast<const uint2*>(base + v0);
-        const bf16* e4 = reinterpret_cast<const bf16*>(&raw);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (__bfloat162float(e4[j]) >= thr) {
-            const int slot = atomicAdd(&n_c, 1);
-            if (slot < MK_ROWCAND) my[slot] = v0 + j;
-          }
+    const float beta = (*a.w1_row_bound) * (*a.w2_row_bound);
+    const bf16* base = base_all + row * a.vocab;
+    const int nc = band_candidates(base, tmax, n_tiles, band_threshold(m, beta), tile_list, raw, cur, &n_tl, &n_c);
+    int np = 1;
+    if (t == 0) {
+      if (tid == 0) {
+        long long an = a.anchors[b];
+        if (an < 0 || an >= a.vocab) {
+          record_status(a.status, LS_DEV_BAD_TOKEN);
+          an = 0;
         }
+        prv[0] = static_cast<int>(an);
       }
+    } else {
+      const float* ptmax = tmax - n_tiles;
+      float pm;
+      int parg;
+      row_max(ptmax, targ - n_tiles, n_tiles, red_v, red_i, pm, parg);
+      np = band_candidates(base - a.vocab, ptmax, n_tiles, band_threshold(pm, beta), tile_list, raw, prv, &n_tl,
+                           &n_c);
     }
     __syncthreads();
-    if (tid == 0) cand_count[row] = (ntl > MK_MAXTILES || n_c > MK_ROWCAND) ? -1 : n_c;
+    const int count = (nc < 1 || np < 1 || np * nc > MK_ROWPAIRS) ? -1 : nc;
+    if (count > 0) {
+      const int R = a.rank;
+      const bf16* w1 = reinterpret_cast<const bf16*>(a.w1);
+      const bf16* w2 = reinterpret_cast<const bf16*>(a.w2);
+      float* pv = pair_all + row * MK_ROWPAIRS;
+      for (int q = warp; q < np * nc; q += nwarps) {
+        const int i = q / nc, j = q - i * nc;
+        const long long pt = prv[i], ct = cur[j];
+        const float bv = __bfloat162float(base[ct]);
+        float acc = 0.0f;
+        for (int k = lane * 8; k < R; k += 256) {
+          const uint4 x = __ldg(reinterpret_cast<const uint4*>(w1 + pt * R + k));
+          const uint4 y = __ldg(reinterpret_cast<const uint4*>(w2 + ct * R + k));
+          const bf16* xe = reinterpret_cast<const bf16*>(&x);
+          const bf16* ye = reinterpret_cast<const bf16*>(&y);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc += __bfloat162float(xe[e]) * __bfloat162float(ye[e]);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) pv[q] = bf16_round(bv + bf16_round(acc));
+      }
+      for (int j = tid; j < nc; j += blockDim.x) cand_all[row * MK_ROWCAND + j] = cur[j];
+    }
+    if (tid == 0) cand_count[row] = count;
   }
+  __threadfence();
   // publish this row; the request's last row to finish continues with the chain
   __syncthreads();
   if (tid == 0) {
@@ -290,23 +363,12 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
   if (!last_row) return;
 
   if (a.w1 != nullptr) {
-    const int R = a.rank;
     if (tid < P) cnt[tid] = __ldcg(&cand_count[(long long)b * P + tid]);
     __syncthreads();
     if (tid == 0) {
-      int ok = 1, total = 0, rows = 0;
-      off[0] = 0;
-      roff[0] = 0;
-      for (int t = 0; t < P; ++t) {
-        const int c = cnt[t];
-        if (c < 1) ok = 0;
-        const int prev_n = t == 0 ? 1 : cnt[t - 1];
-        total += prev_n * (c < 1 ? 0 : c);
-        off[t + 1] = total;
-        rows += c < 1 ? 0 : c;
-        roff[t + 1] = rows;
-      }
-      use_table = ok && total <= MK_MAXPAIRS && rows <= MK_STAGEROWS;
+      int ok = 1;
+      for (int s = 0; s < P; ++s) ok &= cnt[s] >= 1;
+      use_table = ok;
     }
     __syncthreads();
     if (!use_table) {
@@ -314,89 +376,47 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
       int* cand = reinterpret_cast<int*>(dsm + MK_MAXRANK * 4);
       stepwise_chain(a, b, latent, cand, &n_c, tile_list, &n_tl, red_v, red_i);
     } else {
-      const int rows = roff[P];
-      int* tok = reinterpret_cast<int*>(dsm);
-      bf16* w1s = reinterpret_cast<bf16*>(dsm + MK_STAGEROWS * 4);
-      bf16* w2s = w1s + (size_t)(MK_STAGEROWS + 1) * R;
-      float* pair_val = reinterpret_cast<float*>(w2s + (size_t)MK_STAGEROWS * R);
-      for (int i = tid; i < rows; i += blockDim.x) {
-        int t = 0;
-        while (roff[t + 1] <= i) ++t;
-        tok[i] = __ldcg(&cand_all[((long long)b * P + t) * MK_ROWCAND + (i - roff[t])]);
+      int* tok = reinterpret_cast<int*>(dsm);                                  // [P][MK_ROWCAND]
+      float* pv = reinterpret_cast<float*>(dsm + (size_t)P * MK_ROWCAND * 4);  // [P][MK_ROWPAIRS]
+      const long long r0 = (long long)b * P;
+      for (int e = tid; e < P * MK_ROWCAND; e += blockDim.x) {
+        const int s = e / MK_ROWCAND, j = e - s * MK_ROWCAND;
+        if (j < cnt[s]) tok[e] = __ldcg(&cand_all[(r0 + s) * MK_ROWCAND + j]);
       }
-      __syncthreads();
-      const bf16* w1 = reinterpret_cast<const bf16*>(a.w1);
-      const bf16* w2 = reinterpret_cast<const bf16*>(a.w2);
-      const int vec_per_row = R / 8;
-      // w1 row 0 = anchor, w1 row 1 + i = candidate i (a possible previous token)
-      for (int e = tid; e < (rows + 1) * vec_per_row; e += blockDim.x) {
-        const int r = e / vec_per_row, k = (e - r * vec_per_row) * 8;
-        long long v = r == 0 ? a.anchors[b] : tok[r - 1];
-        if (v < 0 || v >= a.vocab) {
-          record_status(a.status, LS_DEV_BAD_TOKEN);
-          v = 0;
-        }
-        *reinterpret_cast<uint4*>(w1s + (size_t)r * R + k) = *reinterpret_cast<const uint4*>(w1 + v * R + k);
-      }
-      for (int e = tid; e < rows * vec_per_row; e += blockDim.x) {
-        const int r = e / vec_per_row, k = (e - r * vec_per_row) * 8;
-        *reinterpret_cast<uint4*>(w2s + (size_t)r * R + k) =
-            *reinterpret_cast<const uint4*>(w2 + (long long)tok[r] * R + k);
-      }
-      __syncthreads();
-      const int total = off[P];
-      const bf16* base_all = reinterpret_cast<const bf16*>(a.base);
-      for (int q = warp; q < total; q += nwarps) {
-        int t = 0;
-        while (off[t + 1] <= q) ++t;
-        const int n_t = cnt[t];
-        const int pi = (q - off[t]) / n_t, ci = (q - off[t]) % n_t;
-        const int prow = t == 0 ? 0 : 1 + roff[t - 1] + pi;  // w1s row of the previous token
-        const int crow = roff[t] + ci;                           // w2s row of the candidate
-        float acc = 0.0f;
-        for (int k = lane * 8; k < R; k += 256) {
-          const uint4 x = *reinterpret_cast<const uint4*>(w1s + (size_t)prow * R + k);
-          const uint4 y = *reinterpret_cast<const uint4*>(w2s + (size_t)crow * R + k);
-          const bf16* xe = reinterpret_cast<const bf16*>(&x);
-          const bf16* ye = reinterpret_cast<const bf16*>(&y);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc += __bfloat162float(xe[e]) * __bfloat162float(ye[e]);
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) {
-          const float bv = __bfloat162float(base_all[((long long)b * P + t) * a.vocab + tok[crow]]);
-          pair_val[q] = bf16_round(bv + bf16_round(acc));
-        }
+      for (int e = tid; e < P * MK_ROWPAIRS; e += blockDim.x) {
+        const int s = e / MK_ROWPAIRS, q = e - s * MK_ROWPAIRS;
+        const int np_s = s == 0 ? 1 : cnt[s - 1];
+        if (q < np_s * cnt[s]) pv[e] = __ldcg(&pair_all[(r0 + s) * MK_ROWPAIRS + q]);
       }
       __syncthreads();
       if (tid == 0) {
-        int pos = 0;  // position of the previous token in the previous step's list (anchor: 0)
-        for (int t = 0; t < P; ++t) {
-          const int n_t = cnt[t];
+        int pos = 0;  // index of the previous step's token in its sorted candidate list (anchor: 0)
+        for (int s = 0; s < P; ++s) {
+          const int n_s = cnt[s];
           float best = -INFINITY;
           int best_tok = 0x7fffffff, best_j = 0;
-          for (int j = 0; j < n_t; ++j) {
-            const float v = pair_val[off[t] + pos * n_t + j];
-            const int tk = tok[roff[t] + j];
+          for (int j = 0; j < n_s; ++j) {
+            const float v = pv[s * MK_ROWPAIRS + pos * n_s + j];
+            const int tk = tok[s * MK_ROWCAND + j];
             if (better(v, tk, best, best_tok)) {
               best = v;
               best_tok = tk;
               best_j = j;
             }
           }
-          red_i[t] = best_tok;
+          red_i[s] = best_tok;
           pos = best_j;
         }
       }
       __syncthreads();
-      if (tid < P) a.tokens[(long long)b * P + tid] = red_i[tid];
+      if (tid < P) a.tokens[r0 + tid] = red_i[tid];
     }
   }
   __syncthreads();
   if (a.target != nullptr && a.accept_out != nullptr && tid == 0) {
     long long acc = 0;
-    for (int t = 0; t < P; ++t) {
-      if (a.target[(long long)b * a.target_ld + t] != __ldcg(&a.tokens[(long long)b * P + t])) break;
+    for (int s = 0; s < P; ++s) {
+      if (a.target[(long long)b * a.target_ld + s] != __ldcg(&a.tokens[(long long)b * P + s])) break;
       ++acc;
     }
     a.accept_out[b] = acc;
@@ -445,9 +465,10 @@ using namespace ls;
 extern "C" size_t ls_markov_workspace_bytes(int batch, int block) {
   if (batch <= 0 || block <= 0) return 0;
   const size_t rows = static_cast<size_t>(batch) * block;
-  // [done counters (batch)] [candidate counts (rows)] [candidates (rows x MK_ROWCAND)]
+  // [256 pad] [done counters (batch)] [candidate counts (rows)]
+  // [candidates (rows x MK_ROWCAND)] [pair values (rows x MK_ROWPAIRS)]
   return 256 + (static_cast<size_t>(batch) * 4 + 255) / 256 * 256 + (rows * 4 + 255) / 256 * 256 +
-         rows * MK_ROWCAND * 4;
+         rows * (MK_ROWCAND + MK_ROWPAIRS) * 4;
 }
 
 extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes) {
@@ -473,19 +494,13 @@ extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* wor
   int* counts = reinterpret_cast<int*>(w);
   w += (rows * 4 + 255) / 256 * 256;
   int* cand = reinterpret_cast<int*>(w);
+  float* pairs = reinterpret_cast<float*>(w + rows * MK_ROWCAND * 4);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  size_t dsmem = 0;
-  if (a->w1 != nullptr) {
-    dsmem = mk_table_bytes(a->rank);
-    if (mk_stepwise_bytes() > dsmem) dsmem = mk_stepwise_bytes();
-  }
-  static size_t configured = 0;
-  if (dsmem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(markov_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dsmem));
-    if (e != cudaSuccess) return set_cuda_error("ls_markov_argmax: cudaFuncSetAttribute", e);
-    configured = dsmem;
-  }
-  markov_kernel<<<static_cast<unsigned>(rows), MK_THREADS, dsmem, st>>>(*a, counts, cand, done);
+  // within the default 48 KiB dynamic shared memory limit: no attribute needed
+  static_assert(mk_table_bytes() <= 48 * 1024 && mk_stepwise_bytes() <= 48 * 1024, "Markov shared memory");
+  const size_t dsmem = a->w1 == nullptr ? 0 : (mk_table_bytes() > mk_stepwise_bytes() ? mk_table_bytes()
+                                                                                         : mk_stepwise_bytes());
+  markov_kernel<<<static_cast<unsigned>(rows), MK_THREADS, dsmem, st>>>(*a, counts, cand, pairs, done);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_markov_argmax: launch", e);
 }
@@ -505,7 +520,7 @@ namespace ls {
 constexpr int MK_STATIC_MAX_DEVICES = 64;
 constexpr size_t MK_STATIC_BYTES =
     256 + 2 * ((static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * 4 + 255) / 256 * 256) +
-    static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * MK_ROWCAND * 4;  // 1 MiB + 8.25 KiB
+    static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * (MK_ROWCAND + MK_ROWPAIRS) * 4;  // 1.5 MiB + 8.25 KiB
 
 static __device__ __align__(256) uint8_t mk_static_scratch[MK_STATIC_BYTES];
 
