@@ -82,18 +82,26 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
     case LS_EPI_RESIDUAL:
     case LS_EPI_MARKOV_ADD: {
       const int f = m_tile * BM + r;
+      // Every global load before the first store: the residual may alias the
+      // output, so loads interleaved with stores would run one round trip each.
+      float add[16];
+      const bool has_add = a.epilogue == LS_EPI_RESIDUAL || a.epilogue == LS_EPI_MARKOV_ADD;
+      if (has_add) {
+        const bf16* src = reinterpret_cast<const bf16*>(a.epilogue == LS_EPI_RESIDUAL ? a.residual : a.base);
+        const long long ld = a.epilogue == LS_EPI_RESIDUAL ? a.res_ld : a.base_ld;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int tok = n0 + j < rows ? n0 + j : rows - 1;
+          add[j] = __bfloat162float(src[(long long)tok * ld + f]);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int tok = n0 + j;
-        if (tok >= rows) break;
+        if (tok >= rows) break;  // padded tokens of the last chunk: no work
         float y = bf16_round(v[j]);
-        if (a.epilogue == LS_EPI_SILU) {
-          y = silu_f(y);
-        } else if (a.epilogue == LS_EPI_RESIDUAL) {
-          y = y + __bfloat162float(reinterpret_cast<const bf16*>(a.residual)[(long long)tok * a.res_ld + f]);
-        } else if (a.epilogue == LS_EPI_MARKOV_ADD) {
-          y = y + __bfloat162float(reinterpret_cast<const bf16*>(a.base)[(long long)tok * a.base_ld + f]);
-        }
+        if (a.epilogue == LS_EPI_SILU) y = silu_f(y);
+        if (has_add) y = y + add[j];
         out[(long long)tok * a.out_ld + f] = __float2bfloat16_rn(y);
       }
       break;
@@ -107,6 +115,27 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
       if (!is_v) {
         // Per-head RMSNorm over the 128 features of this tile (HF rounding),
         // then RoPE with the rotate-half partner exchanged through shared memory.
+        // The norm weight and the 16 tokens' cos/sin are loaded up front.
+        const bf16* nw = reinterpret_cast<const bf16*>(head < a.q_heads ? a.q_norm_w : a.k_norm_w);
+        const float wr = __bfloat162float(nw[r]);
+        float cs[16], sn[16];
+        if (a.rope_table != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int tr = n0 + j < rows ? n0 + j : 0;
+            cs[j] = a.rope_table[(long long)tr * 128 + (r & 63)];
+            sn[j] = a.rope_table[(long long)tr * 128 + 64 + (r & 63)];
+          }
+        } else {
+          const float fr = a.inv_freq[r & 63];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int pos = n0 + j < rows ? a.positions[n0 + j] : 0;
+            const float ang = static_cast<float>(pos) * fr;
+            cs[j] = bf16_round(cosf(ang));
+            sn[j] = bf16_round(sinf(ang));
+          }
+        }
         float ss[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) ss[j] = warp_sum(y[j] * y[j]);
@@ -116,8 +145,6 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
           for (int j = 0; j < 16; ++j) sc->red_v[ew][j] = ss[j];
         }
         epi_bar();
-        const bf16* nw = reinterpret_cast<const bf16*>(head < a.q_heads ? a.q_norm_w : a.k_norm_w);
-        const float wr = __bfloat162float(nw[r]);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const float tot = sc->red_v[0][j] + sc->red_v[1][j] + sc->red_v[2][j] + sc->red_v[3][j];
@@ -127,24 +154,11 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
         }
         epi_bar();
         const int partner = r < 64 ? r + 64 : r - 64;
-        const float fr = a.inv_freq[r & 63];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int tok = n0 + j;
           const float other = sc->xch[partner][j];
           const float rot = r < 64 ? -other : other;
-          float cs, sn;
-          if (a.rope_table != nullptr) {
-            const int tr = tok < rows ? tok : 0;
-            cs = a.rope_table[(long long)tr * 128 + (r & 63)];
-            sn = a.rope_table[(long long)tr * 128 + 64 + (r & 63)];
-          } else {
-            const int pos = tok < rows ? a.positions[tok] : 0;
-            const float ang = static_cast<float>(pos) * fr;
-            cs = bf16_round(cosf(ang));
-            sn = bf16_round(sinf(ang));
-          }
-          y[j] = bf16_round(bf16_round(y[j] * cs) + bf16_round(rot * sn));
+          y[j] = bf16_round(bf16_round(y[j] * cs[j]) + bf16_round(rot * sn[j]));
         }
         epi_bar();  // xch/red reused by the next chunk
       }
@@ -230,6 +244,42 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
     }
     default:
       break;
+  }
+}
+
+// Reduction of a stream-K tile by its last contributor: the fp32 partials of
+// CTAs first..last summed in that order, then the fused epilogue.
+__device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, int first, int last, int first_slot,
+                                            int r, int ew, EpiScratch* sc) {
+  const int bn = P.bn;
+  const int m_tile = t / P.n_tiles;
+  const int n0 = (t - m_tile * P.n_tiles) * bn;
+  for (int c = 0; c < bn; c += 16) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+    // contributors in fixed order, four partials' loads in flight at a time
+    for (int q0 = first; q0 <= last; q0 += 4) {
+      float pv[4][16];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int q = q0 + i;
+        const int q_slot = q == first ? first_slot : 0;
+        const float* qp = P.partials + (static_cast<long long>(q) * 2 + q_slot) * (static_cast<long long>(bn) * BM);
+        if (q <= last) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pv[i][j] = __ldcg(&qp[(c + j) * BM + r]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (q0 + i <= last) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += pv[i][j];
+        }
+      }
+    }
+    if (n0 + c < P.a.rows) final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
   }
 }
 
@@ -422,10 +472,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------
-    // Residual/base reads and all writes wait for the previous kernel.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int ew = warp & 3;  // TMEM lane quarter this warp may access
     const int r = ew * 32 + lane;
+    // Residual/base reads and all writes wait for the previous kernel.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     int acc = 0;
     uint32_t acc_phase = 0u;  // bit i: phase parity of accumulator buffer i
     long long u = u0;
@@ -482,21 +532,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const bool reducer = sc->flag != 0;
         epi_bar();
         if (reducer) {
-          for (int c = 0; c < bn; c += 16) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-#pragma unroll 2
-            for (int q = first; q <= last; ++q) {
-              const int q_t_first = static_cast<int>(unit_begin(q, U, G) / KB);
-              const int q_slot = (q_t_first == t) ? 0 : 1;
-              const float* qp =
-                  P.partials + (static_cast<long long>(q) * 2 + q_slot) * (static_cast<long long>(bn) * BM);
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += __ldcg(&qp[(c + j) * BM + r]);
-            }
-            if (n0 + c < P.a.rows) final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
-          }
+          // Tile t is the first tile of every contributor after `first`, and of
+          // `first` itself only when its range starts exactly at the tile.
+          const int first_slot = unit_begin(first, U, G) == tu0 ? 0 : 1;
+          reduce_tile(P, t, first, last, first_slot, r, ew, sc);
           if (r == 0) atomicExch(&P.counters[t], 0);
         }
       }
