@@ -12,16 +12,21 @@
 // sum rounded to bf16, then merge_normalized_attention (:396-442) over
 // (summary, window, local).
 //
-// B200 layout of the work: the sources are cut into independent tasks so a
-// batch-1 round still spreads over the SMs — window chunks of 128 rows per
-// (request, KV head) serve all G query heads of the group from one shared
-// shared-memory copy (each window byte is read from HBM once), summary chunks
-// of 32 slots per (request, query head), one local task per (request, KV
-// head).  Each warp owns one query head's 16-row tile and keeps an online-
-// softmax state (m, l, acc) over its task in registers, using mma.sync bf16
-// tiles for Q.K^T and P.V.  A combine kernel merges the partial states per
-// source, applies the bf16 rounding of the weighted sum, then merges the three
-// sources by log-sum-exp.
+// B200 layout of the work: one thread-block cluster of 8 CTAs per (request,
+// KV head).  CTAs 0..NW-1 each take a contiguous range of the window rows
+// (every K/V byte of the window is read from HBM once and serves all G query
+// heads of the group), CTAs NW..6 take ranges of the summary slots (each warp
+// its own query head), CTA 7 the P local rows.  Each warp owns one query
+// head's 16-row tile and keeps an online-softmax state (m, l, acc) over its
+// keys in registers (mma.sync bf16 tiles for Q.K^T and P.V).  The states are
+// parked in shared memory and merged across the cluster through distributed
+// shared memory: per source the partial states are rescaled to the source
+// maximum, the weighted sum rounded to bf16 and normalised, then the three
+// sources are merged by log-sum-exp.  No global partials, one launch.
+//
+// Window and summary keys/values do not depend on the QKV projection, so they
+// are staged into shared memory (cp.async) before griddepcontrol.wait: with
+// programmatic dependent launch the loads overlap the tail of the projection.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -29,18 +34,17 @@ namespace ls {
 
 constexpr int AT_PITCH = 136;   // bf16 smem row pitch (ldmatrix conflict-free)
 constexpr int AT_WROWS = 128;   // window rows per shared sub-chunk
-constexpr int AT_GSLOTS = 32;   // summary slots per warp task
+
+constexpr int AT_CLUSTER = 8;   // CTAs per (request, KV head)
+constexpr int AT_MAXPAGES = 264; // window pages one CTA can span (W <= 4096)
 
 struct AttnParams {
   ls_attention_args a;
-  int G;          // query heads per KV head (= warps per CTA)
-  int nsw;        // window tasks per (request, KV head)
-  int wc;         // window rows per window task (multiple of 128)
-  int ngc;        // summary tasks per (request, KV head); each warp takes AT_GSLOTS slots of its head
-  int np;         // partials per (request, head) = nsw + ngc + 1
-  long long n_win, n_glob;
-  float* part_ml;   // [B*Hq*np*16][2]
-  float* part_acc;  // [B*Hq*np*16][128]
+  int G;        // query heads per KV head (= warps per CTA)
+  int nw;       // window CTAs of the cluster (ranks 0..nw-1); summary CTAs nw..6; local CTA 7
+  int wrows;    // window rows per window CTA (multiple of 32)
+  int sslots;   // summary slots per summary CTA (multiple of 32)
+  int sc;       // summary slots per warp chunk (64 when G <= 4, else 32)
 };
 
 struct WarpState {
@@ -61,12 +65,27 @@ __device__ __forceinline__ void ws_init(WarpState& s) {
 __device__ __forceinline__ void load_q_tile(bf16 (*qs)[AT_PITCH], const bf16* qkv, int row_ld, int tok0, int P,
                                             int head) {
   const int lane = threadIdx.x & 31;
-  for (int i = lane; i < 16 * 16; i += 32) {
+  uint4 v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // all eight loads in flight before the first store
+    const int i = lane + 32 * k;
     const int r = i >> 4, col = (i & 15) << 3;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < P) v = *reinterpret_cast<const uint4*>(qkv + (long long)(tok0 + r) * row_ld + head * 128 + col);
-    *reinterpret_cast<uint4*>(&qs[r][col]) = v;
+    v[k] = r < P ? *reinterpret_cast<const uint4*>(qkv + (long long)(tok0 + r) * row_ld + head * 128 + col)
+                 : make_uint4(0, 0, 0, 0);
   }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = lane + 32 * k;
+    *reinterpret_cast<uint4*>(&qs[i >> 4][(i & 15) << 3]) = v[k];
+  }
+}
+
+// exp(x) through the SFU's base-2 exponential (a few ulp; the probabilities it
+// feeds are rounded to bf16).  exp(-inf) = 0.
+__device__ __forceinline__ float fast_exp(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
 }
 
 __device__ __forceinline__ void load_q_frags(uint32_t qf[8][4], const bf16 (*qs)[AT_PITCH]) {
@@ -75,19 +94,24 @@ __device__ __forceinline__ void load_q_frags(uint32_t qf[8][4], const bf16 (*qs)
   for (int ks = 0; ks < 8; ++ks) ldmatrix_x4(qf[ks], &qs[lane & 15][ks * 16 + ((lane >> 4) << 3)]);
 }
 
-// One block of 32 keys: keys/values rows [k0, k0+32) of the smem arrays, of
-// which `valid` (counted from k0) are visible.
-__device__ __forceinline__ void attend_block32(WarpState& st, const uint32_t qf[8][4], const bf16 (*ks)[AT_PITCH],
-                                               const bf16 (*vs)[AT_PITCH], int k0, int valid, float scale) {
+// One block of 8*NT keys: keys/values rows [k0, k0 + 8*NT) of the smem
+// arrays, of which `valid` (counted from k0) are visible.  Larger blocks give
+// the tensor-core chains more independent work per softmax update.
+template <int NT>
+__device__ __forceinline__ void attend_block(WarpState& st, const uint32_t qf[8][4], const bf16 (*ks)[AT_PITCH],
+                                             const bf16 (*vs)[AT_PITCH], int k0, int valid, float scale) {
+  static_assert(NT % 2 == 0, "keys in pairs of 8-key tiles");
   const int lane = threadIdx.x & 31;
   const int t2 = (lane & 3) * 2;
-  float s[4][4];
+  float s[NT][4];
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) s[nt][i] = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < 128; kk += 32) {
+  for (int kk = 0; kk < 128; kk += 32) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
       uint32_t b[4];
       ldmatrix_x4(b, &ks[k0 + nt * 8 + (lane & 7)][kk + ((lane >> 3) << 3)]);
       mma_16816(s[nt], qf[kk / 16], b);
@@ -97,7 +121,7 @@ __device__ __forceinline__ void attend_block32(WarpState& st, const uint32_t qf[
   // bf16 scores, then the softmax scale (fp32); mask invisible keys.
   float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt)
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int key = nt * 8 + t2 + (i & 1);
@@ -113,17 +137,17 @@ __device__ __forceinline__ void attend_block32(WarpState& st, const uint32_t qf[
     mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
     const float mnew = fmaxf(st.m[h], mx[h]);
     muse[h] = mnew == -INFINITY ? 0.0f : mnew;
-    corr[h] = st.m[h] == -INFINITY ? 0.0f : expf(st.m[h] - muse[h]);
+    corr[h] = fast_exp(st.m[h] - muse[h]);  // 0 while the state is empty
     st.m[h] = mnew;
   }
   float psum[2] = {0.0f, 0.0f};
-  uint32_t pa[2][4];
+  uint32_t pa[NT / 2][4];
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
+  for (int nt = 0; nt < NT; ++nt) {
     float p[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      p[i] = s[nt][i] == -INFINITY ? 0.0f : expf(s[nt][i] - muse[i >> 1]);
+      p[i] = fast_exp(s[nt][i] - muse[i >> 1]);  // masked keys: exp(-inf) = 0
       psum[i >> 1] += p[i];
     }
     const int kst = nt >> 1, hi = nt & 1;
@@ -143,9 +167,9 @@ __device__ __forceinline__ void attend_block32(WarpState& st, const uint32_t qf[
     st.o[nt][2] *= corr[1];
     st.o[nt][3] *= corr[1];
   }
-  // P . V : k = 32 keys (2 steps), n = 128 dims (16 tiles, ldmatrix.trans pairs)
+  // P . V : k = 8*NT keys (NT/2 steps of 16), n = 128 dims (16 tiles, ldmatrix.trans pairs)
 #pragma unroll
-  for (int kst = 0; kst < 2; ++kst) {
+  for (int kst = 0; kst < NT / 2; ++kst) {
 #pragma unroll
     for (int dp = 0; dp < 8; ++dp) {
       uint32_t b[4];
@@ -158,277 +182,392 @@ __device__ __forceinline__ void attend_block32(WarpState& st, const uint32_t qf[
   }
 }
 
-__device__ __forceinline__ void store_partial(const AttnParams& p, const WarpState& st, int b, int h, int pi) {
-  const int lane = threadIdx.x & 31;
-  const int g = lane >> 2, t2 = (lane & 3) * 2;
-  const long long base = (((long long)b * p.a.q_heads + h) * p.np + pi) * 16;
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const long long row = base + g + hh * 8;
-    float* acc = p.part_acc + row * 128;
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-      *reinterpret_cast<float2*>(acc + nt * 8 + t2) = make_float2(st.o[nt][hh * 2], st.o[nt][hh * 2 + 1]);
-    if ((lane & 3) == 0) *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(st.m[hh], st.l[hh]);
+// Shared memory of the cluster kernel (byte offsets; identical in every CTA,
+// so a remote CTA's state is at the same offset in its window).
+//   [q tiles: G x 16 x AT_PITCH bf16] [local K/V: 2 x 32 x AT_PITCH bf16]
+//   [buffers: 139,264 B]  — window: 2 sub-chunks x (K, V) x 128 rows;
+//                           summary: per warp one chunk of (K, V) x sc slots;
+//                           after the compute: the parked states
+//                           ml[2][G][16] (float2) then acc[2][G][16][128] (fp32).
+constexpr size_t AT_BUF_BYTES = (size_t)2 * 2 * AT_WROWS * AT_PITCH * 2;
+
+__host__ __device__ inline size_t at_q_bytes(int G) { return (size_t)G * 16 * AT_PITCH * 2; }
+__host__ __device__ inline size_t at_local_bytes() { return (size_t)2 * 32 * AT_PITCH * 2; }
+__host__ __device__ inline size_t at_smem_bytes(int G) { return at_q_bytes(G) + at_local_bytes() + AT_BUF_BYTES; }
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 dsmem_ld_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float2 dsmem_ld_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Stage window rows [r0, r0 + n) (relative to the window start) of KV head g
+// into one (K, V) sub-chunk buffer; rows n..AT_WROWS-1 are zero.  pg holds
+// the page ids of logical pages first_lp.. (-1: invalid, read as zeros).
+__device__ __forceinline__ void stage_window(const AttnParams& p, bf16 (*ks)[AT_PITCH], bf16 (*vs)[AT_PITCH], int g,
+                                             int start, int r0, int n, const int* pg, int first_lp) {
+  const ls_attention_args& a = p.a;
+  const bf16* kk = reinterpret_cast<const bf16*>(a.kv_k);
+  const bf16* vv = reinterpret_cast<const bf16*>(a.kv_v);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < AT_WROWS * 16; i += blockDim.x) {
+    const int r = i >> 4, col = (i & 15) << 3;
+    const int pos = start + r0 + r;
+    const int page = r < n ? pg[(pos >> 4) - first_lp] : -1;
+    if (page >= 0) {
+      const long long off = (((long long)page * 16 + (pos & 15)) * a.kv_heads + g) * 128 + col;
+      cp_async16(&ks[r][col], kk + off);
+      cp_async16(&vs[r][col], vv + off);
+    } else {
+      *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
+    }
   }
 }
 
-__global__ void __launch_bounds__(256) attention_split_kernel(const AttnParams p) {
+// Stage summary slots [s0, s0 + n) of query head h (keys: learned queries,
+// values: the bf16 summary copy, or the fp32 state rounded here) into a
+// (K, V) chunk buffer: this warp writes buffer rows [rb, re) (zeros past n).
+__device__ __forceinline__ void stage_summary(const AttnParams& p, bf16 (*ks)[AT_PITCH], bf16 (*vs)[AT_PITCH], int h,
+                                              int slot, int s0, int n, int rb, int re) {
+  const ls_attention_args& a = p.a;
+  const int lane = threadIdx.x & 31;
+  const bf16* kq = reinterpret_cast<const bf16*>(a.learned_query) + ((long long)h * a.slots_per_head + s0) * 128;
+  const bf16* vb = a.state_bf16 == nullptr ? nullptr
+                                            : reinterpret_cast<const bf16*>(a.state_bf16) +
+                                                  (long long)slot * a.state_bf16_stride +
+                                                  ((long long)h * a.slots_per_head + s0) * 128;
+  const float* vf = a.state_out + (long long)slot * a.state_stride + ((long long)h * a.slots_per_head + s0) * 128;
+#pragma unroll 4
+  for (int i = lane + rb * 16; i < re * 16; i += 32) {
+    const int r = i >> 4, col = (i & 15) << 3;
+    if (r < n) {
+      cp_async16(&ks[r][col], kq + (long long)r * 128 + col);
+      if (vb != nullptr) {
+        cp_async16(&vs[r][col], vb + (long long)r * 128 + col);
+      } else {
+        const float4 v0 = __ldcs(reinterpret_cast<const float4*>(vf + (long long)r * 128 + col));
+        const float4 v1 = __ldcs(reinterpret_cast<const float4*>(vf + (long long)r * 128 + col + 4));
+        uint4 pk;
+        pk.x = pack_bf16(v0.x, v0.y);
+        pk.y = pack_bf16(v0.z, v0.w);
+        pk.z = pack_bf16(v1.x, v1.y);
+        pk.w = pack_bf16(v1.z, v1.w);
+        *reinterpret_cast<uint4*>(&vs[r][col]) = pk;
+      }
+    } else {
+      *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// Park a warp's state (mma C-fragment layout) as ml[slot][warp][16] and
+// acc[slot][warp][16][128].
+__device__ __forceinline__ void park_state(float2* ml, float* acc, int G, int slot, int hw, const WarpState& st) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t2 = (lane & 3) * 2;
+  float* A = acc + ((size_t)slot * G + hw) * 16 * 128;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int row = g + hh * 8;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+      *reinterpret_cast<float2*>(A + row * 128 + nt * 8 + t2) = make_float2(st.o[nt][hh * 2], st.o[nt][hh * 2 + 1]);
+    if ((lane & 3) == 0) ml[((size_t)slot * G + hw) * 16 + row] = make_float2(st.m[hh], st.l[hh]);
+  }
+}
+
+// Fold the parked slot-1 state of head hw (the other warp of the head, same
+// source) into this warp's state.
+__device__ __forceinline__ void fold_parked(const float2* ml, const float* acc, int G, int hw, WarpState& st) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t2 = (lane & 3) * 2;
+  const float* A = acc + ((size_t)G + hw) * 16 * 128;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int row = g + hh * 8;
+    const float2 o = ml[((size_t)G + hw) * 16 + row];
+    const float m = fmaxf(st.m[hh], o.x);
+    const float mu = m == -INFINITY ? 0.0f : m;
+    const float f0 = fast_exp(st.m[hh] - mu), f1 = fast_exp(o.x - mu);
+    st.m[hh] = m;
+    st.l[hh] = st.l[hh] * f0 + o.y * f1;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const float2 v = *reinterpret_cast<const float2*>(A + row * 128 + nt * 8 + t2);
+      st.o[nt][hh * 2] = st.o[nt][hh * 2] * f0 + v.x * f1;
+      st.o[nt][hh * 2 + 1] = st.o[nt][hh * 2 + 1] * f0 + v.y * f1;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   asm volatile("griddepcontrol.launch_dependents;");
   const ls_attention_args& a = p.a;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const int G = p.G;
   const int P = a.block;
+  const int rank = static_cast<int>(cluster_rank());
+  const int cid = blockIdx.x / AT_CLUSTER;
+  const int g = cid % a.kv_heads;
+  const int b = cid / a.kv_heads;
+  const int R = static_cast<int>(blockDim.x >> 5) / G;  // warps per query head (1 or 2)
+  const int hw = warp % G, part = warp / G;               // head within the group, key half
+  const int h = g * G + hw;
   const int row_ld = (a.q_heads + 2 * a.kv_heads) * 128;
   const bf16* qkv = reinterpret_cast<const bf16*>(a.qkv);
-  // smem: per-warp q tile, then the key/value area
-  bf16 (*qs)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw) + warp * 16;
-  bf16* kv_area = reinterpret_cast<bf16*>(smem_raw) + (size_t)G * 16 * AT_PITCH;
+  bf16 (*qs)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw) + hw * 16;
+  bf16 (*lk)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw + at_q_bytes(G));
+  bf16 (*lv)[AT_PITCH] = lk + 32;
+  uint8_t* buf = smem_raw + at_q_bytes(G) + at_local_bytes();
+  float2* park_ml = reinterpret_cast<float2*>(buf);
+  float* park_acc = reinterpret_cast<float*>(buf + (size_t)2 * G * 16 * sizeof(float2));
 
-  long long item = blockIdx.x;
-  if (item < p.n_win) {
-    // ---------------- window task ----------------
-    const int s = static_cast<int>(item % p.nsw);
-    item /= p.nsw;
-    const int g = static_cast<int>(item % a.kv_heads);
-    const int b = static_cast<int>(item / a.kv_heads);
-    const int h = g * G + warp;
-    const int len = a.seq_lens[b];
-    const int wl = min(len, a.window);
-    const int start = len - wl;  // first window position
-    bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(kv_area);
-    bf16 (*vs)[AT_PITCH] = ks + AT_WROWS;
-    load_q_tile(qs, qkv, row_ld, b * P, P, h);
-    __syncwarp();
-    uint32_t qf[8][4];
-    load_q_frags(qf, qs);
-    WarpState st;
-    ws_init(st);
-    const bf16* kk_base = reinterpret_cast<const bf16*>(a.kv_k);
-    const bf16* vv_base = reinterpret_cast<const bf16*>(a.kv_v);
-    const int r_begin = s * p.wc;
-    const int r_end = min(r_begin + p.wc, wl);
-    for (int r0 = r_begin; r0 < r_end; r0 += AT_WROWS) {
-      const int nrows = min(AT_WROWS, r_end - r0);
-      __syncthreads();  // previous sub-chunk fully consumed
-      for (int i = threadIdx.x; i < AT_WROWS * 16; i += blockDim.x) {
-        const int r = i >> 4, col = (i & 15) << 3;
-        if (r < nrows) {
-          const int pos = start + r0 + r;
-          int lp = pos >> 4;
-          if (a.ring_pages > 0) lp %= a.ring_pages;
-          const int page = a.page_table[(long long)b * a.table_stride + lp];
-          if (page >= 0 && page < a.pool_pages) {
-            const long long off = (((long long)page * 16 + (pos & 15)) * a.kv_heads + g) * 128 + col;
-            cp_async16(&ks[r][col], kk_base + off);
-            cp_async16(&vs[r][col], vv_base + off);
-          } else {
-            record_status(a.status, LS_DEV_BAD_INDEX);
-            *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
-          }
-        } else {
-          *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
-        }
+  const int len = a.seq_lens[b];
+  const int wl = len < a.window ? (len > 0 ? len : 0) : a.window;
+  const int wstart = len - wl;
+  int slot = a.slots[b];
+  if (slot < 0 || slot >= a.capacity) {
+    if (threadIdx.x == 0) record_status(a.status, LS_DEV_BAD_INDEX);
+    slot = 0;  // read a valid entry; the status word reports the bad index
+  }
+  const bool is_win = rank < p.nw;
+  const bool is_sum = !is_win && rank < AT_CLUSTER - 1;
+  __shared__ int pg[AT_MAXPAGES];
+  int first_lp = 0;
+
+  // ---- stage the keys/values that do not depend on the projection ----
+  int w_r0 = 0, w_n = 0, n_sub = 0;      // window CTA: rows [w_r0, w_r0 + w_n) in sub-chunks of 128
+  int s_0 = 0, s_n = 0, s_sub = 0;       // summary CTA: slots [s_0, s_0 + s_n) in sub-chunks of 32
+  if (is_win) {
+    w_r0 = rank * p.wrows;
+    w_n = wl - w_r0 < p.wrows ? wl - w_r0 : p.wrows;
+    if (w_n < 0) w_n = 0;
+    n_sub = (w_n + AT_WROWS - 1) / AT_WROWS;
+    // page ids of this CTA's rows, read once (every K/V address depends on them)
+    first_lp = (wstart + w_r0) >> 4;
+    const int n_pages = w_n > 0 ? ((wstart + w_r0 + w_n - 1) >> 4) - first_lp + 1 : 0;
+    for (int i = threadIdx.x; i < n_pages; i += blockDim.x) {
+      int lp = first_lp + i;
+      if (a.ring_pages > 0) lp %= a.ring_pages;
+      int page = a.page_table[(long long)b * a.table_stride + lp];
+      if (page < 0 || page >= a.pool_pages) {
+        record_status(a.status, LS_DEV_BAD_INDEX);
+        page = -1;
       }
+      pg[i] = page;
+    }
+    __syncthreads();
+    for (int i = 0; i < 2 && i < n_sub; ++i) {
+      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + i * 2 * AT_WROWS;
+      const int n = w_n - i * AT_WROWS < AT_WROWS ? w_n - i * AT_WROWS : AT_WROWS;
+      stage_window(p, ks, ks + AT_WROWS, g, wstart, w_r0 + i * AT_WROWS, n, pg, first_lp);
       cp_async_commit();
-      cp_async_wait_all();
-      __syncthreads();
-      for (int k0 = 0; k0 < nrows; k0 += 32) attend_block32(st, qf, ks, vs, k0, nrows - k0, a.softmax_scale);
     }
-    store_partial(p, st, b, h, s);
-  } else if (item < p.n_win + p.n_glob) {
-    // ---------------- summary task ----------------
-    item -= p.n_win;
-    const int c = static_cast<int>(item % p.ngc);
-    item /= p.ngc;
-    const int g = static_cast<int>(item % a.kv_heads);
-    const int b = static_cast<int>(item / a.kv_heads);
-    const int h = g * G + warp;
-    bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(kv_area) + warp * 2 * AT_GSLOTS;
-    bf16 (*vs)[AT_PITCH] = ks + AT_GSLOTS;
-    load_q_tile(qs, qkv, row_ld, b * P, P, h);
-    const int s0 = c * AT_GSLOTS;
-    const int ns = min(AT_GSLOTS, a.slots_per_head - s0);
-    const bf16* kq = reinterpret_cast<const bf16*>(a.learned_query) + ((long long)h * a.slots_per_head + s0) * 128;
-    int slot = a.slots[b];
-    if (slot < 0 || slot >= a.capacity) {
-      if (lane == 0) record_status(a.status, LS_DEV_BAD_INDEX);
-      slot = 0;  // read a valid entry; the status word reports the bad index
-    }
-    if (a.state_bf16 != nullptr) {
-      // bf16 copy of the summary kept by the refresh: straight async copies
-      const bf16* vb = reinterpret_cast<const bf16*>(a.state_bf16) + (long long)slot * a.state_bf16_stride +
-                       ((long long)h * a.slots_per_head + s0) * 128;
-      for (int i = lane; i < AT_GSLOTS * 16; i += 32) {
-        const int r = i >> 4, col = (i & 15) << 3;
-        if (r < ns) {
-          cp_async16(&ks[r][col], kq + (long long)r * 128 + col);
-          cp_async16(&vs[r][col], vb + (long long)r * 128 + col);
-        } else {
-          *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
-        }
-      }
+  } else if (is_sum) {
+    s_0 = (rank - p.nw) * p.sslots;
+    s_n = a.slots_per_head - s_0 < p.sslots ? a.slots_per_head - s_0 : p.sslots;
+    if (s_n < 0) s_n = 0;
+    s_sub = (s_n + p.sc - 1) / p.sc;
+    if (s_sub > 0) {
+      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + hw * 2 * p.sc;
+      stage_summary(p, ks, ks + p.sc, h, slot, s_0, s_n < p.sc ? s_n : p.sc, part * (p.sc / R),
+                    (part + 1) * (p.sc / R));
       cp_async_commit();
-      cp_async_wait_all();
-    } else {
-      const float* vq =
-          a.state_out + (long long)slot * a.state_stride + ((long long)h * a.slots_per_head + s0) * 128;
-      for (int i = lane; i < AT_GSLOTS * 16; i += 32) {
-        const int r = i >> 4, col = (i & 15) << 3;
-        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        if (r < ns) {
-          kv = *reinterpret_cast<const uint4*>(kq + (long long)r * 128 + col);
-          const float4 v0 = __ldcs(reinterpret_cast<const float4*>(vq + (long long)r * 128 + col));
-          const float4 v1 = __ldcs(reinterpret_cast<const float4*>(vq + (long long)r * 128 + col + 4));
-          vv.x = pack_bf16(v0.x, v0.y);
-          vv.y = pack_bf16(v0.z, v0.w);
-          vv.z = pack_bf16(v1.x, v1.y);
-          vv.w = pack_bf16(v1.z, v1.w);
-        }
-        *reinterpret_cast<uint4*>(&ks[r][col]) = kv;
-        *reinterpret_cast<uint4*>(&vs[r][col]) = vv;
-      }
     }
-    __syncwarp();
-    uint32_t qf[8][4];
-    load_q_frags(qf, qs);
-    WarpState st;
-    ws_init(st);
-    if (ns > 0) attend_block32(st, qf, ks, vs, 0, ns, a.softmax_scale);
-    store_partial(p, st, b, h, p.nsw + c);
-  } else {
-    // ---------------- local task ----------------
-    item -= p.n_win + p.n_glob;
-    const int g = static_cast<int>(item % a.kv_heads);
-    const int b = static_cast<int>(item / a.kv_heads);
-    const int h = g * G + warp;
-    bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(kv_area);
-    bf16 (*vs)[AT_PITCH] = ks + 32;
+  }
+
+  // ---- the projection's outputs: query tiles, local keys/values ----
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (part == 0) load_q_tile(qs, qkv, row_ld, b * P, P, h);
+  if (!is_win && !is_sum) {
     for (int i = threadIdx.x; i < 32 * 16; i += blockDim.x) {
       const int r = i >> 4, col = (i & 15) << 3;
       uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
       if (r < P) {
-        const bf16* row = qkv + (long long)(b * P + r) * row_ld;
-        kv = *reinterpret_cast<const uint4*>(row + (a.q_heads + g) * 128 + col);
-        vv = *reinterpret_cast<const uint4*>(row + (a.q_heads + a.kv_heads + g) * 128 + col);
+        const bf16* rowp = qkv + (long long)(b * P + r) * row_ld;
+        kv = *reinterpret_cast<const uint4*>(rowp + (a.q_heads + g) * 128 + col);
+        vv = *reinterpret_cast<const uint4*>(rowp + (a.q_heads + a.kv_heads + g) * 128 + col);
       }
-      *reinterpret_cast<uint4*>(&ks[r][col]) = kv;
-      *reinterpret_cast<uint4*>(&vs[r][col]) = vv;
+      *reinterpret_cast<uint4*>(&lk[r][col]) = kv;
+      *reinterpret_cast<uint4*>(&lv[r][col]) = vv;
     }
-    load_q_tile(qs, qkv, row_ld, b * P, P, h);
-    __syncthreads();
-    uint32_t qf[8][4];
-    load_q_frags(qf, qs);
-    WarpState st;
-    ws_init(st);
-    attend_block32(st, qf, ks, vs, 0, P, a.softmax_scale);
-    store_partial(p, st, b, h, p.np - 1);
   }
-}
+  __syncthreads();
+  uint32_t qf[8][4];
+  load_q_frags(qf, qs);
+  WarpState st;
+  ws_init(st);
 
-// Merge the partial states: per source (window, summary, local) rescale to the
-// source maximum, round the weighted sum to bf16, normalise; then merge the
-// sources by log-sum-exp in the reference's order (summary, window, local).
-__global__ void __launch_bounds__(512) attention_combine_kernel(const AttnParams p) {
-  asm volatile("griddepcontrol.launch_dependents;");
-  const ls_attention_args& a = p.a;
-  const int bh = blockIdx.x;
-  const int b = bh / a.q_heads, h = bh % a.q_heads;
-  const int row = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (row >= a.block) return;
-  const long long base = (long long)bh * p.np * 16;
-  float out_src[3][4];
-  float lse_src[3];
-  // source order in the part array: window [0, nsw), summary [nsw, nsw+ngc), local
-  for (int src = 0; src < 3; ++src) {
-    const int lo = src == 0 ? 0 : (src == 1 ? p.nsw : p.nsw + p.ngc);
-    const int n = src == 0 ? p.nsw : (src == 1 ? p.ngc : 1);  // <= 32 partials per source
-    float m_i = -INFINITY, l_i = 0.0f;
-    if (lane < n) {
-      const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + (base + (lo + lane) * 16 + row) * 2);
-      m_i = ml.x;
-      l_i = ml.y;
+  if (is_win) {
+    for (int i = 0; i < n_sub; ++i) {
+      if (i + 1 < n_sub) cp_async_wait_one(); else cp_async_wait_all();
+      __syncthreads();
+      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + (i & 1) * 2 * AT_WROWS;
+      const int n = w_n - i * AT_WROWS < AT_WROWS ? w_n - i * AT_WROWS : AT_WROWS;
+      if (R == 1) {
+        attend_block<16>(st, qf, ks, ks + AT_WROWS, 0, n, a.softmax_scale);
+      } else if (n > part * 64) {
+        attend_block<8>(st, qf, ks, ks + AT_WROWS, part * 64, n - part * 64, a.softmax_scale);
+      }
+      __syncthreads();  // every warp is done with this buffer
+      if (i + 2 < n_sub) {
+        const int n2 = w_n - (i + 2) * AT_WROWS < AT_WROWS ? w_n - (i + 2) * AT_WROWS : AT_WROWS;
+        stage_window(p, ks, ks + AT_WROWS, g, wstart, w_r0 + (i + 2) * AT_WROWS, n2, pg, first_lp);
+        cp_async_commit();
+      }
     }
-    const float M = warp_max(m_i);
-    const float f_i = (m_i == -INFINITY) ? 0.0f : expf(m_i - M);
-    const float L = warp_sum(l_i * f_i);
-    float wv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const float4* accp = reinterpret_cast<const float4*>(p.part_acc + (base + lo * 16 + row) * 128) + lane;
-#pragma unroll 4
-    for (int i = 0; i < n; ++i) {
-      const float f = __shfl_sync(0xffffffffu, f_i, i);
-      const float4 acc = accp[(long long)i * 16 * 32];
-      wv[0] += acc.x * f;
-      wv[1] += acc.y * f;
-      wv[2] += acc.z * f;
-      wv[3] += acc.w * f;
+  } else if (is_sum) {
+    // one chunk buffer per head; its R warps stage and attend disjoint 32-slot halves
+    bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + hw * 2 * p.sc;
+    const int half = p.sc / R;  // 32
+    for (int i = 0; i < s_sub; ++i) {
+      cp_async_wait_all();
+      __syncthreads();
+      const int n = s_n - i * p.sc < p.sc ? s_n - i * p.sc : p.sc;
+      if (n > part * half) attend_block<4>(st, qf, ks, ks + p.sc, part * half, n - part * half, a.softmax_scale);
+      __syncthreads();  // every warp is done with the buffers
+      if (i + 1 < s_sub) {
+        const int n2 = s_n - (i + 1) * p.sc < p.sc ? s_n - (i + 1) * p.sc : p.sc;
+        stage_summary(p, ks, ks + p.sc, h, slot, s_0 + (i + 1) * p.sc, n2, part * half, (part + 1) * half);
+        cp_async_commit();
+      }
     }
-    const float safe = fmaxf(L, 1.17549435e-38f);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) out_src[src][e] = bf16_round(wv[e]) / safe;
-    lse_src[src] = L > 0.0f ? M + logf(safe) : -INFINITY;
+  } else if (part == 0) {
+    attend_block<4>(st, qf, lk, lv, 0, P, a.softmax_scale);
   }
-  // merge_normalized_attention over (summary, window, local)
-  const int order[3] = {1, 0, 2};
-  float mx = -INFINITY;
-  for (int i = 0; i < 3; ++i) mx = fmaxf(mx, lse_src[i]);
-  const float mxs = mx == -INFINITY ? 0.0f : mx;
-  float tot = 0.0f;
-  for (int i = 0; i < 3; ++i) tot += lse_src[order[i]] == -INFINITY ? 0.0f : expf(lse_src[order[i]] - mxs);
-  const float merged = mxs + logf(tot);
-  const float safe_m = (merged == -INFINITY || merged != merged) ? 0.0f : merged;
-  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (int i = 0; i < 3; ++i) {
-    const int sidx = order[i];
-    const float cf = lse_src[sidx] == -INFINITY ? 0.0f : expf(lse_src[sidx] - safe_m);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[e] += cf * out_src[sidx][e];
+
+  // ---- park the states, merge across the cluster ----
+  cp_async_wait_all();
+  __syncthreads();  // the buffers become the parking area
+  if (R > 1) {
+    // the two warps of a head hold halves of the same source: fold them
+    if (part == 1) park_state(park_ml, park_acc, G, 1, hw, st);
+    __syncthreads();
+    if (part == 0) {
+      fold_parked(park_ml, park_acc, G, hw, st);
+      park_state(park_ml, park_acc, G, 0, hw, st);
+    }
+  } else {
+    park_state(park_ml, park_acc, G, 0, hw, st);
   }
-  bf16* out = reinterpret_cast<bf16*>(a.out) + (long long)(b * a.block + row) * a.q_heads * 128 + h * 128 + lane * 4;
-  __nv_bfloat162 lo2 = __floats2bfloat162_rn(o[0], o[1]);
-  __nv_bfloat162 hi2 = __floats2bfloat162_rn(o[2], o[3]);
-  uint2 pk;
-  pk.x = *reinterpret_cast<uint32_t*>(&lo2);
-  pk.y = *reinterpret_cast<uint32_t*>(&hi2);
-  *reinterpret_cast<uint2*>(out) = pk;
+  cluster_sync_all();
+
+  const int rt = G * P;  // (head, row) states of the group
+  const int j0 = rank * rt / AT_CLUSTER, j1 = (rank + 1) * rt / AT_CLUSTER;
+  const int nwarps = blockDim.x >> 5;
+  for (int j = j0 + warp; j < j1; j += nwarps) {
+    const int hi = j / P, row = j - hi * P;
+    const uint32_t ml_off = smem_u32(park_ml + (size_t)hi * 16 + row) - smem_u32(park_ml);
+    const uint32_t acc_off = smem_u32(park_acc + ((size_t)hi * 16 + row) * 128 + lane * 4) - smem_u32(park_acc);
+    // every rank's state of this (head, row), all remote loads in flight at once
+    float2 mlq[AT_CLUSTER];
+    float4 accq[AT_CLUSTER];
+#pragma unroll
+    for (int q = 0; q < AT_CLUSTER; ++q) {
+      mlq[q] = dsmem_ld_f2(dsmem_addr(park_ml, q) + ml_off);
+      accq[q] = dsmem_ld_f4(dsmem_addr(park_acc, q) + acc_off);
+    }
+    float out_src[3][4];
+    float lse_src[3];
+    // src 0 = window (ranks [0, nw)), 1 = summary (ranks [nw, 7)), 2 = local (rank 7)
+#pragma unroll
+    for (int src = 0; src < 3; ++src) {
+      const int q0 = src == 0 ? 0 : (src == 1 ? p.nw : AT_CLUSTER - 1);
+      const int q1 = src == 0 ? p.nw : (src == 1 ? AT_CLUSTER - 1 : AT_CLUSTER);
+      float M = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < AT_CLUSTER; ++q)
+        if (q >= q0 && q < q1) M = fmaxf(M, mlq[q].x);
+      float L = 0.0f, wv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int q = 0; q < AT_CLUSTER; ++q) {
+        if (q >= q0 && q < q1) {
+          const float f = fast_exp(mlq[q].x - (M == -INFINITY ? 0.0f : M));
+          L += mlq[q].y * f;
+          wv[0] += accq[q].x * f;
+          wv[1] += accq[q].y * f;
+          wv[2] += accq[q].z * f;
+          wv[3] += accq[q].w * f;
+        }
+      }
+      const float safe = fmaxf(L, 1.17549435e-38f);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) out_src[src][e] = __fdividef(bf16_round(wv[e]), safe);
+      lse_src[src] = L > 0.0f ? M + __logf(safe) : -INFINITY;
+    }
+    // merge_normalized_attention over (summary, window, local)
+    const int order[3] = {1, 0, 2};
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) mx = fmaxf(mx, lse_src[i]);
+    const float mxs = mx == -INFINITY ? 0.0f : mx;
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) tot += fast_exp(lse_src[order[i]] - mxs);
+    const float merged = mxs + __logf(tot);
+    const float safe_m = (merged == -INFINITY || merged != merged) ? 0.0f : merged;
+    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const int sidx = order[i];
+      const float cf = fast_exp(lse_src[sidx] - safe_m);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] += cf * out_src[sidx][e];
+    }
+    bf16* out = reinterpret_cast<bf16*>(a.out) + (long long)(b * P + row) * a.q_heads * 128 + (g * G + hi) * 128 +
+                lane * 4;
+    uint2 pk;
+    pk.x = pack_bf16(o[0], o[1]);
+    pk.y = pack_bf16(o[2], o[3]);
+    *reinterpret_cast<uint2*>(out) = pk;
+  }
+  cluster_sync_all();  // keep the parked states alive until every CTA has read them
 }
 
 struct AttnPlan {
-  int G, nsw, wc, ngc, np;
-  long long n_win, n_glob, n_loc;
-  size_t ml_bytes, acc_bytes, smem;
+  int G, nw, wrows, sslots, sc;
+  size_t smem;
 };
 
-static AttnPlan plan_attention(int batch, int q_heads, int kv_heads, int window, int slots) {
+static AttnPlan plan_attention(int q_heads, int kv_heads, int window, int slots) {
   AttnPlan pl{};
   pl.G = q_heads / kv_heads;
-  const int sms = host_sm_count();
-  pl.ngc = (slots + AT_GSLOTS - 1) / AT_GSLOTS;
-  // Window chunk: split the window until the grid covers ~2 waves of SMs.
-  const int max_chunks = (window + AT_WROWS - 1) / AT_WROWS;
-  int nsw = 1;
-  while (nsw < max_chunks &&
-         (long long)batch * kv_heads * (nsw + pl.ngc + 1) < 2LL * sms)
-    nsw *= 2;
-  if (nsw > max_chunks) nsw = max_chunks;
-  pl.wc = ((window + nsw - 1) / nsw + AT_WROWS - 1) / AT_WROWS * AT_WROWS;
-  pl.nsw = (window + pl.wc - 1) / pl.wc;
-  pl.np = pl.nsw + pl.ngc + 1;  // the combine reduces <= 32 partials per source (one per lane)
-  pl.n_win = (long long)batch * kv_heads * pl.nsw;
-  pl.n_glob = (long long)batch * kv_heads * pl.ngc;
-  pl.n_loc = (long long)batch * kv_heads;
-  const size_t rows = (size_t)batch * q_heads * pl.np * 16;
-  pl.ml_bytes = (rows * 2 * sizeof(float) + 255) / 256 * 256;
-  pl.acc_bytes = rows * 128 * sizeof(float);
-  const size_t q_area = (size_t)pl.G * 16 * AT_PITCH * 2;
-  size_t kv = (size_t)2 * AT_WROWS * AT_PITCH * 2;
-  const size_t kv_glob = (size_t)pl.G * 2 * AT_GSLOTS * AT_PITCH * 2;
-  if (kv_glob > kv) kv = kv_glob;
-  pl.smem = q_area + kv;
+  // Split the 7 non-local CTAs between window and summary by bytes read: the
+  // window is W rows shared by the group, the summary S slots per query head.
+  const double wb = (double)window, sb = (double)pl.G * slots;
+  int nw = static_cast<int>(7.0 * wb / (wb + sb) + 0.5);
+  nw = nw < 1 ? 1 : (nw > 6 ? 6 : nw);
+  pl.nw = nw;
+  pl.wrows = ((window + nw - 1) / nw + 31) / 32 * 32;
+  const int ns = AT_CLUSTER - 1 - nw;
+  pl.sslots = ((slots + ns - 1) / ns + 31) / 32 * 32;
+  pl.sc = pl.G <= 4 ? 64 : 32;  // G x sc x (K, V) rows fill the buffer area
+  pl.smem = at_smem_bytes(pl.G);
   return pl;
 }
 
@@ -437,12 +576,17 @@ static AttnPlan plan_attention(int batch, int q_heads, int kv_heads, int window,
 using namespace ls;
 
 extern "C" size_t ls_attention_workspace_bytes(int batch, int q_heads, int kv_heads, int window, int slots_per_head) {
-  if (batch <= 0 || kv_heads <= 0 || q_heads % kv_heads) return 0;
-  AttnPlan pl = plan_attention(batch, q_heads, kv_heads, window, slots_per_head);
-  return pl.ml_bytes + pl.acc_bytes;
+  (void)batch;
+  (void)q_heads;
+  (void)kv_heads;
+  (void)window;
+  (void)slots_per_head;
+  return 0;  // partial states stay on chip (distributed shared memory)
 }
 
 extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void* workspace, size_t workspace_bytes) {
+  (void)workspace;
+  (void)workspace_bytes;
   if (a == nullptr || a->qkv == nullptr || a->kv_k == nullptr || a->kv_v == nullptr || a->page_table == nullptr ||
       a->seq_lens == nullptr || a->learned_query == nullptr || a->state_out == nullptr || a->slots == nullptr ||
       a->out == nullptr)
@@ -452,34 +596,37 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
       a->block > 16 || a->window < 1 || a->window > 32 * 128 || a->slots_per_head < 1 ||
       a->slots_per_head > 32 * 32)
     return set_error(LS_ERR_UNSUPPORTED, "ls_draft_attention: need GQA group <= 8, 1 <= block <= 16");
-  AttnPlan pl = plan_attention(a->batch, a->q_heads, a->kv_heads, a->window, a->slots_per_head);
-  if (workspace == nullptr || workspace_bytes < pl.ml_bytes + pl.acc_bytes)
-    return set_error(LS_ERR_WORKSPACE, "ls_draft_attention: workspace %zu < %zu", workspace_bytes,
-                     pl.ml_bytes + pl.acc_bytes);
+  if ((long long)a->batch * a->kv_heads * AT_CLUSTER > 0x7fffffffLL)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_draft_attention: grid too large");
+  AttnPlan pl = plan_attention(a->q_heads, a->kv_heads, a->window, a->slots_per_head);
   AttnParams p{};
   p.a = *a;
   p.G = pl.G;
-  p.nsw = pl.nsw;
-  p.wc = pl.wc;
-  p.ngc = pl.ngc;
-  p.np = pl.np;
-  p.n_win = pl.n_win;
-  p.n_glob = pl.n_glob;
-  p.part_ml = reinterpret_cast<float*>(workspace);
-  p.part_acc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + pl.ml_bytes);
+  p.nw = pl.nw;
+  p.wrows = pl.wrows;
+  p.sslots = pl.sslots;
+  p.sc = pl.sc;
   static size_t configured = 0;
   if (pl.smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(pl.smem));
+    cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(at_smem_bytes(8)));
     if (e != cudaSuccess) return set_cuda_error("ls_draft_attention: cudaFuncSetAttribute", e);
-    configured = pl.smem;
+    configured = at_smem_bytes(8);
   }
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const long long grid = pl.n_win + pl.n_glob + pl.n_loc;
-  attention_split_kernel<<<static_cast<unsigned>(grid), 32 * pl.G, pl.smem, st>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error("ls_draft_attention: split launch", e);
-  attention_combine_kernel<<<a->batch * a->q_heads, 32 * a->block, 0, st>>>(p);
-  e = cudaGetLastError();
-  return e == cudaSuccess ? LS_OK : set_cuda_error("ls_draft_attention: combine launch", e);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a->batch * a->kv_heads * AT_CLUSTER));
+  cfg.blockDim = dim3(32 * pl.G * (pl.G <= 4 ? 2 : 1));
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = AT_CLUSTER;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attention_cluster_kernel, p);
+  return e == cudaSuccess ? LS_OK : set_cuda_error("ls_draft_attention: launch", e);
 }
