@@ -302,7 +302,7 @@ LS_API size_t ls_markov_workspace_bytes(int batch, int block);
 LS_API int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes);
 
 /* ls_markov_argmax with its scratch in a fixed device array inside this
- * library (1.5 MiB + 8.25 KiB per device) instead of a caller workspace.  No
+ * library (648.25 KiB per device) instead of a caller workspace.  No
  * counterpart in the reference, which allocates its step tensors through
  * PyTorch; this exists for callers that cannot allocate device memory when
  * they propose tokens: a serving process that handed all free HBM to its paged

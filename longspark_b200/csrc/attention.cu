@@ -626,7 +626,7 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, attention_cluster_kernel, p);
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_draft_attention: launch", e);
 }

@@ -16,6 +16,7 @@ constexpr int EW_THREADS = 256;
 __global__ void __launch_bounds__(EW_THREADS) rmsnorm_kernel(const bf16* x, int x_ld, const bf16* w, bf16* out,
                                                              int out_ld, int n, float eps, int mode) {
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x comes from the previous kernel
   __shared__ float red[EW_THREADS / 32];
   const int row = blockIdx.x;
   const bf16* xr = x + (long long)row * x_ld;
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(EW_THREADS)
   const bf16* pr = pos_emb + (long long)i * hidden;
   const bf16* lr = latest + (long long)b * hidden;
   bf16* o = out + (long long)row * 2 * hidden;
+  // token + position embeddings: inputs and weights only, before the wait
   for (int c = threadIdx.x * 8; c < hidden; c += EW_THREADS * 8) {
     const uint4 ea = *reinterpret_cast<const uint4*>(er + c);
     const uint4 pa = *reinterpret_cast<const uint4*>(pr + c);
@@ -91,8 +93,10 @@ __global__ void __launch_bounds__(EW_THREADS)
 #pragma unroll
     for (int j = 0; j < 8; ++j) se[j] = __float2bfloat16_rn(__bfloat162float(ee[j]) + __bfloat162float(pe[j]));
     *reinterpret_cast<uint4*>(o + c) = s;
-    *reinterpret_cast<uint4*>(o + hidden + c) = *reinterpret_cast<const uint4*>(lr + c);
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // `latest` comes from the previous kernel
+  for (int c = threadIdx.x * 8; c < hidden; c += EW_THREADS * 8)
+    *reinterpret_cast<uint4*>(o + hidden + c) = *reinterpret_cast<const uint4*>(lr + c);
 }
 
 }  // namespace ls
@@ -105,10 +109,9 @@ extern "C" int ls_rmsnorm(void* stream, const void* x, int x_ld, const void* w, 
   if (x == nullptr || w == nullptr || out == nullptr || n <= 0 || n % 8 || x_ld % 8 || out_ld % 8 ||
       (mode != 0 && mode != 1))
     return set_error(LS_ERR_INVALID, "ls_rmsnorm: bad arguments (n, x_ld, out_ld multiples of 8; mode 0/1)");
-  rmsnorm_kernel<<<rows, EW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const bf16*>(x), x_ld, reinterpret_cast<const bf16*>(w), reinterpret_cast<bf16*>(out), out_ld,
-      n, eps, mode);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(rmsnorm_kernel, dim3(rows), dim3(EW_THREADS), 0, reinterpret_cast<cudaStream_t>(stream),
+                             reinterpret_cast<const bf16*>(x), x_ld, reinterpret_cast<const bf16*>(w),
+                             reinterpret_cast<bf16*>(out), out_ld, n, eps, mode);
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_rmsnorm: launch", e);
 }
 
@@ -121,9 +124,10 @@ extern "C" int ls_shifted_input(void* stream, const long long* anchors, const in
       hidden % 8 || block < 1 || (positions != nullptr && seq_lens == nullptr) ||
       (rope_table != nullptr && (positions == nullptr || inv_freq == nullptr)))
     return set_error(LS_ERR_INVALID, "ls_shifted_input: bad arguments");
-  shifted_input_kernel<<<batch * block, EW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      anchors, seq_lens, positions, inv_freq, rope_table, reinterpret_cast<const bf16*>(embed), reinterpret_cast<const bf16*>(pos_emb),
-      reinterpret_cast<const bf16*>(latest), reinterpret_cast<bf16*>(out), block, hidden, vocab, mask_token_id, status);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(shifted_input_kernel, dim3(batch * block), dim3(EW_THREADS), 0,
+                             reinterpret_cast<cudaStream_t>(stream), anchors, seq_lens, positions, inv_freq,
+                             rope_table, reinterpret_cast<const bf16*>(embed), reinterpret_cast<const bf16*>(pos_emb),
+                             reinterpret_cast<const bf16*>(latest), reinterpret_cast<bf16*>(out), block, hidden,
+                             vocab, mask_token_id, status);
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_shifted_input: launch", e);
 }

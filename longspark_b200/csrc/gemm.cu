@@ -710,13 +710,8 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  // LONGSPARK_B200_PDL=0 launches with plain stream ordering (for A/B timing).
-  static const bool pdl = [] {
-    const char* e = getenv("LONGSPARK_B200_PDL");
-    return e == nullptr || e[0] != '0';
-  }();
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map_w, map_x, kp);
   if (e != cudaSuccess) return set_cuda_error("ls_gemm: launch", e);
   return LS_OK;

@@ -10,6 +10,9 @@
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "../../include/longspark_b200.h"
 
@@ -24,5 +27,33 @@ int host_sm_count();
 // swizzle (box_inner * 2 must be 128).  Out-of-range rows read as zero.
 int encode_tma_2d_bf16(CUtensorMap* map, const void* base, long long inner, long long outer, long long pitch,
                        int box_inner, int box_outer);
+
+// Programmatic dependent launch: a kernel launched this way may start while
+// the previous kernel of the stream drains; it must execute
+// griddepcontrol.wait before touching anything that kernel writes.
+// LONGSPARK_B200_PDL=0 turns it off (plain stream ordering, for A/B timing).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("LONGSPARK_B200_PDL");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace ls

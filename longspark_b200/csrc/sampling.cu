@@ -34,7 +34,8 @@ constexpr int MK_MAXCAND = 4096;
 constexpr int MK_MAXRANK = 512;
 constexpr int MK_MAXTILES = 1024;
 constexpr int MK_ROWCAND = 128;   // band candidates kept per row
-constexpr int MK_ROWPAIRS = 256;  // (previous candidate, candidate) pair values kept per row
+constexpr int MK_TPT = 8;         // tile maxima per thread held in registers (vocab <= 8 * 256 * 128)
+constexpr int MK_ROWPAIRS = 256;  // (previous candidate, candidate) pairs evaluated per row
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
@@ -124,8 +125,10 @@ __device__ __forceinline__ void row_max(const float* tmax, const int* targ, int 
 // table walk and the step-by-step fallback never run in the same CTA, so they
 // share the region.
 __host__ __device__ constexpr size_t mk_table_bytes() {
-  return static_cast<size_t>(16) * (MK_ROWCAND + MK_ROWPAIRS) * 4;  // candidates + pair values of <= 16 rows
+  // candidates and best-successor bytes of <= 16 rows
+  return static_cast<size_t>(16) * MK_ROWCAND * 5;
 }
+constexpr size_t MK_STAGE_BYTES = 32 * 1024;  // w1/w2 rows of one row's pairs staged in shared memory
 __host__ __device__ constexpr size_t mk_stepwise_bytes() { return MK_MAXCAND * 4 + MK_MAXRANK * 4; }
 
 // Exact step-by-step chain over the per-previous-token band (and over the
@@ -214,52 +217,70 @@ __device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, in
   }
 }
 
-// Band candidates of one row: every token whose bf16 base logit is >= thr,
-// found through the per-128-token tile maxima, sorted by token id (so two CTAs
-// that scan the same row list its candidates in the same order).  Returns the
-// count, or -1 when the band holds more than MK_ROWCAND tokens or MK_MAXTILES
-// tiles.  Block-wide; ends with a barrier.
-__device__ int band_candidates(const bf16* base, const float* tmax, int n_tiles, float thr, int* tile_list,
-                               int* raw, int* out, int* n_tl, int* n_c) {
+// Band candidates of up to two rows at once (this CTA's row and the row
+// before it), from tile maxima already held in registers (tv[r][k] = tile
+// tid + k * blockDim of row r): the tiles whose maximum reaches the row's
+// threshold are listed, their 128 bf16 logits scanned (one warp per tile, all
+// tiles' loads in flight together), and each row's candidates sorted by token
+// id so that every CTA lists a row's band in the same order.  count[r] = -1
+// when the band holds more than MK_ROWCAND tokens or MK_MAXTILES tiles.
+// Block-wide; ends with a barrier.
+__device__ __forceinline__ void band_candidates2(const float (&tv)[2][MK_TPT], int nrow, const bf16* const (&base)[2],
+                                 const float (&thr)[2], int (*tile_list)[MK_MAXTILES], int (*raw)[MK_ROWCAND],
+                                 int* const (&out)[2], int* n_tl, int* n_c, int (&count)[2]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-  if (tid == 0) {
-    *n_tl = 0;
-    *n_c = 0;
+  if (tid < 2) {
+    n_tl[tid] = 0;
+    n_c[tid] = 0;
   }
   __syncthreads();
-  for (int i = tid; i < n_tiles; i += blockDim.x) {
-    if (tmax[i] >= thr) {
-      const int slot = atomicAdd(n_tl, 1);
-      if (slot < MK_MAXTILES) tile_list[slot] = i;
-    }
-  }
-  __syncthreads();
-  const int ntl = *n_tl;
-  if (ntl <= MK_MAXTILES) {
-    for (int ti = warp; ti < ntl; ti += nwarps) {
-      const int v0 = tile_list[ti] * 128 + lane * 4;
-      const uint2 rw = *reinterpret_cast<const uint2*>(base + v0);
-      const bf16* e4 = reinterpret_cast<const bf16*>(&rw);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (__bfloat162float(e4[j]) >= thr) {
-          const int slot = atomicAdd(n_c, 1);
-          if (slot < MK_ROWCAND) raw[slot] = v0 + j;
+  for (int r = 0; r < 2; ++r) {
+    if (r < nrow) {
+#pragma unroll
+      for (int k = 0; k < MK_TPT; ++k) {
+        if (tv[r][k] >= thr[r]) {
+          const int slot = atomicAdd(&n_tl[r], 1);
+          if (slot < MK_MAXTILES) tile_list[r][slot] = tid + k * blockDim.x;
         }
       }
     }
   }
   __syncthreads();
-  const int n = (ntl > MK_MAXTILES || *n_c > MK_ROWCAND) ? -1 : *n_c;
-  // rank sort (token ids of one row are distinct)
-  for (int i = tid; i < n; i += blockDim.x) {
-    const int v = raw[i];
-    int r = 0;
-    for (int j = 0; j < n; ++j) r += raw[j] < v;
-    out[r] = v;
+  const int nt0 = n_tl[0], nt1 = nrow > 1 ? n_tl[1] : 0;
+  const int use0 = nt0 <= MK_MAXTILES ? nt0 : 0, use1 = nt1 <= MK_MAXTILES ? nt1 : 0;
+  for (int ti = warp; ti < use0 + use1; ti += nwarps) {
+    const int r = ti < use0 ? 0 : 1;
+    const bf16* bp = r == 0 ? base[0] : base[1];  // selects, not a dynamically indexed local array
+    const float th = r == 0 ? thr[0] : thr[1];
+    const int v0 = tile_list[r][r == 0 ? ti : ti - use0] * 128 + lane * 4;
+    const uint2 rw = *reinterpret_cast<const uint2*>(bp + v0);
+    const bf16* e4 = reinterpret_cast<const bf16*>(&rw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (__bfloat162float(e4[j]) >= th) {
+        const int slot = atomicAdd(&n_c[r], 1);
+        if (slot < MK_ROWCAND) raw[r][slot] = v0 + j;
+      }
+    }
   }
   __syncthreads();
-  return n;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int ntl = r == 0 ? nt0 : nt1;
+    count[r] = r >= nrow ? 0 : ((ntl > MK_MAXTILES || n_c[r] > MK_ROWCAND) ? -1 : n_c[r]);
+  }
+  // rank sort of both lists (token ids of one row are distinct)
+  const int c0 = count[0] > 0 ? count[0] : 0, c1 = count[1] > 0 ? count[1] : 0;
+  for (int i = tid; i < c0 + c1; i += blockDim.x) {
+    const int r = i < c0 ? 0 : 1;
+    const int n = r == 0 ? c0 : c1;
+    const int v = raw[r][r == 0 ? i : i - c0];
+    int rk = 0;
+    for (int j = 0; j < n; ++j) rk += raw[r][j] < v;
+    (r == 0 ? out[0] : out[1])[rk] = v;
+  }
+  __syncthreads();
 }
 
 // One launch, one CTA per (request, step) row t.
@@ -277,16 +298,19 @@ __device__ int band_candidates(const bf16* base, const float* tmax, int n_tiles,
 // (first maximum by token id, as torch.argmax).  A row whose band overflowed
 // sends the request to the exact step-by-step fallback.  Then the accept check.
 __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args a, int* cand_count, int* cand_all,
-                                                            float* pair_all, int* done) {
+                                                            uint8_t* best_all, int* done) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ float red_v[32];
   __shared__ int red_i[32];
-  __shared__ int tile_list[MK_MAXTILES];
-  __shared__ int raw[MK_ROWCAND], cur[MK_ROWCAND], prv[MK_ROWCAND];
-  __shared__ int n_tl, n_c;
+  __shared__ int tile_list[2][MK_MAXTILES];
+  __shared__ int raw[2][MK_ROWCAND], cur[MK_ROWCAND], prv[MK_ROWCAND];
+  __shared__ int n_tl[2], n_c[2];
+  __shared__ float red2[2][32];
+  __shared__ float pair_vals[MK_ROWPAIRS];
   __shared__ int cnt[16];
   __shared__ int last_row, use_table;
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // logits and tile maxima come from the previous kernel
   const long long row = blockIdx.x;
   const int P = a.block;
   const int b = static_cast<int>(row / P);
@@ -297,15 +321,59 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
   const bf16* base_all = reinterpret_cast<const bf16*>(a.base);
   const float* tmax = a.tile_max + row * n_tiles;
   const int* targ = a.tile_arg + row * n_tiles;
-  float m;
-  int arg;
-  row_max(tmax, targ, n_tiles, red_v, red_i, m, arg);
+  // this row's tile maxima (and the previous row's, for the Markov pairs) in
+  // registers, every load in flight at once
+  const int nrow = (a.w1 != nullptr && t > 0) ? 2 : 1;
+  float tv[2][MK_TPT];
+#pragma unroll
+  for (int k = 0; k < MK_TPT; ++k) {
+    const int i = tid + k * blockDim.x;
+    tv[0][k] = i < n_tiles ? tmax[i] : -INFINITY;
+    tv[1][k] = (nrow > 1 && i < n_tiles) ? tmax[i - n_tiles] : -INFINITY;
+  }
   if (a.w1 == nullptr) {
-    if (tid == 0) a.tokens[row] = arg;
+    // plain argmax: (maximum, lowest index) over the tiles
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int k = 0; k < MK_TPT; ++k) {
+      const int i = tid + k * blockDim.x;
+      if (i < n_tiles) {
+        const int ti = targ[i];
+        if (better(tv[0][k], ti, bv, bi)) {
+          bv = tv[0][k];
+          bi = ti;
+        }
+      }
+    }
+    block_argmax(bv, bi, red_v, red_i);
+    if (tid == 0) a.tokens[row] = bi;
   } else {
+    // row maxima of both rows
+    float mx[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float v = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < MK_TPT; ++k) v = fmaxf(v, tv[r][k]);
+      mx[r] = warp_max(v);
+      if (lane == 0) red2[r][warp] = mx[r];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float v = -INFINITY;
+      for (int w = 0; w < nwarps; ++w) v = fmaxf(v, red2[r][w]);
+      mx[r] = v;
+    }
     const float beta = (*a.w1_row_bound) * (*a.w2_row_bound);
-    const bf16* base = base_all + row * a.vocab;
-    const int nc = band_candidates(base, tmax, n_tiles, band_threshold(m, beta), tile_list, raw, cur, &n_tl, &n_c);
+    const bf16* const base2[2] = {base_all + row * a.vocab, base_all + (row - (nrow > 1 ? 1 : 0)) * a.vocab};
+    const float thr2[2] = {band_threshold(mx[0], beta), band_threshold(mx[1], beta)};
+    int* const out2[2] = {cur, prv};
+    int counts[2];
+    band_candidates2(tv, nrow, base2, thr2, tile_list, raw, out2, n_tl, n_c, counts);
+    const bf16* base = base2[0];
+    const int nc = counts[0];
     int np = 1;
     if (t == 0) {
       if (tid == 0) {
@@ -317,12 +385,7 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
         prv[0] = static_cast<int>(an);
       }
     } else {
-      const float* ptmax = tmax - n_tiles;
-      float pm;
-      int parg;
-      row_max(ptmax, targ - n_tiles, n_tiles, red_v, red_i, pm, parg);
-      np = band_candidates(base - a.vocab, ptmax, n_tiles, band_threshold(pm, beta), tile_list, raw, prv, &n_tl,
-                           &n_c);
+      np = counts[1];
     }
     __syncthreads();
     const int count = (nc < 1 || np < 1 || np * nc > MK_ROWPAIRS) ? -1 : nc;
@@ -330,8 +393,50 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
       const int R = a.rank;
       const bf16* w1 = reinterpret_cast<const bf16*>(a.w1);
       const bf16* w2 = reinterpret_cast<const bf16*>(a.w2);
-      float* pv = pair_all + row * MK_ROWPAIRS;
-      for (int q = warp; q < np * nc; q += nwarps) {
+      float* pv = pair_vals;  // [np][nc] in shared memory
+      const int vpr = R / 8;  // 16-byte vectors per w1/w2 row
+      if ((size_t)(np + nc) * R * 2 + (size_t)nc * 4 <= MK_STAGE_BYTES) {
+        // the np w1 rows and nc w2 rows (and the candidates' base logits) in
+        // shared memory with one batch of loads, then every pair's dot from there
+        uint4* ws = reinterpret_cast<uint4*>(dsm);
+        float* cb = reinterpret_cast<float*>(dsm + (size_t)(np + nc) * R * 2);
+        const int tot = (np + nc) * vpr;
+        for (int e0 = tid; e0 < tot; e0 += 4 * blockDim.x) {
+          uint4 v[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int e = e0 + k * blockDim.x;
+            if (e < tot) {
+              const int rr = e / vpr, c = e - rr * vpr;
+              const uint4* src = rr < np ? reinterpret_cast<const uint4*>(w1 + (long long)prv[rr] * R)
+                                         : reinterpret_cast<const uint4*>(w2 + (long long)cur[rr - np] * R);
+              v[k] = __ldg(src + c);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int e = e0 + k * blockDim.x;
+            if (e < tot) ws[e] = v[k];
+          }
+        }
+        for (int j = tid; j < nc; j += blockDim.x) cb[j] = __bfloat162float(base[cur[j]]);
+        __syncthreads();
+        for (int q = warp; q < np * nc; q += nwarps) {
+          const int i = q / nc, j = q - i * nc;
+          const uint4* x4 = ws + (size_t)i * vpr;
+          const uint4* y4 = ws + (size_t)(np + j) * vpr;
+          float acc = 0.0f;
+          for (int c = lane; c < vpr; c += 32) {
+            const uint4 x = x4[c], y = y4[c];
+            const bf16* xe = reinterpret_cast<const bf16*>(&x);
+            const bf16* ye = reinterpret_cast<const bf16*>(&y);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc += __bfloat162float(xe[e]) * __bfloat162float(ye[e]);
+          }
+          acc = warp_sum(acc);
+          if (lane == 0) pv[q] = bf16_round(cb[j] + bf16_round(acc));
+        }
+      } else for (int q = warp; q < np * nc; q += nwarps) {
         const int i = q / nc, j = q - i * nc;
         const long long pt = prv[i], ct = cur[j];
         const float bv = __bfloat162float(base[ct]);
@@ -348,6 +453,22 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
         if (lane == 0) pv[q] = bf16_round(bv + bf16_round(acc));
       }
       for (int j = tid; j < nc; j += blockDim.x) cand_all[row * MK_ROWCAND + j] = cur[j];
+      __syncthreads();
+      // for every possible previous candidate i, this step's winner (first
+      // maximum by token id, as torch.argmax): one byte per i
+      for (int i = tid; i < np; i += blockDim.x) {
+        float best = -INFINITY;
+        int best_tok = 0x7fffffff, best_j = 0;
+        for (int j = 0; j < nc; ++j) {
+          const float v = pv[i * nc + j];
+          if (better(v, cur[j], best, best_tok)) {
+            best = v;
+            best_tok = cur[j];
+            best_j = j;
+          }
+        }
+        best_all[row * MK_ROWCAND + i] = static_cast<uint8_t>(best_j);
+      }
     }
     if (tid == 0) cand_count[row] = count;
   }
@@ -362,64 +483,64 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
   __syncthreads();
   if (!last_row) return;
 
+  const long long r0 = (long long)b * P;
   if (a.w1 != nullptr) {
-    if (tid < P) cnt[tid] = __ldcg(&cand_count[(long long)b * P + tid]);
+    if (tid < P) cnt[tid] = __ldcg(&cand_count[r0 + tid]);
     __syncthreads();
-    if (tid == 0) {
-      int ok = 1;
-      for (int s = 0; s < P; ++s) ok &= cnt[s] >= 1;
-      use_table = ok;
-    }
-    __syncthreads();
-    if (!use_table) {
+    bool ok = true;
+    for (int s2 = 0; s2 < P; ++s2) ok &= cnt[s2] >= 1;
+    if (!ok) {
       float* latent = reinterpret_cast<float*>(dsm);
       int* cand = reinterpret_cast<int*>(dsm + MK_MAXRANK * 4);
-      stepwise_chain(a, b, latent, cand, &n_c, tile_list, &n_tl, red_v, red_i);
+      stepwise_chain(a, b, latent, cand, &n_c[0], tile_list[0], &n_tl[0], red_v, red_i);
+      __syncthreads();
+      if (tid < P) red_i[tid] = static_cast<int>(__ldcg(&a.tokens[r0 + tid]));
     } else {
-      int* tok = reinterpret_cast<int*>(dsm);                                  // [P][MK_ROWCAND]
-      float* pv = reinterpret_cast<float*>(dsm + (size_t)P * MK_ROWCAND * 4);  // [P][MK_ROWPAIRS]
-      const long long r0 = (long long)b * P;
-      for (int e = tid; e < P * MK_ROWCAND; e += blockDim.x) {
-        const int s = e / MK_ROWCAND, j = e - s * MK_ROWCAND;
-        if (j < cnt[s]) tok[e] = __ldcg(&cand_all[(r0 + s) * MK_ROWCAND + j]);
-      }
-      for (int e = tid; e < P * MK_ROWPAIRS; e += blockDim.x) {
-        const int s = e / MK_ROWPAIRS, q = e - s * MK_ROWPAIRS;
-        const int np_s = s == 0 ? 1 : cnt[s - 1];
-        if (q < np_s * cnt[s]) pv[e] = __ldcg(&pair_all[(r0 + s) * MK_ROWPAIRS + q]);
+      int* tok = reinterpret_cast<int*>(dsm);                               // [P][MK_ROWCAND]
+      uint8_t* bestj = dsm + (size_t)P * MK_ROWCAND * 4;                    // [P][MK_ROWCAND]
+      // every row's candidate tokens and best-successor bytes, all loads in flight together
+      for (int e0 = tid; e0 < P * MK_ROWCAND; e0 += 4 * blockDim.x) {
+        int v[4];
+        uint8_t bj[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int e = e0 + k * blockDim.x;
+          const int s2 = e / MK_ROWCAND, i = e - s2 * MK_ROWCAND;
+          const bool in = e < P * MK_ROWCAND;
+          v[k] = (in && i < cnt[s2]) ? __ldcg(&cand_all[(r0 + s2) * MK_ROWCAND + i]) : 0;
+          bj[k] = (in && i < (s2 == 0 ? 1 : cnt[s2 - 1])) ? __ldcg(&best_all[(r0 + s2) * MK_ROWCAND + i]) : 0;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int e = e0 + k * blockDim.x;
+          if (e < P * MK_ROWCAND) {
+            tok[e] = v[k];
+            bestj[e] = bj[k];
+          }
+        }
       }
       __syncthreads();
       if (tid == 0) {
         int pos = 0;  // index of the previous step's token in its sorted candidate list (anchor: 0)
-        for (int s = 0; s < P; ++s) {
-          const int n_s = cnt[s];
-          float best = -INFINITY;
-          int best_tok = 0x7fffffff, best_j = 0;
-          for (int j = 0; j < n_s; ++j) {
-            const float v = pv[s * MK_ROWPAIRS + pos * n_s + j];
-            const int tk = tok[s * MK_ROWCAND + j];
-            if (better(v, tk, best, best_tok)) {
-              best = v;
-              best_tok = tk;
-              best_j = j;
-            }
-          }
-          red_i[s] = best_tok;
-          pos = best_j;
+        for (int s2 = 0; s2 < P; ++s2) {
+          const int j = bestj[s2 * MK_ROWCAND + pos];
+          red_i[s2] = tok[s2 * MK_ROWCAND + j];
+          pos = j;
         }
       }
       __syncthreads();
       if (tid < P) a.tokens[r0 + tid] = red_i[tid];
     }
+  } else {
+    // no Markov head: the row CTAs wrote the tokens
+    if (tid < P) red_i[tid] = static_cast<int>(__ldcg(&a.tokens[r0 + tid]));
   }
   __syncthreads();
-  if (a.target != nullptr && a.accept_out != nullptr && tid == 0) {
-    long long acc = 0;
-    for (int s = 0; s < P; ++s) {
-      if (a.target[(long long)b * a.target_ld + s] != __ldcg(&a.tokens[(long long)b * P + s])) break;
-      ++acc;
-    }
-    a.accept_out[b] = acc;
+  if (a.target != nullptr && a.accept_out != nullptr && tid < 32) {
+    // longest prefix on which the target agrees: one ballot over the block
+    const bool match = tid < P && a.target[(long long)b * a.target_ld + tid] == static_cast<long long>(red_i[tid]);
+    const unsigned m = __ballot_sync(0xffffffffu, match);
+    if (tid == 0) a.accept_out[b] = __ffs(~m) - 1;
   }
 }
 
@@ -466,9 +587,9 @@ extern "C" size_t ls_markov_workspace_bytes(int batch, int block) {
   if (batch <= 0 || block <= 0) return 0;
   const size_t rows = static_cast<size_t>(batch) * block;
   // [256 pad] [done counters (batch)] [candidate counts (rows)]
-  // [candidates (rows x MK_ROWCAND)] [pair values (rows x MK_ROWPAIRS)]
+  // [candidates (rows x MK_ROWCAND int32)] [best-successor bytes (rows x MK_ROWCAND)]
   return 256 + (static_cast<size_t>(batch) * 4 + 255) / 256 * 256 + (rows * 4 + 255) / 256 * 256 +
-         rows * (MK_ROWCAND + MK_ROWPAIRS) * 4;
+         rows * MK_ROWCAND * 5;
 }
 
 extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes) {
@@ -476,8 +597,9 @@ extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* wor
       a->tokens == nullptr)
     return set_error(LS_ERR_INVALID, "ls_markov_argmax: null pointer argument");
   if (a->batch <= 0) return LS_OK;
-  if (a->vocab <= 0 || a->vocab % 128 || a->block < 1 || a->block > 16)
-    return set_error(LS_ERR_UNSUPPORTED, "ls_markov_argmax: vocab must be a positive multiple of 128, block <= 16");
+  if (a->vocab <= 0 || a->vocab % 128 || a->vocab > MK_TPT * MK_THREADS * 128 || a->block < 1 || a->block > 16)
+    return set_error(LS_ERR_UNSUPPORTED,
+                     "ls_markov_argmax: vocab must be a positive multiple of 128 up to 262144, block <= 16");
   if (a->w1 != nullptr && (a->w2 == nullptr || a->w1_row_bound == nullptr || a->w2_row_bound == nullptr ||
                            a->rank < 64 || a->rank > MK_MAXRANK || a->rank % 64))
     return set_error(LS_ERR_INVALID,
@@ -494,14 +616,19 @@ extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* wor
   int* counts = reinterpret_cast<int*>(w);
   w += (rows * 4 + 255) / 256 * 256;
   int* cand = reinterpret_cast<int*>(w);
-  float* pairs = reinterpret_cast<float*>(w + rows * MK_ROWCAND * 4);
+  uint8_t* best = w + rows * MK_ROWCAND * 4;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // within the default 48 KiB dynamic shared memory limit: no attribute needed
-  static_assert(mk_table_bytes() <= 48 * 1024 && mk_stepwise_bytes() <= 48 * 1024, "Markov shared memory");
-  const size_t dsmem = a->w1 == nullptr ? 0 : (mk_table_bytes() > mk_stepwise_bytes() ? mk_table_bytes()
-                                                                                         : mk_stepwise_bytes());
-  markov_kernel<<<static_cast<unsigned>(rows), MK_THREADS, dsmem, st>>>(*a, counts, cand, pairs, done);
-  cudaError_t e = cudaGetLastError();
+  static_assert(mk_table_bytes() <= 36 * 1024 && mk_stepwise_bytes() <= 36 * 1024 && MK_STAGE_BYTES <= 36 * 1024,
+                "Markov shared memory (with about 11 KiB of static shared memory, under the 48 KiB default)");
+  size_t dsmem = 0;
+  if (a->w1 != nullptr) {
+    dsmem = mk_table_bytes();
+    if (mk_stepwise_bytes() > dsmem) dsmem = mk_stepwise_bytes();
+    if (MK_STAGE_BYTES > dsmem) dsmem = MK_STAGE_BYTES;
+  }
+  cudaError_t e = launch_pdl(markov_kernel, dim3(static_cast<unsigned>(rows)), dim3(MK_THREADS), dsmem, st, *a, counts,
+                             cand, best, done);
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_markov_argmax: launch", e);
 }
 
@@ -520,7 +647,7 @@ namespace ls {
 constexpr int MK_STATIC_MAX_DEVICES = 64;
 constexpr size_t MK_STATIC_BYTES =
     256 + 2 * ((static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * 4 + 255) / 256 * 256) +
-    static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * (MK_ROWCAND + MK_ROWPAIRS) * 4;  // 1.5 MiB + 8.25 KiB
+    static_cast<size_t>(LS_MARKOV_STATIC_MAX_ROWS) * MK_ROWCAND * 5;  // 648.25 KiB
 
 static __device__ __align__(256) uint8_t mk_static_scratch[MK_STATIC_BYTES];
 
