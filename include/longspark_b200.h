@@ -238,12 +238,18 @@ LS_API int ls_draft_attention(void* stream, const ls_attention_args* a, void* wo
 
 /* RMSNorm over rows of length n.  mode 0: SpecForge/HF rounding
  * bf16(w * bf16(x*rstd)) (SF draftfreekv.py:1518-1530); mode 1: F.rms_norm
- * rounding bf16(x*rstd*w) (target final norm, SF draftfreekv.py:3607-3647). */
+ * rounding bf16(x*rstd*w) (target final norm, SF draftfreekv.py:3607-3647).
+ * When w2 != NULL a second norm of the same mode follows in the same launch:
+ * out2 = RMSNorm(out; w2) (two consecutive norms, e.g. the shifted-input norm
+ * and the first decoder layer's input norm, SF draftfreekv.py:1737, 2299). */
 LS_API int ls_rmsnorm(void* stream, const void* x, int x_ld, const void* w, void* out, int out_ld, int rows,
-               int n, float eps, int mode);
+               int n, float eps, int mode, const void* w2, void* out2, int out2_ld);
 
 /* ParallelShiftedInput input rows (SF draftfreekv.py:1692-1739):
  * out[b*block + i] = [bf16(embed[tok_i] + pos_emb[i]) | latest[b]],
+ * where, when latest_norm_w != NULL, latest[b] is first normalised in the same
+ * launch (mode-0 RMSNorm with latest_norm_w, norm_eps: the state encoder's
+ * output norm, SF draftfreekv.py:1540), so `latest` is the encoder output;
  * tok_0 = anchors[b], tok_i = mask_token_id for i > 0.  out is [batch*block, 2*hidden].
  * When positions != NULL also writes the RoPE positions of the block rows,
  * positions[b*block + i] = seq_lens[b] + i (SF draftfreekv.py:3259-3263), and
@@ -252,8 +258,8 @@ LS_API int ls_rmsnorm(void* stream, const void* x, int x_ld, const void* w, void
  * (SF draftfreekv.py:1996-2007). */
 LS_API int ls_shifted_input(void* stream, const long long* anchors, const int* seq_lens, int* positions,
                             const float* inv_freq, float* rope_table, const void* embed, const void* pos_emb,
-                            const void* latest, void* out, int batch, int block, int hidden, int vocab,
-                            int mask_token_id, int* status);
+                            const void* latest, const void* latest_norm_w, float norm_eps, void* out,
+                            int batch, int block, int hidden, int vocab, int mask_token_id, int* status);
 
 /* Gather rows: out[b] = src[idx[b]] (row_bytes each, 16-byte multiples);
  * indices outside [0, src_rows) are recorded in *status and the row is zeroed. */

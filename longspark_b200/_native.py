@@ -71,8 +71,8 @@ SIGNATURES = {
                                 i32, i32, i32, vp]),
     "ls_attention_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
     "ls_draft_attention": (i32, [vp, C.POINTER(AttentionArgs), vp, sz]),
-    "ls_rmsnorm": (i32, [vp, vp, i32, vp, vp, i32, i32, i32, f32, i32]),
-    "ls_shifted_input": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "ls_rmsnorm": (i32, [vp, vp, i32, vp, vp, i32, i32, i32, f32, i32, vp, vp, i32]),
+    "ls_shifted_input": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, f32, vp, i32, i32, i32, i32, i32, vp]),
     "ls_gather_rows": (i32, [vp, vp, i64, vp, vp, i32, i64, vp]),
     "ls_markov_workspace_bytes": (sz, [i32, i32]),
     "ls_markov_argmax": (i32, [vp, C.POINTER(MarkovArgs), vp, sz]),

@@ -145,7 +145,7 @@ class DraftEngine:
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.buf = dict(
             enc_in=torch.zeros(B, s.tap_layers * H, **bf), t=torch.zeros(B, H, **bf), u=torch.zeros(B, H, **bf),
-            latest=torch.zeros(B, H, **bf), xsh=torch.zeros(M, 2 * H, **bf), f1=torch.zeros(M, H, **bf),
+            xsh=torch.zeros(M, 2 * H, **bf), f1=torch.zeros(M, H, **bf),
             g=torch.zeros(M, H, **bf), h=torch.zeros(M, H, **bf), xn=torch.zeros(M, H, **bf),
             qkv=torch.zeros(M, (Hq + 2 * Hkv) * 128, **bf), attn=torch.zeros(M, Hq * 128, **bf),
             act=torch.zeros(M, I, **bf), logits=torch.zeros(M, V, **bf),
@@ -206,17 +206,18 @@ class DraftEngine:
             ops.gather_rows(p.hidden.view(p.hidden.shape[0], -1), slots, enc_in, rows=B, status=st)
         ops.gemm(enc_in, w.enc_w1, b["t"], workspace=ws, epilogue=N.EPI_SILU, rows=B, status=st)
         ops.gemm(b["t"], w.enc_w2, b["u"], workspace=ws, rows=B, status=st)
-        ops.rmsnorm(b["u"], w.enc_norm, b["latest"], s.rms_eps, mode=0, rows=B)
-        # shifted input
-        ops.shifted_input(anchors, seq_lens, b["positions"], w.embed, w.pos_emb, b["latest"], b["xsh"],
+        # shifted input (the encoder's output RMSNorm is applied inside)
+        ops.shifted_input(anchors, seq_lens, b["positions"], w.embed, w.pos_emb, b["u"], b["xsh"],
                           block=P, mask_token_id=s.mask_token_id, status=st, inv_freq=w.inv_freq,
-                          rope_table=b["rope"], batch=B)
+                          rope_table=b["rope"], batch=B, latest_norm_w=w.enc_norm, norm_eps=s.rms_eps)
         ops.gemm(b["xsh"], w.sh_w1, b["f1"], workspace=ws, epilogue=N.EPI_SILU, rows=M, status=st)
         ops.gemm(b["f1"], w.sh_w2, b["g"], workspace=ws, rows=M, status=st)
-        ops.rmsnorm(b["g"], w.sh_norm, b["h"], s.rms_eps, mode=0, rows=M)
+        # shifted-input norm and the first layer's input norm in one launch
+        ops.rmsnorm(b["g"], w.sh_norm, b["h"], s.rms_eps, mode=0, rows=M, w2=w.layers[0]["in_norm"], out2=b["xn"])
         for j, L in enumerate(w.layers):
             v = s.view_layer(j)
-            ops.rmsnorm(b["h"], L["in_norm"], b["xn"], s.rms_eps, mode=0, rows=M)
+            if j > 0:
+                ops.rmsnorm(b["h"], L["in_norm"], b["xn"], s.rms_eps, mode=0, rows=M)
             ops.gemm(b["xn"], L["qkv"], b["qkv"], workspace=ws, epilogue=N.EPI_QKV, rows=M, q_heads=Hq,
                      kv_heads=Hkv, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"], norm_eps=s.rms_eps,
                      positions=b["positions"], inv_freq=w.inv_freq, rope_table=b["rope"], status=st)

@@ -89,22 +89,25 @@ def gemm_workspace_bytes(rows, k, n_out):
     return int(N.lib().ls_gemm_workspace_bytes(rows, k, n_out))
 
 
-def rmsnorm(x, w, out, eps, *, mode=0, rows=None):
-    """mode 0: SpecForge RMSNorm rounding; mode 1: ``F.rms_norm`` rounding."""
+def rmsnorm(x, w, out, eps, *, mode=0, rows=None, w2=None, out2=None):
+    """mode 0: SpecForge RMSNorm rounding; mode 1: ``F.rms_norm`` rounding.
+    With ``w2``/``out2`` a second norm of ``out`` follows in the same launch."""
     _require_cuda(x, w, out)
     rows = x.shape[0] if rows is None else rows
     N.call("ls_rmsnorm", _stream(x.device), _p(x), x.stride(0), _p(w), _p(out), out.stride(0), rows,
-           x.shape[-1], float(eps), int(mode))
+           x.shape[-1], float(eps), int(mode), _p(w2), _p(out2), 0 if out2 is None else out2.stride(0))
     return out
 
 
 def shifted_input(anchors, seq_lens, positions, embed, pos_emb, latest, out, *, block, mask_token_id, status=None,
-                  inv_freq=None, rope_table=None, batch=None):
+                  inv_freq=None, rope_table=None, batch=None, latest_norm_w=None, norm_eps=1e-6):
+    """``latest_norm_w``: ``latest`` is the state encoder's output before its
+    RMSNorm, which is applied here."""
     _require_cuda(anchors, embed, pos_emb, latest, out)
     batch = anchors.shape[0] if batch is None else batch
     N.call("ls_shifted_input", _stream(out.device), _p(anchors), _p(seq_lens), _p(positions), _p(inv_freq),
-           _p(rope_table), _p(embed), _p(pos_emb), _p(latest), _p(out), batch, block, embed.shape[1],
-           embed.shape[0], mask_token_id, _p(status))
+           _p(rope_table), _p(embed), _p(pos_emb), _p(latest), _p(latest_norm_w), float(norm_eps), _p(out), batch,
+           block, embed.shape[1], embed.shape[0], mask_token_id, _p(status))
     return out
 
 
