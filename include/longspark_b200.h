@@ -227,8 +227,9 @@ typedef struct ls_attention_args {
 /* One launch: a cluster of 8 CTAs per (request, KV head) merges its partial
  * softmax states through distributed shared memory, so no workspace is needed
  * (ls_attention_workspace_bytes returns 0; workspace may be NULL).  Launched
- * with programmatic dependent launch: window and summary rows are staged
- * before the kernel waits for the preceding kernel of the stream. */
+ * with programmatic dependent launch: the window rows and the summary keys are
+ * staged before the kernel waits for the preceding kernel of the stream, the
+ * summary values (which a view refresh just before may write) after it. */
 LS_API size_t ls_attention_workspace_bytes(int batch, int q_heads, int kv_heads, int window, int slots_per_head);
 LS_API int ls_draft_attention(void* stream, const ls_attention_args* a, void* workspace, size_t workspace_bytes);
 

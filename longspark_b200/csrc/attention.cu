@@ -24,9 +24,11 @@
 // maximum, the weighted sum rounded to bf16 and normalised, then the three
 // sources are merged by log-sum-exp.  No global partials, one launch.
 //
-// Window and summary keys/values do not depend on the QKV projection, so they
-// are staged into shared memory (cp.async) before griddepcontrol.wait: with
-// programmatic dependent launch the loads overlap the tail of the projection.
+// The window keys/values and the summary keys (learned queries) are written by
+// no kernel of the pass, so they are staged into shared memory (cp.async)
+// before griddepcontrol.wait: with programmatic dependent launch the loads
+// overlap the tail of the preceding kernel.  The summary values come from the
+// view refresh, which may be that preceding kernel: they are staged after it.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -80,13 +82,6 @@ __device__ __forceinline__ void load_q_tile(bf16 (*qs)[AT_PITCH], const bf16* qk
   }
 }
 
-// exp(x) through the SFU's base-2 exponential (a few ulp; the probabilities it
-// feeds are rounded to bf16).  exp(-inf) = 0.
-__device__ __forceinline__ float fast_exp(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
-  return y;
-}
 
 __device__ __forceinline__ void load_q_frags(uint32_t qf[8][4], const bf16 (*qs)[AT_PITCH]) {
   const int lane = threadIdx.x & 31;
@@ -249,8 +244,10 @@ __device__ __forceinline__ void stage_window(const AttnParams& p, bf16 (*ks)[AT_
 // Stage summary slots [s0, s0 + n) of query head h (keys: learned queries,
 // values: the bf16 summary copy, or the fp32 state rounded here) into a
 // (K, V) chunk buffer: this warp writes buffer rows [rb, re) (zeros past n).
+// The keys are weights; the values may be written by the kernel just before
+// this one (the view refresh), so they are staged after the dependency wait.
 __device__ __forceinline__ void stage_summary(const AttnParams& p, bf16 (*ks)[AT_PITCH], bf16 (*vs)[AT_PITCH], int h,
-                                              int slot, int s0, int n, int rb, int re) {
+                                              int slot, int s0, int n, int rb, int re, bool keys, bool values) {
   const ls_attention_args& a = p.a;
   const int lane = threadIdx.x & 31;
   const bf16* kq = reinterpret_cast<const bf16*>(a.learned_query) + ((long long)h * a.slots_per_head + s0) * 128;
@@ -263,7 +260,8 @@ __device__ __forceinline__ void stage_summary(const AttnParams& p, bf16 (*ks)[AT
   for (int i = lane + rb * 16; i < re * 16; i += 32) {
     const int r = i >> 4, col = (i & 15) << 3;
     if (r < n) {
-      cp_async16(&ks[r][col], kq + (long long)r * 128 + col);
+      if (keys) cp_async16(&ks[r][col], kq + (long long)r * 128 + col);
+      if (!values) continue;
       if (vb != nullptr) {
         cp_async16(&vs[r][col], vb + (long long)r * 128 + col);
       } else {
@@ -277,8 +275,8 @@ __device__ __forceinline__ void stage_summary(const AttnParams& p, bf16 (*ks)[AT
         *reinterpret_cast<uint4*>(&vs[r][col]) = pk;
       }
     } else {
-      *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
+      if (keys) *reinterpret_cast<uint4*>(&ks[r][col]) = make_uint4(0, 0, 0, 0);
+      if (values) *reinterpret_cast<uint4*>(&vs[r][col]) = make_uint4(0, 0, 0, 0);
     }
   }
 }
@@ -396,13 +394,19 @@ __global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams
     if (s_sub > 0) {
       bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + hw * 2 * p.sc;
       stage_summary(p, ks, ks + p.sc, h, slot, s_0, s_n < p.sc ? s_n : p.sc, part * (p.sc / R),
-                    (part + 1) * (p.sc / R));
+                    (part + 1) * (p.sc / R), true, false);
       cp_async_commit();
     }
   }
 
   // ---- the projection's outputs: query tiles, local keys/values ----
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (is_sum && s_sub > 0) {
+    bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + hw * 2 * p.sc;
+    stage_summary(p, ks, ks + p.sc, h, slot, s_0, s_n < p.sc ? s_n : p.sc, part * (p.sc / R),
+                  (part + 1) * (p.sc / R), false, true);
+    cp_async_commit();
+  }
   if (part == 0) load_q_tile(qs, qkv, row_ld, b * P, P, h);
   if (!is_win && !is_sum) {
     for (int i = threadIdx.x; i < 32 * 16; i += blockDim.x) {
@@ -453,7 +457,8 @@ __global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams
       __syncthreads();  // every warp is done with the buffers
       if (i + 1 < s_sub) {
         const int n2 = s_n - (i + 1) * p.sc < p.sc ? s_n - (i + 1) * p.sc : p.sc;
-        stage_summary(p, ks, ks + p.sc, h, slot, s_0 + (i + 1) * p.sc, n2, part * half, (part + 1) * half);
+        stage_summary(p, ks, ks + p.sc, h, slot, s_0 + (i + 1) * p.sc, n2, part * half, (part + 1) * half, true,
+                      true);
         cp_async_commit();
       }
     }

@@ -99,13 +99,17 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
 
   const int c = a.commit_lens[b];
   const int len = a.seq_lens[b];
+  // Every exit path waits for the preceding kernel first, so this grid's
+  // completion implies that kernel's (the next kernel relies on it).
   if (c < 1 || c > a.max_commit || c > RF_MAXROWS || len < c) {
     if (tid == 0) record_status(a.status, LS_DEV_BAD_INDEX);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     return;
   }
   const int slot = a.slots[b];
   if (slot < 0 || slot >= a.capacity) {
     if (tid == 0) record_status(a.status, LS_DEV_BAD_INDEX);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     return;
   }
   // Issue the state reads first: each warp's 16 slots (512 B each, float4 per
@@ -115,10 +119,11 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
   float* lse = a.state_lse + st_base * a.slots_per_head + s0;
   const bool warp_active = warp * 16 < nslots;
   float4 o[16];
+  float prior_lse = 0.0f;  // parked in shared memory once it has arrived (after the copies are issued)
   if (warp_active) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) o[i] = __ldcs(reinterpret_cast<const float4*>(out + (long long)(warp * 16 + i) * 128) + lane);
-    if (lane < 16) sm.prior[warp * 16 + lane] = lse[warp * 16 + lane];
+    if (lane < 16) prior_lse = lse[warp * 16 + lane];
   }
 
   // Queries of this head/chunk -> smem (cp.async 16 B pieces).
@@ -130,32 +135,49 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
   }
   cp_async_commit();
 
-  // New K rows (bf16, for the MMA) and V rows (fp32) of this KV head.
+  // New K rows (bf16, for the MMA) and V rows of this KV head: the pool rows
+  // of the committed positions first (one page-table read per row, in
+  // parallel), then every K/V copy in flight at once.
   __shared__ int bad_page;
+  __shared__ long long prow_s[RF_MAXROWS];
   if (tid == 0) bad_page = 0;
   __syncthreads();
-  bool ok = true;
+  if (tid < c) {
+    bool ok = true;
+    const long long prow =
+        paged_row(a.page_table, a.table_stride, a.ring_pages, b, len - c + tid, a.pool_pages, a.status, &ok);
+    prow_s[tid] = prow;
+    if (!ok) bad_page = 1;
+  }
+  __syncthreads();
+  if (bad_page) {  // a bad page id was recorded; leave the state untouched
+    cp_async_wait_all();
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // completes only after the preceding kernel
+    return;
+  }
+  // Everything above reads only the previous rounds' state, the learned
+  // queries and the page table; the committed K/V rows may come from the
+  // kernel just before this one (the window scatter of an update).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const bf16* kvk = reinterpret_cast<const bf16*>(a.kv_k);
   const bf16* kvv = reinterpret_cast<const bf16*>(a.kv_v);
-  for (int i = tid; i < RF_MAXROWS * 16; i += 128) {
+#pragma unroll
+  for (int k4 = 0; k4 < RF_MAXROWS * 16 / 128; ++k4) {
+    const int i = tid + k4 * 128;
     const int r = i >> 4, col = (i & 15) << 3;
-    uint4 kq = make_uint4(0, 0, 0, 0), vq = make_uint4(0, 0, 0, 0);
     if (r < c) {
-      const long long prow = paged_row(a.page_table, a.table_stride, a.ring_pages, b, len - c + r, a.pool_pages,
-                                       a.status, &ok);
-      if (ok) {
-        const long long off = (((long long)layer * a.pool_pages * 16 + prow) * a.kv_heads + hk) * 128 + col;
-        kq = *reinterpret_cast<const uint4*>(kvk + off);
-        vq = *reinterpret_cast<const uint4*>(kvv + off);
-      }
+      const long long off = (((long long)layer * a.pool_pages * 16 + prow_s[r]) * a.kv_heads + hk) * 128 + col;
+      cp_async16(&sm.k[r][col], kvk + off);
+      cp_async16(&sm.v[r][col], kvv + off);
+    } else {
+      *reinterpret_cast<uint4*>(&sm.k[r][col]) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(&sm.v[r][col]) = make_uint4(0, 0, 0, 0);
     }
-    *reinterpret_cast<uint4*>(&sm.k[r][col]) = kq;
-    *reinterpret_cast<uint4*>(&sm.v[r][col]) = vq;
   }
-  if (!ok) bad_page = 1;
+  cp_async_commit();
+  if (warp_active && lane < 16) sm.prior[warp * 16 + lane] = prior_lse;
   cp_async_wait_all();
   __syncthreads();
-  if (bad_page) return;  // a bad page id was recorded; leave the state untouched
 
   if (warp_active) {
     float acc[4][4];
@@ -185,22 +207,22 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e)
-          if (nt * 8 + t2 + e < c) sum += expf(sv[nt * 2 + e] - mx);
+          if (nt * 8 + t2 + e < c) sum += fast_exp(sv[nt * 2 + e] - mx);
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      const float delta = mx + logf(sum);
+      const float delta = mx + __logf(sum);
       const float prior = sm.prior[sl];
       const float m2 = fmaxf(prior, delta);
-      const float merged = m2 + logf(expf(prior - m2) + expf(delta - m2));
+      const float merged = m2 + __logf(fast_exp(prior - m2) + fast_exp(delta - m2));
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int r = nt * 8 + t2 + e;
-          sm.w[sl][r] = r < c ? expf(sv[nt * 2 + e] - merged) : 0.0f;
+          sm.w[sl][r] = r < c ? fast_exp(sv[nt * 2 + e] - merged) : 0.0f;
         }
       if ((lane & 3) == 0) {
-        sm.prior_w[sl] = expf(prior - merged);
+        sm.prior_w[sl] = fast_exp(prior - merged);
         sm.merged[sl] = merged;
       }
     }
@@ -209,10 +231,10 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
     // every new V row stay in registers (packed bf16), the weights of a slot
     // come as float4 broadcasts.  Rows are folded in order r = 0, 1, ...
     const int c4 = (c + 3) & ~3;  // weights beyond c are zero (masked above)
-    for (int r0 = 0; r0 < c; r0 += 16) {
-      uint2 vr[16];
+    for (int r0 = 0; r0 < c; r0 += 8) {
+      uint2 vr[8];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) vr[r] = *reinterpret_cast<const uint2*>(&sm.v[r0 + r][lane * 4]);
+      for (int r = 0; r < 8; ++r) vr[r] = *reinterpret_cast<const uint2*>(&sm.v[r0 + r][lane * 4]);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int sl = warp * 16 + i;
@@ -225,7 +247,7 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
           oi.w *= pw;
         }
 #pragma unroll
-        for (int rq = 0; rq < 16; rq += 4) {
+        for (int rq = 0; rq < 8; rq += 4) {
           if (r0 + rq < c4) {
             const float4 w4 = *reinterpret_cast<const float4*>(&sm.w[sl][r0 + rq]);
             const float ws[4] = {w4.x, w4.y, w4.z, w4.w};
@@ -449,9 +471,10 @@ extern "C" int ls_refresh_views(void* stream, const ls_refresh_args* a) {
   if (rc) return rc;
   const long long chunks = (a->slots_per_head + RF_SLOTS - 1) / RF_SLOTS;
   const long long grid = (long long)a->batch * a->tap_layers * a->q_heads * chunks;
-  refresh_views_kernel<<<static_cast<unsigned>(grid), 128, sizeof(RefreshSmem),
-                         reinterpret_cast<cudaStream_t>(stream)>>>(*a);
-  cudaError_t e = cudaGetLastError();
+  // Programmatic dependent launch: the state, query and page-table reads
+  // overlap the preceding kernel; the kernel waits for it before the K/V rows.
+  cudaError_t e = launch_pdl(refresh_views_kernel, dim3(static_cast<unsigned>(grid)), dim3(128), sizeof(RefreshSmem),
+                             reinterpret_cast<cudaStream_t>(stream), *a);
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_refresh_views: launch", e);
 }
 

@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
   __shared__ float red2[2][32];
   __shared__ float pair_vals[MK_ROWPAIRS];
   __shared__ int cnt[16];
-  __shared__ int last_row, use_table;
+  __shared__ int last_row;
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // logits and tile maxima come from the previous kernel
   const long long row = blockIdx.x;

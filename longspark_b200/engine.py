@@ -174,6 +174,9 @@ class DraftEngine:
             pools.sync_summary_bf16()
         self.graphs = {}
         self.graph_replays = 0
+        # a full round issues the view refresh after the first layer's QKV
+        # projection, whose tail it overlaps (measured ~2 us faster than first)
+        self.refresh_after_qkv = True
 
     # ------------------------------------------------------------------ refresh
     def refresh(self, *, slots, seq_lens, commit_lens, page_table, batch=None):
@@ -186,15 +189,22 @@ class DraftEngine:
                           status=self.buf["status"], batch=batch, state_bf16=p.summary_bf16)
 
     # ------------------------------------------------------------------ drafter
-    def draft(self, *, slots, seq_lens, anchors, page_table, target=None, batch=None, slots_are_rows=False):
+    def draft(self, *, slots, seq_lens, anchors, page_table, target=None, batch=None, slots_are_rows=False,
+              commit_lens=None):
         """One parallel drafter pass: writes ``buf['tokens']`` [B, P] (and
         ``buf['accept']`` [B] when ``target`` is given) and bf16 base logits.
         ``slots_are_rows``: the caller guarantees ``slots == arange(B)``, so the
-        boundary hidden states are read in place instead of gathered."""
+        boundary hidden states are read in place instead of gathered.
+        ``commit_lens``: fold the committed rows into the summary in the same
+        pass (a full round).  With ``refresh_after_qkv`` (the default) the
+        refresh is issued after the first layer's QKV projection: nothing
+        before the attention reads the summary."""
         s, w, p, b = self.shape, self.w, self.pools, self.buf
         B = anchors.shape[0] if batch is None else batch
         P = s.block
         M = B * P
+        if commit_lens is not None and not self.refresh_after_qkv:
+            self.refresh(slots=slots, seq_lens=seq_lens, commit_lens=commit_lens, page_table=page_table, batch=B)
         H, Hq, Hkv = s.hidden, s.q_heads, s.kv_heads
         ws = self.gemm_ws
         st = b["status"]
@@ -221,6 +231,9 @@ class DraftEngine:
             ops.gemm(b["xn"], L["qkv"], b["qkv"], workspace=ws, epilogue=N.EPI_QKV, rows=M, q_heads=Hq,
                      kv_heads=Hkv, q_norm_w=L["q_norm"], k_norm_w=L["k_norm"], norm_eps=s.rms_eps,
                      positions=b["positions"], inv_freq=w.inv_freq, rope_table=b["rope"], status=st)
+            if j == 0 and commit_lens is not None and self.refresh_after_qkv:
+                self.refresh(slots=slots, seq_lens=seq_lens, commit_lens=commit_lens, page_table=page_table,
+                             batch=B)
             ops.draft_attention(qkv=b["qkv"], block=P, kv_k=p.kv_k[v], kv_v=p.kv_v[v], page_table=page_table,
                                 seq_lens=seq_lens, window=s.window, learned_query=w.learned_query[v],
                                 state_out=p.summary_out[:, v], slots=slots, out=b["attn"], workspace=self.attn_ws,
@@ -258,10 +271,10 @@ class DraftEngine:
 
     def round(self, *, slots, seq_lens, commit_lens, anchors, page_table, target=None, batch=None,
               slots_are_rows=False):
-        """Refresh then draft (one full drafting round)."""
-        self.refresh(slots=slots, seq_lens=seq_lens, commit_lens=commit_lens, page_table=page_table, batch=batch)
+        """One full drafting round: the committed rows are folded into the
+        summary and the drafter pass runs (see ``draft``)."""
         self.draft(slots=slots, seq_lens=seq_lens, anchors=anchors, page_table=page_table, target=target,
-                   batch=batch, slots_are_rows=slots_are_rows)
+                   batch=batch, slots_are_rows=slots_are_rows, commit_lens=commit_lens)
 
     # ------------------------------------------------------------------ status
     def device_status(self):
@@ -297,11 +310,9 @@ class GraphedDraft:
 
     def _run(self):
         e = self.engine
-        if self.with_refresh:
-            e.refresh(slots=self.slots, seq_lens=self.seq_lens, commit_lens=self.commit_lens,
-                      page_table=self.page_table, batch=self.batch)
         e.draft(slots=self.slots, seq_lens=self.seq_lens, anchors=self.anchors, page_table=self.page_table,
-                target=self.target, batch=self.batch, slots_are_rows=self.slots_are_rows)
+                target=self.target, batch=self.batch, slots_are_rows=self.slots_are_rows,
+                commit_lens=self.commit_lens if self.with_refresh else None)
 
     def load(self, *, slots, seq_lens, anchors, page_table, commit_lens=None, target=None):
         self.slots.copy_(slots, non_blocking=True)
