@@ -306,7 +306,7 @@ def time_dominant_kernel(eng, reps=20):
 def count_launches(eng, g):
     """Kernels of one round, counted from the native calls of an eager run."""
     from longspark_b200 import _native as N
-    counts = {"ls_draft_attention": 2, "ls_row_norm_bound": 1}
+    counts = {"ls_row_norm_bound": 1}
     seen = []
     orig = N.call
 
