@@ -25,6 +25,7 @@ import math
 from pathlib import Path
 from types import SimpleNamespace
 
+import numpy as np
 import torch
 
 from . import ops
@@ -142,6 +143,24 @@ class LongSparkDraft:
         self.graphs = {}
         self.fallbacks = 0
         self._logits = None
+        # Step path: a decode update stages its rows and metadata and launches
+        # nothing; the next propose for the same requests replays one graph
+        # (page-table gather, window scatter, drafter pass with the refresh).
+        rows = n * s.max_commit
+        self._stage_k = torch.zeros(s.tap_layers, rows, s.kv_heads, s.head_dim, dtype=torch.bfloat16, device=dev)
+        self._stage_v = torch.zeros_like(self._stage_k)
+        self._stage_h = torch.zeros(n, s.tap_layers * s.hidden, dtype=torch.bfloat16, device=dev)
+        # metadata block: slots, lengths, counts, offsets (int32 x n each), anchors (int64 x n)
+        self._meta_bytes = 4 * 4 * n + 8 * n
+        self._meta_host = torch.zeros(self._meta_bytes, dtype=torch.uint8).pin_memory()
+        hb = self._meta_host.numpy()  # numpy views of the pinned block: writes cost no torch op
+        self._meta_np = (hb[:4 * n].view(np.int32), hb[4 * n:8 * n].view(np.int32), hb[8 * n:12 * n].view(np.int32),
+                         hb[12 * n:16 * n].view(np.int32), hb[16 * n:].view(np.int64))
+        self._meta_dev = torch.zeros(self._meta_bytes, dtype=torch.uint8, device=dev)
+        self._meta_done = torch.cuda.Event()  # the last copy out of the host block has run
+        self._meta_done.record()
+        self._pending = None  # (ids, batch) of a staged, not yet applied decode update
+        self._step_graphs = {}
 
     # ------------------------------------------------------------------ state
     @property
@@ -152,11 +171,45 @@ class LongSparkDraft:
     def free_slots(self):
         return self.table.free_slots
 
+    # ------------------------------------------------------------------ staging
+    def _meta_views(self, t):
+        """(slots, lengths, counts, offsets, anchors) views of a metadata block."""
+        n = self.capacity
+        i32 = t[:16 * n].view(torch.int32)
+        return i32[:n], i32[n:2 * n], i32[2 * n:3 * n], i32[3 * n:], t[16 * n:].view(torch.int64)
+
+    def _host_meta(self):
+        """numpy views (slots, lengths, counts, offsets, anchors) of the pinned
+        host metadata block, once its previous copy has run."""
+        self._meta_done.synchronize()
+        return self._meta_np
+
+    def _push_meta(self):
+        self._meta_dev.copy_(self._meta_host, non_blocking=True)
+        self._meta_done.record()
+
+    def _flush(self):
+        """Apply a staged decode update now (window scatter + refresh)."""
+        if self._pending is None:
+            return
+        ids, B = self._pending
+        self._pending = None
+        self._push_meta()
+        slot_t, lens_t, cnt_t, off_t, _ = (v[:B] for v in self._meta_views(self._meta_dev))
+        table = self.pools.page_table.index_select(0, slot_t)
+        st = self.engine.buf["status"]
+        ops.window_scatter(keys=self._stage_k, values=self._stage_v, row_offsets=off_t, counts=cnt_t, seq_lens=lens_t,
+                           kv_k=self.pools.kv_k, kv_v=self.pools.kv_v, page_table=table,
+                           ring_pages=self.pools.ring_pages, last_hidden=self._stage_h, hidden_pool=self.pools.hidden,
+                           slots=slot_t, status=st, batch=B)
+        self.engine.refresh(slots=slot_t, seq_lens=lens_t, commit_lens=cnt_t, page_table=table, batch=B)
+
     @torch.inference_mode()
     def update(self, packets, *, prefill=False):
         meta, counts, keys, values, hidden, extra = unpack_packets(packets)
         if not meta:
             return
+        self._flush()
         dev = self.device
         if prefill:
             if "global_output" not in extra:
@@ -165,6 +218,19 @@ class LongSparkDraft:
         else:
             commit = self.table.decode(meta, counts)
         B = len(meta)
+        if not prefill:
+            # stage rows and metadata; the next propose of these requests applies them
+            total = keys.shape[1]
+            self._stage_k[:, :total].copy_(keys, non_blocking=True)
+            self._stage_v[:, :total].copy_(values, non_blocking=True)
+            self._stage_h[:B].copy_(hidden.reshape(B, -1), non_blocking=True)
+            slot_h, lens_h, cnt_h, off_h, _ = self._host_meta()
+            slot_h[:B] = commit.slots
+            lens_h[:B] = commit.lengths
+            cnt_h[:B] = commit.counts
+            off_h[:B] = commit.offsets
+            self._pending = (tuple(m["id"] for m in meta), B)
+            return
         slot_t = torch.tensor(commit.slots, dtype=torch.int32, device=dev)
         lens_t = torch.tensor(commit.lengths, dtype=torch.int32, device=dev)
         cnt_t = torch.tensor(commit.counts, dtype=torch.int32, device=dev)
@@ -176,12 +242,9 @@ class LongSparkDraft:
                            seq_lens=lens_t, kv_k=self.pools.kv_k, kv_v=self.pools.kv_v, page_table=table,
                            ring_pages=self.pools.ring_pages, last_hidden=hidden.to(dev, torch.bfloat16).contiguous(),
                            hidden_pool=self.pools.hidden, slots=slot_t, status=st)
-        if prefill:
-            self.pools.summary_out.index_copy_(0, slot_t.long(), extra["global_output"].to(dev, torch.float32))
-            self.pools.summary_lse.index_copy_(0, slot_t.long(), extra["global_lse"].to(dev, torch.float32))
-            self.pools.sync_summary_bf16(slot_t)
-        else:
-            self.engine.refresh(slots=slot_t, seq_lens=lens_t, commit_lens=cnt_t, page_table=table, batch=B)
+        self.pools.summary_out.index_copy_(0, slot_t.long(), extra["global_output"].to(dev, torch.float32))
+        self.pools.summary_lse.index_copy_(0, slot_t.long(), extra["global_lse"].to(dev, torch.float32))
+        self.pools.sync_summary_bf16(slot_t)
 
     # ------------------------------------------------------------------ propose
     def _graph_for(self, batch):
@@ -203,11 +266,35 @@ class LongSparkDraft:
         return torch.ones(size, dtype=torch.int32, device=self.device)
 
     @torch.inference_mode()
+    def _step_graph(self, B):
+        """Graph of one full step for exactly B requests: page-table gather,
+        window scatter of the staged rows, drafter pass with the refresh."""
+        g = self._step_graphs.get(B)
+        if g is None:
+            g = StepGraph(self, B)
+            self._step_graphs[B] = g
+        return g
+
     def propose(self, ids, anchors, temperature):
         if temperature != 0:
             raise NotImplementedError("sampled (T > 0) proposals are not implemented by the B200 drafter")
         dev = self.device
         B = len(ids)
+        if self._pending is not None and self.use_graph and self._pending[0] == tuple(ids):
+            self.table.lookup(ids)  # the reference's unknown-request error
+            _, _, _, _, anc_h = self._host_meta()
+            on_device = torch.is_tensor(anchors) and anchors.is_cuda
+            if not on_device:
+                anc_h[:B] = anchors.reshape(-1).numpy() if torch.is_tensor(anchors) else np.asarray(anchors)
+            self._pending = None
+            self._push_meta()
+            if on_device:  # device anchors (e.g. the target's bonus tokens): no host round trip
+                self._meta_views(self._meta_dev)[4][:B].copy_(anchors.reshape(-1))
+            g = self._step_graph(B)
+            g.replay()
+            self.engine.graph_replays += 1
+            return self._propose_outputs(B, self._meta_views(self._meta_dev)[4][:B], B)
+        self._flush()
         slot_list, len_list = self.table.lookup(ids)
         slots = torch.tensor(slot_list, dtype=torch.int32, device=dev)
         lengths = torch.tensor(len_list, dtype=torch.int32, device=dev)
@@ -228,17 +315,22 @@ class LongSparkDraft:
         else:
             self.engine.draft(slots=slots, seq_lens=lengths, anchors=anchor_t, page_table=table, batch=B)
             run_batch, run_anchors = B, anchor_t
+        return self._propose_outputs(B, run_anchors, run_batch)
+
+    def _propose_outputs(self, B, run_anchors, run_batch):
         tokens = self.engine.buf["tokens"][:B].clone()
         logits = None
         if self.materialize_logits:
             s = self.shape
             if self._logits is None:
-                self._logits = torch.empty(self.capacity * s.block, s.vocab, dtype=torch.bfloat16, device=dev)
+                self._logits = torch.empty(self.capacity * s.block, s.vocab, dtype=torch.bfloat16,
+                                           device=self.device)
             self.engine.corrected_logits(run_anchors, self._logits, batch=run_batch)
             logits = self._logits[:B * s.block].view(B, s.block, s.vocab).clone()
         return tokens, logits, None
 
     def release(self, ids):
+        self._flush()
         self.table.release(ids)
 
     def graph_stats(self):
@@ -248,3 +340,44 @@ class LongSparkDraft:
     def device_status(self):
         """Device status word of the kernels (0 = ok); synchronises."""
         return self.engine.device_status()
+
+
+class StepGraph:
+    """CUDA graph of one full drafting step for a fixed batch B, reading the
+    drafter's staged rows and metadata block: gather of the requests' page-table
+    rows, window scatter of the committed K/V rows and boundary hidden states,
+    then the drafter pass with the view refresh (``DraftEngine.draft``)."""
+
+    def __init__(self, d: "LongSparkDraft", B: int):
+        self.d, self.B = d, B
+        slot_t, lens_t, cnt_t, off_t, anc_t = (v[:B] for v in d._meta_views(d._meta_dev))
+        self.args = (slot_t, lens_t, cnt_t, off_t, anc_t)
+        self.table = torch.zeros(B, d.pools.page_table.shape[1], dtype=torch.int32, device=d.device)
+        s = torch.cuda.Stream(device=d.device)
+        s.wait_stream(torch.cuda.current_stream(d.device))
+        with torch.cuda.stream(s):
+            # warm-up (kernel attributes, module loading) without the refresh:
+            # the scatter is idempotent, the refresh would fold the rows twice
+            torch.index_select(d.pools.page_table, 0, self.args[0], out=self.table)
+            d.engine.draft(slots=self.args[0], seq_lens=self.args[1], anchors=self.args[4], page_table=self.table,
+                           batch=B)
+        torch.cuda.current_stream(d.device).wait_stream(s)
+        torch.cuda.synchronize(d.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self._run()
+        torch.cuda.current_stream(d.device).wait_stream(s)
+
+    def _run(self):
+        d, B = self.d, self.B
+        slot_t, lens_t, cnt_t, off_t, anc_t = self.args
+        torch.index_select(d.pools.page_table, 0, slot_t, out=self.table)
+        ops.window_scatter(keys=d._stage_k, values=d._stage_v, row_offsets=off_t, counts=cnt_t, seq_lens=lens_t,
+                           kv_k=d.pools.kv_k, kv_v=d.pools.kv_v, page_table=self.table,
+                           ring_pages=d.pools.ring_pages, last_hidden=d._stage_h, hidden_pool=d.pools.hidden,
+                           slots=slot_t, status=d.engine.buf["status"], batch=B)
+        d.engine.draft(slots=slot_t, seq_lens=lens_t, anchors=anc_t, page_table=self.table, batch=B,
+                       commit_lens=cnt_t)
+
+    def replay(self):
+        self.graph.replay()

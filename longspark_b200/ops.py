@@ -232,10 +232,13 @@ def refresh_views(*, kv_k, kv_v, page_table, seq_lens, commit_lens, slots, learn
 
 
 def window_scatter(*, keys, values, row_offsets, counts, seq_lens, kv_k, kv_v, page_table, ring_pages=0,
-                   last_hidden=None, hidden_pool=None, slots=None, status=None):
-    """Packet K/V rows -> paged pool at their positions; last hidden -> slot pool."""
+                   last_hidden=None, hidden_pool=None, slots=None, status=None, batch=None):
+    """Packet K/V rows -> paged pool at their positions; last hidden -> slot pool.
+    ``keys``/``values`` [L, total_rows, Hkv, 128]: request b owns rows
+    [row_offsets[b], row_offsets[b] + counts[b])."""
     L, total, hkv, d = keys.shape if keys is not None else (kv_k.shape[0], 0, kv_k.shape[3], 128)
-    batch = counts.shape[0] if counts is not None else slots.shape[0]
+    if batch is None:
+        batch = counts.shape[0] if counts is not None else slots.shape[0]
     hidden = hidden_pool.shape[-1] if hidden_pool is not None else 0
     N.call("ls_window_scatter", _stream(kv_k.device), _p(keys), _p(values), total, _p(row_offsets), _p(counts),
            _p(seq_lens), _p(kv_k), _p(kv_v), kv_k.shape[1], _p(page_table),
