@@ -51,6 +51,8 @@ def parse():
                     help="untimed load before the timed steps, so clock samples see the GPU busy")
     ap.add_argument("--contexts", type=str, default=",".join(str(c) for c in CONTEXTS),
                     help="comma-separated context lengths of the sweep (the headline is the largest)")
+    ap.add_argument("--batch-sweep", type=str, default="8,32,128",
+                    help="BASELINE config 4 concurrency sweep: requests per GPU (contexts U[2K, 32K]); '' to skip")
     return ap.parse_args()
 
 
@@ -229,6 +231,35 @@ def build_round(shape, ctx, batch, dev, seed):
     g.load(slots=torch.arange(batch, dtype=torch.int32, device=dev), seq_lens=v["seq_lens"], anchors=v["anchors"],
            page_table=v["page_table"], commit_lens=commit, target=target)
     return eng, g, v
+
+
+def concurrency_round(shape, batch, dev, seed, steps=30):
+    """one graph-replayed round for ``batch`` requests with
+    per-request contexts uniform in [2K, 32K]; returns (ms per round, status)."""
+    import torch
+    from longspark_b200.engine import DraftEngine, DraftWeights, GraphedDraft, ViewPools
+    from longspark_b200.synthetic import make_views, make_weights
+
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    W = make_weights(shape, device=dev, gen=gen)
+    weights = DraftWeights(shape, W, dev)
+    del W
+    ctxs = torch.randint(2048, 32769, (batch,), generator=torch.Generator().manual_seed(seed + batch)).tolist()
+    v = make_views(shape, batch, ctxs, device=dev, gen=gen, extra_rows=shape.max_commit)
+    pools = ViewPools(kv_k=v["kv_k"], kv_v=v["kv_v"], page_table=v["page_table"], summary_out=v["summary_out"],
+                      summary_lse=v["summary_lse"], hidden=v["hidden"])
+    eng = DraftEngine(shape, weights, pools, max_batch=batch, device=dev)
+    g = GraphedDraft(eng, batch, with_refresh=True, with_target=True, slots_are_rows=True)
+    g.load(slots=torch.arange(batch, dtype=torch.int32, device=dev), seq_lens=v["seq_lens"], anchors=v["anchors"],
+           page_table=v["page_table"],
+           commit_lens=torch.full((batch,), shape.max_commit, dtype=torch.int32, device=dev),
+           target=torch.randint(0, shape.vocab, (batch, shape.block + 1), device=dev, generator=gen))
+    g.capture()
+    ms = time_graph(g, steps, 3, 1)
+    status = eng.device_status()
+    del g, eng, pools, v, weights
+    torch.cuda.empty_cache()
+    return ms, status
 
 
 def algorithmic_bytes(shape, eng, batch):
@@ -447,6 +478,14 @@ def run_b200(args):
                "path": "LongSparkDraft.update(batch packet from pinned host) + propose(T=0) + tokens.cpu()",
                "device_status": e_status}
 
+    batch_sweep = []
+    for bs in [int(x) for x in args.batch_sweep.split(",") if x.strip()]:
+        ms_b, st_b = concurrency_round(shape, bs, dev, seed=2000 + rank)
+        ms_b = dist_max(ms_b, world)
+        batch_sweep.append({"requests_per_gpu": bs, "round_us": round(ms_b * 1e3, 1),
+                            "draft_tokens_per_s": round(bs * shape.block * world / (ms_b * 1e-3), 1),
+                            "device_status": st_b})
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, threads = cpu_round_sample(shape, HEADLINE_CTX, rounds=3)
@@ -469,6 +508,9 @@ def run_b200(args):
                        "graph": "refresh + drafter pass + Markov chain + accept in one CUDA graph"},
             "round_latency_us": round(ms * 1e3, 1),
             "ctx_sweep": sweep,
+            "batch_sweep": batch_sweep,
+            "batch_sweep_note": ("BASELINE config 4: per-request contexts uniform in [2K, 32K], 16 committed rows "
+                                 "per request per round, requests sharded over GPUs (value per box)"),
             "round_hbm_gbs": round(headline["abytes"] / (ms * 1e-3) / 1e9, 1),
             "round_algorithmic_bytes": headline["abytes"],
             "roofline": {"bound": "hbm", "kernel": "vocabulary projection GEMM (tcgen05, LS_EPI_LMHEAD)",
