@@ -339,6 +339,90 @@ LS_API int ls_accept(void* stream, const long long* target, int target_ld, const
  * to *out (device fp32). */
 LS_API int ls_row_norm_bound(void* stream, const void* m, int vocab, int rank, float* out);
 
+/* ------------------------------------------------------------------------- */
+/* Tensor parallelism of the drafter over NVLink (one process per GPU).       */
+/* No counterpart in the reference, which forces the drafter to one GPU       */
+/* (SP global16_native_draft_executor.py:1101-1105); the design precedent is  */
+/* the target's push/pull custom allreduce over IPC-mapped peer buffers       */
+/* (vendor/sglang jit_kernel/csrc/distributed/custom_all_reduce_push.cuh).    */
+/*                                                                            */
+/* Every rank allocates one "symmetric heap" of the same size with           */
+/* ls_ipc_alloc, exchanges the 64-byte handles (any host channel), opens the  */
+/* peers' heaps with ls_ipc_open, and fills an ls_tp_group.  A buffer at      */
+/* offset X of this rank's heap is reached on rank p at heap[p] + X, so a      */
+/* kernel addresses the same buffer on every rank from one local pointer.     */
+/* The heap holds, at sync_offset, a sync region of ls_tp_sync_bytes() bytes  */
+/* (flags and exchange slots; zero it on every rank, then put a host barrier  */
+/* between the ranks before the first TP launch).  Plain peer loads and       */
+/* stores only: no multicast object, no TMA from peer memory.                 */
+/* Every wait on a peer is bounded (2 s of %globaltimer); a wait that gives   */
+/* up writes LS_DEV_TIMEOUT_PEER to the status word and the kernel returns;   */
+/* the flags are then inconsistent: zero the sync region on every rank (after */
+/* a host barrier) before the next TP launch.                                 */
+/* ------------------------------------------------------------------------- */
+#define LS_TP_MAX_RANKS 8
+#define LS_TP_WIRE_F32 0  /* partial tiles cross NVLink as fp32                */
+#define LS_TP_WIRE_BF16 1 /* partial tiles cross NVLink rounded to bf16 (as a  */
+                          /* bf16 row-parallel linear + bf16 allreduce does)   */
+#define LS_DEV_TIMEOUT_PEER 105
+
+typedef struct ls_tp_group {
+  int world;                      /* ranks, 1..LS_TP_MAX_RANKS                   */
+  int rank;                       /* this process's rank                         */
+  void* heap[LS_TP_MAX_RANKS];    /* every rank's heap, mapped in this process    */
+  size_t heap_bytes;              /* size of each heap (the same on every rank)   */
+  size_t sync_offset;             /* sync region offset (256-byte aligned)        */
+} ls_tp_group;
+
+/* cudaMalloc of `bytes` on the current device plus its IPC handle
+ * (cudaIpcGetMemHandle, 64 bytes written to handle_out). */
+LS_API int ls_ipc_alloc(size_t bytes, void** ptr_out, void* handle_out);
+/* Map a peer's allocation from its 64-byte handle (cudaIpcOpenMemHandle with
+ * lazy peer access). */
+LS_API int ls_ipc_open(const void* handle, void** ptr_out);
+LS_API int ls_ipc_close(void* ptr);
+LS_API int ls_ipc_free(void* ptr);
+
+/* Bytes of the sync region for row-parallel GEMMs with up to `rows` tokens and
+ * `n_out` output features on `world` ranks with the given wire format (take
+ * the maximum over the GEMMs that share the region). */
+LS_API size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire);
+
+/* Row-parallel GEMM fused with the allreduce of its output over the group:
+ *   out = epilogue(sum over ranks of x_r . w_r^T)   on every rank,
+ * where x_r / w_r are this rank's k-slice (a.x, a.w, a.k are local).
+ * Epilogues LS_EPI_STORE and LS_EPI_RESIDUAL (residual: this rank's copy,
+ * identical on every rank; may alias out).  `a.out` must lie inside this
+ * rank's heap.  Output tile t belongs to rank t % world: every rank sends its
+ * fp32 (or bf16, per `wire`) partial of tile t to the owner's exchange slot
+ * with peer stores and a release flag as soon as its tensor cores finish the
+ * tile; after finishing its own tiles, the owner sums the world partials in
+ * rank order, applies the epilogue once and stores the bf16 result into every
+ * rank's `out`, then flags each rank.  The kernel returns when this rank's
+ * `out` is complete.  Launch it on every rank with the same shapes, in the
+ * same order relative to the other TP launches. */
+LS_API int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_tp_group* g, int wire, void* workspace,
+                             size_t workspace_bytes);
+
+/* Device-side barrier over the group (one small kernel): returns when every
+ * rank has reached it; the writes of kernels before it on every rank are then
+ * visible to kernels after it on every rank.  `slot` in [0, 16) selects an
+ * epoch counter; each slot must be used by every rank the same number of
+ * times. */
+LS_API int ls_tp_barrier(void* stream, const ls_tp_group* g, int slot, int* status);
+
+/* ls_markov_argmax over a vocabulary sharded by 128-token tiles: rank s holds
+ * tiles [s * tiles_per_shard, min((s + 1) * tiles_per_shard, vocab / 128)) of
+ * the LM head, i.e. its logits [batch*block, n_s * 128] and tile maxima
+ * [batch*block, n_s] (LS_EPI_LMHEAD output of its weight shard; tile_arg
+ * local to the shard).  a.base / a.tile_max / a.tile_arg are this rank's
+ * shard, inside its heap, at the same offsets on every rank; a.vocab is the
+ * full vocabulary; w1/w2 are full (replicated).  Every rank reads the band
+ * tiles it needs from the owning rank's heap and computes the same tokens.
+ * Put an ls_tp_barrier between the LM-head GEMMs and this call. */
+LS_API int ls_markov_argmax_tp(void* stream, const ls_markov_args* a, const ls_tp_group* g, int tiles_per_shard,
+                               void* workspace, size_t workspace_bytes);
+
 #ifdef __cplusplus
 }
 #endif

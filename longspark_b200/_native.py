@@ -16,6 +16,9 @@ LIB_PATH = Path(__file__).resolve().parent / "_native" / "liblongspark_b200.so"
 LS_OK = 0
 W_ROWMAJOR, W_TILED = 0, 1
 EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_QKV, EPI_GATEUP, EPI_LMHEAD, EPI_MARKOV_ADD = range(7)
+TP_MAX_RANKS = 8
+TP_WIRE_F32, TP_WIRE_BF16 = 0, 1
+DEV_TIMEOUT_PEER = 105
 
 vp = C.c_void_p
 i32 = C.c_int
@@ -56,6 +59,10 @@ class MarkovArgs(C.Structure):
                 ("status", vp)]
 
 
+class TpGroup(C.Structure):
+    _fields_ = [("world", i32), ("rank", i32), ("heap", vp * TP_MAX_RANKS), ("heap_bytes", sz), ("sync_offset", sz)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "ls_version": (i32, []),
@@ -79,6 +86,14 @@ SIGNATURES = {
     "ls_markov_argmax_static": (i32, [vp, C.POINTER(MarkovArgs)]),
     "ls_accept": (i32, [vp, vp, i32, vp, vp, i32, i32]),
     "ls_row_norm_bound": (i32, [vp, vp, i32, i32, vp]),
+    "ls_ipc_alloc": (i32, [sz, C.POINTER(vp), vp]),
+    "ls_ipc_open": (i32, [vp, C.POINTER(vp)]),
+    "ls_ipc_close": (i32, [vp]),
+    "ls_ipc_free": (i32, [vp]),
+    "ls_tp_sync_bytes": (sz, [i32, i32, i32, i32]),
+    "ls_gemm_allreduce": (i32, [vp, C.POINTER(GemmArgs), C.POINTER(TpGroup), i32, vp, sz]),
+    "ls_tp_barrier": (i32, [vp, C.POINTER(TpGroup), i32, vp]),
+    "ls_markov_argmax_tp": (i32, [vp, C.POINTER(MarkovArgs), C.POINTER(TpGroup), i32, vp, sz]),
 }
 
 _lib = None

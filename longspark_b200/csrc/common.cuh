@@ -22,6 +22,7 @@
 #define LS_DEV_TIMEOUT_MMA 102
 #define LS_DEV_TIMEOUT_EPILOGUE 103
 #define LS_DEV_TIMEOUT_REDUCE 104
+#define LS_DEV_TIMEOUT_PEER 105  // a tensor-parallel peer did not arrive
 #define LS_DEV_BAD_INDEX 110
 #define LS_DEV_BAD_TOKEN 111
 

@@ -18,6 +18,7 @@
 // TMEM owner, warps 2-5 = epilogue (TMEM -> registers -> fused epilogue).
 #include "common.cuh"
 #include "host_common.h"
+#include "tp_common.cuh"
 
 #include <algorithm>
 #include <stdlib.h>
@@ -49,6 +50,8 @@ struct GemmKernelParams {
   uint32_t tmem_cols;
   float* partials;   // [grid * 2][bn][128]
   int* counters;     // [tiles]
+  TpView tp;         // tp.world > 0: row-parallel GEMM fused with the allreduce (ls_gemm_allreduce)
+  int tp_wire;       // LS_TP_WIRE_*
 };
 
 __device__ __forceinline__ long long unit_begin(long long c, long long units, long long grid) {
@@ -247,6 +250,167 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Row-parallel GEMM fused with the allreduce of its output (ls_gemm_allreduce).
+// Tile t belongs to rank t % world.  A finished tile (this rank's k-slice) is
+// stored straight into the owner's exchange slot [t / world][this rank] with
+// peer stores, then flagged; no rank waits while it still has tiles to send.
+// After its own units, each CTA finalises the owned tiles assigned to it: it
+// waits for all `world` partials, sums them in rank order (the same bits
+// whatever the arrival order), applies the epilogue once and stores the bf16
+// result into every rank's output, then flags each rank.  Last, the CTA waits
+// for its share of the tiles other ranks own, so the kernel ends with this
+// rank's output complete.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ size_t tp_tile_bytes(const GemmKernelParams& P) {
+  return static_cast<size_t>(P.bn) * BM * (P.tp_wire == LS_TP_WIRE_BF16 ? 2 : 4);
+}
+
+// Exchange slot of (tile t, source rank src) in the heap of t's owner.
+__device__ __forceinline__ uint8_t* tp_slot(const GemmKernelParams& P, int t, int src) {
+  const int W = P.tp.world;
+  return P.tp.sync[t % W] + TP_XCH_OFF + (static_cast<size_t>(t / W) * W + src) * tp_tile_bytes(P);
+}
+
+// Chunk [c, c + 16) of tile t (first token n0) into the owner's slot.
+__device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, int n0, int c, const float (&v)[16],
+                                              int r) {
+  uint8_t* slot = tp_slot(P, t, P.tp.rank);
+  const int lim = P.a.rows - n0 - c;  // tokens of the chunk that exist
+  if (P.tp_wire == LS_TP_WIRE_BF16) {
+    bf16* s = reinterpret_cast<bf16*>(slot) + static_cast<size_t>(c) * BM + r;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < lim) s[j * BM] = __float2bfloat16_rn(v[j]);
+  } else {
+    float* s = reinterpret_cast<float*>(slot) + static_cast<size_t>(c) * BM + r;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < lim) s[j * BM] = v[j];
+  }
+}
+
+// After the last chunk of tile t (all 128 epilogue threads): release the
+// slot's stores to the owner.
+__device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int r) {
+  fence_sys();
+  epi_bar();
+  if (r == 0) st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), 1u);
+}
+
+// Summed 16-token chunk of an owned tile: the STORE / RESIDUAL epilogue
+// (residual from this rank's copy), stored into every rank's output.
+__device__ __forceinline__ void tp_final_store(const GemmKernelParams& P, int m_tile, int n0, const float (&v)[16],
+                                               int r) {
+  const ls_gemm_args& a = P.a;
+  const int f = m_tile * BM + r;
+  const bool res = a.epilogue == LS_EPI_RESIDUAL;
+  float add[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) add[j] = 0.0f;
+  if (res) {
+    const bf16* src = reinterpret_cast<const bf16*>(a.residual);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int tok = n0 + j < a.rows ? n0 + j : a.rows - 1;
+      add[j] = __bfloat162float(src[(long long)tok * a.res_ld + f]);
+    }
+  }
+  bf16 y[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) y[j] = __float2bfloat16_rn(bf16_round(v[j]) + add[j]);
+  bf16* out = reinterpret_cast<bf16*>(a.out);
+  for (int p = 0; p < P.tp.world; ++p) {
+    bf16* o = tp_peer(P.tp, p, out);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int tok = n0 + j;
+      if (tok >= a.rows) break;
+      o[(long long)tok * a.out_ld + f] = y[j];
+    }
+  }
+}
+
+__device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScratch* sc, volatile int* abort_flag) {
+  const int W = P.tp.world, me = P.tp.rank;
+  const int tiles = P.m_tiles * P.n_tiles;
+  int* status = P.a.status;
+  const int n_owned = tiles > me ? (tiles - me + W - 1) / W : 0;
+  for (int tl = blockIdx.x; tl < n_owned; tl += gridDim.x) {
+    const int t = tl * W + me;
+    if (r == 0) sc->flag = 1;
+    epi_bar();
+    if (r < W) {
+      uint32_t* fl = tp_arrive_flag(P.tp, me, t, r);
+      if (wait_flag(fl, 1u, abort_flag, status))
+        *fl = 0u;
+      else
+        sc->flag = 0;
+    }
+    epi_bar();
+    const bool go = sc->flag != 0;
+    epi_bar();
+    if (!go) return;
+    const int m_tile = t / P.n_tiles;
+    const int n0 = (t - m_tile * P.n_tiles) * P.bn;
+    const bool wire16 = P.tp_wire == LS_TP_WIRE_BF16;
+    for (int c = 0; c < P.bn && n0 + c < P.a.rows; c += 16) {
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+      // ranks in order, four slots' loads in flight at a time
+      for (int s0 = 0; s0 < W; s0 += 4) {
+        float pv[4][16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (s0 + i < W) {
+            const uint8_t* slot = tp_slot(P, t, s0 + i);
+            if (wire16) {
+              const unsigned short* q = reinterpret_cast<const unsigned short*>(slot) + static_cast<size_t>(c) * BM + r;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) pv[i][j] = __bfloat162float(__ushort_as_bfloat16(__ldcg(q + j * BM)));
+            } else {
+              const float* q = reinterpret_cast<const float*>(slot) + static_cast<size_t>(c) * BM + r;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) pv[i][j] = __ldcg(q + j * BM);
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (s0 + i < W) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += pv[i][j];
+          }
+        }
+      }
+      tp_final_store(P, m_tile, n0 + c, v, r);
+    }
+    fence_sys();
+    epi_bar();
+    if (r < W && r != me) st_release_sys(tp_done_flag(P.tp, r, t), 1u);
+  }
+  // this rank's copies of the tiles the other ranks own
+  if (r == 0) {
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      if (t % W == me) continue;
+      uint32_t* fl = tp_done_flag(P.tp, me, t);
+      if (!wait_flag(fl, 1u, abort_flag, status)) break;
+      *fl = 0u;
+    }
+  }
+}
+
+// A finished 16-token chunk: the fused epilogue, or (row-parallel TP) the send
+// of the partial to the tile's owner.
+__device__ __forceinline__ void emit_chunk(const GemmKernelParams& P, int t, int m_tile, int n0, int c,
+                                           const float (&v)[16], int r, int ew, EpiScratch* sc) {
+  if (P.tp.world > 0)
+    tp_send_chunk(P, t, n0, c, v, r);
+  else
+    final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
+}
+
 // Reduction of a stream-K tile by its last contributor: the fp32 partials of
 // CTAs first..last summed in that order, then the fused epilogue.
 __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, int first, int last, int first_slot,
@@ -279,7 +443,7 @@ __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, in
         }
       }
     }
-    if (n0 + c < P.a.rows) final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
+    if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc);
   }
 }
 
@@ -504,10 +668,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int c = 0; c < bn; c += 16) {
           float v[16];
           tmem_ld16(t_addr + c, v);
-          if (n0 + c < P.a.rows) final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
+          if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
+        if (P.tp.world > 0) tp_publish(P, t, r);
       } else {
         // Partial tile: park the fp32 partial, the last contributor reduces.
         const int slot = (t == t_first) ? 0 : 1;
@@ -537,12 +702,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int first_slot = unit_begin(first, U, G) == tu0 ? 0 : 1;
           reduce_tile(P, t, first, last, first_slot, r, ew, sc);
           if (r == 0) atomicExch(&P.counters[t], 0);
+          if (P.tp.world > 0) tp_publish(P, t, r);
         }
       }
       acc_phase ^= 1u << acc;
       acc ^= 1;
       u += k1 - k0;
     }
+    if (P.tp.world > 0 && !*abort_flag) tp_finish(P, r, sc, abort_flag);
   }
 
   tc_fence_before();
@@ -615,7 +782,10 @@ extern "C" size_t ls_gemm_workspace_bytes(int rows, int k, int n_out) {
   return p.counter_bytes + p.partial_bytes;
 }
 
-extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes) {
+namespace ls {
+
+static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes, const TpView* tp,
+                       int wire) {
   if (a == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm: null args");
   if (a->x == nullptr || a->w == nullptr || a->out == nullptr)
     return set_error(LS_ERR_INVALID, "ls_gemm: null x/w/out");
@@ -688,6 +858,10 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
   kp.tmem_cols = cols;
   kp.counters = reinterpret_cast<int*>(workspace);
   kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + p.counter_bytes);
+  if (tp != nullptr) {
+    kp.tp = *tp;
+    kp.tp_wire = wire;
+  }
 
   const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.stages);
   static int configured_smem = 0;
@@ -715,6 +889,49 @@ extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, siz
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map_w, map_x, kp);
   if (e != cudaSuccess) return set_cuda_error("ls_gemm: launch", e);
   return LS_OK;
+}
+
+}  // namespace ls
+
+extern "C" int ls_gemm(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes) {
+  return gemm_launch(stream, a, workspace, workspace_bytes, nullptr, 0);
+}
+
+extern "C" size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire) {
+  if (world < 1 || world > LS_TP_MAX_RANKS || rows <= 0 || n_out <= 0 || n_out % BM ||
+      (wire != LS_TP_WIRE_F32 && wire != LS_TP_WIRE_BF16))
+    return 0;
+  const int bn = pick_bn(rows);
+  const long long tiles = static_cast<long long>(n_out / BM) * ((rows + bn - 1) / bn);
+  const long long owned = (tiles + world - 1) / world;
+  return TP_XCH_OFF + static_cast<size_t>(owned) * world * bn * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);
+}
+
+extern "C" int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_tp_group* g, int wire, void* workspace,
+                                 size_t workspace_bytes) {
+  TpView v;
+  int rc = make_tp_view(g, &v, "ls_gemm_allreduce");
+  if (rc) return rc;
+  if (a == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm_allreduce: null args");
+  if (a->epilogue != LS_EPI_STORE && a->epilogue != LS_EPI_RESIDUAL)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_gemm_allreduce: only the STORE and RESIDUAL epilogues reduce over ranks");
+  if (wire != LS_TP_WIRE_F32 && wire != LS_TP_WIRE_BF16)
+    return set_error(LS_ERR_INVALID, "ls_gemm_allreduce: unknown wire format %d", wire);
+  if (g->world == 1) return gemm_launch(stream, a, workspace, workspace_bytes, nullptr, 0);
+  if (a->rows <= 0 || a->n_out <= 0 || a->n_out % BM || a->out_ld < a->n_out || a->out == nullptr)
+    return set_error(LS_ERR_INVALID, "ls_gemm_allreduce: bad rows/n_out/out_ld");
+  const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out);
+  if (static_cast<long long>(p.m_tiles) * p.n_tiles > TP_MAX_TILES)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_gemm_allreduce: %d x %d output tiles exceed %d", p.m_tiles, p.n_tiles,
+                     TP_MAX_TILES);
+  const size_t need = ls_tp_sync_bytes(g->world, a->rows, a->n_out, wire);
+  if (g->sync_offset + need > g->heap_bytes)
+    return set_error(LS_ERR_WORKSPACE, "ls_gemm_allreduce: sync region needs %zu bytes at offset %zu of a %zu-byte heap",
+                     need, g->sync_offset, g->heap_bytes);
+  const size_t out_bytes = (static_cast<size_t>(a->rows - 1) * a->out_ld + a->n_out) * 2;
+  if (!in_own_heap(g, a->out, out_bytes) || (reinterpret_cast<uintptr_t>(a->out) & 1))
+    return set_error(LS_ERR_INVALID, "ls_gemm_allreduce: out must lie inside this rank's heap");
+  return gemm_launch(stream, a, workspace, workspace_bytes, &v, wire);
 }
 
 // Row-major [n_out, k] -> (row tile, k tile) tiles of 128 x 64, rows of each

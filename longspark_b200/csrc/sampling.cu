@@ -22,12 +22,53 @@
 // values.  The tokens are identical to the full scan's.  A request whose band
 // overflows the candidate buffers is evaluated step by step, over the whole
 // vocabulary if needed.
+#include <string.h>
+
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
 #include "host_common.h"
+#include "tp_common.cuh"
 
 namespace ls {
+
+// Where the logits and tile maxima of a row live.  One GPU: shard 0 holds the
+// whole vocabulary (T = vocab / 128).  Vocabulary-parallel LM head: shard s
+// (rank s, reached through its heap) holds tiles [s*T, s*T + tiles[s]) with row
+// strides tiles[s] (maxima) and 128*tiles[s] (logits), and its tile_arg values
+// are shard-local token ids.
+struct VocabShards {
+  const bf16* base[LS_TP_MAX_RANKS];
+  const float* tmax[LS_TP_MAX_RANKS];
+  const int* targ[LS_TP_MAX_RANKS];
+  int tiles[LS_TP_MAX_RANKS];
+  int T;
+  int world;
+};
+
+__device__ __forceinline__ int vs_shard(const VocabShards& vs, int tile) { return vs.world > 1 ? tile / vs.T : 0; }
+
+__device__ __forceinline__ float vs_tmax(const VocabShards& vs, long long row, int tile) {
+  const int s = vs_shard(vs, tile);
+  return vs.tmax[s][row * vs.tiles[s] + (tile - s * vs.T)];
+}
+
+// global token id of the maximum of a tile
+__device__ __forceinline__ int vs_targ(const VocabShards& vs, long long row, int tile) {
+  const int s = vs_shard(vs, tile);
+  return vs.targ[s][row * vs.tiles[s] + (tile - s * vs.T)] + s * vs.T * 128;
+}
+
+// the 128 logits of a tile
+__device__ __forceinline__ const bf16* vs_tile(const VocabShards& vs, long long row, int tile) {
+  const int s = vs_shard(vs, tile);
+  return vs.base[s] + (row * vs.tiles[s] + (tile - s * vs.T)) * 128;
+}
+
+__device__ __forceinline__ float vs_logit(const VocabShards& vs, long long row, int v) {
+  return __bfloat162float(vs_tile(vs, row, v >> 7)[v & 127]);
+}
 
 constexpr int MK_THREADS = 256;
 constexpr int MK_MAXCAND = 4096;
@@ -108,14 +149,16 @@ __device__ __forceinline__ float band_threshold(float m, float beta_exact) {
   return m - 2.0f * beta - margin;
 }
 
-__device__ __forceinline__ void row_max(const float* tmax, const int* targ, int n_tiles, float* red_v, int* red_i,
+__device__ __forceinline__ void row_max(const VocabShards& vs, long long row, int n_tiles, float* red_v, int* red_i,
                                         float& bv, int& bi) {
   bv = -INFINITY;
   bi = 0x7fffffff;
   for (int i = threadIdx.x; i < n_tiles; i += blockDim.x) {
-    if (better(tmax[i], targ[i], bv, bi)) {
-      bv = tmax[i];
-      bi = targ[i];
+    const float m = vs_tmax(vs, row, i);
+    const int mi = vs_targ(vs, row, i);
+    if (better(m, mi, bv, bi)) {
+      bv = m;
+      bi = mi;
     }
   }
   block_argmax(bv, bi, red_v, red_i);
@@ -134,21 +177,17 @@ __host__ __device__ constexpr size_t mk_stepwise_bytes() { return MK_MAXCAND * 4
 // Exact step-by-step chain over the per-previous-token band (and over the
 // whole vocabulary when that band does not fit); used when the candidate
 // lists overflowed.
-__device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, int* cand, int* n_cand, int* tile_list,
-                               int* n_tl, float* red_v, int* red_i) {
+__device__ void stepwise_chain(const ls_markov_args& a, const VocabShards& vs, int b, float* latent, int* cand,
+                               int* n_cand, int* tile_list, int* n_tl, float* red_v, int* red_i) {
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int n_tiles = a.vocab / 128;
-  const bf16* base_all = reinterpret_cast<const bf16*>(a.base);
   long long prev = a.anchors[b];
   for (int t = 0; t < a.block; ++t) {
     const long long row = (long long)b * a.block + t;
-    const bf16* base = base_all + row * a.vocab;
-    const float* tmax = a.tile_max + row * n_tiles;
-    const int* targ = a.tile_arg + row * n_tiles;
     float bv;
     int bi;
-    row_max(tmax, targ, n_tiles, red_v, red_i, bv, bi);
+    row_max(vs, row, n_tiles, red_v, red_i, bv, bi);
     if (prev < 0 || prev >= a.vocab) {
       if (tid == 0) record_status(a.status, LS_DEV_BAD_TOKEN);
       prev = 0;
@@ -168,7 +207,7 @@ __device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, in
     }
     __syncthreads();
     for (int i = tid; i < n_tiles; i += blockDim.x) {
-      if (tmax[i] >= thr) {
+      if (vs_tmax(vs, row, i) >= thr) {
         const int slot = atomicAdd(n_tl, 1);
         if (slot < MK_MAXTILES) tile_list[slot] = i;
       }
@@ -180,7 +219,7 @@ __device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, in
     } else {
       for (int ti = warp; ti < ntl; ti += nwarps) {
         const int v0 = tile_list[ti] * 128 + lane * 4;
-        const uint2 raw = *reinterpret_cast<const uint2*>(base + v0);
+        const uint2 raw = *reinterpret_cast<const uint2*>(vs_tile(vs, row, tile_list[ti]) + lane * 4);
         const bf16* e4 = reinterpret_cast<const bf16*>(&raw);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -204,7 +243,7 @@ __device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, in
       float acc = 0.0f;
       for (int k = lane; k < a.rank; k += 32) acc += latent[k] * __bfloat162float(w2r[k]);
       acc = warp_sum(acc);
-      const float sv = bf16_round(__bfloat162float(base[v]) + bf16_round(acc));
+      const float sv = bf16_round(vs_logit(vs, row, v) + bf16_round(acc));
       if (better(sv, v, best, best_i)) {
         best = sv;
         best_i = v;
@@ -225,9 +264,9 @@ __device__ void stepwise_chain(const ls_markov_args& a, int b, float* latent, in
 // id so that every CTA lists a row's band in the same order.  count[r] = -1
 // when the band holds more than MK_ROWCAND tokens or MK_MAXTILES tiles.
 // Block-wide; ends with a barrier.
-__device__ __forceinline__ void band_candidates2(const float (&tv)[2][MK_TPT], int nrow, const bf16* const (&base)[2],
-                                 const float (&thr)[2], int (*tile_list)[MK_MAXTILES], int (*raw)[MK_ROWCAND],
-                                 int* const (&out)[2], int* n_tl, int* n_c, int (&count)[2]) {
+__device__ __forceinline__ void band_candidates2(const float (&tv)[2][MK_TPT], int nrow, const VocabShards& vs,
+                                 const long long (&rows)[2], const float (&thr)[2], int (*tile_list)[MK_MAXTILES],
+                                 int (*raw)[MK_ROWCAND], int* const (&out)[2], int* n_tl, int* n_c, int (&count)[2]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   if (tid < 2) {
     n_tl[tid] = 0;
@@ -251,10 +290,11 @@ __device__ __forceinline__ void band_candidates2(const float (&tv)[2][MK_TPT], i
   const int use0 = nt0 <= MK_MAXTILES ? nt0 : 0, use1 = nt1 <= MK_MAXTILES ? nt1 : 0;
   for (int ti = warp; ti < use0 + use1; ti += nwarps) {
     const int r = ti < use0 ? 0 : 1;
-    const bf16* bp = r == 0 ? base[0] : base[1];  // selects, not a dynamically indexed local array
+    const long long row = r == 0 ? rows[0] : rows[1];  // selects, not a dynamically indexed local array
     const float th = r == 0 ? thr[0] : thr[1];
-    const int v0 = tile_list[r][r == 0 ? ti : ti - use0] * 128 + lane * 4;
-    const uint2 rw = *reinterpret_cast<const uint2*>(bp + v0);
+    const int tile = tile_list[r][r == 0 ? ti : ti - use0];
+    const int v0 = tile * 128 + lane * 4;
+    const uint2 rw = *reinterpret_cast<const uint2*>(vs_tile(vs, row, tile) + lane * 4);
     const bf16* e4 = reinterpret_cast<const bf16*>(&rw);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -297,8 +337,9 @@ __device__ __forceinline__ void band_candidates2(const float (&tv)[2][MK_TPT], i
 // the token is the best candidate of C_t given the previous step's choice
 // (first maximum by token id, as torch.argmax).  A row whose band overflowed
 // sends the request to the exact step-by-step fallback.  Then the accept check.
-__global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args a, int* cand_count, int* cand_all,
-                                                            uint8_t* best_all, int* done) {
+__global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args a, const VocabShards vs,
+                                                            int* cand_count, int* cand_all, uint8_t* best_all,
+                                                            int* done) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ float red_v[32];
   __shared__ int red_i[32];
@@ -318,9 +359,6 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int n_tiles = a.vocab / 128;
-  const bf16* base_all = reinterpret_cast<const bf16*>(a.base);
-  const float* tmax = a.tile_max + row * n_tiles;
-  const int* targ = a.tile_arg + row * n_tiles;
   // this row's tile maxima (and the previous row's, for the Markov pairs) in
   // registers, every load in flight at once
   const int nrow = (a.w1 != nullptr && t > 0) ? 2 : 1;
@@ -328,8 +366,8 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
 #pragma unroll
   for (int k = 0; k < MK_TPT; ++k) {
     const int i = tid + k * blockDim.x;
-    tv[0][k] = i < n_tiles ? tmax[i] : -INFINITY;
-    tv[1][k] = (nrow > 1 && i < n_tiles) ? tmax[i - n_tiles] : -INFINITY;
+    tv[0][k] = i < n_tiles ? vs_tmax(vs, row, i) : -INFINITY;
+    tv[1][k] = (nrow > 1 && i < n_tiles) ? vs_tmax(vs, row - 1, i) : -INFINITY;
   }
   if (a.w1 == nullptr) {
     // plain argmax: (maximum, lowest index) over the tiles
@@ -339,7 +377,7 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
     for (int k = 0; k < MK_TPT; ++k) {
       const int i = tid + k * blockDim.x;
       if (i < n_tiles) {
-        const int ti = targ[i];
+        const int ti = vs_targ(vs, row, i);
         if (better(tv[0][k], ti, bv, bi)) {
           bv = tv[0][k];
           bi = ti;
@@ -367,12 +405,11 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
       mx[r] = v;
     }
     const float beta = (*a.w1_row_bound) * (*a.w2_row_bound);
-    const bf16* const base2[2] = {base_all + row * a.vocab, base_all + (row - (nrow > 1 ? 1 : 0)) * a.vocab};
+    const long long rows2[2] = {row, row - (nrow > 1 ? 1 : 0)};
     const float thr2[2] = {band_threshold(mx[0], beta), band_threshold(mx[1], beta)};
     int* const out2[2] = {cur, prv};
     int counts[2];
-    band_candidates2(tv, nrow, base2, thr2, tile_list, raw, out2, n_tl, n_c, counts);
-    const bf16* base = base2[0];
+    band_candidates2(tv, nrow, vs, rows2, thr2, tile_list, raw, out2, n_tl, n_c, counts);
     const int nc = counts[0];
     int np = 1;
     if (t == 0) {
@@ -419,7 +456,7 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
             if (e < tot) ws[e] = v[k];
           }
         }
-        for (int j = tid; j < nc; j += blockDim.x) cb[j] = __bfloat162float(base[cur[j]]);
+        for (int j = tid; j < nc; j += blockDim.x) cb[j] = vs_logit(vs, row, cur[j]);
         __syncthreads();
         for (int q = warp; q < np * nc; q += nwarps) {
           const int i = q / nc, j = q - i * nc;
@@ -439,7 +476,7 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
       } else for (int q = warp; q < np * nc; q += nwarps) {
         const int i = q / nc, j = q - i * nc;
         const long long pt = prv[i], ct = cur[j];
-        const float bv = __bfloat162float(base[ct]);
+        const float bv = vs_logit(vs, row, static_cast<int>(ct));
         float acc = 0.0f;
         for (int k = lane * 8; k < R; k += 256) {
           const uint4 x = __ldg(reinterpret_cast<const uint4*>(w1 + pt * R + k));
@@ -492,7 +529,7 @@ __global__ void __launch_bounds__(MK_THREADS) markov_kernel(const ls_markov_args
     if (!ok) {
       float* latent = reinterpret_cast<float*>(dsm);
       int* cand = reinterpret_cast<int*>(dsm + MK_MAXRANK * 4);
-      stepwise_chain(a, b, latent, cand, &n_c[0], tile_list[0], &n_tl[0], red_v, red_i);
+      stepwise_chain(a, vs, b, latent, cand, &n_c[0], tile_list[0], &n_tl[0], red_v, red_i);
       __syncthreads();
       if (tid < P) red_i[tid] = static_cast<int>(__ldcg(&a.tokens[r0 + tid]));
     } else {
@@ -592,7 +629,10 @@ extern "C" size_t ls_markov_workspace_bytes(int batch, int block) {
          rows * MK_ROWCAND * 5;
 }
 
-extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes) {
+namespace ls {
+
+static int markov_launch(void* stream, const ls_markov_args* a, const VocabShards* shards, void* workspace,
+                         size_t workspace_bytes) {
   if (a == nullptr || a->base == nullptr || a->tile_max == nullptr || a->tile_arg == nullptr || a->anchors == nullptr ||
       a->tokens == nullptr)
     return set_error(LS_ERR_INVALID, "ls_markov_argmax: null pointer argument");
@@ -627,9 +667,63 @@ extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* wor
     if (mk_stepwise_bytes() > dsmem) dsmem = mk_stepwise_bytes();
     if (MK_STAGE_BYTES > dsmem) dsmem = MK_STAGE_BYTES;
   }
-  cudaError_t e = launch_pdl(markov_kernel, dim3(static_cast<unsigned>(rows)), dim3(MK_THREADS), dsmem, st, *a, counts,
-                             cand, best, done);
+  VocabShards vs;
+  if (shards != nullptr) {
+    vs = *shards;
+  } else {
+    memset(&vs, 0, sizeof(vs));
+    vs.base[0] = reinterpret_cast<const bf16*>(a->base);
+    vs.tmax[0] = a->tile_max;
+    vs.targ[0] = a->tile_arg;
+    vs.T = vs.tiles[0] = a->vocab / 128;
+    vs.world = 1;
+  }
+  cudaError_t e = launch_pdl(markov_kernel, dim3(static_cast<unsigned>(rows)), dim3(MK_THREADS), dsmem, st, *a, vs,
+                             counts, cand, best, done);
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_markov_argmax: launch", e);
+}
+
+}  // namespace ls
+
+extern "C" int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspace, size_t workspace_bytes) {
+  return markov_launch(stream, a, nullptr, workspace, workspace_bytes);
+}
+
+extern "C" int ls_markov_argmax_tp(void* stream, const ls_markov_args* a, const ls_tp_group* g, int tiles_per_shard,
+                                   void* workspace, size_t workspace_bytes) {
+  TpView v;
+  int rc = make_tp_view(g, &v, "ls_markov_argmax_tp");
+  if (rc) return rc;
+  if (a == nullptr || a->base == nullptr || a->tile_max == nullptr || a->tile_arg == nullptr)
+    return set_error(LS_ERR_INVALID, "ls_markov_argmax_tp: null pointer argument");
+  if (a->vocab <= 0 || a->vocab % 128) return set_error(LS_ERR_UNSUPPORTED, "ls_markov_argmax_tp: vocab %% 128 != 0");
+  const int n_tiles = a->vocab / 128;
+  const int T = tiles_per_shard;
+  if (T <= 0 || static_cast<long long>(T) * g->world < n_tiles || static_cast<long long>(T) * (g->world - 1) >= n_tiles)
+    return set_error(LS_ERR_INVALID,
+                     "ls_markov_argmax_tp: %d tiles per shard do not cover %d tiles over %d ranks with every shard "
+                     "non-empty",
+                     T, n_tiles, g->world);
+  VocabShards vs;
+  memset(&vs, 0, sizeof(vs));
+  vs.T = T;
+  vs.world = g->world;
+  const long long rows = static_cast<long long>(a->batch) * a->block;
+  const int mine = std::min(T, n_tiles - g->rank * T);
+  if (a->batch > 0 &&
+      (!in_own_heap(g, a->base, static_cast<size_t>(rows) * mine * 128 * 2) ||
+       !in_own_heap(g, a->tile_max, static_cast<size_t>(rows) * mine * 4) ||
+       !in_own_heap(g, a->tile_arg, static_cast<size_t>(rows) * mine * 4)))
+    return set_error(LS_ERR_INVALID, "ls_markov_argmax_tp: logits and tile maxima must lie inside this rank's heap");
+  const uint8_t* own = static_cast<const uint8_t*>(g->heap[g->rank]);
+  for (int s = 0; s < g->world; ++s) {
+    const uint8_t* hp = static_cast<const uint8_t*>(g->heap[s]);
+    vs.base[s] = reinterpret_cast<const bf16*>(hp + (static_cast<const uint8_t*>(a->base) - own));
+    vs.tmax[s] = reinterpret_cast<const float*>(hp + (reinterpret_cast<const uint8_t*>(a->tile_max) - own));
+    vs.targ[s] = reinterpret_cast<const int*>(hp + (reinterpret_cast<const uint8_t*>(a->tile_arg) - own));
+    vs.tiles[s] = std::min(T, n_tiles - s * T);
+  }
+  return markov_launch(stream, a, &vs, workspace, workspace_bytes);
 }
 
 // ---------------------------------------------------------------------------

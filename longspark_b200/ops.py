@@ -60,11 +60,9 @@ class TiledWeight:
         return 2
 
 
-def gemm(x, w, out, *, workspace, epilogue=N.EPI_STORE, rows=None, residual=None, q_heads=0, kv_heads=0,
-         q_norm_w=None, k_norm_w=None, norm_eps=1e-6, positions=None, inv_freq=None, rope_table=None,
-         tile_max=None, tile_arg=None, base=None, status=None):
-    """out = epilogue(x[:rows] @ w.T) on the tcgen05 tensor cores (see ``ls_gemm``).
-    ``w`` is a row-major [n_out, k] bf16 tensor or a ``TiledWeight``."""
+def _gemm_args(x, w, out, *, workspace, epilogue=N.EPI_STORE, rows=None, residual=None, q_heads=0, kv_heads=0,
+               q_norm_w=None, k_norm_w=None, norm_eps=1e-6, positions=None, inv_freq=None, rope_table=None,
+               tile_max=None, tile_arg=None, base=None, status=None):
     tiled = isinstance(w, TiledWeight)
     wt = w.data if tiled else w
     _require_cuda(x, wt, out, workspace)
@@ -81,8 +79,34 @@ def gemm(x, w, out, *, workspace, epilogue=N.EPI_STORE, rows=None, residual=None
                    q_norm_w=_p(q_norm_w), k_norm_w=_p(k_norm_w), norm_eps=norm_eps, positions=_p(positions),
                    inv_freq=_p(inv_freq), rope_table=_p(rope_table), tile_max=_p(tile_max), tile_arg=_p(tile_arg), base=_p(base),
                    base_ld=0 if base is None else base.stride(0), status=_p(status))
+    return a
+
+
+def gemm(x, w, out, *, workspace, **kw):
+    """out = epilogue(x[:rows] @ w.T) on the tcgen05 tensor cores (see ``ls_gemm``).
+    ``w`` is a row-major [n_out, k] bf16 tensor or a ``TiledWeight``.  Keywords:
+    epilogue, rows, residual, q_heads, kv_heads, q_norm_w, k_norm_w, norm_eps,
+    positions, inv_freq, rope_table, tile_max, tile_arg, base, status."""
+    a = _gemm_args(x, w, out, workspace=workspace, **kw)
     N.call("ls_gemm", _stream(x.device), C.byref(a), _p(workspace), workspace.numel() * workspace.element_size())
     return out
+
+
+def gemm_allreduce(x, w, out, *, group, workspace, wire=N.TP_WIRE_F32, **kw):
+    """Row-parallel GEMM fused with the allreduce of its output over the
+    tensor-parallel ``group`` (``ls_gemm_allreduce``): ``x``/``w`` are this rank's
+    k-slice, ``out`` (inside the group's heap) receives the sum over ranks with
+    the STORE or RESIDUAL epilogue on every rank."""
+    a = _gemm_args(x, w, out, workspace=workspace, **kw)
+    N.call("ls_gemm_allreduce", _stream(x.device), C.byref(a), C.byref(group.struct), wire, _p(workspace),
+           workspace.numel() * workspace.element_size())
+    return out
+
+
+def tp_barrier(group, *, slot=0, status=None, device=None):
+    """Device-side barrier over the tensor-parallel group (``ls_tp_barrier``)."""
+    N.call("ls_tp_barrier", _stream(device if device is not None else group.device), C.byref(group.struct), slot,
+           _p(status))
 
 
 def gemm_workspace_bytes(rows, k, n_out):
@@ -283,15 +307,23 @@ def markov_workspace_bytes(batch, block):
 
 
 def markov_argmax(*, base, tile_max, tile_arg, anchors, tokens, block, workspace, w1=None, w2=None, w1_bound=None,
-                  w2_bound=None, target=None, accept_out=None, status=None, batch=None):
-    """Greedy Markov chain (or plain argmax without a head) over bf16 base logits."""
+                  w2_bound=None, target=None, accept_out=None, status=None, batch=None, group=None,
+                  tiles_per_shard=None, vocab=None):
+    """Greedy Markov chain (or plain argmax without a head) over bf16 base logits.
+    With a tensor-parallel ``group``, ``base``/``tile_max``/``tile_arg`` are this
+    rank's vocabulary shard (``tiles_per_shard`` 128-token tiles per rank, the
+    full ``vocab``), inside the group's heap (``ls_markov_argmax_tp``)."""
     _require_cuda(base, tile_max, tile_arg, anchors, tokens, workspace)
     batch = anchors.shape[0] if batch is None else batch
     a = N.MarkovArgs(base=_p(base), tile_max=_p(tile_max), tile_arg=_p(tile_arg), w1=_p(w1), w2=_p(w2),
                      w1_row_bound=_p(w1_bound), w2_row_bound=_p(w2_bound), rank=0 if w1 is None else w1.shape[1],
                      anchors=_p(anchors), tokens=_p(tokens), target=_p(target),
                      target_ld=0 if target is None else target.stride(0), accept_out=_p(accept_out), batch=batch,
-                     block=block, vocab=base.shape[-1], status=_p(status))
+                     block=block, vocab=base.shape[-1] if vocab is None else vocab, status=_p(status))
+    if group is not None:
+        N.call("ls_markov_argmax_tp", _stream(tokens.device), C.byref(a), C.byref(group.struct), tiles_per_shard,
+               _p(workspace), workspace.numel() * workspace.element_size())
+        return tokens
     N.call("ls_markov_argmax", _stream(tokens.device), C.byref(a), _p(workspace),
            workspace.numel() * workspace.element_size())
     return tokens

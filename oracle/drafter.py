@@ -29,7 +29,7 @@ import numpy as np
 
 __all__ = [
     "bf16_round", "bf16_bits", "from_bf16_bits", "rnd",
-    "linear", "silu", "rmsnorm_hf", "rmsnorm_fused", "feed_forward",
+    "linear", "row_parallel_linear", "silu", "rmsnorm_hf", "rmsnorm_fused", "feed_forward",
     "state_encoder", "shifted_input", "rope_tables", "apply_rotary",
     "attention_statistics", "statistics_as_normalized", "merge_normalized_attention",
     "window_positions", "gather_window", "attend", "decoder_layer", "project_logits",
@@ -74,6 +74,32 @@ def linear(x, w, prec):
     return rnd(np.matmul(x, w.T, dtype=np.float32), prec)
 
 
+def row_parallel_linear(x, w, prec, tp=None):
+    """A row-parallel ``nn.Linear`` over ``tp = (world, wire)`` ranks: rank r
+    holds the k-slice ``[r*K/world, (r+1)*K/world)`` of the input features and
+    of ``w``; each rank's fp32 partial crosses the wire as fp32
+    (``wire == "f32"``) or rounded to bf16 (``"bf16"``, what a bf16
+    RowParallelLinear + bf16 allreduce does: SGLang
+    ``srt/layers/linear.py`` RowParallelLinear, reduce_results), and the
+    partials are added in rank order in fp32 before the output rounding.
+    ``tp=None`` or world 1 is ``linear``.  The drafter itself has no tensor
+    parallelism in the reference (forced TP1,
+    SP global16_native_draft_executor.py:1101-1105): this is the split the
+    tensor-parallel kernels implement, restated for their parity tests."""
+    if tp is None or tp[0] == 1:
+        return linear(x, w, prec)
+    world, wire = tp
+    k = w.shape[1]
+    ks = k // world
+    acc = None
+    for r in range(world):
+        part = np.matmul(x[..., r * ks:(r + 1) * ks], w[:, r * ks:(r + 1) * ks].T, dtype=np.float32)
+        if wire == "bf16":
+            part = bf16_round(part)
+        acc = part if acc is None else (acc + part).astype(np.float32)
+    return rnd(acc, prec)
+
+
 def silu(x, prec):
     """``F.silu`` (computed in fp32, rounded once to the input dtype)."""
     x = np.asarray(x, dtype=np.float32)
@@ -99,23 +125,24 @@ def rmsnorm_fused(x, w, eps, prec):
     return rnd(x * (np.float32(1.0) / np.sqrt(var + np.float32(eps))) * w, prec)
 
 
-def feed_forward(x, w1, w2, prec):
-    """``FeedForward`` = Linear -> SiLU -> Linear (SF draftfreekv.py:1498-1516)."""
-    return linear(silu(linear(x, w1, prec), prec), w2, prec)
+def feed_forward(x, w1, w2, prec, tp=None):
+    """``FeedForward`` = Linear -> SiLU -> Linear (SF draftfreekv.py:1498-1516);
+    under ``tp`` the second Linear is row-parallel (``row_parallel_linear``)."""
+    return row_parallel_linear(silu(linear(x, w1, prec), prec), w2, prec, tp)
 
 
-def state_encoder(hidden, W, prec, eps=1e-6):
+def state_encoder(hidden, W, prec, eps=1e-6, tp=None):
     """``DraftStateEncoder.forward`` (SF draftfreekv.py:1533-1540).
 
     hidden: [B, L_tap, H] -> [B, H]."""
     b = hidden.shape[0]
     x = hidden.reshape(b, -1)
     y = feed_forward(x, W["draft_state_encoder.proj.net.0.weight"],
-                     W["draft_state_encoder.proj.net.2.weight"], prec)
+                     W["draft_state_encoder.proj.net.2.weight"], prec, tp)
     return rmsnorm_hf(y, W["draft_state_encoder.norm.weight"], eps, prec)
 
 
-def shifted_input(anchors, latest, W, block, mask_token_id, prec, eps=1e-6):
+def shifted_input(anchors, latest, W, block, mask_token_id, prec, eps=1e-6, tp=None):
     """``ParallelShiftedInput.forward`` (SF draftfreekv.py:1658-1739).
 
     Token layout ``[x_t, MASK, ...]`` embedded with the target embedding, plus
@@ -130,7 +157,7 @@ def shifted_input(anchors, latest, W, block, mask_token_id, prec, eps=1e-6):
     lat = np.broadcast_to(latest[:, None, :], tok.shape)
     x = np.concatenate([tok, lat], axis=-1)
     y = feed_forward(x, W["parallel_shifted_input.proj.net.0.weight"],
-                     W["parallel_shifted_input.proj.net.2.weight"], prec)
+                     W["parallel_shifted_input.proj.net.2.weight"], prec, tp)
     return rmsnorm_hf(y, W["parallel_shifted_input.norm.weight"], eps, prec)
 
 
@@ -270,7 +297,7 @@ def attend(q, k_loc, v_loc, qg, summary_out, win_k, win_v, win_len, prec):
 # Decoder layer, logits, sampling
 # ----------------------------------------------------------------------------
 
-def decoder_layer(h, cos, sin, Wl, view, shape, prec):
+def decoder_layer(h, cos, sin, Wl, view, shape, prec, tp=None):
     """One drafter decoder layer.
 
     ``Qwen3KVFreeParallelDecoderLayer.forward_global16_raw256`` (SF
@@ -281,7 +308,10 @@ def decoder_layer(h, cos, sin, Wl, view, shape, prec):
     fused ``SiluAndMul``, SP global16_native_draft_executor.py:628-633, rounds once
     instead; this restatement follows the PyTorch drafter it is pinned against.)
 
-    h [B, P, H]; view = dict(qg, summary_out, win_k, win_v, win_len)."""
+    h [B, P, H]; view = dict(qg, summary_out, win_k, win_v, win_len).  Under
+    ``tp`` the o_proj and down_proj are row-parallel (``row_parallel_linear``);
+    head-parallel attention and column-parallel projections compute the same
+    values as one GPU."""
     b, p, hdim = h.shape
     hq, hkv, d = shape.q_heads, shape.kv_heads, shape.head_dim
     eps = shape.rms_eps
@@ -297,12 +327,12 @@ def decoder_layer(h, cos, sin, Wl, view, shape, prec):
     a = attend(q, k, v, view["qg"], view["summary_out"], view["win_k"], view["win_v"],
                view["win_len"], prec)
     a = np.ascontiguousarray(a.transpose(0, 2, 1, 3)).reshape(b, p, hq * d)
-    h = rnd(h + linear(a, Wl["self_attn.o_proj.weight"], prec), prec)
+    h = rnd(h + row_parallel_linear(a, Wl["self_attn.o_proj.weight"], prec, tp), prec)
     x = rmsnorm_hf(h, Wl["post_attention_layernorm.weight"], eps, prec)
     gate = linear(x, Wl["mlp.gate_proj.weight"], prec)
     up = linear(x, Wl["mlp.up_proj.weight"], prec)
     act = rnd(silu(gate, prec) * up, prec)
-    return rnd(h + linear(act, Wl["mlp.down_proj.weight"], prec), prec)
+    return rnd(h + row_parallel_linear(act, Wl["mlp.down_proj.weight"], prec, tp), prec)
 
 
 def project_logits(h, W, final_eps, prec):
@@ -502,22 +532,24 @@ def build_views(kv_k, kv_v, table, seq_lens, summary_out, learned_query, window,
     return views
 
 
-def draft_pass(W, shape, anchors, positions, hidden, views, inv_freq, prec):
+def draft_pass(W, shape, anchors, positions, hidden, views, inv_freq, prec, tp=None):
     """``_forward_parallel_shifted_qwen_global16_raw256`` (SF
     draftfreekv.py:3231-3353) followed by the logits projection: returns
     bf16-rounded (or fp32) base logits [B, P, V] and the final block states.
 
     anchors [B] (the last accepted token ``x_t``), positions [B] (its position,
     i.e. the committed length), hidden [B, L_tap, H] (boundary state), views: one
-    dict per drafter layer (see ``decoder_layer``)."""
-    latest = state_encoder(hidden, W, prec)
-    h = shifted_input(np.asarray(anchors), latest, W, shape.block, shape.mask_token_id, prec)
+    dict per drafter layer (see ``decoder_layer``).  ``tp = (world, wire)``: the
+    tensor-parallel split of the four row-parallel projections (state-encoder
+    and shifted-input second Linears, o_proj, down_proj)."""
+    latest = state_encoder(hidden, W, prec, tp=tp)
+    h = shifted_input(np.asarray(anchors), latest, W, shape.block, shape.mask_token_id, prec, tp=tp)
     pos = np.asarray(positions, dtype=np.int64)[:, None] + np.arange(shape.block)[None, :]
     cos, sin = rope_tables(pos, inv_freq, prec)
     j = 0
     while f"parallel_qwen_layers.{j}.self_attn.q_proj.weight" in W:
         Wl = {k[len(f"parallel_qwen_layers.{j}."):]: v for k, v in W.items()
               if k.startswith(f"parallel_qwen_layers.{j}.")}
-        h = decoder_layer(h, cos, sin, Wl, views[j], shape, prec)
+        h = decoder_layer(h, cos, sin, Wl, views[j], shape, prec, tp)
         j += 1
     return project_logits(h, W, shape.final_eps, prec), h
