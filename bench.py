@@ -53,6 +53,11 @@ def parse():
                     help="comma-separated context lengths of the sweep (the headline is the largest)")
     ap.add_argument("--batch-sweep", type=str, default="8,32,128",
                     help="BASELINE config 4 concurrency sweep: requests per GPU (contexts U[2K, 32K]); '' to skip")
+    ap.add_argument("--tp", action="store_true",
+                    help="BASELINE config 5: the 14B drafter tensor-parallel over the torchrun ranks (batch 32, 64K "
+                         "context), fused peer-store allreduce vs NCCL allreduce")
+    ap.add_argument("--tp-batch", type=int, default=32)
+    ap.add_argument("--tp-ctx", type=int, default=65536)
     return ap.parse_args()
 
 
@@ -532,6 +537,185 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_tp(args):
+    """one rank per GPU, the 14B-shaped drafter split by
+    KV-head group.  Times the whole round (refresh + pass + sharded Markov chain
+    + accept, one CUDA graph) with the row-parallel projections fused with the
+    peer-store allreduce (fp32 and bf16 partials) and with a plain GEMM followed
+    by an NCCL allreduce, plus the two decoder-layer projections alone."""
+    import torch
+    import torch.distributed as dist
+    from longspark_b200 import _native as N
+    from longspark_b200 import ops
+    from longspark_b200.config import CFG3
+    from longspark_b200.engine import GraphedDraft, ViewPools
+    from longspark_b200.synthetic import make_views, make_weights
+    from longspark_b200.tp import TPDraftEngine, dist_helpers, local_shape, shard_state_dict
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shape = CFG3.shape
+    batch, ctx = args.tp_batch, args.tp_ctx
+    loc = local_shape(shape, world)
+    if world > 1:
+        all_gather, bar = dist_helpers()
+    else:
+        all_gather, bar = (lambda b: [b]), (lambda: None)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    nvlink_gbs = 770.0  # measured peer copy per direction on this pool
+
+    gen = torch.Generator(device=dev).manual_seed(5)  # the same on every rank: replicated inputs agree
+    W = make_weights(shape, device=dev, gen=gen)
+    Wl = {k: t.clone() for k, t in shard_state_dict(W, shape, rank, world).items()}
+    del W
+    torch.cuda.empty_cache()
+    # this rank's heads of the paged pool and summary state, generated directly
+    v = make_views(loc, batch, ctx, device=dev, gen=gen, extra_rows=shape.max_commit)
+    pools = ViewPools(kv_k=v["kv_k"], kv_v=v["kv_v"], page_table=v["page_table"], summary_out=v["summary_out"],
+                      summary_lse=v["summary_lse"], hidden=v["hidden"])
+    commit = torch.full((batch,), shape.max_commit, dtype=torch.int32, device=dev)
+    target = torch.randint(0, shape.vocab, (batch, shape.block + 1), device=dev, generator=gen)
+    slots = torch.arange(batch, dtype=torch.int32, device=dev)
+    M = batch * shape.block
+
+    def round_ms(eng, graphed=True):
+        g = GraphedDraft(eng, batch, with_refresh=True, with_target=True, slots_are_rows=True)
+        g.load(slots=slots, seq_lens=v["seq_lens"], anchors=v["anchors"], page_table=v["page_table"],
+               commit_lens=commit, target=target)
+        if graphed:
+            g.capture()
+            ms = time_graph(g, args.steps, max(3, args.warmup), world)
+        else:
+            for _ in range(max(3, args.warmup)):
+                g._run()
+            torch.cuda.synchronize()
+            barrier(world)
+            st = torch.cuda.current_stream()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(args.steps):
+                g._run()
+            e1.record(st)
+            torch.cuda.synchronize()
+            barrier(world)
+            ms = e0.elapsed_time(e1) / args.steps
+        tokens = eng.buf["tokens"][:batch].clone()
+        del g
+        return dist_max(ms, world), tokens
+
+    def projections(eng, mode):
+        """us per launch of o_proj and down_proj with their allreduce (graph of
+        20 launches each; 'gemm' = the local GEMM alone, no reduction)."""
+        b, L = eng.buf, eng.w.layers[0]
+        out = {}
+        for name, x, w_ in (("o_proj", b["attn"], L["o"]), ("down_proj", b["act"], L["down"])):
+            def launch():
+                if mode == "fused":
+                    ops.gemm_allreduce(x, w_, b["h"], group=eng.group, workspace=eng.gemm_ws, wire=eng.wire,
+                                       epilogue=N.EPI_RESIDUAL, residual=b["h"], rows=M, status=b["status"])
+                elif mode == "nccl":
+                    ops.gemm(x, w_, b["g"], workspace=eng.gemm_ws, rows=M, status=b["status"])
+                    dist.all_reduce(b["g"][:M])
+                else:
+                    ops.gemm(x, w_, b["g"], workspace=eng.gemm_ws, rows=M, status=b["status"])
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    launch()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                for _ in range(20):
+                    launch()
+            for _ in range(3):
+                gr.replay()
+            torch.cuda.synchronize()
+            barrier(world)
+            st = torch.cuda.current_stream()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(10):
+                gr.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+            barrier(world)
+            out[name] = round(dist_max(e0.elapsed_time(e1) / 200 * 1e3, world), 2)
+            del gr
+        return out
+
+    results = {}
+    for mode, wire in (("fused", N.TP_WIRE_F32), ("fused", N.TP_WIRE_BF16), ("nccl", N.TP_WIRE_BF16)):
+        if mode == "nccl" and world == 1:
+            continue
+        eng = TPDraftEngine(shape, Wl, pools, batch, rank=rank, world=world, device=dev, all_gather=all_gather,
+                            barrier=bar, allreduce=mode, wire=wire, pg=dist.group.WORLD if world > 1 else None)
+        key = mode if mode == "nccl" else f"fused_{'bf16' if wire == N.TP_WIRE_BF16 else 'f32'}"
+        try:
+            ms, _ = round_ms(eng, graphed=True)
+            graphed = True
+        except RuntimeError as e:  # NCCL capture unsupported here: time it eagerly
+            if mode != "nccl":
+                raise
+            torch.cuda.synchronize()
+            ms, _ = round_ms(eng, graphed=False)
+            graphed = False
+        status = eng.device_status()
+        try:
+            proj = projections(eng, mode if world > 1 else "gemm")
+        except RuntimeError as e:
+            proj = {"error": str(e)[:200]}
+        gemm_only = projections(eng, "gemm") if key == "fused_f32" else None
+        results[key] = {"round_us": round(ms * 1e3, 1),
+                        "draft_tokens_per_s": round(M / (ms * 1e-3), 1), "graphed": graphed,
+                        "device_status": status, "projection_us": proj}
+        if gemm_only is not None:
+            results["gemm_only_projection_us"] = gemm_only
+        eng.close()
+        del eng
+        pools.summary_bf16 = None
+        torch.cuda.empty_cache()
+        barrier(world)
+
+    head = results["fused_f32"]
+    # fused projection roofline: the slower of the weight stream (HBM) and the
+    # NVLink bytes a rank must send (its partials of the tiles others own and
+    # the results of its own tiles to every other rank; receives are symmetric)
+    H = shape.hidden
+    roof = {}
+    for name, kdim in (("o_proj", loc.q_heads * 128), ("down_proj", loc.inter)):
+        wbytes = H * kdim * 2
+        link = (world - 1) / world * M * H * (4 + 2) if world > 1 else 0
+        t_us = max(wbytes / (hbm_peak * 1e9), link / (nvlink_gbs * 1e9)) * 1e6
+        got = head["projection_us"][name]
+        roof[name] = {"target_us": round(t_us, 2), "achieved_us": got, "frac": round(t_us / got, 3),
+                      "weight_bytes": wbytes, "nvlink_bytes_sent": int(link)}
+    if rank == 0:
+        line = {
+            "metric": "cfg5 TP drafter round: draft tokens/s per box (fused peer-store allreduce vs NCCL)",
+            "value": head["draft_tokens_per_s"], "unit": "draft tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(head["round_us"] / 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) paged K/V of this rank's heads)",
+            "config": {"workload": "cfg5-qwen3-14b drafter, tensor-parallel by KV-head group (BASELINE configs[4])",
+                       "batch": batch, "ctx": ctx, "tp": world, "hidden": shape.hidden, "q_heads": shape.q_heads,
+                       "kv_heads": shape.kv_heads, "inter": shape.inter, "vocab": shape.vocab,
+                       "window": shape.window, "slots": shape.slots, "verify_block": shape.block + 1,
+                       "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights and K/V of every round)",
+                       "nccl_nvls": os.environ.get("NCCL_NVLS_ENABLE", "default")},
+            "modes": results,
+            "projection_roofline": roof,
+            "projection_roofline_note": ("target = max(weight bytes / measured HBM copy GB/s, bytes this rank sends "
+                                         "over NVLink / 770 GB/s measured peer copy); fp32 partials + bf16 results"),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_reference(args):
     """The reference arm: the reference drafter's CPU path (numpy restatement,
     fp32) on the host cores, same metric/unit/config; rank 0 only."""
@@ -563,6 +747,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.tp:
+        run_tp(args)
     else:
         run_b200(args)
 
