@@ -255,12 +255,14 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
 // Tile t belongs to rank t % world.  A finished tile (this rank's k-slice) is
 // stored straight into the owner's exchange slot [t / world][this rank] with
 // peer stores, then flagged; no rank waits while it still has tiles to send.
-// After its own units, each CTA finalises the owned tiles assigned to it: it
-// waits for all `world` partials, sums them in rank order (the same bits
-// whatever the arrival order), applies the epilogue once and stores the bf16
-// result into every rank's output, then flags each rank.  Last, the CTA waits
-// for its share of the tiles other ranks own, so the kernel ends with this
-// rank's output complete.
+// After its own units, the CTAs finalise the owned tiles in units of
+// TP_GROUP tokens spread over the whole grid (so every SM pushes results over
+// NVLink): a unit waits for the tile's `world` partials, sums them in rank
+// order (the same bits whatever the arrival order), applies the epilogue once,
+// stores the bf16 result into every rank's output and flags each rank.  Last,
+// the epilogue threads wait for the groups other ranks own, so the kernel ends
+// with this rank's output complete.  Flags carry this launch's epoch + 1
+// (tp_common.cuh).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ size_t tp_tile_bytes(const GemmKernelParams& P) {
   return static_cast<size_t>(P.bn) * BM * (P.tp_wire == LS_TP_WIRE_BF16 ? 2 : 4);
@@ -292,10 +294,10 @@ __device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, 
 
 // After the last chunk of tile t (all 128 epilogue threads): release the
 // slot's stores to the owner.
-__device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int r) {
+__device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int r, uint32_t tgt) {
   fence_sys();
   epi_bar();
-  if (r == 0) st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), 1u);
+  if (r == 0) st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), tgt);
 }
 
 // Summed 16-token chunk of an owned tile: the STORE / RESIDUAL epilogue
@@ -331,30 +333,30 @@ __device__ __forceinline__ void tp_final_store(const GemmKernelParams& P, int m_
   }
 }
 
-__device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScratch* sc, volatile int* abort_flag) {
+__device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScratch* sc, volatile int* abort_flag,
+                                       uint32_t tgt) {
   const int W = P.tp.world, me = P.tp.rank;
   const int tiles = P.m_tiles * P.n_tiles;
+  const int rows = P.a.rows;
   int* status = P.a.status;
+  const int gpt = (P.bn + TP_GROUP - 1) / TP_GROUP;  // token groups per tile
   const int n_owned = tiles > me ? (tiles - me + W - 1) / W : 0;
-  for (int tl = blockIdx.x; tl < n_owned; tl += gridDim.x) {
+  const bool wire16 = P.tp_wire == LS_TP_WIRE_BF16;
+  for (int uu = blockIdx.x; uu < n_owned * gpt; uu += gridDim.x) {
+    const int tl = uu / gpt, gi = uu - tl * gpt;
     const int t = tl * W + me;
+    const int m_tile = t / P.n_tiles;
+    const int n0 = (t - m_tile * P.n_tiles) * P.bn;
+    const int c0 = gi * TP_GROUP;
+    if (n0 + c0 >= rows) continue;  // the tile's last rows do not exist
     if (r == 0) sc->flag = 1;
     epi_bar();
-    if (r < W) {
-      uint32_t* fl = tp_arrive_flag(P.tp, me, t, r);
-      if (wait_flag(fl, 1u, abort_flag, status))
-        *fl = 0u;
-      else
-        sc->flag = 0;
-    }
+    if (r < W && !wait_flag(tp_arrive_flag(P.tp, me, t, r), tgt, abort_flag, status)) sc->flag = 0;
     epi_bar();
     const bool go = sc->flag != 0;
     epi_bar();
     if (!go) return;
-    const int m_tile = t / P.n_tiles;
-    const int n0 = (t - m_tile * P.n_tiles) * P.bn;
-    const bool wire16 = P.tp_wire == LS_TP_WIRE_BF16;
-    for (int c = 0; c < P.bn && n0 + c < P.a.rows; c += 16) {
+    for (int c = c0; c < c0 + TP_GROUP && c < P.bn && n0 + c < rows; c += 16) {
       float v[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = 0.0f;
@@ -388,16 +390,13 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
     }
     fence_sys();
     epi_bar();
-    if (r < W && r != me) st_release_sys(tp_done_flag(P.tp, r, t), 1u);
+    if (r < W && r != me) st_release_sys(tp_done_flag(P.tp, r, t, gi), tgt);
   }
-  // this rank's copies of the tiles the other ranks own
-  if (r == 0) {
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-      if (t % W == me) continue;
-      uint32_t* fl = tp_done_flag(P.tp, me, t);
-      if (!wait_flag(fl, 1u, abort_flag, status)) break;
-      *fl = 0u;
-    }
+  // this rank's copies of the groups the other ranks own, one wait per thread
+  for (int q = blockIdx.x * 128 + r; q < tiles * gpt; q += gridDim.x * 128) {
+    const int t = q / gpt, gi = q - t * gpt;
+    if (t % W == me || (t % P.n_tiles) * P.bn + gi * TP_GROUP >= rows) continue;
+    if (!wait_flag(tp_done_flag(P.tp, me, t, gi), tgt, abort_flag, status)) break;
   }
 }
 
@@ -640,6 +639,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int r = ew * 32 + lane;
     // Residual/base reads and all writes wait for the previous kernel.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // TP launch: the epoch value this launch's flags carry (the previous
+    // launch's last CTA advanced the counter before that launch completed)
+    const uint32_t tp_tgt =
+        P.tp.world > 0 ? *reinterpret_cast<volatile uint32_t*>(tp_epoch_word(P.tp, TP_GEMM_EPOCH)) + 1u : 0u;
     int acc = 0;
     uint32_t acc_phase = 0u;  // bit i: phase parity of accumulator buffer i
     long long u = u0;
@@ -672,7 +675,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
-        if (P.tp.world > 0) tp_publish(P, t, r);
+        if (P.tp.world > 0) tp_publish(P, t, r, tp_tgt);
       } else {
         // Partial tile: park the fp32 partial, the last contributor reduces.
         const int slot = (t == t_first) ? 0 : 1;
@@ -702,14 +705,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int first_slot = unit_begin(first, U, G) == tu0 ? 0 : 1;
           reduce_tile(P, t, first, last, first_slot, r, ew, sc);
           if (r == 0) atomicExch(&P.counters[t], 0);
-          if (P.tp.world > 0) tp_publish(P, t, r);
+          if (P.tp.world > 0) tp_publish(P, t, r, tp_tgt);
         }
       }
       acc_phase ^= 1u << acc;
       acc ^= 1;
       u += k1 - k0;
     }
-    if (P.tp.world > 0 && !*abort_flag) tp_finish(P, r, sc, abort_flag);
+    if (P.tp.world > 0) {
+      if (!*abort_flag) tp_finish(P, r, sc, abort_flag, tp_tgt);
+      // the last CTA out advances this rank's GEMM epoch for the next launch
+      epi_bar();
+      if (r == 0) {
+        uint32_t* exits = tp_epoch_word(P.tp, TP_GEMM_EXITS);
+        if (atomicAdd(exits, 1u) == gridDim.x - 1) {
+          *exits = 0u;
+          *tp_epoch_word(P.tp, TP_GEMM_EPOCH) = tp_tgt;
+        }
+      }
+    }
   }
 
   tc_fence_before();

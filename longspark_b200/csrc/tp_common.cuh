@@ -3,20 +3,23 @@
 //
 // Layout of the sync region every rank keeps in its symmetric heap (at
 // ls_tp_group.sync_offset), all counters uint32:
-//   TP_EPOCH_OFF     epoch[16]              this rank's barrier epochs, by slot
-//   TP_BAR_FLAG_OFF  bar[16][8]             epoch each source rank reached, by slot
+//   TP_EPOCH_OFF     epoch[16]               this rank's barrier epochs, by slot
+//                    [32] GEMM epoch, [33] GEMM exit counter
+//   TP_BAR_FLAG_OFF  bar[16][8]              epoch each source rank reached, by slot
 //   TP_ARRIVE_OFF    arrive[TP_MAX_TILES][8] owner side: source rank's partial of tile t landed
-//   TP_DONE_OFF      done[TP_MAX_TILES]     receiver side: tile t's owner stored the result here
+//   TP_DONE_OFF      done[TP_MAX_TILES][8]   receiver side: the owner stored token group g of tile t here
 //   TP_XCH_OFF       exchange slots of the row-parallel GEMMs (sized per call)
 //
 // Protocol: a producer stores data into the consumer's heap with plain peer
 // stores, then every storing thread issues fence.acq_rel.sys, the CTA
 // synchronises, and one thread sets the flag with st.release.sys.  The
 // consumer polls the flag (in its own memory) with ld.acquire.sys, bounded by
-// LS_PEER_WAIT_NS, and clears arrive/done flags after reading them.  A flag is
-// set again only after its consumer has passed a later point of the same
-// launch sequence (every rank takes part in every TP launch), so a clear never
-// races with the next set.
+// LS_PEER_WAIT_NS.  Flags carry epochs, never cleared: every rank counts its
+// fused-GEMM launches (the last CTA of a launch bumps the GEMM epoch), all
+// ranks make the same launches in the same order, so launch e sets and waits
+// for the value e + 1 everywhere.  A rank cannot set a flag for launch e + 1
+// before every rank has finished launch e (each launch ends by waiting for
+// every other rank's results), so a wait never sees a later launch's flag.
 #pragma once
 
 #include "../../include/longspark_b200.h"
@@ -31,11 +34,16 @@ namespace ls {
 constexpr int TP_MAX_TILES = 4096;
 constexpr int TP_BARRIER_SLOTS = 16;
 constexpr size_t TP_EPOCH_OFF = 0;
+constexpr int TP_GEMM_EPOCH = 32;   // index in the epoch words
+constexpr int TP_GEMM_EXITS = 33;
+constexpr int TP_GROUP = 32;        // tokens per finalisation unit
+constexpr int TP_MAX_GROUPS = 8;    // 256-token tiles / TP_GROUP
 constexpr size_t TP_BAR_FLAG_OFF = 256;
 constexpr size_t TP_ARRIVE_OFF = 4096;
 constexpr size_t TP_DONE_OFF = TP_ARRIVE_OFF + static_cast<size_t>(TP_MAX_TILES) * LS_TP_MAX_RANKS * 4;
-constexpr size_t TP_XCH_OFF = TP_DONE_OFF + static_cast<size_t>(TP_MAX_TILES) * 4;
+constexpr size_t TP_XCH_OFF = TP_DONE_OFF + static_cast<size_t>(TP_MAX_TILES) * TP_MAX_GROUPS * 4;
 static_assert(TP_XCH_OFF % 256 == 0, "exchange slots must stay 256-byte aligned");
+static_assert((TP_GEMM_EXITS + 1) * 4 <= TP_BAR_FLAG_OFF, "epoch words overlap the barrier flags");
 static_assert(TP_BAR_FLAG_OFF + TP_BARRIER_SLOTS * LS_TP_MAX_RANKS * 4 <= TP_ARRIVE_OFF, "barrier flags overlap");
 
 struct TpView {
@@ -86,8 +94,12 @@ __device__ __forceinline__ uint32_t* tp_arrive_flag(const TpView& v, int owner, 
   return reinterpret_cast<uint32_t*>(v.sync[owner] + TP_ARRIVE_OFF) + static_cast<size_t>(tile) * LS_TP_MAX_RANKS + src;
 }
 
-__device__ __forceinline__ uint32_t* tp_done_flag(const TpView& v, int dst, int tile) {
-  return reinterpret_cast<uint32_t*>(v.sync[dst] + TP_DONE_OFF) + tile;
+__device__ __forceinline__ uint32_t* tp_done_flag(const TpView& v, int dst, int tile, int group) {
+  return reinterpret_cast<uint32_t*>(v.sync[dst] + TP_DONE_OFF) + static_cast<size_t>(tile) * TP_MAX_GROUPS + group;
+}
+
+__device__ __forceinline__ uint32_t* tp_epoch_word(const TpView& v, int idx) {
+  return reinterpret_cast<uint32_t*>(v.sync[v.rank] + TP_EPOCH_OFF) + idx;
 }
 
 // Host side: validate an ls_tp_group and build the device view.

@@ -152,3 +152,33 @@ def test_two_rank_row_parallel_projections_gloo():
         res = dict(out)
     for r in range(world):
         assert all(res[r].values()), res[r]
+
+
+def test_tp_entry_points_validate_without_gpu():
+    """Argument errors come back as status codes before any CUDA call."""
+    import ctypes as C
+
+    from longspark_b200 import _native as N
+    lib = N.lib()
+    assert lib.ls_tp_sync_bytes(2, 480, 5120, N.TP_WIRE_F32) > lib.ls_tp_sync_bytes(2, 480, 5120, N.TP_WIRE_BF16)
+    assert lib.ls_tp_sync_bytes(0, 480, 5120, 0) == 0
+    assert lib.ls_tp_sync_bytes(9, 480, 5120, 0) == 0
+    assert lib.ls_tp_sync_bytes(2, 480, 5000, 0) == 0  # n_out not a multiple of 128
+    assert lib.ls_tp_sync_bytes(2, 480, 5120, 7) == 0  # unknown wire format
+    # exchange slots: ceil(tiles / world) * world slots of one 256-token tile each
+    tiles = 40 * 2
+    assert lib.ls_tp_sync_bytes(8, 480, 5120, 0) - lib.ls_tp_sync_bytes(8, 480, 5120, 1) == \
+        (tiles + 7) // 8 * 8 * 256 * 128 * 2
+    g = N.TpGroup(world=0, rank=0, heap=(C.c_void_p * 8)(), heap_bytes=1 << 20, sync_offset=0)
+    a = N.GemmArgs()
+    assert lib.ls_gemm_allreduce(None, C.byref(a), C.byref(g), 0, None, 0) == 1
+    assert b"world" in lib.ls_last_error()
+    heaps = (C.c_void_p * 8)(0x100000, 0x200000)
+    g = N.TpGroup(world=2, rank=1, heap=heaps, heap_bytes=1 << 20, sync_offset=0)
+    a.epilogue = N.EPI_QKV
+    assert lib.ls_gemm_allreduce(None, C.byref(a), C.byref(g), 0, None, 0) == 3  # unsupported epilogue
+    assert lib.ls_tp_barrier(None, C.byref(g), 16, None) == 1  # slot out of range
+    m = N.MarkovArgs(base=0x100100, tile_max=0x100200, tile_arg=0x100300, vocab=4096, batch=1, block=1)
+    assert lib.ls_markov_argmax_tp(None, C.byref(m), C.byref(g), 8, None, 0) == 1  # 16 tiles cannot cover 32
+    g.sync_offset = 100  # not 256-byte aligned
+    assert lib.ls_tp_barrier(None, C.byref(g), 0, None) == 1
