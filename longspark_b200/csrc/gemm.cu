@@ -293,11 +293,15 @@ __device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, 
 }
 
 // After the last chunk of tile t (all 128 epilogue threads): release the
-// slot's stores to the owner.
+// slot's stores to the owner.  The named barrier orders every epilogue
+// thread's stores before thread 0's system-scope fence, which is cumulative
+// over them, so one fence per tile publishes the whole slot.
 __device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int r, uint32_t tgt) {
-  fence_sys();
   epi_bar();
-  if (r == 0) st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), tgt);
+  if (r == 0) {
+    fence_sys();
+    st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), tgt);
+  }
 }
 
 // Summed 16-token chunk of an owned tile: the STORE / RESIDUAL epilogue
@@ -388,9 +392,21 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
       }
       tp_final_store(P, m_tile, n0 + c, v, r);
     }
-    fence_sys();
-    epi_bar();
-    if (r < W && r != me) st_release_sys(tp_done_flag(P.tp, r, t, gi), tgt);
+  }
+  // one system-scope fence for all of this CTA's finalised groups, then their
+  // done flags on every other rank
+  epi_bar();
+  if (r == 0) fence_sys();
+  epi_bar();
+  const int cta = static_cast<int>(blockIdx.x), grid = static_cast<int>(gridDim.x);
+  const int my_units = cta < n_owned * gpt ? (n_owned * gpt - cta + grid - 1) / grid : 0;
+  for (int k = r; k < my_units * W; k += 128) {
+    const int uu = cta + (k / W) * grid;
+    const int dst = k - (k / W) * W;
+    const int tl = uu / gpt, gi = uu - tl * gpt;
+    const int t = tl * W + me;
+    if (dst == me || (t % P.n_tiles) * P.bn + gi * TP_GROUP >= rows) continue;
+    st_release_sys(tp_done_flag(P.tp, dst, t, gi), tgt);
   }
   // this rank's copies of the groups the other ranks own, one wait per thread
   for (int q = blockIdx.x * 128 + r; q < tiles * gpt; q += gridDim.x * 128) {
