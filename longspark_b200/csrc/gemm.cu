@@ -775,12 +775,26 @@ struct GemmPlan {
   size_t partial_bytes, counter_bytes;
 };
 
+// Token tile: as wide as the tokens (up to 256), halved (down to 64) while the
+// grid would have fewer output tiles than SMs (twice the SMs for k <= 1024):
+// with few tiles every tile is split along k, and the fp32 partial round
+// trips of the split tiles cost more than the extra weight re-reads of a
+// narrower tile (measured at 480 tokens: o_proj-like 5120 x 2560 58 -> 50 us,
+// 5120 x 640 72 -> 32 us; wide shapes keep 256).
+static int plan_bn(int rows, int k, int n_out, int sms) {
+  int bn = pick_bn(rows);
+  const long long m_tiles = n_out / BM;
+  const long long want = (k <= 1024 ? 2LL : 1LL) * sms;
+  while (bn > 64 && m_tiles * ((rows + bn - 1) / bn) < want) bn /= 2;
+  return bn;
+}
+
 static GemmPlan plan_gemm(int rows, int k, int n_out) {
   GemmPlan p{};
-  p.bn = pick_bn(rows);
+  const int sms = host_sm_count();
+  p.bn = plan_bn(rows, k, n_out, sms);
   p.n_tiles = (rows + p.bn - 1) / p.bn;
   p.m_tiles = n_out / BM;
-  const int sms = host_sm_count();
   // Pipeline stages of up to 4 k-blocks (64 KiB of weights): HBM streams best
   // with a few large requests in flight per SM.  Smaller stages when the tile
   // count is low (stream-K balance) or the token tile is wide (shared memory).
@@ -931,10 +945,17 @@ extern "C" size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire) {
   if (world < 1 || world > LS_TP_MAX_RANKS || rows <= 0 || n_out <= 0 || n_out % BM ||
       (wire != LS_TP_WIRE_F32 && wire != LS_TP_WIRE_BF16))
     return 0;
-  const int bn = pick_bn(rows);
-  const long long tiles = static_cast<long long>(n_out / BM) * ((rows + bn - 1) / bn);
-  const long long owned = (tiles + world - 1) / world;
-  return TP_XCH_OFF + static_cast<size_t>(owned) * world * bn * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);
+  // the exchange slots of any token tile the plan can pick for these rows
+  // (plan_bn halves pick_bn down to 64 depending on k)
+  size_t need = 0;
+  for (int bn = pick_bn(rows);; bn /= 2) {
+    const long long tiles = static_cast<long long>(n_out / BM) * ((rows + bn - 1) / bn);
+    const long long owned = (tiles + world - 1) / world;
+    const size_t b = static_cast<size_t>(owned) * world * bn * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);
+    need = b > need ? b : need;
+    if (bn <= 64) break;
+  }
+  return TP_XCH_OFF + need;
 }
 
 extern "C" int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_tp_group* g, int wire, void* workspace,
