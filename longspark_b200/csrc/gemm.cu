@@ -781,11 +781,18 @@ struct GemmPlan {
 // trips of the split tiles cost more than the extra weight re-reads of a
 // narrower tile (measured at 480 tokens: o_proj-like 5120 x 2560 58 -> 50 us,
 // 5120 x 640 72 -> 32 us; wide shapes keep 256).
+// Next narrower token tile: half, rounded up to a multiple of 16 (the MMA N
+// step and the epilogue's 16-token chunk), never below 64.
+static int narrower_bn(int bn) {
+  const int h = (bn / 2 + 15) / 16 * 16;
+  return h < 64 ? 64 : h;
+}
+
 static int plan_bn(int rows, int k, int n_out, int sms) {
   int bn = pick_bn(rows);
   const long long m_tiles = n_out / BM;
   const long long want = (k <= 1024 ? 2LL : 1LL) * sms;
-  while (bn > 64 && m_tiles * ((rows + bn - 1) / bn) < want) bn /= 2;
+  while (bn > 64 && m_tiles * ((rows + bn - 1) / bn) < want) bn = narrower_bn(bn);
   return bn;
 }
 
@@ -946,9 +953,9 @@ extern "C" size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire) {
       (wire != LS_TP_WIRE_F32 && wire != LS_TP_WIRE_BF16))
     return 0;
   // the exchange slots of any token tile the plan can pick for these rows
-  // (plan_bn halves pick_bn down to 64 depending on k)
+  // (plan_bn narrows pick_bn down to 64 depending on k)
   size_t need = 0;
-  for (int bn = pick_bn(rows);; bn /= 2) {
+  for (int bn = pick_bn(rows);; bn = narrower_bn(bn)) {
     const long long tiles = static_cast<long long>(n_out / BM) * ((rows + bn - 1) / bn);
     const long long owned = (tiles + world - 1) / world;
     const size_t b = static_cast<size_t>(owned) * world * bn * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);

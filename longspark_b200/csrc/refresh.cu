@@ -228,23 +228,29 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
     }
     __syncwarp();
     // State update: lanes cover the 128 dims as float4; the lane's 4 dims of
-    // every new V row stay in registers (packed bf16), the weights of a slot
-    // come as float4 broadcasts.  Rows are folded in order r = 0, 1, ...
+    // every new V row are converted to fp32 once per 8-row block, the weights
+    // of a slot come as float4 broadcasts, and each weight is applied to two
+    // dims per packed FMA (the same fmaf per element as a scalar loop).  Rows
+    // are folded in order r = 0, 1, ...
     const int c4 = (c + 3) & ~3;  // weights beyond c are zero (masked above)
     for (int r0 = 0; r0 < c; r0 += 8) {
-      uint2 vr[8];
+      float2 v01[8], v23[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) vr[r] = *reinterpret_cast<const uint2*>(&sm.v[r0 + r][lane * 4]);
+      for (int r = 0; r < 8; ++r) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(&sm.v[r0 + r][lane * 4]);
+        v01[r] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        v23[r] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+      }
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int sl = warp * 16 + i;
-        float4 oi = o[i];
+        float2 a01 = make_float2(o[i].x, o[i].y), a23 = make_float2(o[i].z, o[i].w);
         if (r0 == 0) {
           const float pw = sm.prior_w[sl];
-          oi.x *= pw;
-          oi.y *= pw;
-          oi.z *= pw;
-          oi.w *= pw;
+          a01.x *= pw;
+          a01.y *= pw;
+          a23.x *= pw;
+          a23.y *= pw;
         }
 #pragma unroll
         for (int rq = 0; rq < 8; rq += 4) {
@@ -253,16 +259,13 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
             const float ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr[rq + e].x));
-              const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr[rq + e].y));
-              oi.x += ws[e] * v01.x;
-              oi.y += ws[e] * v01.y;
-              oi.z += ws[e] * v23.x;
-              oi.w += ws[e] * v23.y;
+              const float2 w2 = make_float2(ws[e], ws[e]);
+              a01 = ffma2(w2, v01[rq + e], a01);
+              a23 = ffma2(w2, v23[rq + e], a23);
             }
           }
         }
-        o[i] = oi;
+        o[i] = make_float4(a01.x, a01.y, a23.x, a23.y);
       }
     }
 #pragma unroll

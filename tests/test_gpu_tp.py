@@ -1,8 +1,9 @@
-"""Tensor-parallel drafting on 2 GPUs (one process per GPU): the fused
-row-parallel GEMM + peer-store allreduce, the vocabulary-sharded Markov chain,
-and the whole round against the oracle (fused and NCCL allreduce).  Skipped
-with fewer than 2 GPUs."""
+"""Tensor-parallel drafting on 2 GPUs (one process per GPU; LS_TP_TEST_WORLD
+= 4 or 8 runs the same tests over more ranks): the fused row-parallel GEMM +
+peer-store allreduce, the vocabulary-sharded Markov chain, and the whole round
+against the oracle (fused and NCCL allreduce).  Skipped with fewer GPUs."""
 
+import os
 import socket
 
 import pytest
@@ -13,7 +14,7 @@ import tp_workers
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+WORLD = int(os.environ.get("LS_TP_TEST_WORLD", "2"))
 
 
 @pytest.fixture(autouse=True)

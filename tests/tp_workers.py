@@ -20,7 +20,8 @@ from longspark_b200.synthetic import make_views, make_weights, rope_inv_freq
 from longspark_b200.tp import (SymmetricHeap, TPDraftEngine, TPGroup, dist_helpers, shard_state_dict, shard_views,
                                vocab_shards)
 
-TP_SMALL = DraftShape(hidden=1024, q_heads=16, kv_heads=4, inter=2048, vocab=32768, tap_layers=2, draft_layers=1,
+# splits over 2, 4 and 8 ranks (8 KV heads, 1024 = 8 x 128 hidden, 256 vocabulary tiles)
+TP_SMALL = DraftShape(hidden=1024, q_heads=16, kv_heads=8, inter=2048, vocab=32768, tap_layers=2, draft_layers=1,
                       slots=64, window=512, block=15, max_commit=16, markov_rank=64, mask_token_id=32000)
 
 
@@ -62,7 +63,7 @@ GEMM_CASES = [  # rows, k (total), n_out, epilogue, wire
     (37, 1536, 640, "residual", "bf16"),
     (480, 2048, 1024, "residual", "f32"),
     (480, 1024, 2048, "store", "bf16"),
-    (3, 640, 256, "store", "f32"),
+    (3, 1024, 256, "store", "f32"),
 ]
 
 
