@@ -33,6 +33,9 @@ def _rand(*shape, std=1.0):
     (300, 256, 384),       # two token tiles of 256
     (16, 20480, 4096),     # state-encoder shape (5 taps x 4096)
     (16, 4096, 151936),    # vocabulary projection
+    (480, 256, 65664),     # wide 256-row tiles, odd block count (513): the last tile has one block
+    (480, 2560, 5120),     # narrowed token tile (128)
+    (480, 640, 5120),      # narrowed token tile (64), short k
 ])
 def test_gemm_store_matches_fp32(rows, k, n):
     x = _rand(rows, k)
@@ -110,8 +113,10 @@ def test_gemm_qkv_norm_rope():
     assert_bf16_close(to_np(out), ref, steps=1.0, exact_frac=0.95, what="qkv")
 
 
-def test_gemm_lm_head_tile_argmax():
-    rows, k, v = 15, 512, 1024 * 8
+@pytest.mark.parametrize("rows,k,v", [(15, 512, 1024 * 8), (300, 512, 151936)])
+def test_gemm_lm_head_tile_argmax(rows, k, v):
+    """Per-128-token tile maxima; (300, 512, 151936) runs the wide 256-row
+    tiles over the odd 1187-block vocabulary."""
     x = _rand(rows, k)
     w = _rand(v, k, std=0.05)
     out = torch.empty(rows, v, dtype=torch.bfloat16, device="cuda")
@@ -157,7 +162,8 @@ def test_gemms_of_different_shapes_share_one_workspace():
         assert_bf16_close(to_np(out), to_np(ref), steps=1.0, exact_frac=0.97, what=f"shared ws {rows}x{k}x{n}")
 
 
-@pytest.mark.parametrize("rows,k,n", [(15, 4096, 4096), (1, 20480, 4096), (16, 4096, 151936), (300, 256, 384)])
+@pytest.mark.parametrize("rows,k,n", [(15, 4096, 4096), (1, 20480, 4096), (16, 4096, 151936), (300, 256, 384),
+                                      (480, 256, 65664)])
 def test_tiled_weights_match_row_major(rows, k, n):
     """The tensor-core tile layout streams the same weights: results are bit-identical."""
     x = _rand(rows, k)
