@@ -58,6 +58,10 @@ def parse():
                          "context), fused peer-store allreduce vs NCCL allreduce")
     ap.add_argument("--tp-batch", type=int, default=32)
     ap.add_argument("--tp-ctx", type=int, default=65536)
+    ap.add_argument("--calls", action="store_true",
+                    help="diagnostic: device time of every native call of one eager round (one GPU), not a bench line")
+    ap.add_argument("--calls-shape", default="cfg2", help="cfg2, or cfg5-tpN: the per-rank shapes of config 5 at TP N")
+    ap.add_argument("--calls-ctx", type=int, default=4096)
     return ap.parse_args()
 
 
@@ -716,6 +720,57 @@ def run_tp(args):
         dist.destroy_process_group()
 
 
+def run_calls(args):
+    """Per-native-call device time of an eager round on one GPU: CUDA events
+    around every C-ABI call, median over ``--steps`` rounds (first discarded).
+    ``--calls-shape cfg5-tpN`` uses the per-rank shapes of config 5 at TP N
+    (that rank's heads and intermediate slice, the full vocabulary)."""
+    import torch
+    from longspark_b200 import _native as N
+    from longspark_b200.config import CFG2, CFG3
+    from longspark_b200.tp import local_shape
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.calls_shape == "cfg2":
+        shape = CFG2.shape
+    elif args.calls_shape.startswith("cfg5-tp"):
+        shape = local_shape(CFG3.shape, int(args.calls_shape[len("cfg5-tp"):]))
+    else:
+        raise SystemExit(f"unknown --calls-shape {args.calls_shape}")
+    eng, g, v = build_round(shape, args.calls_ctx, args.batch, dev, seed=1000)
+    orig = N.call
+    records = []
+
+    def timed(name, *a):
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        r = orig(name, *a)
+        e1.record(st)
+        records.append((name, e0, e1))
+        return r
+
+    N.call = timed
+    per = {}
+    try:
+        for _ in range(max(2, min(args.steps, 20))):
+            records.clear()
+            g._run()
+            torch.cuda.synchronize()
+            for i, (name, e0, e1) in enumerate(records):
+                per.setdefault((i, name), []).append(e0.elapsed_time(e1) * 1e3)
+    finally:
+        N.call = orig
+    print(f"# {args.calls_shape}: {shape.q_heads} q / {shape.kv_heads} KV heads, H={shape.hidden}, I={shape.inter}, "
+          f"V={shape.vocab}, batch {args.batch}, ctx {args.calls_ctx}; median us per call (eager, events)")
+    tot = 0.0
+    for (i, name), ts in sorted(per.items()):
+        m = statistics.median(ts[1:])
+        tot += m
+        print(f"{i:2d} {name:28s} {m:9.1f}")
+    print(f"sum {tot:.1f} us; device status {eng.device_status()}")
+
+
 def run_reference(args):
     """The reference arm: the reference drafter's CPU path (numpy restatement,
     fp32) on the host cores, same metric/unit/config; rank 0 only."""
@@ -749,6 +804,8 @@ def main():
         run_reference(args)
     elif args.tp:
         run_tp(args)
+    elif args.calls:
+        run_calls(args)
     else:
         run_b200(args)
 

@@ -277,22 +277,46 @@ __device__ __forceinline__ uint8_t* tp_slot(const GemmKernelParams& P, int t, in
   return P.tp.sync[t % W] + TP_XCH_OFF + (static_cast<size_t>(t / W) * W + src) * tp_tile_bytes(P);
 }
 
-// Chunk [c, c + 16) of tile t (first token n0) into the owner's slot.
+// Chunk [c, c + 16) of tile t (first token n0) into the owner's slot
+// ([token][128 features], fp32 or bf16).  The chunk goes through the
+// epilogue scratch first so that every thread sends 16 contiguous bytes and a
+// warp instruction writes 512 contiguous bytes across NVLink (one token row
+// per thread would give 128- or 64-byte writes).  All 128 epilogue threads.
+constexpr int TP_STAGE_PITCH_F = 132;   // fp32 stage row pitch (528 B, 16-byte aligned)
+constexpr int TP_STAGE_PITCH_H = 136;   // bf16 stage row pitch (272 B)
+static_assert(16 * TP_STAGE_PITCH_F * 4 <= sizeof(float) * 128 * 17, "TP stage must fit the epilogue scratch");
+static_assert(sizeof(EpiScratch) + 15 <= EPI_SCRATCH_BYTES, "epilogue scratch slack for its 16-byte alignment");
+
 __device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, int n0, int c, const float (&v)[16],
-                                              int r) {
+                                              int r, EpiScratch* sc) {
   uint8_t* slot = tp_slot(P, t, P.tp.rank);
   const int lim = P.a.rows - n0 - c;  // tokens of the chunk that exist
   if (P.tp_wire == LS_TP_WIRE_BF16) {
-    bf16* s = reinterpret_cast<bf16*>(slot) + static_cast<size_t>(c) * BM + r;
+    bf16* sg = reinterpret_cast<bf16*>(&sc->xch[0][0]);
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < lim) s[j * BM] = __float2bfloat16_rn(v[j]);
+    for (int j = 0; j < 16; ++j) sg[j * TP_STAGE_PITCH_H + r] = __float2bfloat16_rn(v[j]);
+    epi_bar();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int idx = r + i * 128, j = idx >> 4, q = idx & 15;  // token j, features 8q..8q+7
+      if (j < lim)
+        *reinterpret_cast<uint4*>(slot + (static_cast<size_t>(c + j) * BM + 8 * q) * 2) =
+            *reinterpret_cast<const uint4*>(&sg[j * TP_STAGE_PITCH_H + 8 * q]);
+    }
   } else {
-    float* s = reinterpret_cast<float*>(slot) + static_cast<size_t>(c) * BM + r;
+    float* sg = &sc->xch[0][0];
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < lim) s[j * BM] = v[j];
+    for (int j = 0; j < 16; ++j) sg[j * TP_STAGE_PITCH_F + r] = v[j];
+    epi_bar();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = r + i * 128, j = idx >> 5, q = idx & 31;  // token j, features 4q..4q+3
+      if (j < lim)
+        *reinterpret_cast<float4*>(slot + (static_cast<size_t>(c + j) * BM + 4 * q) * 4) =
+            *reinterpret_cast<const float4*>(&sg[j * TP_STAGE_PITCH_F + 4 * q]);
+    }
   }
+  epi_bar();  // the stage is reused by the next chunk
 }
 
 // After the last chunk of tile t (all 128 epilogue threads): release the
@@ -308,9 +332,11 @@ __device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int
 }
 
 // Summed 16-token chunk of an owned tile: the STORE / RESIDUAL epilogue
-// (residual from this rank's copy), stored into every rank's output.
+// (residual from this rank's copy), stored into every rank's output through
+// the epilogue scratch, 16 contiguous bytes per thread.  All 128 epilogue
+// threads.
 __device__ __forceinline__ void tp_final_store(const GemmKernelParams& P, int m_tile, int n0, const float (&v)[16],
-                                               int r) {
+                                               int r, EpiScratch* sc) {
   const ls_gemm_args& a = P.a;
   const int f = m_tile * BM + r;
   const bool res = a.epilogue == LS_EPI_RESIDUAL;
@@ -325,17 +351,25 @@ __device__ __forceinline__ void tp_final_store(const GemmKernelParams& P, int m_
       add[j] = __bfloat162float(src[(long long)tok * a.res_ld + f]);
     }
   }
-  bf16 y[16];
+  bf16* sg = reinterpret_cast<bf16*>(&sc->xch[0][0]);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) y[j] = __float2bfloat16_rn(bf16_round(v[j]) + add[j]);
+  for (int j = 0; j < 16; ++j) sg[j * TP_STAGE_PITCH_H + r] = __float2bfloat16_rn(bf16_round(v[j]) + add[j]);
+  epi_bar();
+  uint4 y[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int idx = r + i * 128, j = idx >> 4, q = idx & 15;  // token j, features 8q..8q+7 of the tile
+    y[i] = *reinterpret_cast<const uint4*>(&sg[j * TP_STAGE_PITCH_H + 8 * q]);
+  }
+  epi_bar();  // the stage is reused by the next chunk
   bf16* out = reinterpret_cast<bf16*>(a.out);
   for (int p = 0; p < P.tp.world; ++p) {
     bf16* o = tp_peer(P.tp, p, out);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int tok = n0 + j;
-      if (tok >= a.rows) break;
-      o[(long long)tok * a.out_ld + f] = y[j];
+    for (int i = 0; i < 2; ++i) {
+      const int idx = r + i * 128, j = idx >> 4, q = idx & 15;
+      if (n0 + j < a.rows)
+        *reinterpret_cast<uint4*>(o + (long long)(n0 + j) * a.out_ld + m_tile * BM + 8 * q) = y[i];
     }
   }
 }
@@ -393,7 +427,7 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
           }
         }
       }
-      tp_final_store(P, m_tile, n0 + c, v, r);
+      tp_final_store(P, m_tile, n0 + c, v, r, sc);
     }
   }
   // one system-scope fence for all of this CTA's finalised groups, then their
@@ -424,7 +458,7 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
 __device__ __forceinline__ void emit_chunk(const GemmKernelParams& P, int t, int m_tile, int n0, int c,
                                            const float (&v)[16], int r, int ew, EpiScratch* sc) {
   if (P.tp.world > 0)
-    tp_send_chunk(P, t, n0, c, v, r);
+    tp_send_chunk(P, t, n0, c, v, r, sc);
   else
     final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
 }
@@ -536,7 +570,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* done_bar = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  EpiScratch* sc = reinterpret_cast<EpiScratch*>(reinterpret_cast<uint8_t*>(tmem_holder) + 64);
+  // 16-byte aligned: the TP exchange stages chunks in it with 16-byte accesses
+  // (the barriers before it end at an 8-byte boundary; EPI_SCRATCH_BYTES has
+  // the slack for the padding)
+  EpiScratch* sc = reinterpret_cast<EpiScratch*>((reinterpret_cast<uintptr_t>(tmem_holder) + 64 + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1029,8 +1066,10 @@ extern "C" int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_t
   if (wire != LS_TP_WIRE_F32 && wire != LS_TP_WIRE_BF16)
     return set_error(LS_ERR_INVALID, "ls_gemm_allreduce: unknown wire format %d", wire);
   if (g->world == 1) return gemm_launch(stream, a, workspace, workspace_bytes, nullptr, 0);
-  if (a->rows <= 0 || a->n_out <= 0 || a->n_out % BM || a->out_ld < a->n_out || a->out == nullptr)
-    return set_error(LS_ERR_INVALID, "ls_gemm_allreduce: bad rows/n_out/out_ld");
+  if (a->rows <= 0 || a->n_out <= 0 || a->n_out % BM || a->out_ld < a->n_out || a->out_ld % 8 || a->out == nullptr ||
+      (reinterpret_cast<uintptr_t>(a->out) & 15))
+    return set_error(LS_ERR_INVALID,
+                     "ls_gemm_allreduce: bad rows/n_out/out_ld (out 16-byte aligned, out_ld a multiple of 8)");
   const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out, false);
   if (static_cast<long long>(p.m_tiles) * p.n_tiles > TP_MAX_TILES)
     return set_error(LS_ERR_UNSUPPORTED, "ls_gemm_allreduce: %d x %d output tiles exceed %d", p.m_tiles, p.n_tiles,
