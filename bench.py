@@ -343,6 +343,28 @@ def time_dominant_kernel(eng, reps=20):
     return sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps
 
 
+def time_prefill_summary(eng, v, batch, reps=5):
+    """ls_prefill_summary over the whole synthetic prefix of every request
+    (the state a prefill packet would carry): ms per launch (CUDA events,
+    after one warm-up launch) and the algorithmic FLOPs of one launch
+    (4 * D flops per (learned query, prefix key): q.k and p.v)."""
+    import torch
+    s = eng.shape
+    slots = torch.arange(batch, dtype=torch.int32, device=eng.device)
+    lens = v["seq_lens"][:batch]
+    eng.prefill_summary(slots=slots, seq_lens=lens, page_table=v["page_table"], batch=batch)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        eng.prefill_summary(slots=slots, seq_lens=lens, page_table=v["page_table"], batch=batch)
+    e1.record(st)
+    torch.cuda.synchronize()
+    flops = 4.0 * s.head_dim * s.tap_layers * s.q_heads * s.slots * float(lens.sum().item())
+    return e0.elapsed_time(e1) / reps, flops, eng.device_status()
+
+
 def count_launches(eng, g):
     """Kernels of one round, counted from the native calls of an eager run."""
     from longspark_b200 import _native as N
@@ -435,6 +457,7 @@ def run_b200(args):
         peaks = json.loads(pp.read_text())
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    tensor_peak = float(peaks.get("bf16_tflops", 1590.0))
 
     # context sweep (each context its own synthetic cache; same weights seed)
     sweep = []
@@ -453,8 +476,9 @@ def run_b200(args):
             status = eng.device_status()
             dom_ms = time_dominant_kernel(eng)
             abytes = algorithmic_bytes(shape, eng, batch)
+            pf_ms, pf_flops, pf_status = time_prefill_summary(eng, v, batch)
             headline = dict(ms=ms_max, clocks=clk.summary(), launches=launches, status=status, dom_ms=dom_ms,
-                            abytes=abytes, eng=eng)
+                            abytes=abytes, eng=eng, prefill=(pf_ms, pf_flops, pf_status))
         else:
             ms_max = dist_max(time_graph(g, steps, 3, world), world)
             abytes = algorithmic_bytes(shape, eng, batch)
@@ -528,6 +552,18 @@ def run_b200(args):
                          "traffic": traffic, "algorithmic_bytes_per_launch": lm_bytes,
                          "launch_ms": round(headline["dom_ms"], 4)},
             "cpu_baseline": cpu,
+            "prefill_summary": {
+                "what": "ls_prefill_summary: fp32 (output, lse) of the 5 x 32 x 256 learned queries over the whole "
+                        f"{head_ctx}-token prefix (replaces the target's FA3 summary pass)",
+                "ms": round(headline["prefill"][0], 3),
+                "tflops": round(headline["prefill"][1] / (headline["prefill"][0] * 1e-3) / 1e12, 1),
+                "roofline": {"bound": "tensor", "peak": tensor_peak, "unit": "TFLOP/s",
+                             "frac": round(headline["prefill"][1] / (headline["prefill"][0] * 1e-3) / 1e12
+                                           / tensor_peak, 3),
+                             "note": "mma.sync (legacy tensor path) with a bf16 high + residual split of the "
+                                     "softmax weights (P.V issued twice); algorithmic flops = 4 * 128 per "
+                                     "(query, key)"},
+                "device_status": headline["prefill"][2]},
             "e2e": e2e,
             "gpu_launches": headline["launches"] * args.steps,
             "gpu_launches_per_step": headline["launches"],

@@ -340,6 +340,43 @@ LS_API int ls_accept(void* stream, const long long* target, int target_ld, const
 LS_API int ls_row_norm_bound(void* stream, const void* m, int vocab, int rank, float* out);
 
 /* ------------------------------------------------------------------------- */
+/* Prefill summary: the fp32 (output, lse) summary state of every learned     */
+/* query over a request's whole committed prefix [0, seq_lens[b]), read from  */
+/* the paged K/V pool (which must hold the whole prefix: the target's cache,  */
+/* not a window ring):                                                        */
+/*   lse[s] = logsumexp_r(scale * q[s] . k[r]),                               */
+/*   out[s] = sum_r exp(scale * q[s] . k[r] - lse[s]) * v[r].                  */
+/* Replaces the target's FA3 pass over 16 qlen-1 sequences per tapped layer   */
+/* (LS engine/target.py:230-253); definition: global_state_from_full_prefix   */
+/* (SF global16_raw256.py:829-869).  Scores unrounded fp32; the softmax       */
+/* weights enter the P.V tensor-core products as bf16 high part + bf16        */
+/* residual, so the result follows the fp32 definition.  An empty prefix      */
+/* writes output 0, lse -inf.  Writes state_out / state_lse (and the bf16     */
+/* copy of the first bf16_layers layers) of slot slots[b].                    */
+/* Needs q_heads % kv_heads == 0, slots % 16 == 0, (q_heads/kv_heads) * slots */
+/* % 64 == 0, seq_lens[b] <= table_stride * 16.                               */
+/* ------------------------------------------------------------------------- */
+typedef struct ls_prefill_args {
+  const void* kv_k;          /* [tap_layers, pool_pages, 16, kv_heads, 128] bf16 */
+  const void* kv_v;
+  long long pool_pages;
+  const int* page_table;     /* [batch, table_stride] */
+  int table_stride;
+  const int* seq_lens;       /* [batch] prefix length */
+  const int* slots;          /* [batch] state slot */
+  const void* learned_query; /* [tap_layers, q_heads, slots_per_head, 128] bf16 */
+  float* state_out;          /* [capacity, tap_layers, q_heads, slots_per_head, 128] */
+  float* state_lse;          /* [capacity, tap_layers, q_heads, slots_per_head] */
+  void* state_bf16;          /* optional [capacity, bf16_layers, q_heads, slots_per_head, 128] bf16 */
+  int bf16_layers;
+  int capacity, batch, tap_layers, q_heads, kv_heads, slots_per_head;
+  float softmax_scale;
+  int* status;
+} ls_prefill_args;
+
+LS_API int ls_prefill_summary(void* stream, const ls_prefill_args* a);
+
+/* ------------------------------------------------------------------------- */
 /* Tensor parallelism of the drafter over NVLink (one process per GPU).       */
 /* No counterpart in the reference, which forces the drafter to one GPU       */
 /* (SP global16_native_draft_executor.py:1101-1105); the design precedent is  */

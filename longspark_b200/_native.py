@@ -59,6 +59,13 @@ class MarkovArgs(C.Structure):
                 ("status", vp)]
 
 
+class PrefillArgs(C.Structure):
+    _fields_ = [("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("page_table", vp), ("table_stride", i32),
+                ("seq_lens", vp), ("slots", vp), ("learned_query", vp), ("state_out", vp), ("state_lse", vp),
+                ("state_bf16", vp), ("bf16_layers", i32), ("capacity", i32), ("batch", i32), ("tap_layers", i32),
+                ("q_heads", i32), ("kv_heads", i32), ("slots_per_head", i32), ("softmax_scale", f32), ("status", vp)]
+
+
 class TpGroup(C.Structure):
     _fields_ = [("world", i32), ("rank", i32), ("heap", vp * TP_MAX_RANKS), ("heap_bytes", sz), ("sync_offset", sz)]
 
@@ -86,6 +93,7 @@ SIGNATURES = {
     "ls_markov_argmax_static": (i32, [vp, C.POINTER(MarkovArgs)]),
     "ls_accept": (i32, [vp, vp, i32, vp, vp, i32, i32]),
     "ls_row_norm_bound": (i32, [vp, vp, i32, i32, vp]),
+    "ls_prefill_summary": (i32, [vp, C.POINTER(PrefillArgs)]),
     "ls_ipc_alloc": (i32, [sz, C.POINTER(vp), vp]),
     "ls_ipc_open": (i32, [vp, C.POINTER(vp)]),
     "ls_ipc_close": (i32, [vp]),

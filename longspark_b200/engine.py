@@ -188,6 +188,16 @@ class DraftEngine:
                           ring_pages=p.ring_pages, softmax_scale=self.shape.head_dim ** -0.5,
                           status=self.buf["status"], batch=batch, state_bf16=p.summary_bf16)
 
+    def prefill_summary(self, *, slots, seq_lens, page_table, batch=None):
+        """Compute the summary state of requests from their whole prefix in the
+        pool (``ls_prefill_summary``), replacing the state the target would
+        export with a prefill packet; the pool must hold the whole prefix."""
+        p = self.pools
+        ops.prefill_summary(kv_k=p.kv_k, kv_v=p.kv_v, page_table=page_table, seq_lens=seq_lens, slots=slots,
+                            learned_query=self.w.learned_query, state_out=p.summary_out, state_lse=p.summary_lse,
+                            softmax_scale=self.shape.head_dim ** -0.5, status=self.buf["status"], batch=batch,
+                            state_bf16=p.summary_bf16)
+
     # ------------------------------------------------------------------ drafter
     def draft(self, *, slots, seq_lens, anchors, page_table, target=None, batch=None, slots_are_rows=False,
               commit_lens=None):

@@ -255,6 +255,35 @@ def refresh_views(*, kv_k, kv_v, page_table, seq_lens, commit_lens, slots, learn
     N.call("ls_refresh_views", _stream(state_out.device), C.byref(a))
 
 
+def prefill_summary(*, kv_k, kv_v, page_table, seq_lens, slots, learned_query, state_out, state_lse,
+                    softmax_scale=128 ** -0.5, status=None, batch=None, state_bf16=None):
+    """Full-prefix summary state (``ls_prefill_summary``): for each request b,
+    every tapped layer and query head, the (output, lse) of the learned
+    queries over pool rows [0, seq_lens[b]) written at slot ``slots[b]``.
+
+    kv_k/kv_v [L_tap, pages, 16, Hkv, 128] bf16 holding the whole prefix;
+    page_table [B, max_pages] int32; learned_query [L_tap, Hq, S, 128] bf16;
+    state_out [cap, L_tap, Hq, S, 128] fp32; state_lse [cap, L_tap, Hq, S]."""
+    _require_cuda(kv_k, kv_v, page_table, seq_lens, slots, learned_query, state_out, state_lse)
+    L, pages, ps, hkv, d = kv_k.shape
+    if ps != 16 or d != 128 or kv_v.shape != kv_k.shape:
+        raise ValueError("KV pool must be [layers, pages, 16, kv_heads, 128]")
+    _, hq, s, _ = learned_query.shape
+    if state_out.shape[1:] != (L, hq, s, 128) or state_lse.shape[1:] != (L, hq, s):
+        raise ValueError("summary state does not match the learned queries")
+    for t, name in ((page_table, "page_table"), (seq_lens, "seq_lens"), (slots, "slots")):
+        if t.dtype != torch.int32:
+            raise ValueError(f"{name} must be int32")
+    batch = seq_lens.shape[0] if batch is None else batch
+    a = N.PrefillArgs(kv_k=_p(kv_k), kv_v=_p(kv_v), pool_pages=pages, page_table=_p(page_table),
+                      table_stride=page_table.stride(0), seq_lens=_p(seq_lens), slots=_p(slots),
+                      learned_query=_p(learned_query), state_out=_p(state_out), state_lse=_p(state_lse),
+                      state_bf16=_p(state_bf16), bf16_layers=0 if state_bf16 is None else state_bf16.shape[1],
+                      capacity=state_out.shape[0], batch=batch, tap_layers=L, q_heads=hq, kv_heads=hkv,
+                      slots_per_head=s, softmax_scale=float(softmax_scale), status=_p(status))
+    N.call("ls_prefill_summary", _stream(state_out.device), C.byref(a))
+
+
 def window_scatter(*, keys, values, row_offsets, counts, seq_lens, kv_k, kv_v, page_table, ring_pages=0,
                    last_hidden=None, hidden_pool=None, slots=None, status=None, batch=None):
     """Packet K/V rows -> paged pool at their positions; last hidden -> slot pool.

@@ -48,9 +48,11 @@ def test_struct_layouts_match_the_header(lib):
     from longspark_b200 import _native as N
     text = HEADER.read_text()
     for cname, py in (("ls_gemm_args", N.GemmArgs), ("ls_refresh_args", N.RefreshArgs),
-                      ("ls_attention_args", N.AttentionArgs), ("ls_markov_args", N.MarkovArgs)):
+                      ("ls_attention_args", N.AttentionArgs), ("ls_markov_args", N.MarkovArgs),
+                      ("ls_prefill_args", N.PrefillArgs), ("ls_tp_group", N.TpGroup)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+        body = re.sub(r"\[[^\]]*\]", "", body)  # array declarators: the name is what precedes them
         names = []
         for decl in body.split(";"):
             decl = decl.strip()
