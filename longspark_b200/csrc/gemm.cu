@@ -46,9 +46,6 @@ struct GemmKernelParams {
   int kg;            // k-blocks per unit and per pipeline stage (1, 2 or 4)
   long long units;   // tiles * kb
   int grid;          // CTAs
-  int mh;            // 128-row weight blocks per tile (2: "wide" 256-row tiles, two MMAs sharing the tokens)
-  int m128;          // 128-row weight blocks in all (n_out / 128)
-  int nacc;          // TMEM accumulator sets (2: double-buffered, 1 when mh * bn * 2 > 512 columns)
   int stages;
   uint32_t tmem_cols;
   float* partials;   // [grid * 2][bn][128]
@@ -241,8 +238,8 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
           }
         }
         if (tok < rows) {
-          a.tile_max[(long long)tok * P.m128 + m_tile] = bv;
-          a.tile_arg[(long long)tok * P.m128 + m_tile] = bi;
+          a.tile_max[(long long)tok * P.m_tiles + m_tile] = bv;
+          a.tile_arg[(long long)tok * P.m_tiles + m_tile] = bi;
         }
       }
       epi_bar();
@@ -468,47 +465,35 @@ __device__ __forceinline__ void emit_chunk(const GemmKernelParams& P, int t, int
 __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, int first, int last, int first_slot,
                                             int r, int ew, EpiScratch* sc) {
   const int bn = P.bn;
-  const int mt = t / P.n_tiles;
-  const int n0 = (t - mt * P.n_tiles) * bn;
-  const long long slot_floats = static_cast<long long>(P.mh) * bn * BM;
-  for (int h = 0; h < P.mh; ++h) {
-    const int m_tile = mt * P.mh + h;
-    if (m_tile >= P.m128) break;
-    for (int c = 0; c < bn; c += 16) {
-      float v[16];
+  const int m_tile = t / P.n_tiles;
+  const int n0 = (t - m_tile * P.n_tiles) * bn;
+  for (int c = 0; c < bn; c += 16) {
+    float v[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-      // contributors in fixed order, four partials' loads in flight at a time
-      for (int q0 = first; q0 <= last; q0 += 4) {
-        float pv[4][16];
+    for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+    // contributors in fixed order, four partials' loads in flight at a time
+    for (int q0 = first; q0 <= last; q0 += 4) {
+      float pv[4][16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int q = q0 + i;
-          const int q_slot = q == first ? first_slot : 0;
-          const float* qp = P.partials + (static_cast<long long>(q) * 2 + q_slot) * slot_floats +
-                            static_cast<long long>(h) * bn * BM;
-          if (q <= last) {
+      for (int i = 0; i < 4; ++i) {
+        const int q = q0 + i;
+        const int q_slot = q == first ? first_slot : 0;
+        const float* qp = P.partials + (static_cast<long long>(q) * 2 + q_slot) * (static_cast<long long>(bn) * BM);
+        if (q <= last) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) pv[i][j] = __ldcg(&qp[(c + j) * BM + r]);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (q0 + i <= last) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += pv[i][j];
-          }
+          for (int j = 0; j < 16; ++j) pv[i][j] = __ldcg(&qp[(c + j) * BM + r]);
         }
       }
-      if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (q0 + i <= last) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += pv[i][j];
+        }
+      }
     }
+    if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc);
   }
-}
-
-// 128-row weight blocks of tile t (mh, or fewer for the last tile).
-__device__ __forceinline__ int tile_halves(const GemmKernelParams& P, int t) {
-  const int rest = P.m128 - (t / P.n_tiles) * P.mh;
-  return rest < P.mh ? rest : P.mh;
 }
 
 // Producer helpers: stage `st` receives unit u's KG k-blocks of weights (one
@@ -519,25 +504,15 @@ __device__ __forceinline__ void gemm_load_a(const GemmKernelParams& P, const CUt
                                             long long u, uint64_t pol) {
   const int t = static_cast<int>(u / P.kb);
   const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
-  const int mt = t / P.n_tiles;
-  const int halves = tile_halves(P, t);
-  for (int h = 0; h < halves; ++h) {
-    const int blk = mt * P.mh + h;
-    uint8_t* dst = a_buf + st * a_stage_bytes + h * P.kg * A_STAGE_BYTES;
-    if (tiled_w) {
-      // KG consecutive tiles of one row block are contiguous in the tiled layout
-      bulk_load(dst, w_tiles + (static_cast<long long>(blk) * P.kb * P.kg + kb0) * (BM * BK), P.kg * A_STAGE_BYTES,
-                &full[st], pol);
-    } else {
-      for (int j = 0; j < P.kg; ++j)
-        tma_load_2d(dst + j * A_STAGE_BYTES, map_w, &full[st], (kb0 + j) * BK, blk * BM, pol);
-    }
+  const int m_tile = t / P.n_tiles;
+  if (tiled_w) {
+    // KG consecutive tiles of one row block are contiguous in the tiled layout
+    bulk_load(a_buf + st * a_stage_bytes,
+              w_tiles + (static_cast<long long>(m_tile) * P.kb * P.kg + kb0) * (BM * BK), a_stage_bytes, &full[st], pol);
+  } else {
+    for (int j = 0; j < P.kg; ++j)
+      tma_load_2d(a_buf + st * a_stage_bytes + j * A_STAGE_BYTES, map_w, &full[st], (kb0 + j) * BK, m_tile * BM, pol);
   }
-}
-
-// Bytes a stage of unit u receives (its tile may have one 128-row block only).
-__device__ __forceinline__ int stage_tx_bytes(const GemmKernelParams& P, long long u, int b_stage_bytes) {
-  return tile_halves(P, static_cast<int>(u / P.kb)) * P.kg * A_STAGE_BYTES + b_stage_bytes;
 }
 
 __device__ __forceinline__ void gemm_load_b(const GemmKernelParams& P, const CUtensorMap* map_x, uint8_t* b_buf,
@@ -558,8 +533,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int S = P.stages;
   const int bn = P.bn;
   const int KG = P.kg;
-  const int b_blk_bytes = bn * BK * 2;                 // one k-block of activations
-  const int a_stage_bytes = P.mh * KG * A_STAGE_BYTES;  // one stage = KG k-blocks of mh weight blocks
+  const int b_blk_bytes = bn * BK * 2;          // one k-block of activations
+  const int a_stage_bytes = KG * A_STAGE_BYTES;  // one stage = KG k-blocks
   const int b_stage_bytes = KG * b_blk_bytes;
   uint8_t* a_buf = smem;
   uint8_t* b_buf = a_buf + S * a_stage_bytes;
@@ -625,7 +600,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // weight tiles before waiting for it, then add the activation tiles.
       const int pre = static_cast<int>((u1 - u0) < S ? (u1 - u0) : S);
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], stage_tx_bytes(P, u0 + i, b_stage_bytes));
+        mbar_arrive_expect_tx(&full[i], a_stage_bytes + b_stage_bytes);
         gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, i, u0 + i, pol_w);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -635,7 +610,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       long long issued = pre;
       for (long long u = u0 + pre; u < u1; ++u) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full[stage], stage_tx_bytes(P, u, b_stage_bytes));
+        mbar_arrive_expect_tx(&full[stage], a_stage_bytes + b_stage_bytes);
         gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, stage, u, pol_w);
         gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, u, pol_x);
         ++issued;
@@ -677,8 +652,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P.mh * bn);
-        const int halves = tile_halves(P, t);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * bn);
         for (int kb = k0; kb < k1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, status, LS_DEV_TIMEOUT_MMA)) {
             ok = false;
@@ -686,19 +660,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           tc_fence_after();
           for (int j = 0; j < KG; ++j) {
+            const uint32_t a_addr = smem_u32(a_buf + stage * a_stage_bytes + j * A_STAGE_BYTES);
             const uint32_t b_addr = smem_u32(b_buf + stage * b_stage_bytes + j * b_blk_bytes);
+            const uint64_t a_desc = sdesc_kmajor_sw128(a_addr);
             const uint64_t b_desc = sdesc_kmajor_sw128(b_addr);
-            // wide tiles: the same token block against both 128-row weight blocks
-            for (int h = 0; h < halves; ++h) {
-              const uint32_t a_addr =
-                  smem_u32(a_buf + stage * a_stage_bytes + (h * KG + j) * A_STAGE_BYTES);
-              const uint64_t a_desc = sdesc_kmajor_sw128(a_addr);
 #pragma unroll
-              for (int kk = 0; kk < BK / 16; ++kk) {
-                // +32 bytes along K inside the 128-byte swizzled row (encoded >> 4).
-                tc_mma_bf16(d_tmem + static_cast<uint32_t>(h * bn), a_desc + 2 * kk, b_desc + 2 * kk, idesc,
-                            (kb > k0 || j > 0 || kk > 0) ? 1u : 0u);
-              }
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              // +32 bytes along K inside the 128-byte swizzled row (encoded >> 4).
+              tc_mma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb > k0 || j > 0 || kk > 0) ? 1u : 0u);
             }
           }
           tc_commit(&empty[stage]);
@@ -710,7 +679,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!ok) break;
         tc_commit(&acc_full[acc]);
         acc_phase ^= 1u << acc;
-        acc = acc + 1 == P.nacc ? 0 : acc + 1;
+        acc ^= 1;
         u += k1 - k0;
       }
       // Drain: wait until every MMA issued by this thread has completed.
@@ -746,20 +715,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       epi_bar();
       if (!go) break;
       tc_fence_after();
-      const int mt = t / P.n_tiles;
-      const int n_tile = t - mt * P.n_tiles;
+      const int m_tile = t / P.n_tiles;
+      const int n_tile = t - m_tile * P.n_tiles;
       const int n0 = n_tile * P.bn;
       const bool full_tile = (k0 == 0 && k1 == KB);
-      const int halves = tile_halves(P, t);
-      const uint32_t t_addr =
-          tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * P.mh * bn);
+      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * bn);
       if (full_tile) {
-        for (int h = 0; h < halves; ++h) {
-          for (int c = 0; c < bn; c += 16) {
-            float v[16];
-            tmem_ld16(t_addr + h * bn + c, v);
-            if (n0 + c < P.a.rows) emit_chunk(P, t, mt * P.mh + h, n0, c, v, r, ew, sc);
-          }
+        for (int c = 0; c < bn; c += 16) {
+          float v[16];
+          tmem_ld16(t_addr + c, v);
+          if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
@@ -767,15 +732,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       } else {
         // Partial tile: park the fp32 partial, the last contributor reduces.
         const int slot = (t == t_first) ? 0 : 1;
-        float* part =
-            P.partials + (static_cast<long long>(blockIdx.x) * 2 + slot) * (static_cast<long long>(P.mh) * bn * BM);
-        for (int h = 0; h < halves; ++h) {
-          for (int c = 0; c < bn; c += 16) {
-            float v[16];
-            tmem_ld16(t_addr + h * bn + c, v);
+        float* part = P.partials + (static_cast<long long>(blockIdx.x) * 2 + slot) * (static_cast<long long>(bn) * BM);
+        for (int c = 0; c < bn; c += 16) {
+          float v[16];
+          tmem_ld16(t_addr + c, v);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) __stcg(&part[(static_cast<long long>(h) * bn + c + j) * BM + r], v[j]);
-          }
+          for (int j = 0; j < 16; ++j) __stcg(&part[(c + j) * BM + r], v[j]);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
@@ -800,7 +762,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
       acc_phase ^= 1u << acc;
-      acc = acc + 1 == P.nacc ? 0 : acc + 1;
+      acc ^= 1;
       u += k1 - k0;
     }
     if (P.tp.world > 0) {
@@ -833,19 +795,19 @@ static int pick_bn(int rows) {
   return r16 > 256 ? 256 : r16;
 }
 
-static int pick_stages(int bn, int kg, int mh) {
+static int pick_stages(int bn, int kg) {
   const int budget = 227 * 1024 - 1024 - 256 - EPI_SCRATCH_BYTES - 512;
-  int s = budget / (kg * (mh * A_STAGE_BYTES + bn * BK * 2));
+  int s = budget / (kg * (A_STAGE_BYTES + bn * BK * 2));
   return s > 12 ? 12 : s;
 }
 
-static size_t gemm_smem_bytes(int bn, int kg, int stages, int mh) {
-  return 1024 + static_cast<size_t>(stages) * kg * (mh * A_STAGE_BYTES + bn * BK * 2) + (2 * stages + 5) * 8 + 64 +
+static size_t gemm_smem_bytes(int bn, int kg, int stages) {
+  return 1024 + static_cast<size_t>(stages) * kg * (A_STAGE_BYTES + bn * BK * 2) + (2 * stages + 5) * 8 + 64 +
          EPI_SCRATCH_BYTES;
 }
 
 struct GemmPlan {
-  int bn, n_tiles, m_tiles, kb, kg, grid, stages, mh, m128, nacc;
+  int bn, n_tiles, m_tiles, kb, kg, grid, stages;
   long long units;
   size_t partial_bytes, counter_bytes;
 };
@@ -857,37 +819,30 @@ static int narrower_bn(int bn) {
   return h < 64 ? 64 : h;
 }
 
-// Token tile: as wide as the tokens (up to 256), narrowed (down to 64) while
-// the grid would have fewer output tiles than SMs (twice the SMs for
-// k <= 1024): with few tiles every tile is split along k, and the fp32
-// partial round trips of the split tiles cost more than the extra weight
-// re-reads of a narrower tile (measured at 480 tokens: o_proj-like
-// 5120 x 2560 58 -> 50 us, 5120 x 640 72 -> 32 us; wide shapes keep 256).
+// Token tile: as wide as the tokens (up to 256), narrowed while the grid would
+// have fewer output tiles than SMs (twice the SMs for k <= 1024): with few
+// tiles every tile is split along k, and the fp32 partial round trips of the
+// split tiles cost more than the extra weight re-reads of a narrower tile.
+// The floor is 128 tokens for long reductions, where the operand traffic of a
+// 64-token tile costs more than the imbalance it removes; 64 for k <= 1024 or
+// at most 128 tokens.  Measured at 480 tokens (8B/14B drafter shapes):
+// 5120 x 640 72 -> 32 us (64), 4096 x 4096 73 -> 56 us (128),
+// 4096 x 12288 108 -> 102 us (128, 159 us at 64); wide shapes keep 256.
 static int plan_bn(int rows, int k, int n_out, int sms) {
   int bn = pick_bn(rows);
   const long long m_tiles = n_out / BM;
   const long long want = (k <= 1024 ? 2LL : 1LL) * sms;
-  while (bn > 64 && m_tiles * ((rows + bn - 1) / bn) < want) bn = narrower_bn(bn);
+  const int floor_bn = (k <= 1024 || rows <= 128) ? 64 : 128;
+  while (bn > floor_bn && m_tiles * ((rows + bn - 1) / bn) < want) bn = narrower_bn(bn);
   return bn;
 }
 
-// allow_wide: 256-row tiles (two 128-row weight blocks against one token
-// block, mh = 2) when the token tile is wide and there are at least two such
-// tiles per SM.  The MMA then reads 64 KiB of operands per 256 x bn x 64
-// step instead of 48 KiB per 128 x bn x 64, which is what bounds the many-
-// token vocabulary projection (L2 -> shared memory traffic).
-static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide = true) {
+static GemmPlan plan_gemm(int rows, int k, int n_out) {
   GemmPlan p{};
   const int sms = host_sm_count();
   p.bn = plan_bn(rows, k, n_out, sms);
   p.n_tiles = (rows + p.bn - 1) / p.bn;
-  p.m128 = n_out / BM;
-  p.mh = 1;
-  if (allow_wide && p.bn >= 192 && p.m128 >= 2 &&
-      static_cast<long long>((p.m128 + 1) / 2) * p.n_tiles >= 2LL * sms && pick_stages(p.bn, 1, 2) >= 3)
-    p.mh = 2;
-  p.m_tiles = (p.m128 + p.mh - 1) / p.mh;
-  p.nacc = 2 * p.mh * p.bn <= 512 ? 2 : 1;
+  p.m_tiles = n_out / BM;
   // Pipeline stages of up to 4 k-blocks (64 KiB of weights): HBM streams best
   // with a few large requests in flight per SM.  Smaller stages when the tile
   // count is low (stream-K balance) or the token tile is wide (shared memory).
@@ -895,7 +850,7 @@ static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide = true) {
   p.kg = 1;
   for (int kg = 4; kg > 1; kg >>= 1) {
     if (k % (BK * kg)) continue;
-    if (pick_stages(p.bn, kg, p.mh) < 3) continue;
+    if (pick_stages(p.bn, kg) < 3) continue;
     if (tiles * (k / (BK * kg)) < 4LL * sms) continue;
     p.kg = kg;
     break;
@@ -903,8 +858,8 @@ static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide = true) {
   p.kb = k / (BK * p.kg);
   p.units = tiles * p.kb;
   p.grid = static_cast<int>(std::min<long long>(sms, p.units));
-  p.stages = pick_stages(p.bn, p.kg, p.mh);
-  p.partial_bytes = static_cast<size_t>(p.grid) * 2 * p.mh * p.bn * BM * sizeof(float);
+  p.stages = pick_stages(p.bn, p.kg);
+  p.partial_bytes = static_cast<size_t>(p.grid) * 2 * p.bn * BM * sizeof(float);
   p.counter_bytes = COUNTER_BYTES;
   return p;
 }
@@ -915,9 +870,8 @@ using namespace ls;
 
 extern "C" size_t ls_gemm_workspace_bytes(int rows, int k, int n_out) {
   if (rows <= 0 || k <= 0 || n_out <= 0) return 0;
-  // either plan (wide for ls_gemm, narrow for ls_gemm_allreduce) fits
-  const GemmPlan p = plan_gemm(rows, k, n_out, true), q = plan_gemm(rows, k, n_out, false);
-  return p.counter_bytes + std::max(p.partial_bytes, q.partial_bytes);
+  const GemmPlan p = plan_gemm(rows, k, n_out);
+  return p.counter_bytes + p.partial_bytes;
 }
 
 namespace ls {
@@ -959,7 +913,7 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
     default:
       return set_error(LS_ERR_INVALID, "ls_gemm: unknown epilogue %d", a->epilogue);
   }
-  GemmPlan p = plan_gemm(a->rows, a->k, a->n_out, tp == nullptr);
+  GemmPlan p = plan_gemm(a->rows, a->k, a->n_out);
   if (static_cast<long long>(p.m_tiles) * p.n_tiles > MAX_TILES)
     return set_error(LS_ERR_UNSUPPORTED, "ls_gemm: %d x %d tiles exceed the %d tile counters", p.m_tiles, p.n_tiles,
                      MAX_TILES);
@@ -991,11 +945,8 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
   kp.units = p.units;
   kp.grid = p.grid;
   kp.stages = p.stages;
-  kp.mh = p.mh;
-  kp.m128 = p.m128;
-  kp.nacc = p.nacc;
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(p.nacc * p.mh * p.bn)) cols <<= 1;
+  while (cols < static_cast<uint32_t>(2 * p.bn)) cols <<= 1;
   kp.tmem_cols = cols;
   kp.counters = reinterpret_cast<int*>(workspace);
   kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + p.counter_bytes);
@@ -1004,7 +955,7 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
     kp.tp_wire = wire;
   }
 
-  const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.stages, p.mh);
+  const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.stages);
   static int configured_smem = 0;
   if (configured_smem < static_cast<int>(smem)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1070,7 +1021,7 @@ extern "C" int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_t
       (reinterpret_cast<uintptr_t>(a->out) & 15))
     return set_error(LS_ERR_INVALID,
                      "ls_gemm_allreduce: bad rows/n_out/out_ld (out 16-byte aligned, out_ld a multiple of 8)");
-  const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out, false);
+  const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out);
   if (static_cast<long long>(p.m_tiles) * p.n_tiles > TP_MAX_TILES)
     return set_error(LS_ERR_UNSUPPORTED, "ls_gemm_allreduce: %d x %d output tiles exceed %d", p.m_tiles, p.n_tiles,
                      TP_MAX_TILES);

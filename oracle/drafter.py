@@ -33,7 +33,7 @@ __all__ = [
     "state_encoder", "shifted_input", "rope_tables", "apply_rotary",
     "attention_statistics", "statistics_as_normalized", "merge_normalized_attention",
     "window_positions", "gather_window", "attend", "decoder_layer", "project_logits",
-    "markov_sample", "greedy_argmax", "accept_lengths", "position_scores", "merge_accepted",
+    "markov_sample", "markov_sample_gumbel", "gumbel_hash_uniform", "greedy_argmax", "accept_lengths", "position_scores", "merge_accepted",
     "full_prefix_state", "refresh_views", "draft_pass", "build_views", "DraftShapeOracle",
 ]
 
@@ -375,6 +375,72 @@ def markov_sample(base_logits, anchors, W, prec, forced=None):
         toks[:, t] = greedy_argmax(step)
         prev = toks[:, t] if forced is None else np.asarray(forced[:, t], dtype=np.int64)
     return toks, corrected
+
+
+def gumbel_hash_uniform(seed, b, t, v):
+    """Uniform in (0, 1) from a counter-based hash of (seed, request b, step t,
+    token v): the random source of the tensor-core-free T > 0 sampler.  Two
+    rounds of the lowbias32 integer mixer (C. Wellons) over a linear mix of the
+    counters; 24 bits of the result, centred in their interval.  uint32
+    arithmetic, identical to the CUDA side."""
+    M = np.uint64(0xFFFFFFFF)
+    s = np.uint64(seed)
+    seed_lo = s & M
+    seed_hi = (s >> np.uint64(32)) & M
+
+    def mix(x):
+        x = x & M
+        x ^= x >> np.uint64(16)
+        x = (x * np.uint64(0x7FEB352D)) & M
+        x ^= x >> np.uint64(15)
+        x = (x * np.uint64(0x846CA68B)) & M
+        x ^= x >> np.uint64(16)
+        return x
+
+    v = np.asarray(v, dtype=np.uint64)
+    x = ((v * np.uint64(0x9E3779B1)) & M) ^ ((np.uint64(t) * np.uint64(0x85EBCA77)) & M) \
+        ^ ((np.uint64(b) * np.uint64(0xC2B2AE3D)) & M) ^ seed_lo
+    x = mix(mix(x) ^ seed_hi)
+    return (((x >> np.uint64(8)).astype(np.float64) + 0.5) * 2.0 ** -24).astype(np.float32)
+
+
+def markov_sample_gumbel(base_logits, anchors, W, prec, temperature, seed):
+    """``DSparkVanillaMarkovHead.sample_block_tokens`` at T > 0 (SF
+    draftfreekv.py:2366-2407) and the proposal probability of
+    ``LongSparkDraft.propose`` (LS engine/draft.py:284-286): per step,
+    ``step = bf16(base[t] + bf16(w2 . w1[prev]))``, a token drawn from
+    ``softmax(step / T)`` feeds the next step, and ``q = softmax(step / T)[tok]``.
+    The reference draws with ``torch.multinomial``; here the draw is the
+    Gumbel-max of ``step / T + g`` with ``g = -log(-log(u))`` and ``u`` from
+    ``gumbel_hash_uniform(seed, b, t, v)`` -- the same distribution, and a
+    reproducible one.  Returns tokens [B, P] int64, q [B, P] fp32, corrected
+    logits [B, P, V]."""
+    w1 = W.get("parallel_markov_head.markov_w1.weight")
+    w2 = W.get("parallel_markov_head.markov_w2.weight")
+    b_n, p_n, vocab = base_logits.shape
+    prev = np.asarray(anchors, dtype=np.int64).copy()
+    toks = np.zeros((b_n, p_n), dtype=np.int64)
+    q = np.zeros((b_n, p_n), dtype=np.float32)
+    corrected = np.zeros_like(base_logits)
+    inv_t = np.float32(1.0) / np.float32(temperature)
+    ids = np.arange(vocab)
+    for t in range(p_n):
+        if w1 is None:
+            step = base_logits[:, t]
+        else:
+            step = rnd(base_logits[:, t] + linear(w1[prev], w2, prec), prec)
+        corrected[:, t] = step
+        for b in range(b_n):
+            z = step[b].astype(np.float32) * inv_t
+            u = gumbel_hash_uniform(seed, b, t, ids)
+            g = -np.log(-np.log(u))
+            tok = int(np.argmax(z + g))
+            m = z.max()
+            e = np.exp(z - m)
+            q[b, t] = e[tok] / e.sum(dtype=np.float32)
+            toks[b, t] = tok
+        prev = toks[:, t].copy()
+    return toks, q, corrected
 
 
 def accept_lengths(target_tokens, draft_tokens):

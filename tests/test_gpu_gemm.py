@@ -33,7 +33,7 @@ def _rand(*shape, std=1.0):
     (300, 256, 384),       # two token tiles of 256
     (16, 20480, 4096),     # state-encoder shape (5 taps x 4096)
     (16, 4096, 151936),    # vocabulary projection
-    (480, 256, 65664),     # wide 256-row tiles, odd block count (513): the last tile has one block
+    (480, 256, 65664),     # many tokens over an odd count (513) of 128-row blocks
     (480, 2560, 5120),     # narrowed token tile (128)
     (480, 640, 5120),      # narrowed token tile (64), short k
 ])
@@ -115,8 +115,8 @@ def test_gemm_qkv_norm_rope():
 
 @pytest.mark.parametrize("rows,k,v", [(15, 512, 1024 * 8), (300, 512, 151936)])
 def test_gemm_lm_head_tile_argmax(rows, k, v):
-    """Per-128-token tile maxima; (300, 512, 151936) runs the wide 256-row
-    tiles over the odd 1187-block vocabulary."""
+    """Per-128-token tile maxima; (300, 512, 151936) covers two token tiles
+    over the full 1187-tile vocabulary."""
     x = _rand(rows, k)
     w = _rand(v, k, std=0.05)
     out = torch.empty(rows, v, dtype=torch.bfloat16, device="cuda")
