@@ -330,6 +330,31 @@ LS_API int ls_markov_argmax(void* stream, const ls_markov_args* a, void* workspa
 #define LS_MARKOV_STATIC_MAX_ROWS 1024
 LS_API int ls_markov_argmax_static(void* stream, const ls_markov_args* a);
 
+/* Temperature > 0: step `step` of the sampled chain for every request.  Draws
+ * token ~ softmax(logits[b] / T) (the reference's multinomial draw,
+ * SF draftfreekv.py:2366-2407) as the Gumbel-max of logits / T + g with
+ * g = -log(-log(u)), u = a 24-bit uniform from a counter-based hash of
+ * (seed, b, step, token) (two lowbias32 rounds; restated by the oracle), and
+ * writes tokens[b, step], q[b, step] = softmax(logits[b] / T)[token] (the
+ * proposal probability of LS engine/draft.py:284-286) and prev[b] (int32 copy
+ * of the token, the next step's Markov row index).  logits: the step's bf16
+ * logits of request b at logits + b * logits_ld (base logits, or the
+ * Markov-corrected step logits written by an LS_EPI_MARKOV_ADD GEMM). */
+typedef struct ls_sample_step_args {
+  const void* logits;
+  long long logits_ld;
+  int batch, vocab, block, step;
+  float temperature;
+  unsigned long long seed;
+  long long* tokens;  /* [batch, block] */
+  float* q;           /* optional [batch, block] */
+  int* prev;          /* optional [batch] */
+  int* status;
+} ls_sample_step_args;
+
+LS_API size_t ls_sample_step_workspace_bytes(int batch);
+LS_API int ls_sample_step(void* stream, const ls_sample_step_args* a, void* workspace, size_t workspace_bytes);
+
 /* Greedy accept check: accept[b] = number of leading i < block with
  * target[b, i] == draft[b, i] (LS engine/target.py:472-477). */
 LS_API int ls_accept(void* stream, const long long* target, int target_ld, const long long* draft, long long* accept,

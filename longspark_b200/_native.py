@@ -59,6 +59,12 @@ class MarkovArgs(C.Structure):
                 ("status", vp)]
 
 
+class SampleStepArgs(C.Structure):
+    _fields_ = [("logits", vp), ("logits_ld", i64), ("batch", i32), ("vocab", i32), ("block", i32), ("step", i32),
+                ("temperature", f32), ("seed", C.c_ulonglong), ("tokens", vp), ("q", vp), ("prev", vp),
+                ("status", vp)]
+
+
 class PrefillArgs(C.Structure):
     _fields_ = [("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("page_table", vp), ("table_stride", i32),
                 ("seq_lens", vp), ("slots", vp), ("learned_query", vp), ("state_out", vp), ("state_lse", vp),
@@ -94,6 +100,8 @@ SIGNATURES = {
     "ls_accept": (i32, [vp, vp, i32, vp, vp, i32, i32]),
     "ls_row_norm_bound": (i32, [vp, vp, i32, i32, vp]),
     "ls_prefill_summary": (i32, [vp, C.POINTER(PrefillArgs)]),
+    "ls_sample_step_workspace_bytes": (sz, [i32]),
+    "ls_sample_step": (i32, [vp, C.POINTER(SampleStepArgs), vp, sz]),
     "ls_ipc_alloc": (i32, [sz, C.POINTER(vp), vp]),
     "ls_ipc_open": (i32, [vp, C.POINTER(vp)]),
     "ls_ipc_close": (i32, [vp]),

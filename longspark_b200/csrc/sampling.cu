@@ -786,6 +786,163 @@ extern "C" int ls_markov_argmax_static(void* stream, const ls_markov_args* a) {
   return ls_markov_argmax(stream, a, scratch, MK_STATIC_BYTES);
 }
 
+// ---------------------------------------------------------------------------
+// Temperature > 0: one step of the sampled chain for every request.
+//
+// Reference: DSparkVanillaMarkovHead.sample_block_tokens with temperature > 0
+// (vendor/specforge/modeling/draft/draftfreekv.py:2366-2407) draws
+// multinomial(softmax(step.float() / T)) with step = bf16(base[t] + bf16(bias));
+// LongSparkDraft.propose returns q = softmax(corrected.float() / T)[token]
+// (src/longspark/engine/draft.py:284-286).  The draw here is the Gumbel-max
+// of step / T + g, g = -log(-log(u)), which has the same distribution; u comes
+// from a counter-based hash of (seed, request, step, token) so that a round
+// is reproducible (and restated exactly by the CPU oracle).  The step logits
+// are the caller's (the Markov-bias GEMM writes them); one CTA per (request,
+// vocabulary slice) keeps the slice's best key and its (max, sum-exp), and the
+// request's last slice to finish merges the slices in order.
+// ---------------------------------------------------------------------------
+namespace ls {
+
+constexpr int SS_THREADS = 256;
+constexpr int SS_MAX_SPLIT = 64;
+
+struct SsPartial {
+  float key, z, m, s;
+  int idx;
+};
+
+__device__ __forceinline__ uint32_t lowbias32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+// Uniform in (0, 1): 24 bits of two lowbias32 rounds over the counters.
+__device__ __forceinline__ float hash_uniform(unsigned long long seed, int b, int t, int v) {
+  uint32_t x = static_cast<uint32_t>(v) * 0x9E3779B1u ^ static_cast<uint32_t>(t) * 0x85EBCA77u ^
+               static_cast<uint32_t>(b) * 0xC2B2AE3Du ^ static_cast<uint32_t>(seed);
+  x = lowbias32(lowbias32(x) ^ static_cast<uint32_t>(seed >> 32));
+  return (static_cast<float>(x >> 8) + 0.5f) * 5.9604644775390625e-08f;  // * 2^-24
+}
+
+__device__ __forceinline__ void ss_merge(SsPartial& a, const SsPartial& o) {
+  if (o.key > a.key || (o.key == a.key && o.idx < a.idx)) {
+    a.key = o.key;
+    a.idx = o.idx;
+    a.z = o.z;
+  }
+  if (o.m > a.m) {
+    a.s = a.s * expf(a.m - o.m) + o.s;
+    a.m = o.m;
+  } else if (o.m > -INFINITY) {
+    a.s += o.s * expf(o.m - a.m);
+  }
+}
+
+__global__ void __launch_bounds__(SS_THREADS) sample_step_kernel(const ls_sample_step_args a, int split,
+                                                                 SsPartial* parts, int* done) {
+  __shared__ SsPartial red[SS_THREADS / 32];
+  __shared__ int last;
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the step logits come from the previous kernel
+  const int b = blockIdx.x / split, part = blockIdx.x - (blockIdx.x / split) * split;
+  const int chunk = (a.vocab + split - 1) / split;
+  const int v0 = part * chunk, v1 = min(a.vocab, v0 + chunk);
+  const bf16* row = reinterpret_cast<const bf16*>(a.logits) + (long long)b * a.logits_ld;
+  SsPartial acc{-INFINITY, 0.0f, -INFINITY, 0.0f, 0x7fffffff};
+  for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    const float z = __fdiv_rn(__bfloat162float(row[v]), a.temperature);
+    const float g = -logf(-logf(hash_uniform(a.seed, b, a.step, v)));
+    const float key = z + g;
+    if (key > acc.key) {  // v increases: the first maximum stays
+      acc.key = key;
+      acc.idx = v;
+      acc.z = z;
+    }
+    if (z > acc.m) {
+      acc.s = acc.s * expf(acc.m - z) + 1.0f;
+      acc.m = z;
+    } else {
+      acc.s += expf(z - acc.m);
+    }
+  }
+  // warp, then block
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    SsPartial x;
+    x.key = __shfl_xor_sync(0xffffffffu, acc.key, o);
+    x.idx = __shfl_xor_sync(0xffffffffu, acc.idx, o);
+    x.z = __shfl_xor_sync(0xffffffffu, acc.z, o);
+    x.m = __shfl_xor_sync(0xffffffffu, acc.m, o);
+    x.s = __shfl_xor_sync(0xffffffffu, acc.s, o);
+    ss_merge(acc, x);
+  }
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    SsPartial t = red[0];
+    for (int w = 1; w < SS_THREADS / 32; ++w) ss_merge(t, red[w]);
+    parts[(long long)b * SS_MAX_SPLIT + part] = t;
+    __threadfence();
+    const int prev = atomic_add_acq_rel_gpu(&done[b], 1);
+    last = prev == split - 1;
+    if (last) {
+      done[b] = 0;
+      SsPartial r{-INFINITY, 0.0f, -INFINITY, 0.0f, 0x7fffffff};
+      for (int i = 0; i < split; ++i) {
+        const SsPartial* src = &parts[(long long)b * SS_MAX_SPLIT + i];
+        SsPartial x;  // other CTAs' partials: read through L2
+        x.key = __ldcg(&src->key);
+        x.z = __ldcg(&src->z);
+        x.m = __ldcg(&src->m);
+        x.s = __ldcg(&src->s);
+        x.idx = __ldcg(&src->idx);
+        ss_merge(r, x);
+      }
+      const long long o = (long long)b * a.block + a.step;
+      a.tokens[o] = r.idx;
+      if (a.q != nullptr) a.q[o] = expf(r.z - r.m) / r.s;
+      if (a.prev != nullptr) a.prev[b] = r.idx;
+    }
+  }
+}
+
+}  // namespace ls
+
+extern "C" size_t ls_sample_step_workspace_bytes(int batch) {
+  if (batch <= 0) return 0;
+  return 256 + (static_cast<size_t>(batch) * 4 + 255) / 256 * 256 + static_cast<size_t>(batch) * SS_MAX_SPLIT * sizeof(SsPartial);
+}
+
+extern "C" int ls_sample_step(void* stream, const ls_sample_step_args* a, void* workspace, size_t workspace_bytes) {
+  if (a == nullptr || a->logits == nullptr || a->tokens == nullptr)
+    return set_error(LS_ERR_INVALID, "ls_sample_step: null pointer argument");
+  if (a->batch <= 0) return LS_OK;
+  if (a->vocab <= 0 || a->block < 1 || a->step < 0 || a->step >= a->block || a->logits_ld < a->vocab)
+    return set_error(LS_ERR_INVALID, "ls_sample_step: bad vocab/block/step/logits_ld");
+  if (!(a->temperature > 0.0f) || !isfinite(a->temperature))
+    return set_error(LS_ERR_INVALID, "ls_sample_step: temperature must be positive and finite (T = 0 is "
+                                     "ls_markov_argmax)");
+  const size_t need = ls_sample_step_workspace_bytes(a->batch);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(LS_ERR_WORKSPACE, "ls_sample_step: workspace %zu < %zu", workspace_bytes, need);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return set_error(LS_ERR_INVALID, "ls_sample_step: workspace must be 256-byte aligned");
+  int* done = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + 256);
+  SsPartial* parts = reinterpret_cast<SsPartial*>(static_cast<uint8_t*>(workspace) + 256 +
+                                                  (static_cast<size_t>(a->batch) * 4 + 255) / 256 * 256);
+  int split = (2 * host_sm_count() + a->batch - 1) / a->batch;
+  split = split < 1 ? 1 : (split > SS_MAX_SPLIT ? SS_MAX_SPLIT : split);
+  if (split > a->vocab) split = a->vocab;
+  cudaError_t e = launch_pdl(sample_step_kernel, dim3(static_cast<unsigned>(a->batch * split)), dim3(SS_THREADS), 0,
+                             reinterpret_cast<cudaStream_t>(stream), *a, split, parts, done);
+  return e == cudaSuccess ? LS_OK : set_cuda_error("ls_sample_step: launch", e);
+}
+
 extern "C" int ls_accept(void* stream, const long long* target, int target_ld, const long long* draft, long long* accept,
                          int batch, int block) {
   if (batch <= 0) return LS_OK;

@@ -143,6 +143,10 @@ class LongSparkDraft:
         self.graphs = {}
         self.fallbacks = 0
         self._logits = None
+        # T > 0: every proposal draws with a fresh seed derived from this one
+        self._temperature = 0.0
+        self._sample_seed = int(_cfg(config, "seed", 0))
+        self._sample_round = 0
         # Step path: a decode update stages its rows and metadata and launches
         # nothing; the next propose for the same requests replays one graph
         # (page-table gather, window scatter, drafter pass with the refresh).
@@ -276,8 +280,9 @@ class LongSparkDraft:
         return g
 
     def propose(self, ids, anchors, temperature):
-        if temperature != 0:
-            raise NotImplementedError("sampled (T > 0) proposals are not implemented by the B200 drafter")
+        if temperature < 0:
+            raise ValueError("temperature must be >= 0")
+        self._temperature = float(temperature)
         dev = self.device
         B = len(ids)
         if self._pending is not None and self.use_graph and self._pending[0] == tuple(ids):
@@ -318,6 +323,8 @@ class LongSparkDraft:
         return self._propose_outputs(B, run_anchors, run_batch)
 
     def _propose_outputs(self, B, run_anchors, run_batch):
+        if self._temperature > 0:
+            return self._sampled_outputs(B, run_anchors, run_batch)
         tokens = self.engine.buf["tokens"][:B].clone()
         logits = None
         if self.materialize_logits:
@@ -328,6 +335,22 @@ class LongSparkDraft:
             self.engine.corrected_logits(run_anchors, self._logits, batch=run_batch)
             logits = self._logits[:B * s.block].view(B, s.block, s.vocab).clone()
         return tokens, logits, None
+
+    def _sampled_outputs(self, B, run_anchors, run_batch):
+        """T > 0: the step loop over the pass's base logits (``DraftEngine.sample``)
+        with a fresh seed per proposal; returns (tokens, corrected logits or
+        None, q) like ``LongSparkDraft.propose`` (LS engine/draft.py:281-286)."""
+        s = self.shape
+        self._sample_round += 1
+        seed = (self._sample_seed * 0x9E3779B97F4A7C15 + self._sample_round) & (2 ** 64 - 1)
+        if self.materialize_logits and self._logits is None:
+            self._logits = torch.empty(self.capacity * s.block, s.vocab, dtype=torch.bfloat16, device=self.device)
+        corr = self.engine.sample(run_anchors[:run_batch], temperature=self._temperature, seed=seed,
+                                  corrected=self._logits, batch=run_batch)
+        tokens = self.engine.buf["tokens"][:B].clone()
+        q = self.engine.buf["q"][:B].clone()
+        logits = corr[:B].clone() if self.materialize_logits else None
+        return tokens, logits, q
 
     def release(self, ids):
         self._flush()

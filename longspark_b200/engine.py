@@ -160,7 +160,7 @@ class DraftEngine:
         gemm_shapes = [(B, s.tap_layers * H, H), (B, H, H), (M, 2 * H, H), (M, H, H),
                        (M, H, (Hq + 2 * Hkv) * 128), (M, Hq * 128, H), (M, H, 2 * I), (M, I, H), (M, H, V)]
         if s.markov_rank:
-            gemm_shapes.append((M, s.markov_rank, V))
+            gemm_shapes += [(M, s.markov_rank, V), (B, s.markov_rank, V)]
         # the largest token count needs the largest stream-K workspace (token tile,
         # tile count and grid all grow with it)
         ws = max(ops.gemm_workspace_bytes(r0, k, n) for (r0, k, n) in gemm_shapes)
@@ -263,6 +263,49 @@ class DraftEngine:
                           tokens=b["tokens"], block=P, workspace=self.markov_ws, w1=w.w1, w2=w.w2,
                           w1_bound=w.w1_bound, w2_bound=w.w2_bound, target=target,
                           accept_out=b["accept"] if target is not None else None, status=st, batch=B)
+
+    def sample(self, anchors, *, temperature, seed, corrected=None, batch=None):
+        """Sampled (T > 0) proposals from the base logits of the last pass, the
+        reference's step loop (``sample_block_tokens``, SF draftfreekv.py:
+        2366-2407): for each step t the Markov-corrected step logits are one
+        tcgen05 GEMM of the previous tokens' w1 rows against w2 with the
+        LS_EPI_MARKOV_ADD epilogue, written into ``corrected`` [B*P, V] (the
+        ``corrected`` tensor the reference returns), then ``ls_sample_step``
+        draws the token from softmax(step / T) and its probability q.  Writes
+        ``buf['tokens']`` [B, P] and ``buf['q']`` [B, P]; returns ``corrected``
+        viewed [B, P, V] (the base logits themselves without a Markov head)."""
+        s, b, w = self.shape, self.buf, self.w
+        B = anchors.shape[0] if batch is None else batch
+        P, V = s.block, s.vocab
+        M = B * P
+        dev = self.device
+        if "sample_ws" not in b:
+            b["sample_ws"] = torch.zeros(max(256, ops.sample_step_workspace_bytes(self.max_batch)),
+                                         dtype=torch.uint8, device=dev)
+            b["prev"] = torch.zeros(self.max_batch, dtype=torch.int32, device=dev)
+            b["q"] = torch.zeros(self.max_batch, P, dtype=torch.float32, device=dev)
+            if w.w1 is not None:
+                b["xw"] = torch.zeros(self.max_batch, s.markov_rank, dtype=torch.bfloat16, device=dev)
+        st = b["status"]
+        prev = b["prev"][:B]
+        prev.copy_(anchors[:B])
+        base = b["logits"][:M].view(B, P, V)
+        if w.w1 is not None:
+            if corrected is None:
+                if "corrected" not in b:
+                    b["corrected"] = torch.empty(self.max_batch * P, V, dtype=torch.bfloat16, device=dev)
+                corrected = b["corrected"]
+            corr = corrected[:M].view(B, P, V)
+        else:
+            corr = base
+        for t in range(P):
+            if w.w1 is not None:
+                ops.gather_rows(w.w1, prev, b["xw"], rows=B, status=st)
+                ops.gemm(b["xw"], w.w2, corr[:, t], workspace=self.gemm_ws, epilogue=N.EPI_MARKOV_ADD, rows=B,
+                         base=base[:, t], status=st)
+            ops.sample_step(logits=corr[:, t], step=t, block=P, temperature=temperature, seed=seed,
+                            tokens=b["tokens"], workspace=b["sample_ws"], q=b["q"], prev=prev, status=st, batch=B)
+        return corr
 
     def corrected_logits(self, anchors, out, batch=None):
         """Markov-corrected logits of the last pass, ``base + bias(prev)`` per step

@@ -358,6 +358,27 @@ def markov_argmax(*, base, tile_max, tile_arg, anchors, tokens, block, workspace
     return tokens
 
 
+def sample_step_workspace_bytes(batch):
+    return N.lib().ls_sample_step_workspace_bytes(batch)
+
+
+def sample_step(*, logits, step, block, temperature, seed, tokens, workspace, q=None, prev=None, status=None,
+                batch=None):
+    """One step of the T > 0 chain (``ls_sample_step``): ``logits`` [B, V] view
+    (row stride = its stride(0)) of the step's bf16 logits; writes column
+    ``step`` of ``tokens`` [B, block] int64 and ``q`` [B, block] fp32, and
+    ``prev`` [B] int32."""
+    _require_cuda(logits, tokens, workspace)
+    if logits.dtype != torch.bfloat16 or logits.stride(-1) != 1:
+        raise ValueError("step logits must be bf16 with unit stride along the vocabulary")
+    batch = logits.shape[0] if batch is None else batch
+    a = N.SampleStepArgs(logits=_p(logits), logits_ld=logits.stride(0), batch=batch, vocab=logits.shape[-1],
+                         block=block, step=step, temperature=float(temperature), seed=int(seed) & (2 ** 64 - 1),
+                         tokens=_p(tokens), q=_p(q), prev=_p(prev), status=_p(status))
+    N.call("ls_sample_step", _stream(tokens.device), C.byref(a), _p(workspace),
+           workspace.numel() * workspace.element_size())
+
+
 def accept_lengths(target, draft, out):
     """Greedy accepted-prefix length (``src/longspark/engine/target.py:472-477``)."""
     _require_cuda(target, draft, out)

@@ -404,7 +404,7 @@ def gumbel_hash_uniform(seed, b, t, v):
     return (((x >> np.uint64(8)).astype(np.float64) + 0.5) * 2.0 ** -24).astype(np.float32)
 
 
-def markov_sample_gumbel(base_logits, anchors, W, prec, temperature, seed):
+def markov_sample_gumbel(base_logits, anchors, W, prec, temperature, seed, forced=None):
     """``DSparkVanillaMarkovHead.sample_block_tokens`` at T > 0 (SF
     draftfreekv.py:2366-2407) and the proposal probability of
     ``LongSparkDraft.propose`` (LS engine/draft.py:284-286): per step,
@@ -413,8 +413,10 @@ def markov_sample_gumbel(base_logits, anchors, W, prec, temperature, seed):
     The reference draws with ``torch.multinomial``; here the draw is the
     Gumbel-max of ``step / T + g`` with ``g = -log(-log(u))`` and ``u`` from
     ``gumbel_hash_uniform(seed, b, t, v)`` -- the same distribution, and a
-    reproducible one.  Returns tokens [B, P] int64, q [B, P] fp32, corrected
-    logits [B, P, V]."""
+    reproducible one.  ``forced`` ([B, P]) feeds the given tokens back as the
+    previous tokens (to follow a chain past a near-tie).  Returns tokens
+    [B, P] int64, q [B, P] fp32, corrected logits [B, P, V] and the gap
+    between the two largest keys per step [B, P]."""
     w1 = W.get("parallel_markov_head.markov_w1.weight")
     w2 = W.get("parallel_markov_head.markov_w2.weight")
     b_n, p_n, vocab = base_logits.shape
@@ -422,8 +424,9 @@ def markov_sample_gumbel(base_logits, anchors, W, prec, temperature, seed):
     toks = np.zeros((b_n, p_n), dtype=np.int64)
     q = np.zeros((b_n, p_n), dtype=np.float32)
     corrected = np.zeros_like(base_logits)
-    inv_t = np.float32(1.0) / np.float32(temperature)
+    temp = np.float32(temperature)
     ids = np.arange(vocab)
+    gap = np.zeros((b_n, p_n), dtype=np.float32)
     for t in range(p_n):
         if w1 is None:
             step = base_logits[:, t]
@@ -431,16 +434,19 @@ def markov_sample_gumbel(base_logits, anchors, W, prec, temperature, seed):
             step = rnd(base_logits[:, t] + linear(w1[prev], w2, prec), prec)
         corrected[:, t] = step
         for b in range(b_n):
-            z = step[b].astype(np.float32) * inv_t
+            z = (step[b].astype(np.float32) / temp).astype(np.float32)
             u = gumbel_hash_uniform(seed, b, t, ids)
             g = -np.log(-np.log(u))
-            tok = int(np.argmax(z + g))
+            key = (z + g).astype(np.float32)
+            tok = int(np.argmax(key))
+            top2 = np.partition(key, -2)[-2:]
+            gap[b, t] = top2[1] - top2[0]
             m = z.max()
             e = np.exp(z - m)
             q[b, t] = e[tok] / e.sum(dtype=np.float32)
             toks[b, t] = tok
-        prev = toks[:, t].copy()
-    return toks, q, corrected
+        prev = toks[:, t].copy() if forced is None else np.asarray(forced[:, t], dtype=np.int64)
+    return toks, q, corrected, gap
 
 
 def accept_lengths(target_tokens, draft_tokens):

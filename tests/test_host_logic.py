@@ -113,3 +113,20 @@ def test_target_from_draft_gives_requested_accept_length():
     acc = (tgt[:, :15] == draft).long().cumprod(1).sum(1)
     assert torch.equal(acc, k)
     assert 1.5 < k.float().mean() < 4.5  # geometric with mean 3
+
+
+def test_sampling_hash_is_uniform_and_counter_based():
+    """The T > 0 noise source: deterministic in (seed, request, step, token),
+    different across each counter, and uniform on (0, 1)."""
+    import numpy as np
+    import oracle as O
+    v = np.arange(1 << 18)
+    u = O.gumbel_hash_uniform(7, 0, 0, v)
+    assert np.array_equal(u, O.gumbel_hash_uniform(7, 0, 0, v))
+    assert 0.0 < u.min() and u.max() < 1.0
+    hist = np.histogram(u, bins=16, range=(0, 1))[0]
+    assert np.abs(hist / len(v) * 16 - 1).max() < 0.02
+    for other in (O.gumbel_hash_uniform(8, 0, 0, v), O.gumbel_hash_uniform(7, 1, 0, v),
+                  O.gumbel_hash_uniform(7, 0, 1, v), O.gumbel_hash_uniform(7 << 32, 0, 0, v)):
+        assert np.mean(other == u) < 1e-3
+        assert abs(np.corrcoef(other, u)[0, 1]) < 0.01

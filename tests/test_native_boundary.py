@@ -49,7 +49,8 @@ def test_struct_layouts_match_the_header(lib):
     text = HEADER.read_text()
     for cname, py in (("ls_gemm_args", N.GemmArgs), ("ls_refresh_args", N.RefreshArgs),
                       ("ls_attention_args", N.AttentionArgs), ("ls_markov_args", N.MarkovArgs),
-                      ("ls_prefill_args", N.PrefillArgs), ("ls_tp_group", N.TpGroup)):
+                      ("ls_prefill_args", N.PrefillArgs), ("ls_tp_group", N.TpGroup),
+                      ("ls_sample_step_args", N.SampleStepArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         body = re.sub(r"\[[^\]]*\]", "", body)  # array declarators: the name is what precedes them
