@@ -232,5 +232,16 @@ def test_longspark_draft_api_prefill_update_propose():
     toks_ref, corrected = O.markov_sample(base, np.array(anchors), Wn, "bf16", forced=gt)
     assert tokens_exact_or_tied(gt, corrected, what="api tokens") <= 2
     assert_bf16_close(to_np(logits), corrected, steps=4.0, exact_frac=0.3, what="api corrected logits")
+    # T > 0 on the same state: sampled tokens with their proposal probabilities
+    # (LS engine/draft.py:284-286), corrected logits as at T = 0 for the sampled chain
+    t2, l2, q2 = d.propose(ids, anchors, 0.8)
+    assert q2 is not None and q2.shape == (2, shape.block) and l2.shape == (2, shape.block, shape.vocab)
+    assert ((q2 > 0) & (q2 <= 1)).all() and ((t2 >= 0) & (t2 < shape.vocab)).all()
+    assert d.device_status() == 0
+    _, q_ref, corr_ref, _ = O.markov_sample_gumbel(to_np(d.engine.buf["logits"][:2 * shape.block]).reshape(
+        2, shape.block, shape.vocab), np.array(anchors), Wn, "bf16", 0.8, 0, forced=t2.cpu().numpy())
+    assert_bf16_close(to_np(l2), corr_ref, steps=1.0, exact_frac=0.98, what="api T>0 corrected logits")
+    t3, _, _ = d.propose(ids, anchors, 0.8)  # a fresh seed each proposal
+    assert not torch.equal(t2, t3)
     d.release(["a"])
     assert 1 in d.free_slots or 0 in d.free_slots
