@@ -365,6 +365,43 @@ def time_prefill_summary(eng, v, batch, reps=5):
     return e0.elapsed_time(e1) / reps, flops, eng.device_status()
 
 
+def time_sampled_round(eng, g, steps=50):
+    """T > 0 round (LongSparkDraft.propose(temperature > 0)): the drafter pass
+    (with the refresh) plus the 15-step sampled chain, one CUDA graph; ms per
+    replay and the HBM bytes the chain adds per round (the Markov w2 matrix
+    once per step, the reference's algorithm)."""
+    import torch
+    s, b = eng.shape, eng.buf
+    B = g.batch
+
+    def run():
+        g._run()
+        eng.sample(g.anchors, temperature=0.8, seed=12345, batch=B)
+
+    side = torch.cuda.Stream(device=eng.device)
+    side.wait_stream(torch.cuda.current_stream(eng.device))
+    with torch.cuda.stream(side):
+        run()
+    torch.cuda.current_stream(eng.device).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        run()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    del graph
+    chain_bytes = s.block * (eng.w.w2.numel() * 2 if eng.w.w2 is not None else 0)
+    return e0.elapsed_time(e1) / steps, chain_bytes, eng.device_status()
+
+
 def count_launches(eng, g):
     """Kernels of one round, counted from the native calls of an eager run."""
     from longspark_b200 import _native as N
@@ -477,8 +514,10 @@ def run_b200(args):
             dom_ms = time_dominant_kernel(eng)
             abytes = algorithmic_bytes(shape, eng, batch)
             pf_ms, pf_flops, pf_status = time_prefill_summary(eng, v, batch)
+            sr_ms, sr_bytes, sr_status = time_sampled_round(eng, g)
             headline = dict(ms=ms_max, clocks=clk.summary(), launches=launches, status=status, dom_ms=dom_ms,
-                            abytes=abytes, eng=eng, prefill=(pf_ms, pf_flops, pf_status))
+                            abytes=abytes, eng=eng, prefill=(pf_ms, pf_flops, pf_status),
+                            sampled=(sr_ms, sr_bytes, sr_status))
         else:
             ms_max = dist_max(time_graph(g, steps, 3, world), world)
             abytes = algorithmic_bytes(shape, eng, batch)
@@ -564,6 +603,15 @@ def run_b200(args):
                                      "softmax weights (P.V issued twice); algorithmic flops = 4 * 128 per "
                                      "(query, key)"},
                 "device_status": headline["prefill"][2]},
+            "sampled_round": {
+                "what": "temperature 0.8: drafter pass with the refresh, then the 15-step chain (per step one "
+                        "Markov-bias GEMM over the whole vocabulary and one Gumbel-max draw), one CUDA graph",
+                "round_us": round(headline["sampled"][0] * 1e3, 1),
+                "draft_tokens_per_s": round(tokens_per_round * world / (headline["sampled"][0] * 1e-3), 1),
+                "hbm_gbs": round((headline["abytes"] + headline["sampled"][1]) / (headline["sampled"][0] * 1e-3)
+                                 / 1e9, 1),
+                "algorithmic_bytes": headline["abytes"] + headline["sampled"][1],
+                "device_status": headline["sampled"][2]},
             "e2e": e2e,
             "gpu_launches": headline["launches"] * args.steps,
             "gpu_launches_per_step": headline["launches"],
