@@ -62,6 +62,8 @@ def parse():
                     help="diagnostic: device time of every native call of one eager round (one GPU), not a bench line")
     ap.add_argument("--calls-shape", default="cfg2", help="cfg2, or cfg5-tpN: the per-rank shapes of config 5 at TP N")
     ap.add_argument("--calls-ctx", type=int, default=4096)
+    ap.add_argument("--calls-temperature", type=float, default=0.0,
+                    help="> 0: the round includes the sampled chain (DraftEngine.sample)")
     return ap.parse_args()
 
 
@@ -840,6 +842,8 @@ def run_calls(args):
         for _ in range(max(2, min(args.steps, 20))):
             records.clear()
             g._run()
+            if args.calls_temperature > 0:
+                eng.sample(g.anchors, temperature=args.calls_temperature, seed=7, batch=args.batch)
             torch.cuda.synchronize()
             for i, (name, e0, e1) in enumerate(records):
                 per.setdefault((i, name), []).append(e0.elapsed_time(e1) * 1e3)

@@ -890,12 +890,21 @@ __global__ void __launch_bounds__(SS_THREADS) sample_step_kernel(const ls_sample
     __threadfence();
     const int prev = atomic_add_acq_rel_gpu(&done[b], 1);
     last = prev == split - 1;
-    if (last) {
-      done[b] = 0;
-      SsPartial r{-INFINITY, 0.0f, -INFINITY, 0.0f, 0x7fffffff};
-      for (int i = 0; i < split; ++i) {
+    if (last) done[b] = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  // The request's last slice merges all slices: warp 0 loads them (one or
+  // two per lane, read through L2) and merges them in a fixed butterfly order,
+  // so the same inputs always give the same bits.
+  if (warp == 0) {
+    SsPartial r{-INFINITY, 0.0f, -INFINITY, 0.0f, 0x7fffffff};
+#pragma unroll
+    for (int k = 0; k < SS_MAX_SPLIT / 32; ++k) {
+      const int i = lane + 32 * k;
+      if (i < split) {
         const SsPartial* src = &parts[(long long)b * SS_MAX_SPLIT + i];
-        SsPartial x;  // other CTAs' partials: read through L2
+        SsPartial x;
         x.key = __ldcg(&src->key);
         x.z = __ldcg(&src->z);
         x.m = __ldcg(&src->m);
@@ -903,6 +912,18 @@ __global__ void __launch_bounds__(SS_THREADS) sample_step_kernel(const ls_sample
         x.idx = __ldcg(&src->idx);
         ss_merge(r, x);
       }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      SsPartial x;
+      x.key = __shfl_xor_sync(0xffffffffu, r.key, o);
+      x.idx = __shfl_xor_sync(0xffffffffu, r.idx, o);
+      x.z = __shfl_xor_sync(0xffffffffu, r.z, o);
+      x.m = __shfl_xor_sync(0xffffffffu, r.m, o);
+      x.s = __shfl_xor_sync(0xffffffffu, r.s, o);
+      ss_merge(r, x);
+    }
+    if (lane == 0) {
       const long long o = (long long)b * a.block + a.step;
       a.tokens[o] = r.idx;
       if (a.q != nullptr) a.q[o] = expf(r.z - r.m) / r.s;

@@ -74,12 +74,15 @@ class DraftWeights:
         if shape.markov_rank:
             self.w1 = t("parallel_markov_head.markov_w1.weight")
             self.w2 = t("parallel_markov_head.markov_w2.weight")
+            # tile copy for the full-vocabulary bias GEMMs (T > 0 chain, corrected
+            # logits); the greedy chain gathers rows of the row-major copy
+            self.w2_tiled = ops.TiledWeight(self.w2)
             self.w1_bound = torch.zeros(1, dtype=torch.float32, device=dev)
             self.w2_bound = torch.zeros(1, dtype=torch.float32, device=dev)
             ops.row_norm_bound(self.w1, self.w1_bound)
             ops.row_norm_bound(self.w2, self.w2_bound)
         else:
-            self.w1 = self.w2 = self.w1_bound = self.w2_bound = None
+            self.w1 = self.w2 = self.w1_bound = self.w2_bound = self.w2_tiled = None
         if inv_freq is None:
             d = shape.head_dim
             inv_freq = 1.0 / (float(shape.rope_theta) ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
@@ -301,7 +304,7 @@ class DraftEngine:
         for t in range(P):
             if w.w1 is not None:
                 ops.gather_rows(w.w1, prev, b["xw"], rows=B, status=st)
-                ops.gemm(b["xw"], w.w2, corr[:, t], workspace=self.gemm_ws, epilogue=N.EPI_MARKOV_ADD, rows=B,
+                ops.gemm(b["xw"], w.w2_tiled, corr[:, t], workspace=self.gemm_ws, epilogue=N.EPI_MARKOV_ADD, rows=B,
                          base=base[:, t], status=st)
             ops.sample_step(logits=corr[:, t], step=t, block=P, temperature=temperature, seed=seed,
                             tokens=b["tokens"], workspace=b["sample_ws"], q=b["q"], prev=prev, status=st, batch=B)
@@ -318,7 +321,7 @@ class DraftEngine:
             return out
         prev = torch.cat([anchors[:B, None], b["tokens"][:B, :-1]], dim=1).reshape(-1)
         x = w.w1.index_select(0, prev)
-        ops.gemm(x, w.w2, out, workspace=self.gemm_ws, epilogue=N.EPI_MARKOV_ADD, rows=M, base=b["logits"],
+        ops.gemm(x, w.w2_tiled, out, workspace=self.gemm_ws, epilogue=N.EPI_MARKOV_ADD, rows=M, base=b["logits"],
                  status=b["status"])
         return out
 
