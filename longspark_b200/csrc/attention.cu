@@ -185,10 +185,18 @@ __device__ __forceinline__ void attend_block(WarpState& st, const uint32_t qf[8]
 //                           after the compute: the parked states
 //                           ml[2][G][16] (float2) then acc[2][G][16][128] (fp32).
 constexpr size_t AT_BUF_BYTES = (size_t)2 * 2 * AT_WROWS * AT_PITCH * 2;
+// Many-request mode (more clusters than two waves at one CTA per SM): 64-row
+// window sub-chunks, one warp per query head and at most 204 registers per
+// thread, so two CTAs share an SM and one CTA's staging latency hides behind
+// the other's compute.
+constexpr int AT_WROWS_MANY = 64;
+constexpr size_t AT_BUF_BYTES_MANY = (size_t)2 * 2 * AT_WROWS_MANY * AT_PITCH * 2;
 
 __host__ __device__ inline size_t at_q_bytes(int G) { return (size_t)G * 16 * AT_PITCH * 2; }
 __host__ __device__ inline size_t at_local_bytes() { return (size_t)2 * 32 * AT_PITCH * 2; }
-__host__ __device__ inline size_t at_smem_bytes(int G) { return at_q_bytes(G) + at_local_bytes() + AT_BUF_BYTES; }
+__host__ __device__ inline size_t at_smem_bytes(int G, bool many = false) {
+  return at_q_bytes(G) + at_local_bytes() + (many ? AT_BUF_BYTES_MANY : AT_BUF_BYTES);
+}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -218,15 +226,15 @@ __device__ __forceinline__ float2 dsmem_ld_f2(uint32_t addr) {
 __device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // Stage window rows [r0, r0 + n) (relative to the window start) of KV head g
-// into one (K, V) sub-chunk buffer; rows n..AT_WROWS-1 are zero.  pg holds
+// into one (K, V) sub-chunk buffer of wsub rows; rows n..wsub-1 are zero.  pg holds
 // the page ids of logical pages first_lp.. (-1: invalid, read as zeros).
 __device__ __forceinline__ void stage_window(const AttnParams& p, bf16 (*ks)[AT_PITCH], bf16 (*vs)[AT_PITCH], int g,
-                                             int start, int r0, int n, const int* pg, int first_lp) {
+                                             int start, int r0, int n, const int* pg, int first_lp, int wsub) {
   const ls_attention_args& a = p.a;
   const bf16* kk = reinterpret_cast<const bf16*>(a.kv_k);
   const bf16* vv = reinterpret_cast<const bf16*>(a.kv_v);
 #pragma unroll 4
-  for (int i = threadIdx.x; i < AT_WROWS * 16; i += blockDim.x) {
+  for (int i = threadIdx.x; i < wsub * 16; i += blockDim.x) {
     const int r = i >> 4, col = (i & 15) << 3;
     const int pos = start + r0 + r;
     const int page = r < n ? pg[(pos >> 4) - first_lp] : -1;
@@ -321,7 +329,9 @@ __device__ __forceinline__ void fold_parked(const float2* ml, const float* acc, 
   }
 }
 
-__global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams p) {
+template <bool MANY>
+__global__ void __launch_bounds__(MANY ? 160 : 256, MANY ? 2 : 1) attention_cluster_kernel(const AttnParams p) {
+  constexpr int WSUB = MANY ? AT_WROWS_MANY : AT_WROWS;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   asm volatile("griddepcontrol.launch_dependents;");
   const ls_attention_args& a = p.a;
@@ -365,7 +375,7 @@ __global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams
     w_r0 = rank * p.wrows;
     w_n = wl - w_r0 < p.wrows ? wl - w_r0 : p.wrows;
     if (w_n < 0) w_n = 0;
-    n_sub = (w_n + AT_WROWS - 1) / AT_WROWS;
+    n_sub = (w_n + WSUB - 1) / WSUB;
     // page ids of this CTA's rows, read once (every K/V address depends on them)
     first_lp = (wstart + w_r0) >> 4;
     const int n_pages = w_n > 0 ? ((wstart + w_r0 + w_n - 1) >> 4) - first_lp + 1 : 0;
@@ -381,9 +391,9 @@ __global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams
     }
     __syncthreads();
     for (int i = 0; i < 2 && i < n_sub; ++i) {
-      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + i * 2 * AT_WROWS;
-      const int n = w_n - i * AT_WROWS < AT_WROWS ? w_n - i * AT_WROWS : AT_WROWS;
-      stage_window(p, ks, ks + AT_WROWS, g, wstart, w_r0 + i * AT_WROWS, n, pg, first_lp);
+      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + i * 2 * WSUB;
+      const int n = w_n - i * WSUB < WSUB ? w_n - i * WSUB : WSUB;
+      stage_window(p, ks, ks + WSUB, g, wstart, w_r0 + i * WSUB, n, pg, first_lp, WSUB);
       cp_async_commit();
     }
   } else if (is_sum) {
@@ -431,29 +441,34 @@ __global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams
     for (int i = 0; i < n_sub; ++i) {
       if (i + 1 < n_sub) cp_async_wait_one(); else cp_async_wait_all();
       __syncthreads();
-      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + (i & 1) * 2 * AT_WROWS;
-      const int n = w_n - i * AT_WROWS < AT_WROWS ? w_n - i * AT_WROWS : AT_WROWS;
+      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + (i & 1) * 2 * WSUB;
+      const int n = w_n - i * WSUB < WSUB ? w_n - i * WSUB : WSUB;
       if (R == 1) {
-        attend_block<16>(st, qf, ks, ks + AT_WROWS, 0, n, a.softmax_scale);
+        attend_block<WSUB / 8>(st, qf, ks, ks + WSUB, 0, n, a.softmax_scale);
       } else if (n > part * 64) {
-        attend_block<8>(st, qf, ks, ks + AT_WROWS, part * 64, n - part * 64, a.softmax_scale);
+        attend_block<8>(st, qf, ks, ks + WSUB, part * 64, n - part * 64, a.softmax_scale);
       }
       __syncthreads();  // every warp is done with this buffer
       if (i + 2 < n_sub) {
-        const int n2 = w_n - (i + 2) * AT_WROWS < AT_WROWS ? w_n - (i + 2) * AT_WROWS : AT_WROWS;
-        stage_window(p, ks, ks + AT_WROWS, g, wstart, w_r0 + (i + 2) * AT_WROWS, n2, pg, first_lp);
+        const int n2 = w_n - (i + 2) * WSUB < WSUB ? w_n - (i + 2) * WSUB : WSUB;
+        stage_window(p, ks, ks + WSUB, g, wstart, w_r0 + (i + 2) * WSUB, n2, pg, first_lp, WSUB);
         cp_async_commit();
       }
     }
   } else if (is_sum) {
     // one chunk buffer per head; its R warps stage and attend disjoint 32-slot halves
     bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(buf) + hw * 2 * p.sc;
-    const int half = p.sc / R;  // 32
+    const int half = p.sc / R;  // 32, or 16 with five or more heads in the many-request mode
     for (int i = 0; i < s_sub; ++i) {
       cp_async_wait_all();
       __syncthreads();
       const int n = s_n - i * p.sc < p.sc ? s_n - i * p.sc : p.sc;
-      if (n > part * half) attend_block<4>(st, qf, ks, ks + p.sc, part * half, n - part * half, a.softmax_scale);
+      if (n > part * half) {
+        if (half == 32)
+          attend_block<4>(st, qf, ks, ks + p.sc, part * half, n - part * half, a.softmax_scale);
+        else
+          attend_block<2>(st, qf, ks, ks + p.sc, part * half, n - part * half, a.softmax_scale);
+      }
       __syncthreads();  // every warp is done with the buffers
       if (i + 1 < s_sub) {
         const int n2 = s_n - (i + 1) * p.sc < p.sc ? s_n - (i + 1) * p.sc : p.sc;
@@ -555,13 +570,17 @@ __global__ void __launch_bounds__(256) attention_cluster_kernel(const AttnParams
 }
 
 struct AttnPlan {
-  int G, nw, wrows, sslots, sc;
+  int G, nw, wrows, sslots, sc, threads;
+  bool many;
   size_t smem;
 };
 
-static AttnPlan plan_attention(int q_heads, int kv_heads, int window, int slots) {
+static AttnPlan plan_attention(int q_heads, int kv_heads, int window, int slots, int batch) {
   AttnPlan pl{};
   pl.G = q_heads / kv_heads;
+  // many-request mode when the clusters would take more than two waves at one
+  // CTA per SM (and the group fits its 160-thread launch bound)
+  pl.many = pl.G <= 5 && static_cast<long long>(batch) * kv_heads * AT_CLUSTER > 2LL * host_sm_count();
   // Split the 7 non-local CTAs between window and summary by bytes read: the
   // window is W rows shared by the group, the summary S slots per query head.
   const double wb = (double)window, sb = (double)pl.G * slots;
@@ -571,8 +590,13 @@ static AttnPlan plan_attention(int q_heads, int kv_heads, int window, int slots)
   pl.wrows = ((window + nw - 1) / nw + 31) / 32 * 32;
   const int ns = AT_CLUSTER - 1 - nw;
   pl.sslots = ((slots + ns - 1) / ns + 31) / 32 * 32;
-  pl.sc = pl.G <= 4 ? 64 : 32;  // G x sc x (K, V) rows fill the buffer area
-  pl.smem = at_smem_bytes(pl.G);
+  // G x sc x (K, V) rows fill the buffer area
+  if (pl.many)
+    pl.sc = pl.G <= 4 ? 32 : 16;
+  else
+    pl.sc = pl.G <= 4 ? 64 : 32;
+  pl.threads = 32 * pl.G * ((pl.G <= 4 && !pl.many) ? 2 : 1);
+  pl.smem = at_smem_bytes(pl.G, pl.many);
   return pl;
 }
 
@@ -603,7 +627,7 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
     return set_error(LS_ERR_UNSUPPORTED, "ls_draft_attention: need GQA group <= 8, 1 <= block <= 16");
   if ((long long)a->batch * a->kv_heads * AT_CLUSTER > 0x7fffffffLL)
     return set_error(LS_ERR_UNSUPPORTED, "ls_draft_attention: grid too large");
-  AttnPlan pl = plan_attention(a->q_heads, a->kv_heads, a->window, a->slots_per_head);
+  AttnPlan pl = plan_attention(a->q_heads, a->kv_heads, a->window, a->slots_per_head, a->batch);
   AttnParams p{};
   p.a = *a;
   p.G = pl.G;
@@ -611,16 +635,19 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
   p.wrows = pl.wrows;
   p.sslots = pl.sslots;
   p.sc = pl.sc;
-  static size_t configured = 0;
-  if (pl.smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(at_smem_bytes(8)));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_cluster_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(at_smem_bytes(5, true)));
     if (e != cudaSuccess) return set_cuda_error("ls_draft_attention: cudaFuncSetAttribute", e);
-    configured = at_smem_bytes(8);
+    configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a->batch * a->kv_heads * AT_CLUSTER));
-  cfg.blockDim = dim3(32 * pl.G * (pl.G <= 4 ? 2 : 1));
+  cfg.blockDim = dim3(pl.threads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[2];
@@ -632,6 +659,7 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attention_cluster_kernel, p);
+  cudaError_t e = pl.many ? cudaLaunchKernelEx(&cfg, attention_cluster_kernel<true>, p)
+                          : cudaLaunchKernelEx(&cfg, attention_cluster_kernel<false>, p);
   return e == cudaSuccess ? LS_OK : set_cuda_error("ls_draft_attention: launch", e);
 }

@@ -114,6 +114,10 @@ def test_reference_api_scores_and_merge():
     (32, 8, 64, 512, 15, (4096,)),
     (40, 8, 256, 2048, 15, (5000, 1999)),
     (32, 8, 256, 1024, 15, (1024, 17, 3000)),
+    # many requests: two CTAs per SM, 64-row window sub-chunks, one warp per head
+    (32, 8, 256, 1024, 15, tuple(900 + 37 * i for i in range(40))),
+    (40, 8, 256, 2048, 15, tuple(2100 + 301 * i for i in range(12))),
+    (8, 2, 16, 256, 7, tuple(5 + 23 * i for i in range(30))),
 ])
 def test_attention_matches_oracle(q_heads, kv_heads, slots, window, block, contexts):
     g = torch.Generator().manual_seed(11)
