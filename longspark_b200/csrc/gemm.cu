@@ -52,6 +52,7 @@ struct GemmKernelParams {
   int* counters;     // [tiles]
   TpView tp;         // tp.world > 0: row-parallel GEMM fused with the allreduce (ls_gemm_allreduce)
   int tp_wire;       // LS_TP_WIRE_*
+  int tp_oneshot;    // 1: every rank pushes its partials to every rank and reduces all tiles itself
 };
 
 __device__ __forceinline__ long long unit_begin(long long c, long long units, long long grid) {
@@ -268,10 +269,20 @@ __device__ __forceinline__ size_t tp_tile_bytes(const GemmKernelParams& P) {
   return static_cast<size_t>(P.bn) * BM * (P.tp_wire == LS_TP_WIRE_BF16 ? 2 : 4);
 }
 
-// Exchange slot of (tile t, source rank src) in the heap of t's owner.
-__device__ __forceinline__ uint8_t* tp_slot(const GemmKernelParams& P, int t, int src) {
+// Exchange slot of (tile t, source rank src) in the heap of rank dst.  Two-
+// step: only the tile's owner (t % world) holds slots, [t / world][src].  One-
+// shot: every rank holds [t][src] for every tile, in two halves by launch
+// parity: a rank can run one launch ahead of another (it finished its own
+// reduction) and write the next launch's partials while that rank still reads
+// this launch's, never two ahead (the next launch's reduction needs that
+// rank's partials, which it sends only after this launch).
+__device__ __forceinline__ uint8_t* tp_slot(const GemmKernelParams& P, int dst, int t, int src, uint32_t tgt) {
   const int W = P.tp.world;
-  return P.tp.sync[t % W] + TP_XCH_OFF + (static_cast<size_t>(t / W) * W + src) * tp_tile_bytes(P);
+  if (P.tp_oneshot) {
+    const size_t half = static_cast<size_t>(P.m_tiles) * P.n_tiles * W * tp_tile_bytes(P);
+    return P.tp.sync[dst] + TP_XCH_OFF + (tgt & 1u) * half + (static_cast<size_t>(t) * W + src) * tp_tile_bytes(P);
+  }
+  return P.tp.sync[dst] + TP_XCH_OFF + (static_cast<size_t>(t / W) * W + src) * tp_tile_bytes(P);
 }
 
 // Chunk [c, c + 16) of tile t (first token n0) into the owner's slot
@@ -285,32 +296,48 @@ static_assert(16 * TP_STAGE_PITCH_F * 4 <= sizeof(float) * 128 * 17, "TP stage m
 static_assert(sizeof(EpiScratch) + 15 <= EPI_SCRATCH_BYTES, "epilogue scratch slack for its 16-byte alignment");
 
 __device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, int n0, int c, const float (&v)[16],
-                                              int r, EpiScratch* sc) {
-  uint8_t* slot = tp_slot(P, t, P.tp.rank);
+                                              int r, EpiScratch* sc, uint32_t tgt) {
   const int lim = P.a.rows - n0 - c;  // tokens of the chunk that exist
+  // destinations: the owner (two-step) or every rank (one-shot)
+  const int d0 = P.tp_oneshot ? 0 : t % P.tp.world;
+  const int d1 = P.tp_oneshot ? P.tp.world : d0 + 1;
   if (P.tp_wire == LS_TP_WIRE_BF16) {
     bf16* sg = reinterpret_cast<bf16*>(&sc->xch[0][0]);
 #pragma unroll
     for (int j = 0; j < 16; ++j) sg[j * TP_STAGE_PITCH_H + r] = __float2bfloat16_rn(v[j]);
     epi_bar();
+    uint4 y[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int idx = r + i * 128, j = idx >> 4, q = idx & 15;  // token j, features 8q..8q+7
-      if (j < lim)
-        *reinterpret_cast<uint4*>(slot + (static_cast<size_t>(c + j) * BM + 8 * q) * 2) =
-            *reinterpret_cast<const uint4*>(&sg[j * TP_STAGE_PITCH_H + 8 * q]);
+      y[i] = *reinterpret_cast<const uint4*>(&sg[j * TP_STAGE_PITCH_H + 8 * q]);
+    }
+    for (int d = d0; d < d1; ++d) {
+      uint8_t* slot = tp_slot(P, d, t, P.tp.rank, tgt);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int idx = r + i * 128, j = idx >> 4, q = idx & 15;
+        if (j < lim) *reinterpret_cast<uint4*>(slot + (static_cast<size_t>(c + j) * BM + 8 * q) * 2) = y[i];
+      }
     }
   } else {
     float* sg = &sc->xch[0][0];
 #pragma unroll
     for (int j = 0; j < 16; ++j) sg[j * TP_STAGE_PITCH_F + r] = v[j];
     epi_bar();
+    float4 y[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int idx = r + i * 128, j = idx >> 5, q = idx & 31;  // token j, features 4q..4q+3
-      if (j < lim)
-        *reinterpret_cast<float4*>(slot + (static_cast<size_t>(c + j) * BM + 4 * q) * 4) =
-            *reinterpret_cast<const float4*>(&sg[j * TP_STAGE_PITCH_F + 4 * q]);
+      y[i] = *reinterpret_cast<const float4*>(&sg[j * TP_STAGE_PITCH_F + 4 * q]);
+    }
+    for (int d = d0; d < d1; ++d) {
+      uint8_t* slot = tp_slot(P, d, t, P.tp.rank, tgt);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int idx = r + i * 128, j = idx >> 5, q = idx & 31;
+        if (j < lim) *reinterpret_cast<float4*>(slot + (static_cast<size_t>(c + j) * BM + 4 * q) * 4) = y[i];
+      }
     }
   }
   epi_bar();  // the stage is reused by the next chunk
@@ -322,8 +349,11 @@ __device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, 
 // over them, so one fence per tile publishes the whole slot.
 __device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int r, uint32_t tgt) {
   epi_bar();
-  if (r == 0) {
-    fence_sys();
+  if (r == 0) fence_sys();
+  if (P.tp_oneshot) {
+    epi_bar();  // thread 0's fence before any flag
+    if (r < P.tp.world) st_release_sys(tp_arrive_flag(P.tp, r, t, P.tp.rank), tgt);
+  } else if (r == 0) {
     st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), tgt);
   }
 }
@@ -333,7 +363,7 @@ __device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int
 // the epilogue scratch, 16 contiguous bytes per thread.  All 128 epilogue
 // threads.
 __device__ __forceinline__ void tp_final_store(const GemmKernelParams& P, int m_tile, int n0, const float (&v)[16],
-                                               int r, EpiScratch* sc) {
+                                               int r, EpiScratch* sc, bool all_ranks) {
   const ls_gemm_args& a = P.a;
   const int f = m_tile * BM + r;
   const bool res = a.epilogue == LS_EPI_RESIDUAL;
@@ -360,7 +390,8 @@ __device__ __forceinline__ void tp_final_store(const GemmKernelParams& P, int m_
   }
   epi_bar();  // the stage is reused by the next chunk
   bf16* out = reinterpret_cast<bf16*>(a.out);
-  for (int p = 0; p < P.tp.world; ++p) {
+  const int p0 = all_ranks ? 0 : P.tp.rank, p1 = all_ranks ? P.tp.world : P.tp.rank + 1;
+  for (int p = p0; p < p1; ++p) {
     bf16* o = tp_peer(P.tp, p, out);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -378,11 +409,12 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
   const int rows = P.a.rows;
   int* status = P.a.status;
   const int gpt = (P.bn + TP_GROUP - 1) / TP_GROUP;  // token groups per tile
-  const int n_owned = tiles > me ? (tiles - me + W - 1) / W : 0;
+  // two-step: this rank's owned tiles; one-shot: every tile, all reduced here
+  const int n_owned = P.tp_oneshot ? tiles : (tiles > me ? (tiles - me + W - 1) / W : 0);
   const bool wire16 = P.tp_wire == LS_TP_WIRE_BF16;
   for (int uu = blockIdx.x; uu < n_owned * gpt; uu += gridDim.x) {
     const int tl = uu / gpt, gi = uu - tl * gpt;
-    const int t = tl * W + me;
+    const int t = P.tp_oneshot ? tl : tl * W + me;
     const int m_tile = t / P.n_tiles;
     const int n0 = (t - m_tile * P.n_tiles) * P.bn;
     const int c0 = gi * TP_GROUP;
@@ -404,7 +436,7 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           if (s0 + i < W) {
-            const uint8_t* slot = tp_slot(P, t, s0 + i);
+            const uint8_t* slot = tp_slot(P, me, t, s0 + i, tgt);
             if (wire16) {
               const unsigned short* q = reinterpret_cast<const unsigned short*>(slot) + static_cast<size_t>(c) * BM + r;
 #pragma unroll
@@ -424,9 +456,10 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
           }
         }
       }
-      tp_final_store(P, m_tile, n0 + c, v, r, sc);
+      tp_final_store(P, m_tile, n0 + c, v, r, sc, !P.tp_oneshot);
     }
   }
+  if (P.tp_oneshot) return;  // every rank reduced every tile itself: nothing to publish or wait for
   // one system-scope fence for all of this CTA's finalised groups, then their
   // done flags on every other rank
   epi_bar();
@@ -453,9 +486,9 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
 // A finished 16-token chunk: the fused epilogue, or (row-parallel TP) the send
 // of the partial to the tile's owner.
 __device__ __forceinline__ void emit_chunk(const GemmKernelParams& P, int t, int m_tile, int n0, int c,
-                                           const float (&v)[16], int r, int ew, EpiScratch* sc) {
+                                           const float (&v)[16], int r, int ew, EpiScratch* sc, uint32_t tp_tgt) {
   if (P.tp.world > 0)
-    tp_send_chunk(P, t, n0, c, v, r, sc);
+    tp_send_chunk(P, t, n0, c, v, r, sc, tp_tgt);
   else
     final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
 }
@@ -463,7 +496,7 @@ __device__ __forceinline__ void emit_chunk(const GemmKernelParams& P, int t, int
 // Reduction of a stream-K tile by its last contributor: the fp32 partials of
 // CTAs first..last summed in that order, then the fused epilogue.
 __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, int first, int last, int first_slot,
-                                            int r, int ew, EpiScratch* sc) {
+                                            int r, int ew, EpiScratch* sc, uint32_t tp_tgt) {
   const int bn = P.bn;
   const int m_tile = t / P.n_tiles;
   const int n0 = (t - m_tile * P.n_tiles) * bn;
@@ -492,7 +525,7 @@ __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, in
         }
       }
     }
-    if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc);
+    if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc, tp_tgt);
   }
 }
 
@@ -724,7 +757,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int c = 0; c < bn; c += 16) {
           float v[16];
           tmem_ld16(t_addr + c, v);
-          if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc);
+          if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc, tp_tgt);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
@@ -756,7 +789,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           // Tile t is the first tile of every contributor after `first`, and of
           // `first` itself only when its range starts exactly at the tile.
           const int first_slot = unit_begin(first, U, G) == tu0 ? 0 : 1;
-          reduce_tile(P, t, first, last, first_slot, r, ew, sc);
+          reduce_tile(P, t, first, last, first_slot, r, ew, sc, tp_tgt);
           if (r == 0) atomicExch(&P.counters[t], 0);
           if (P.tp.world > 0) tp_publish(P, t, r, tp_tgt);
         }
@@ -876,6 +909,11 @@ extern "C" size_t ls_gemm_workspace_bytes(int rows, int k, int n_out) {
 
 namespace ls {
 
+// One-shot exchange (every rank sends each partial to every rank, W - 1 times
+// the partial bytes, one NVLink hop) for up to four ranks; owner reduce +
+// broadcast (two hops, about twice the partial bytes in all) above that.
+static bool tp_oneshot(int world) { return world <= 4; }
+
 static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes, const TpView* tp,
                        int wire) {
   if (a == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm: null args");
@@ -953,6 +991,7 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
   if (tp != nullptr) {
     kp.tp = *tp;
     kp.tp_wire = wire;
+    kp.tp_oneshot = tp_oneshot(tp->world) ? 1 : 0;
   }
 
   const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.stages);
@@ -999,7 +1038,9 @@ extern "C" size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire) {
   for (int bn = pick_bn(rows);; bn = narrower_bn(bn)) {
     const long long tiles = static_cast<long long>(n_out / BM) * ((rows + bn - 1) / bn);
     const long long owned = (tiles + world - 1) / world;
-    const size_t b = static_cast<size_t>(owned) * world * bn * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);
+    const size_t tile_bytes = static_cast<size_t>(bn) * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);
+    const size_t b = tp_oneshot(world) ? 2 * static_cast<size_t>(tiles) * world * tile_bytes
+                                       : static_cast<size_t>(owned) * world * tile_bytes;
     need = b > need ? b : need;
     if (bn <= 64) break;
   }
