@@ -285,47 +285,60 @@ __device__ __forceinline__ uint8_t* tp_slot(const GemmKernelParams& P, int dst, 
   return P.tp.sync[dst] + TP_XCH_OFF + (static_cast<size_t>(t / W) * W + src) * tp_tile_bytes(P);
 }
 
-// Chunk [c, c + 16) of tile t (first token n0) into the destination slots
-// ([token][128 features], fp32 or bf16), through the epilogue scratch and the
-// bulk-copy engine.  All 128 epilogue threads.  The result broadcast of the
-// two-step exchange (tp_final_store) stages its bf16 rows with a padded pitch
-// and stores them with 16-byte thread stores.
-constexpr int TP_STAGE_PITCH_H = 136;   // bf16 stage row pitch of tp_final_store (272 B)
-static_assert(16 * BM * 4 <= sizeof(float) * 128 * 17, "a staged fp32 chunk must fit the epilogue scratch");
+// Chunk [c, c + 16) of tile t (first token n0) into the owner's slot
+// ([token][128 features], fp32 or bf16).  The chunk goes through the
+// epilogue scratch first so that every thread sends 16 contiguous bytes and a
+// warp instruction writes 512 contiguous bytes across NVLink (one token row
+// per thread would give 128- or 64-byte writes).  All 128 epilogue threads.
+constexpr int TP_STAGE_PITCH_F = 132;   // fp32 stage row pitch (528 B, 16-byte aligned)
+constexpr int TP_STAGE_PITCH_H = 136;   // bf16 stage row pitch (272 B)
+static_assert(16 * TP_STAGE_PITCH_F * 4 <= sizeof(float) * 128 * 17, "TP stage must fit the epilogue scratch");
 static_assert(sizeof(EpiScratch) + 15 <= EPI_SCRATCH_BYTES, "epilogue scratch slack for its 16-byte alignment");
 
 __device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, int n0, int c, const float (&v)[16],
                                               int r, EpiScratch* sc, uint32_t tgt) {
-  // The chunk is staged contiguously ([16 tokens][128 features], the slot's
-  // own layout) and thread 0 hands it to the bulk-copy engine, one copy per
-  // destination: TMA moves 4-8 KiB per instruction across NVLink where thread
-  // stores would issue 16-byte pieces.
   const int lim = P.a.rows - n0 - c;  // tokens of the chunk that exist
-  const int nrow = lim < 16 ? lim : 16;
-  const int d0 = P.tp_oneshot ? 0 : t % P.tp.world;  // the owner (two-step) or every rank (one-shot)
+  // destinations: the owner (two-step) or every rank (one-shot)
+  const int d0 = P.tp_oneshot ? 0 : t % P.tp.world;
   const int d1 = P.tp_oneshot ? P.tp.world : d0 + 1;
-  const bool wire16 = P.tp_wire == LS_TP_WIRE_BF16;
-  if (wire16) {
+  if (P.tp_wire == LS_TP_WIRE_BF16) {
     bf16* sg = reinterpret_cast<bf16*>(&sc->xch[0][0]);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) sg[j * BM + r] = __float2bfloat16_rn(v[j]);
+    for (int j = 0; j < 16; ++j) sg[j * TP_STAGE_PITCH_H + r] = __float2bfloat16_rn(v[j]);
+    epi_bar();
+    uint4 y[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int idx = r + i * 128, j = idx >> 4, q = idx & 15;  // token j, features 8q..8q+7
+      y[i] = *reinterpret_cast<const uint4*>(&sg[j * TP_STAGE_PITCH_H + 8 * q]);
+    }
+    for (int d = d0; d < d1; ++d) {
+      uint8_t* slot = tp_slot(P, d, t, P.tp.rank, tgt);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int idx = r + i * 128, j = idx >> 4, q = idx & 15;
+        if (j < lim) *reinterpret_cast<uint4*>(slot + (static_cast<size_t>(c + j) * BM + 8 * q) * 2) = y[i];
+      }
+    }
   } else {
     float* sg = &sc->xch[0][0];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) sg[j * BM + r] = v[j];
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // this thread's stage writes -> the copy engine
-  epi_bar();
-  if (r == 0) {
-    const uint32_t src = smem_u32(&sc->xch[0][0]);
-    const uint32_t bytes = static_cast<uint32_t>(nrow) * BM * (wire16 ? 2 : 4);
-    for (int d = d0; d < d1; ++d) {
-      uint8_t* dst = tp_slot(P, d, t, P.tp.rank, tgt) + static_cast<size_t>(c) * BM * (wire16 ? 2 : 4);
-      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
-                   : "memory");
+    for (int j = 0; j < 16; ++j) sg[j * TP_STAGE_PITCH_F + r] = v[j];
+    epi_bar();
+    float4 y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = r + i * 128, j = idx >> 5, q = idx & 31;  // token j, features 4q..4q+3
+      y[i] = *reinterpret_cast<const float4*>(&sg[j * TP_STAGE_PITCH_F + 4 * q]);
     }
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the stage has been read
+    for (int d = d0; d < d1; ++d) {
+      uint8_t* slot = tp_slot(P, d, t, P.tp.rank, tgt);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int idx = r + i * 128, j = idx >> 5, q = idx & 31;
+        if (j < lim) *reinterpret_cast<float4*>(slot + (static_cast<size_t>(c + j) * BM + 4 * q) * 4) = y[i];
+      }
+    }
   }
   epi_bar();  // the stage is reused by the next chunk
 }
@@ -335,17 +348,13 @@ __device__ __forceinline__ void tp_send_chunk(const GemmKernelParams& P, int t, 
 // thread's stores before thread 0's system-scope fence, which is cumulative
 // over them, so one fence per tile publishes the whole slot.
 __device__ __forceinline__ void tp_publish(const GemmKernelParams& P, int t, int r, uint32_t tgt) {
-  // thread 0 issued every bulk copy of the tile: wait until they have landed,
-  // order them before its system-scope release, then flag the destinations
-  if (r == 0) {
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    fence_sys();
-    if (P.tp_oneshot) {
-      for (int d = 0; d < P.tp.world; ++d) st_release_sys(tp_arrive_flag(P.tp, d, t, P.tp.rank), tgt);
-    } else {
-      st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), tgt);
-    }
+  epi_bar();
+  if (r == 0) fence_sys();
+  if (P.tp_oneshot) {
+    epi_bar();  // thread 0's fence before any flag
+    if (r < P.tp.world) st_release_sys(tp_arrive_flag(P.tp, r, t, P.tp.rank), tgt);
+  } else if (r == 0) {
+    st_release_sys(tp_arrive_flag(P.tp, t % P.tp.world, t, P.tp.rank), tgt);
   }
 }
 
