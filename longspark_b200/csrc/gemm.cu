@@ -910,9 +910,11 @@ extern "C" size_t ls_gemm_workspace_bytes(int rows, int k, int n_out) {
 namespace ls {
 
 // One-shot exchange (every rank sends each partial to every rank, W - 1 times
-// the partial bytes, one NVLink hop) for up to four ranks; owner reduce +
-// broadcast (two hops, about twice the partial bytes in all) above that.
-static bool tp_oneshot(int world) { return world <= 4; }
+// the partial bytes, one NVLink hop) for two ranks, where it sends the same
+// bytes as owner reduce + broadcast with one hop fewer; owner reduce +
+// broadcast (about twice the partial bytes in all) from four ranks, where
+// one-shot's 3x partial bytes made o_proj 85 -> 110 us at TP4.
+static bool tp_oneshot(int world) { return world == 2; }
 
 static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, size_t workspace_bytes, const TpView* tp,
                        int wire) {
