@@ -455,14 +455,18 @@ LS_API size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire);
  * where x_r / w_r are this rank's k-slice (a.x, a.w, a.k are local).
  * Epilogues LS_EPI_STORE and LS_EPI_RESIDUAL (residual: this rank's copy,
  * identical on every rank; may alias out).  `a.out` must lie inside this
- * rank's heap.  Output tile t belongs to rank t % world: every rank sends its
- * fp32 (or bf16, per `wire`) partial of tile t to the owner's exchange slot
- * with peer stores and a release flag as soon as its tensor cores finish the
- * tile; after finishing its own tiles, the owner sums the world partials in
- * rank order, applies the epilogue once and stores the bf16 result into every
- * rank's `out`, then flags each rank.  The kernel returns when this rank's
- * `out` is complete.  Launch it on every rank with the same shapes, in the
- * same order relative to the other TP launches. */
+ * rank's heap (16-byte aligned, out_ld a multiple of 8).  As soon as its
+ * tensor cores finish an output tile, a rank peer-stores its fp32 (or bf16,
+ * per `wire`) partial and raises a release flag:
+ *  - two ranks (one-shot): to both ranks; each rank then sums the two
+ *    partials of every tile in rank order and applies the epilogue itself;
+ *  - four or more ranks (owner reduce + broadcast): to the tile's owner
+ *    (rank t % world), which sums the partials in rank order, applies the
+ *    epilogue once and stores the bf16 result into every rank's `out`, then
+ *    flags each rank.
+ * Either way every rank ends with the same bits, and the kernel returns when
+ * this rank's `out` is complete.  Launch it on every rank with the same
+ * shapes, in the same order relative to the other TP launches. */
 LS_API int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_tp_group* g, int wire, void* workspace,
                              size_t workspace_bytes);
 
