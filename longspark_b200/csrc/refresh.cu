@@ -14,8 +14,13 @@
 // head dimension of a slot stays in one CTA (the reference's LSE-publication
 // race, global16_raw256_incremental.py:559-562, cannot occur), slots are
 // independent so chunks are.  Scores use warp-level bf16 MMA with fp32
-// accumulation (exact products, like tl.dot); the state update is fp32 FMA
-// with coalesced float4 traffic.  HBM traffic per (request, layer, head):
+// accumulation (exact products, like tl.dot).  The state update also runs on
+// the MMA units: the fp32 state is read straight into the accumulator
+// fragments, scaled, and the fp32 weights enter as three bf16 terms (their sum
+// within 2^-27 of the weight) against the exact bf16 V rows, so the update
+// keeps fp32 accuracy with ~3x fewer instructions than fp32 FMAs (the
+// chained-refresh tests hold 3e-5 over 12 steps and 1e-4 over 200 rounds).
+// HBM traffic per (request, layer, head):
 // read+write of S*(128+1) fp32 state, read of S*128 bf16 queries; the few new
 // K/V rows come from L2 after the first head of their group.
 #include "common.cuh"
@@ -30,11 +35,7 @@ constexpr int RF_QPITCH = 136; // bf16 row pitch in smem (272 B: ldmatrix rows h
 struct RefreshSmem {
   bf16 q[RF_SLOTS][RF_QPITCH];
   bf16 k[RF_MAXROWS][RF_QPITCH];
-  bf16 v[RF_MAXROWS][128];
-  float w[RF_SLOTS][RF_MAXROWS + 4];  // row pitch 36 floats: float4 reads stay 16-byte aligned
-  float prior_w[RF_SLOTS];
-  float merged[RF_SLOTS];
-  float prior[RF_SLOTS];
+  bf16 v[RF_MAXROWS][RF_QPITCH];
 };
 
 __device__ __forceinline__ long long paged_row(const int* table, int table_stride, int ring_pages, int b, int pos,
@@ -80,6 +81,18 @@ __device__ __forceinline__ void warp_slot_scores(const bf16 (*q)[RF_QPITCH], con
   }
 }
 
+// Three bf16 terms whose sum is w to within 2^-27 |w| (each term is the bf16
+// rounding of what the terms before it left), so a bf16 MMA of the terms
+// against bf16 V rows adds the products of the fp32 weight.
+__device__ __forceinline__ void split3_bf16(float w0, float w1, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  const float h0 = bf16_round(w0), h1 = bf16_round(w1);
+  const float r0 = w0 - h0, r1 = w1 - h1;
+  const float m0 = bf16_round(r0), m1 = bf16_round(r1);
+  hi = pack_bf16(h0, h1);
+  mid = pack_bf16(m0, m1);
+  lo = pack_bf16(r0 - m0, r1 - m1);
+}
+
 __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_args a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   asm volatile("griddepcontrol.launch_dependents;");
@@ -96,6 +109,7 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
   const int s0 = chunk * RF_SLOTS;
   const int nslots = min(RF_SLOTS, a.slots_per_head - s0);  // multiple of 16
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t2 = (lane & 3) * 2;
 
   const int c = a.commit_lens[b];
   const int len = a.seq_lens[b];
@@ -112,18 +126,27 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
     asm volatile("griddepcontrol.wait;" ::: "memory");
     return;
   }
-  // Issue the state reads first: each warp's 16 slots (512 B each, float4 per
-  // lane) stay in flight while the queries and new rows load and the scores run.
+  // Issue the state reads first, straight into the layout of the MMA
+  // accumulators that fold the new rows in: o[j] holds dims 8j + t2, +1 of
+  // slots g (o[j][0..1]) and g + 8 (o[j][2..3]) of this warp's 16 slots.
+  // They stay in flight while the queries and new rows load and the scores run.
   const long long st_base = ((long long)slot * a.tap_layers + layer) * a.q_heads + h;
-  float* out = a.state_out + (st_base * a.slots_per_head + s0) * 128;
-  float* lse = a.state_lse + st_base * a.slots_per_head + s0;
+  float* out = a.state_out + (st_base * a.slots_per_head + s0 + warp * 16) * 128;
+  float* lse = a.state_lse + st_base * a.slots_per_head + s0 + warp * 16;
   const bool warp_active = warp * 16 < nslots;
-  float4 o[16];
-  float prior_lse = 0.0f;  // parked in shared memory once it has arrived (after the copies are issued)
+  float o[16][4];
+  float prior_lse = 0.0f;  // slot 16*warp + lane, lanes < 16
   if (warp_active) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) o[i] = __ldcs(reinterpret_cast<const float4*>(out + (long long)(warp * 16 + i) * 128) + lane);
-    if (lane < 16) prior_lse = lse[warp * 16 + lane];
+    for (int j = 0; j < 16; ++j) {
+      const float2 lo = __ldcs(reinterpret_cast<const float2*>(out + g * 128 + j * 8 + t2));
+      const float2 hi = __ldcs(reinterpret_cast<const float2*>(out + (g + 8) * 128 + j * 8 + t2));
+      o[j][0] = lo.x;
+      o[j][1] = lo.y;
+      o[j][2] = hi.x;
+      o[j][3] = hi.y;
+    }
+    if (lane < 16) prior_lse = lse[lane];
   }
 
   // Queries of this head/chunk -> smem (cp.async 16 B pieces).
@@ -175,115 +198,99 @@ __global__ void __launch_bounds__(128) refresh_views_kernel(const ls_refresh_arg
     }
   }
   cp_async_commit();
-  if (warp_active && lane < 16) sm.prior[warp * 16 + lane] = prior_lse;
   cp_async_wait_all();
   __syncthreads();
+  if (!warp_active) return;
 
-  if (warp_active) {
-    float acc[4][4];
-    const int n_tiles = (c + 7) >> 3;
-    warp_slot_scores(sm.q, sm.k, warp * 16, n_tiles, acc);
-    // Each slot row lives in a quad: lanes 4g..4g+3 hold slot g (regs 0,1) and g+8 (regs 2,3).
-    const int g = lane >> 2, t2 = (lane & 3) * 2;
+  float acc[4][4];
+  const int n_tiles = (c + 7) >> 3;
+  warp_slot_scores(sm.q, sm.k, warp * 16, n_tiles, acc);
+  // Online-softmax merge per slot.  The scores of slot g + 8*half sit in the
+  // quad of lanes 4g..4g+3 (rows 8nt + t2 + {0,1} in acc[nt][2*half + {0,1}]);
+  // they become the fp32 weights exp(s - merged) in place.
+  float pw[2];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int sl = warp * 16 + g + half * 8;
-      float sv[8];
-      float mx = -INFINITY;
+  for (int half = 0; half < 2; ++half) {
+    float mx = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int r = nt * 8 + t2 + e;
-          const float s = acc[nt][half * 2 + e] * a.softmax_scale;
-          sv[nt * 2 + e] = s;
-          if (r < c) mx = fmaxf(mx, s);
-        }
+      for (int e = 0; e < 2; ++e) {
+        const float s = acc[nt][half * 2 + e] * a.softmax_scale;
+        acc[nt][half * 2 + e] = s;
+        if (nt * 8 + t2 + e < c) mx = fmaxf(mx, s);
       }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      float sum = 0.0f;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    float sum = 0.0f;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-        for (int e = 0; e < 2; ++e)
-          if (nt * 8 + t2 + e < c) sum += fast_exp(sv[nt * 2 + e] - mx);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      const float delta = mx + __logf(sum);
-      const float prior = sm.prior[sl];
-      const float m2 = fmaxf(prior, delta);
-      const float merged = m2 + __logf(fast_exp(prior - m2) + fast_exp(delta - m2));
+      for (int e = 0; e < 2; ++e)
+        if (nt * 8 + t2 + e < c) sum += fast_exp(acc[nt][half * 2 + e] - mx);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float delta = mx + __logf(sum);
+    const float prior = __shfl_sync(0xffffffffu, prior_lse, g + half * 8);
+    const float m2 = fmaxf(prior, delta);
+    const float merged = m2 + __logf(fast_exp(prior - m2) + fast_exp(delta - m2));
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int r = nt * 8 + t2 + e;
-          sm.w[sl][r] = r < c ? fast_exp(sv[nt * 2 + e] - merged) : 0.0f;
-        }
-      if ((lane & 3) == 0) {
-        sm.prior_w[sl] = fast_exp(prior - merged);
-        sm.merged[sl] = merged;
+      for (int e = 0; e < 2; ++e) {
+        const int r = nt * 8 + t2 + e;
+        acc[nt][half * 2 + e] = r < c ? fast_exp(acc[nt][half * 2 + e] - merged) : 0.0f;
       }
-    }
-    __syncwarp();
-    // State update: lanes cover the 128 dims as float4; the lane's 4 dims of
-    // every new V row are converted to fp32 once per 8-row block, the weights
-    // of a slot come as float4 broadcasts, and each weight is applied to two
-    // dims per packed FMA (the same fmaf per element as a scalar loop).  Rows
-    // are folded in order r = 0, 1, ...
-    const int c4 = (c + 3) & ~3;  // weights beyond c are zero (masked above)
-    for (int r0 = 0; r0 < c; r0 += 8) {
-      float2 v01[8], v23[8];
+    pw[half] = fast_exp(prior - merged);
+    if ((lane & 3) == 0) lse[g + half * 8] = merged;
+  }
+  // State update on the tensor cores: out' = out * pw + W . V with W the
+  // [16 slots x c rows] fp32 weights as three bf16 terms (W's accumulator
+  // layout is the A-operand layout of the next MMA) and V the new rows
+  // (bf16, exact), fp32 accumulation on top of the scaled state.
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(&sm.v[r0 + r][lane * 4]);
-        v01[r] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-        v23[r] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-      }
+  for (int j = 0; j < 16; ++j) {
+    o[j][0] *= pw[0];
+    o[j][1] *= pw[0];
+    o[j][2] *= pw[1];
+    o[j][3] *= pw[1];
+  }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int sl = warp * 16 + i;
-        float2 a01 = make_float2(o[i].x, o[i].y), a23 = make_float2(o[i].z, o[i].w);
-        if (r0 == 0) {
-          const float pw = sm.prior_w[sl];
-          a01.x *= pw;
-          a01.y *= pw;
-          a23.x *= pw;
-          a23.y *= pw;
-        }
+  for (int kb = 0; kb < RF_MAXROWS / 16; ++kb) {
+    if (kb * 16 < c) {
+      uint32_t ah[4], am[4], al[4];
+      split3_bf16(acc[2 * kb][0], acc[2 * kb][1], ah[0], am[0], al[0]);
+      split3_bf16(acc[2 * kb][2], acc[2 * kb][3], ah[1], am[1], al[1]);
+      split3_bf16(acc[2 * kb + 1][0], acc[2 * kb + 1][1], ah[2], am[2], al[2]);
+      split3_bf16(acc[2 * kb + 1][2], acc[2 * kb + 1][3], ah[3], am[3], al[3]);
 #pragma unroll
-        for (int rq = 0; rq < 8; rq += 4) {
-          if (r0 + rq < c4) {
-            const float4 w4 = *reinterpret_cast<const float4*>(&sm.w[sl][r0 + rq]);
-            const float ws[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 w2 = make_float2(ws[e], ws[e]);
-              a01 = ffma2(w2, v01[rq + e], a01);
-              a23 = ffma2(w2, v23[rq + e], a23);
-            }
-          }
-        }
-        o[i] = make_float4(a01.x, a01.y, a23.x, a23.y);
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t bv[4];
+        const int row = kb * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        ldmatrix_x4_trans(bv, &sm.v[row][dp * 16 + ((lane >> 4) << 3)]);
+        mma_16816(o[2 * dp], ah, bv);
+        mma_16816(o[2 * dp + 1], ah, bv + 2);
+        mma_16816(o[2 * dp], am, bv);
+        mma_16816(o[2 * dp + 1], am, bv + 2);
+        mma_16816(o[2 * dp], al, bv);
+        mma_16816(o[2 * dp + 1], al, bv + 2);
       }
     }
+  }
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      __stcs(reinterpret_cast<float4*>(out + (long long)(warp * 16 + i) * 128) + lane, o[i]);
-    if (a.state_bf16 != nullptr && layer < a.bf16_layers) {
-      // bf16 copy read by the drafter attention (same rounding it would apply)
-      bf16* ob = reinterpret_cast<bf16*>(a.state_bf16) +
-                 ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * a.slots_per_head + s0) * 128;
+  for (int j = 0; j < 16; ++j) {
+    __stcs(reinterpret_cast<float2*>(out + g * 128 + j * 8 + t2), make_float2(o[j][0], o[j][1]));
+    __stcs(reinterpret_cast<float2*>(out + (g + 8) * 128 + j * 8 + t2), make_float2(o[j][2], o[j][3]));
+  }
+  if (a.state_bf16 != nullptr && layer < a.bf16_layers) {
+    // bf16 copy read by the drafter attention (same rounding it would apply)
+    bf16* ob = reinterpret_cast<bf16*>(a.state_bf16) +
+               ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * a.slots_per_head + s0 + warp * 16) * 128;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        uint2 pk;
-        pk.x = pack_bf16(o[i].x, o[i].y);
-        pk.y = pack_bf16(o[i].z, o[i].w);
-        *reinterpret_cast<uint2*>(ob + (long long)(warp * 16 + i) * 128 + lane * 4) = pk;
-      }
+    for (int j = 0; j < 16; ++j) {
+      *reinterpret_cast<uint32_t*>(ob + g * 128 + j * 8 + t2) = pack_bf16(o[j][0], o[j][1]);
+      *reinterpret_cast<uint32_t*>(ob + (g + 8) * 128 + j * 8 + t2) = pack_bf16(o[j][2], o[j][3]);
     }
-    if (lane < 16) lse[warp * 16 + lane] = sm.merged[warp * 16 + lane];
   }
 }
 

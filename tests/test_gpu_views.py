@@ -24,19 +24,22 @@ def _cuda():
 # (a) refresh
 # --------------------------------------------------------------------------
 
-@pytest.mark.parametrize("q_heads,kv_heads,slots,max_commit", [(32, 8, 16, 8), (40, 8, 16, 8), (32, 8, 256, 16),
-                                                                  (40, 8, 64, 16)])
-def test_refresh_chain_matches_oracle(q_heads, kv_heads, slots, max_commit):
+@pytest.mark.parametrize("q_heads,kv_heads,slots,max_commit,batch", [
+    (32, 8, 16, 8, 3), (40, 8, 16, 8, 3), (32, 8, 256, 16, 3), (40, 8, 64, 16, 3),
+    (40, 8, 256, 32, 8),  # 2560 units: several per persistent CTA, up to 32 rows
+    (32, 8, 80, 5, 12),   # a 16-slot last chunk in every head
+])
+def test_refresh_chain_matches_oracle(q_heads, kv_heads, slots, max_commit, batch):
     """The reference's own protocol (tests/gpu/test_gqa5_attention.py:20-50):
     random bf16 queries and rows, random initial state, permuted pool slots,
     accept lengths ((arange(B) + step) % V) + 1, chained steps, tolerance 3e-5."""
     g = torch.Generator().manual_seed(980426)
-    L, batch, steps = 2, 3, 12
+    L, steps = 2, 12
     shape = DraftShape(hidden=512, q_heads=q_heads, kv_heads=kv_heads, inter=512, vocab=1024, tap_layers=L,
                        draft_layers=1, slots=slots, window=256, block=7, max_commit=max_commit, markov_rank=0,
                        mask_token_id=0)
     capacity = batch + 3
-    ctx0 = [37, 300, 1000]
+    ctx0 = [37, 300, 1000, 64, 17, 2048, 5, 999, 100, 16, 31, 700][:batch]
     v = make_views(shape, batch, ctx0, seed=5, extra_rows=steps * max_commit, gen=g)
     q = torch.randn(L, q_heads, slots, 128, generator=g).to(torch.bfloat16)
     out0 = torch.randn(capacity, L, q_heads, slots, 128, generator=g)
@@ -72,6 +75,52 @@ def test_refresh_chain_matches_oracle(q_heads, kv_heads, slots, max_commit):
     assert int(status.item()) == 0
     np.testing.assert_allclose(to_np(st_out), ref_out, rtol=3e-5, atol=3e-5)
     np.testing.assert_allclose(to_np(st_lse), ref_lse, rtol=3e-5, atol=3e-5)
+
+
+def test_refresh_bad_page_leaves_request_untouched():
+    """A committed row on a page id outside the pool: the status word reads
+    LS_DEV_BAD_INDEX, that request's state is unchanged, the other requests
+    (units before and after it in every CTA's range) match the oracle."""
+    g = torch.Generator().manual_seed(7)
+    L, batch, Hq, Hkv, S, V = 2, 6, 32, 8, 256, 16
+    shape = DraftShape(hidden=512, q_heads=Hq, kv_heads=Hkv, inter=512, vocab=1024, tap_layers=L, draft_layers=1,
+                       slots=S, window=256, block=7, max_commit=V, markov_rank=0, mask_token_id=0)
+    ctx = [100, 200, 300, 400, 500, 600]
+    v = make_views(shape, batch, ctx, seed=9, extra_rows=V, gen=g)
+    q = torch.randn(L, Hq, S, 128, generator=g).to(torch.bfloat16)
+    out0 = torch.randn(batch, L, Hq, S, 128, generator=g)
+    lse0 = torch.randn(batch, L, Hq, S, generator=g)
+    commit = np.full(batch, V)
+    lens = np.array(ctx) + commit
+    table = v["page_table"].clone()
+    bad_b = 3
+    table[bad_b, (lens[bad_b] - 1) // 16] = int(v["kv_k"].shape[1])  # one past the pool
+    dev = "cuda"
+    st_out, st_lse = out0.to(dev), lse0.to(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.refresh_views(kv_k=v["kv_k"].to(dev), kv_v=v["kv_v"].to(dev), page_table=table.to(dev),
+                      seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev),
+                      commit_lens=torch.tensor(commit, dtype=torch.int32, device=dev),
+                      slots=torch.arange(batch, dtype=torch.int32, device=dev), learned_query=q.to(dev),
+                      state_out=st_out, state_lse=st_lse, max_commit=V, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 110
+    kk, vv = O.from_bf16_bits(v["kv_k"].view(torch.int16).numpy()), O.from_bf16_bits(v["kv_v"].view(torch.int16).numpy())
+    nk = np.zeros((L, batch, V, Hkv, 128), np.float32)
+    nv = np.zeros_like(nk)
+    for b in range(batch):
+        for r in range(V):
+            pos = lens[b] - V + r
+            page = int(v["page_table"][b, pos // 16])
+            nk[:, b, r] = kk[:, page, pos % 16]
+            nv[:, b, r] = vv[:, page, pos % 16]
+    ref_out, ref_lse = O.refresh_views(out0.numpy().copy(), lse0.numpy().copy(), np.arange(batch), to_np(q), nk, nv,
+                                       commit, 128 ** -0.5)
+    go, gl = to_np(st_out), to_np(st_lse)
+    assert np.array_equal(go[bad_b], out0[bad_b].numpy()) and np.array_equal(gl[bad_b], lse0[bad_b].numpy())
+    keep = [b for b in range(batch) if b != bad_b]
+    np.testing.assert_allclose(go[keep], ref_out[keep], rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(gl[keep], ref_lse[keep], rtol=3e-5, atol=3e-5)
 
 
 def test_reference_api_scores_and_merge():
