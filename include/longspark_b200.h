@@ -194,6 +194,63 @@ LS_API int ls_window_scatter(void* stream, const void* keys, const void* values,
                       int batch, int tap_layers, int kv_heads, int hidden, int* status);
 
 /* ------------------------------------------------------------------------- */
+/* Target-side export of the accepted rows, fused: launched on the target's   */
+/* GPU after its verify pass, one kernel gathers each request's exported K/V  */
+/* rows from the target's KV pool and stores them straight into the          */
+/* drafter's paged pool through the drafter's page table — the drafter's own  */
+/* GPU memory, or a peer GPU's reached over NVLink through an IPC mapping     */
+/* (ls_ipc_open) or peer access — plus the boundary hidden states into its    */
+/* hidden pool.  Replaces the target's gather (LS engine/target.py:213-228,   */
+/* LS engine/state_export.py:14-47: index_select per layer, then a            */
+/* dist.gather of the heads to rank 0 under target TP), the message transport */
+/* (LS engine/transport.py) and the drafter's window scatter: under target TP */
+/* every rank stores its own KV-head slice (head_offset), with no gather.    */
+/* Plain 16-byte loads and stores only (no multicast, no TMA).  The index    */
+/* arrays live in memory the launching GPU can read (its own, or a mapped     */
+/* peer's).  The caller orders the export before the drafter's update of the  */
+/* same requests (the update message, or an event, after this launch          */
+/* completes).                                                                */
+/* ------------------------------------------------------------------------- */
+#define LS_EXPORT_MAX_LAYERS 8
+
+typedef struct ls_export_args {
+  const void* src_k[LS_EXPORT_MAX_LAYERS]; /* tapped layer l: the target's K pool [src_rows, src_heads, 128] bf16 */
+  const void* src_v[LS_EXPORT_MAX_LAYERS]; /* same for V                                            */
+  long long src_rows;
+  int src_heads;            /* KV heads in a source row (this rank's slice under target TP)        */
+  const long long* locations; /* [total_rows] source row of each exported row, request-major       */
+  long long total_rows;
+  const int* row_offsets;   /* [batch] first entry of request b in locations                       */
+  const int* counts;        /* [batch] rows exported for request b                                 */
+  const int* seq_lens;      /* [batch] drafter length after the commit: row i of request b lands at
+                               position seq_lens[b] - counts[b] + i                                 */
+  void* dst_k;              /* drafter pool [tap_layers, pool_pages, 16, dst_heads, 128] bf16       */
+  void* dst_v;
+  long long pool_pages;
+  int dst_heads;
+  int head_offset;          /* drafter head of source head 0 (head_offset + src_heads <= dst_heads) */
+  const int* page_table;    /* [batch, table_stride] drafter page-table rows of the requests        */
+  int table_stride;
+  int ring_pages;           /* > 0: logical page p at column p % ring_pages                        */
+  const void* last_hidden;  /* optional [batch, tap_layers * hidden] bf16 -> hidden_pool[slots[b]]  */
+  void* hidden_pool;        /* [capacity, tap_layers * hidden] bf16                                 */
+  const int* slots;         /* [batch] drafter pool slots (with last_hidden)                        */
+  int capacity;
+  int hidden;
+  int batch;
+  int tap_layers;
+  int* status;              /* optional device status word: LS_DEV_BAD_INDEX for a location, page,
+                               position or slot out of range (that row is skipped)                  */
+} ls_export_args;
+
+LS_API int ls_export_rows(void* stream, const ls_export_args* a);
+
+/* Let kernels on the current device load and store peer_device's memory (the
+ * export into a drafter on another GPU of the same process); a no-op when it
+ * is already enabled or peer_device is the current device. */
+LS_API int ls_enable_peer_access(int peer_device);
+
+/* ------------------------------------------------------------------------- */
 /* (b) Drafter attention over [summary | window | local rows]                */
 /* Replaces Global16Raw256PagedDraftContext.attend (SP global16_raw256.py:   */
 /* 1431-1647) and fused_global_local_raw_attention                           */

@@ -17,6 +17,7 @@ LS_OK = 0
 W_ROWMAJOR, W_TILED = 0, 1
 EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_QKV, EPI_GATEUP, EPI_LMHEAD, EPI_MARKOV_ADD = range(7)
 TP_MAX_RANKS = 8
+EXPORT_MAX_LAYERS = 8
 TP_WIRE_F32, TP_WIRE_BF16 = 0, 1
 DEV_TIMEOUT_PEER = 105
 
@@ -76,6 +77,15 @@ class TpGroup(C.Structure):
     _fields_ = [("world", i32), ("rank", i32), ("heap", vp * TP_MAX_RANKS), ("heap_bytes", sz), ("sync_offset", sz)]
 
 
+class ExportArgs(C.Structure):
+    _fields_ = [("src_k", vp * EXPORT_MAX_LAYERS), ("src_v", vp * EXPORT_MAX_LAYERS), ("src_rows", i64),
+                ("src_heads", i32), ("locations", vp), ("total_rows", i64), ("row_offsets", vp), ("counts", vp),
+                ("seq_lens", vp), ("dst_k", vp), ("dst_v", vp), ("pool_pages", i64), ("dst_heads", i32),
+                ("head_offset", i32), ("page_table", vp), ("table_stride", i32), ("ring_pages", i32),
+                ("last_hidden", vp), ("hidden_pool", vp), ("slots", vp), ("capacity", i32), ("hidden", i32),
+                ("batch", i32), ("tap_layers", i32), ("status", vp)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "ls_version": (i32, []),
@@ -89,6 +99,8 @@ SIGNATURES = {
     "ls_refresh_views": (i32, [vp, C.POINTER(RefreshArgs)]),
     "ls_window_scatter": (i32, [vp, vp, vp, i64, vp, vp, vp, vp, vp, i64, vp, i32, i32, vp, vp, i32, vp, i32,
                                 i32, i32, i32, vp]),
+    "ls_export_rows": (i32, [vp, C.POINTER(ExportArgs)]),
+    "ls_enable_peer_access": (i32, [i32]),
     "ls_attention_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
     "ls_draft_attention": (i32, [vp, C.POINTER(AttentionArgs), vp, sz]),
     "ls_rmsnorm": (i32, [vp, vp, i32, vp, vp, i32, i32, i32, f32, i32, vp, vp, i32]),

@@ -164,6 +164,7 @@ class LongSparkDraft:
         self._meta_done = torch.cuda.Event()  # the last copy out of the host block has run
         self._meta_done.record()
         self._pending = None  # (ids, batch) of a staged, not yet applied decode update
+        self._pending_in_pool = None  # (slots, lengths, counts) of rows exported in place, not yet folded
         self._step_graphs = {}
 
     # ------------------------------------------------------------------ state
@@ -194,6 +195,12 @@ class LongSparkDraft:
 
     def _flush(self):
         """Apply a staged decode update now (window scatter + refresh)."""
+        if self._pending_in_pool is not None:
+            slot_t, lens_t, cnt_t = self._pending_in_pool
+            self._pending_in_pool = None
+            table = self.pools.page_table.index_select(0, slot_t)
+            self.engine.refresh(slots=slot_t, seq_lens=lens_t, commit_lens=cnt_t, page_table=table,
+                                batch=slot_t.shape[0])
         if self._pending is None:
             return
         ids, B = self._pending
@@ -208,6 +215,33 @@ class LongSparkDraft:
                            slots=slot_t, status=st, batch=B)
         self.engine.refresh(slots=slot_t, seq_lens=lens_t, commit_lens=cnt_t, page_table=table, batch=B)
 
+    def export_destination(self, ids, lengths, commit_lens, device=None):
+        """Where a target stores this decode step's rows in place
+        (``export.export_rows``): validates the commit exactly as the
+        matching ``update`` will (unknown request, out-of-order commit) and
+        returns the pool addresses, the requests' page-table rows, slots and
+        post-commit lengths, with the index arrays on ``device`` (the exporting
+        GPU; peer access to this drafter's GPU is enabled from it).  After the
+        export has run, ``update`` with a message whose ``keys`` is None
+        (``export_counts`` = ``commit_lens``) folds the rows into the summary."""
+        from .export import ExportDestination, enable_peer_access
+
+        meta = [dict(id=i, length=n, commit_len=c) for i, n, c in zip(ids, lengths, commit_lens, strict=True)]
+        self._flush()
+        slot_list = self.table.check_decode(meta, list(commit_lens))
+        dev = self.device
+        slots = torch.tensor(slot_list, dtype=torch.int32, device=dev)
+        p, s = self.pools, self.shape
+        dest = ExportDestination(
+            kv_k=p.kv_k.data_ptr(), kv_v=p.kv_v.data_ptr(), pool_pages=p.kv_k.shape[1], heads=s.kv_heads,
+            tap_layers=s.tap_layers, ring_pages=p.ring_pages, page_table=p.page_table.index_select(0, slots),
+            seq_lens=torch.tensor(list(lengths), dtype=torch.int32, device=dev), slots=slots,
+            hidden_pool=p.hidden.data_ptr(), capacity=p.hidden.shape[0], hidden=s.hidden, keepalive=p)
+        if device is not None and torch.device(device) != dev:
+            enable_peer_access(device, dev)
+            dest = dest.to(device)
+        return dest
+
     @torch.inference_mode()
     def update(self, packets, *, prefill=False):
         meta, counts, keys, values, hidden, extra = unpack_packets(packets)
@@ -215,6 +249,17 @@ class LongSparkDraft:
             return
         self._flush()
         dev = self.device
+        if keys is None:
+            # rows and hidden states already stored in place by the target
+            # (export.export_rows into export_destination): fold them in at the
+            # next proposal
+            if prefill:
+                raise ValueError("prefill messages carry their rows and summary state")
+            commit = self.table.decode(meta, counts)
+            self._pending_in_pool = (torch.tensor(commit.slots, dtype=torch.int32, device=dev),
+                                     torch.tensor(commit.lengths, dtype=torch.int32, device=dev),
+                                     torch.tensor(commit.counts, dtype=torch.int32, device=dev))
+            return
         if prefill:
             if "global_output" not in extra:
                 raise ValueError("prefill packets must carry global_output / global_lse")

@@ -55,8 +55,9 @@ class RequestTable:
             slots.append(slot)
         return Commit(slots, [m["length"] for m in meta], list(counts), _offsets(counts))
 
-    def decode(self, meta, counts):
-        """Validate a decode commit for every request first, then apply it."""
+    def check_decode(self, meta, counts):
+        """Validate a decode commit for every request without applying it;
+        returns the requests' slots."""
         slots = []
         for m, c in zip(meta, counts):
             if m["id"] not in self.requests:
@@ -67,6 +68,11 @@ class RequestTable:
             if c != m["commit_len"]:
                 raise ValueError("decode batch must contain exactly the committed KV rows")
             slots.append(slot)
+        return slots
+
+    def decode(self, meta, counts):
+        """Validate a decode commit for every request first, then apply it."""
+        slots = self.check_decode(meta, counts)
         for m in meta:
             self.requests[m["id"]][1] = m["length"]
         return Commit(slots, [m["length"] for m in meta], list(counts), _offsets(counts))
@@ -104,10 +110,14 @@ def unpack_packets(packets):
         counts = list(packets["export_counts"])
         if len(counts) != len(meta):
             raise ValueError("batched export counts disagree with request metadata")
-        keys, values = packets["keys"], packets["values"]
+        keys, values = packets.get("keys"), packets.get("values")
+        extra = {k: packets[k] for k in ("global_output", "global_lse") if k in packets}
+        if keys is None:  # rows and hidden states already stored in place (export.export_rows)
+            if values is not None or packets.get("last_hidden") is not None:
+                raise ValueError("a message without keys carries no values or hidden states either")
+            return meta, counts, None, None, None, extra
         if keys.shape != values.shape or keys.shape[1] != sum(counts):
             raise ValueError("batched tensor extent disagrees with export counts")
-        extra = {k: packets[k] for k in ("global_output", "global_lse") if k in packets}
         return meta, counts, keys, values, packets["last_hidden"], extra
     meta = [dict(id=p["id"], length=p["length"], commit_len=p.get("commit_len", p["keys"].shape[1]))
             for p in packets]

@@ -32,7 +32,7 @@ __all__ = [
     "linear", "row_parallel_linear", "silu", "rmsnorm_hf", "rmsnorm_fused", "feed_forward",
     "state_encoder", "shifted_input", "rope_tables", "apply_rotary",
     "attention_statistics", "statistics_as_normalized", "merge_normalized_attention",
-    "window_positions", "gather_window", "attend", "decoder_layer", "project_logits",
+    "window_positions", "gather_window", "export_rows", "attend", "decoder_layer", "project_logits",
     "markov_sample", "markov_sample_gumbel", "gumbel_hash_uniform", "greedy_argmax", "accept_lengths", "position_scores", "merge_accepted",
     "full_prefix_state", "refresh_views", "draft_pass", "build_views", "DraftShapeOracle",
 ]
@@ -266,6 +266,33 @@ def gather_window(pool, page_table_row, length, window, page_size, ring_pages=0)
     pages = page_table_row[lp]
     rows = pool[pages, pos % page_size]  # [n, Hkv, D]
     return np.ascontiguousarray(rows.transpose(1, 0, 2))
+
+
+def export_rows(pool_k, pool_v, src_k, src_v, locations, counts, seq_lens, page_table, ring_pages=0,
+                head_offset=0, page_size=16):
+    """The target-side export restated: the target gathers ``k[locations]`` /
+    ``v[locations]`` per tapped layer (``TargetModel._kv_rows``, LS
+    engine/target.py:213-228; ``gather_selected_kv``, LS engine/state_export.py:
+    14-47) and the drafter stores row i of request b at position
+    ``seq_lens[b] - counts[b] + i`` of its window (``LongSparkDraft.update``,
+    LS engine/draft.py:207-212, 257-260), here through the paged table as in
+    ``gather_window``.  pool_k/pool_v [L, pages, page, H, D] (updated in place,
+    heads [head_offset, head_offset + h)); src_k/src_v [L, rows, h, D];
+    locations request-major."""
+    off = 0
+    for b, c in enumerate(counts):
+        for i in range(int(c)):
+            pos = int(seq_lens[b]) - int(c) + i
+            lp = pos // page_size
+            if ring_pages:
+                lp %= ring_pages
+            page = int(page_table[b][lp])
+            src = int(locations[off + i])
+            h = src_k.shape[2]
+            pool_k[:, page, pos % page_size, head_offset:head_offset + h] = src_k[:, src]
+            pool_v[:, page, pos % page_size, head_offset:head_offset + h] = src_v[:, src]
+        off += int(c)
+    return pool_k, pool_v
 
 
 def attend(q, k_loc, v_loc, qg, summary_out, win_k, win_v, win_len, prec):

@@ -62,6 +62,27 @@ def test_unpack_batch_message_checks_extents():
         unpack_packets(dict(msg, format="v0"))
 
 
+def test_metadata_only_message_for_rows_exported_in_place():
+    """A batch message whose keys are None (the rows were stored in the
+    drafter's pool by the target's export) carries metadata only."""
+    msg = dict(format=BATCH_FORMAT, ids=["a"], lengths=[10], commit_lens=[3], export_counts=[3], keys=None,
+               values=None, last_hidden=None)
+    meta, counts, k, v, h, extra = unpack_packets(msg)
+    assert counts == [3] and k is None and v is None and h is None
+    with pytest.raises(ValueError, match="no values"):
+        unpack_packets(dict(msg, values=torch.zeros(1, 3, 8, 128)))
+
+
+def test_check_decode_validates_without_applying():
+    t = RequestTable(capacity=2, max_commit=8, window=256)
+    t.prefill(_meta(["a", "b"], [50, 60], [50, 60]), [50, 60])
+    slots = t.check_decode(_meta(["a", "b"], [52, 63], [2, 3]), [2, 3])
+    assert slots == [t.requests["a"][0], t.requests["b"][0]]
+    assert t.requests["a"][1] == 50 and t.requests["b"][1] == 60
+    with pytest.raises(RuntimeError, match="out-of-order"):
+        t.check_decode(_meta(["a"], [53], [2]), [2])
+
+
 def test_request_sharding_partitions_ids():
     ids = [f"req{i}" for i in range(100)]
     for world in (1, 2, 4, 8):

@@ -50,7 +50,7 @@ def test_struct_layouts_match_the_header(lib):
     for cname, py in (("ls_gemm_args", N.GemmArgs), ("ls_refresh_args", N.RefreshArgs),
                       ("ls_attention_args", N.AttentionArgs), ("ls_markov_args", N.MarkovArgs),
                       ("ls_prefill_args", N.PrefillArgs), ("ls_tp_group", N.TpGroup),
-                      ("ls_sample_step_args", N.SampleStepArgs)):
+                      ("ls_sample_step_args", N.SampleStepArgs), ("ls_export_args", N.ExportArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         body = re.sub(r"\[[^\]]*\]", "", body)  # array declarators: the name is what precedes them
@@ -76,3 +76,29 @@ def test_version_and_errors_without_gpu(lib):
     rc = lib.ls_gemm(None, ctypes.byref(a), None, 0)
     assert rc == 3 and b"k%64" in lib.ls_last_error()
     assert lib.ls_accept(None, None, 0, None, None, 1, 1) == 1
+
+
+def test_export_rows_validates_on_the_host(lib):
+    """ls_export_rows checks its arguments before any CUDA call."""
+    from longspark_b200 import _native as N
+    a = N.ExportArgs(batch=1, tap_layers=2, src_rows=10, src_heads=4, locations=16, row_offsets=16, counts=16,
+                     seq_lens=16, dst_k=16, dst_v=16, pool_pages=4, dst_heads=8, head_offset=6, page_table=16,
+                     table_stride=1)
+    assert lib.ls_export_rows(None, ctypes.byref(a)) == 1
+    assert b"null source pool" in lib.ls_last_error()
+    for l in range(2):
+        a.src_k[l] = a.src_v[l] = 32
+    assert lib.ls_export_rows(None, ctypes.byref(a)) == 1
+    assert b"head_offset + src_heads <= dst_heads" in lib.ls_last_error()
+    a.head_offset = 4
+    a.tap_layers = N.EXPORT_MAX_LAYERS + 1
+    assert lib.ls_export_rows(None, ctypes.byref(a)) == 3
+    a.tap_layers = 2
+    a.dst_k = 24
+    assert lib.ls_export_rows(None, ctypes.byref(a)) == 1
+    assert b"16-byte aligned" in lib.ls_last_error()
+    a.dst_k, a.last_hidden, a.hidden_pool, a.slots, a.capacity, a.hidden = 16, 16, 16, 16, 2, 100
+    assert lib.ls_export_rows(None, ctypes.byref(a)) == 1
+    assert b"hidden % 8" in lib.ls_last_error()
+    a.batch = 0
+    assert lib.ls_export_rows(None, ctypes.byref(a)) == 0

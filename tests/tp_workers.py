@@ -260,3 +260,55 @@ def engine_worker(rank, world, port, allreduce, wire):
         ties = tokens_exact_or_tied(tokens.cpu().numpy(), corrected, what=f"TP {allreduce}/{wire} tokens")
         assert ties <= 3
     finish([eng])
+
+
+# ----------------------------------------------------------------------------
+# Target-side export: every rank stores its KV-head slice into rank 0's pool
+# ----------------------------------------------------------------------------
+
+def export_worker(rank, world, port):
+    """Each rank plays one target TP rank holding heads [r*h, (r+1)*h) of the
+    target pool and exports them with ls_export_rows into the drafter pool on
+    rank 0 (a symmetric-heap buffer, reached from the other ranks through its
+    IPC mapping); rank 0 then holds the full-head rows (oracle gather + store)."""
+    from longspark_b200.export import ExportDestination, export_rows
+
+    dev = init(rank, world, port)
+    g = torch.Generator().manual_seed(77)
+    L, H, R, B = 2, 8, 3000, 3
+    counts = [5, 16, 1]
+    lens = torch.tensor([500, 37, 1200], dtype=torch.int32)
+    stride = (int(lens.max()) + 15) // 16
+    pages = B * stride + 4
+    src_k = torch.randn(L, R, H, 128, generator=g).to(torch.bfloat16)
+    src_v = torch.randn(L, R, H, 128, generator=g).to(torch.bfloat16)
+    loc = torch.randperm(R, generator=g)[:sum(counts)]
+    table = torch.randperm(pages, generator=g)[:B * stride].view(B, stride).to(torch.int32)
+    ag, _ = dist_helpers()
+    pool_bytes = L * pages * 16 * H * 128 * 2
+    heap = SymmetricHeap(2 * pool_bytes, rank=rank, world=world, device=dev, all_gather=ag)
+    pk = heap.carve((L, pages, 16, H, 128), torch.bfloat16)
+    pv = heap.carve((L, pages, 16, H, 128), torch.bfloat16)
+    pk.fill_(-2.0)
+    pv.fill_(-2.0)
+    torch.cuda.synchronize()
+    dist.barrier()
+    dest = ExportDestination(kv_k=heap.peers[0] + heap.offset_of(pk), kv_v=heap.peers[0] + heap.offset_of(pv),
+                             pool_pages=pages, heads=H, tap_layers=L, ring_pages=0, page_table=table.to(dev),
+                             seq_lens=lens.to(dev), slots=torch.zeros(B, dtype=torch.int32, device=dev))
+    h = H // world
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    export_rows(dest, src_k=[src_k[l, :, rank * h:(rank + 1) * h].contiguous().to(dev) for l in range(L)],
+                src_v=[src_v[l, :, rank * h:(rank + 1) * h].contiguous().to(dev) for l in range(L)],
+                locations=loc, counts=counts, head_offset=rank * h, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"rank {rank}: status {int(status.item())}"
+    dist.barrier()  # every rank's stores have completed
+    if rank == 0:
+        fill = torch.full((L, pages, 16, H, 128), -2.0).to(torch.bfloat16)
+        bits = lambda t: t.cpu().view(torch.int16).numpy().copy()  # noqa: E731  (fresh arrays: the oracle writes)
+        ref_k, ref_v = O.export_rows(bits(fill), bits(fill), bits(src_k), bits(src_v), loc.numpy(), counts,
+                                     lens.numpy(), table.numpy())
+        np.testing.assert_array_equal(bits(pk), ref_k)
+        np.testing.assert_array_equal(bits(pv), ref_v)
+    finish([heap])
