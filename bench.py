@@ -404,6 +404,50 @@ def time_sampled_round(eng, g, steps=50):
     return e0.elapsed_time(e1) / steps, chain_bytes, eng.device_status()
 
 
+def time_export(shape, dev, batch=32, reps=20):
+    """ls_export_rows for one decode step at the cfg2 shapes: ``batch``
+    requests x max_commit rows of every tapped layer gathered from a target
+    pool and stored into a drafter pool on the same GPU (LongSparkDraft's ring
+    layout), plus the boundary hidden states; median ms per launch over
+    ``reps`` launches, each after a 256 MiB L2 flush, and the bytes it moves."""
+    import torch
+    from longspark_b200.export import ExportDestination, export_rows
+    s = shape
+    L, H, c, ring = s.tap_layers, s.kv_heads, s.max_commit, s.window // 16
+    rows = batch * c
+    gen = torch.Generator(device=dev).manual_seed(5)
+    src_k = [torch.randn(4 * rows, H, 128, device=dev, generator=gen).to(torch.bfloat16) for _ in range(L)]
+    src_v = [torch.randn(4 * rows, H, 128, device=dev, generator=gen).to(torch.bfloat16) for _ in range(L)]
+    loc = torch.randperm(4 * rows, device=dev, generator=gen)[:rows]
+    pool_k = torch.zeros(L, batch * ring, 16, H, 128, dtype=torch.bfloat16, device=dev)
+    pool_v = torch.zeros_like(pool_k)
+    hid = torch.zeros(batch, L * s.hidden, dtype=torch.bfloat16, device=dev)
+    last_hidden = torch.randn(batch, L, s.hidden, device=dev, generator=gen).to(torch.bfloat16)
+    slots = torch.arange(batch, dtype=torch.int32, device=dev)
+    table = (slots[:, None] * ring + torch.arange(ring, dtype=torch.int32, device=dev)[None]).contiguous()
+    lens = torch.full((batch,), 32768 + c, dtype=torch.int32, device=dev)
+    dest = ExportDestination(kv_k=pool_k.data_ptr(), kv_v=pool_v.data_ptr(), pool_pages=batch * ring, heads=H,
+                             tap_layers=L, ring_pages=ring, page_table=table, seq_lens=lens, slots=slots,
+                             hidden_pool=hid.data_ptr(), capacity=batch, hidden=s.hidden)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    counts = [c] * batch
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ts = []
+    for i in range(reps + 2):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        export_rows(dest, src_k=src_k, src_v=src_v, locations=loc, counts=counts, last_hidden=last_hidden,
+                    status=status)
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            ts.append(e0.elapsed_time(e1))
+    ts.sort()
+    moved = 2 * (2 * L * rows * H * 128 * 2) + 2 * batch * L * s.hidden * 2  # K and V read + written, hidden
+    return ts[len(ts) // 2], moved, int(status.item())
+
+
 def count_launches(eng, g):
     """Kernels of one round, counted from the native calls of an eager run."""
     from longspark_b200 import _native as N
@@ -517,9 +561,10 @@ def run_b200(args):
             abytes = algorithmic_bytes(shape, eng, batch)
             pf_ms, pf_flops, pf_status = time_prefill_summary(eng, v, batch)
             sr_ms, sr_bytes, sr_status = time_sampled_round(eng, g)
+            ex_ms, ex_bytes, ex_status = time_export(shape, dev)
             headline = dict(ms=ms_max, clocks=clk.summary(), launches=launches, status=status, dom_ms=dom_ms,
                             abytes=abytes, eng=eng, prefill=(pf_ms, pf_flops, pf_status),
-                            sampled=(sr_ms, sr_bytes, sr_status))
+                            sampled=(sr_ms, sr_bytes, sr_status), export=(ex_ms, ex_bytes, ex_status))
         else:
             ms_max = dist_max(time_graph(g, steps, 3, world), world)
             abytes = algorithmic_bytes(shape, eng, batch)
@@ -614,6 +659,14 @@ def run_b200(args):
                                  / 1e9, 1),
                 "algorithmic_bytes": headline["abytes"] + headline["sampled"][1],
                 "device_status": headline["sampled"][2]},
+            "export_rows": {
+                "what": "ls_export_rows: one decode step's accepted rows (32 requests x 16 rows x 5 tapped layers, "
+                        "K and V) gathered from a target pool and stored into a drafter pool on the same GPU, plus "
+                        "the boundary hidden states; median over 20 launches, each after a 256 MiB L2 flush",
+                "us": round(headline["export"][0] * 1e3, 2),
+                "bytes": headline["export"][1],
+                "gbs": round(headline["export"][1] / (headline["export"][0] * 1e-3) / 1e9, 1),
+                "device_status": headline["export"][2]},
             "e2e": e2e,
             "gpu_launches": headline["launches"] * args.steps,
             "gpu_launches_per_step": headline["launches"],
