@@ -65,18 +65,22 @@ class ExportDestination:
                                  self.slots.to(dev), self.hidden_pool, self.capacity, self.hidden, self.keepalive)
 
 
-def export_rows(dest: ExportDestination, *, src_k, src_v, locations, counts, head_offset=0, last_hidden=None,
-                status=None):
-    """Store each request's exported rows into the drafter pool ``dest``.
+class PreparedExport:
+    """The argument block of one ``ls_export_rows`` launch with the device
+    arrays it points to; ``launch()`` only enqueues the kernel (repeat
+    launches re-store the same rows)."""
 
-    src_k, src_v: one tensor per tapped layer, the target's K/V pool
-    ``[rows, heads_local, 128]`` bf16 on the exporting GPU; locations: int64
-    ``[total]`` source rows, request-major (request b owns ``counts[b]``
-    consecutive entries); row i of request b lands at drafter position
-    ``dest.seq_lens[b] - counts[b] + i``, heads ``[head_offset, head_offset +
-    heads_local)``.  last_hidden ``[batch, tap_layers, hidden]`` bf16 (one
-    rank under target TP) goes to ``hidden_pool[dest.slots[b]]``.  Launches on
-    the exporting GPU's current stream; nothing is waited for."""
+    def __init__(self, args, device, keep):
+        self.args, self.device, self._keep = args, device, keep
+
+    def launch(self):
+        N.call("ls_export_rows", _stream(self.device), C.byref(self.args))
+
+
+def prepare_export(dest: ExportDestination, *, src_k, src_v, locations, counts, head_offset=0, last_hidden=None,
+                   status=None):
+    """Check the arguments of :func:`export_rows` and stage its device arrays
+    (row offsets, counts, locations) without launching."""
     L = len(src_k)
     if L != len(src_v) or L != dest.tap_layers or L > N.EXPORT_MAX_LAYERS:
         raise ValueError(f"export needs {dest.tap_layers} tapped layers of K and V (at most {N.EXPORT_MAX_LAYERS})")
@@ -114,7 +118,23 @@ def export_rows(dest: ExportDestination, *, src_k, src_v, locations, counts, hea
     a.last_hidden, a.hidden_pool, a.slots = _p(last_hidden), dest.hidden_pool or None, _p(dest.slots)
     a.capacity, a.hidden, a.batch, a.tap_layers = dest.capacity, dest.hidden, B, L
     a.status = _p(status)
-    N.call("ls_export_rows", _stream(dev), C.byref(a))
+    return PreparedExport(a, dev, (src_k, src_v, loc, offsets, counts_t, last_hidden, dest, status))
+
+
+def export_rows(dest: ExportDestination, *, src_k, src_v, locations, counts, head_offset=0, last_hidden=None,
+                status=None):
+    """Store each request's exported rows into the drafter pool ``dest``.
+
+    src_k, src_v: one tensor per tapped layer, the target's K/V pool
+    ``[rows, heads_local, 128]`` bf16 on the exporting GPU; locations: int64
+    ``[total]`` source rows, request-major (request b owns ``counts[b]``
+    consecutive entries); row i of request b lands at drafter position
+    ``dest.seq_lens[b] - counts[b] + i``, heads ``[head_offset, head_offset +
+    heads_local)``.  last_hidden ``[batch, tap_layers, hidden]`` bf16 (one
+    rank under target TP) goes to ``hidden_pool[dest.slots[b]]``.  Launches on
+    the exporting GPU's current stream; nothing is waited for."""
+    prepare_export(dest, src_k=src_k, src_v=src_v, locations=locations, counts=counts, head_offset=head_offset,
+                   last_hidden=last_hidden, status=status).launch()
 
 
 def enable_peer_access(device, peer):
