@@ -151,3 +151,17 @@ def test_sampling_hash_is_uniform_and_counter_based():
                   O.gumbel_hash_uniform(7, 0, 1, v), O.gumbel_hash_uniform(7 << 32, 0, 0, v)):
         assert np.mean(other == u) < 1e-3
         assert abs(np.corrcoef(other, u)[0, 1]) < 0.01
+
+
+def test_export_arguments_are_checked_on_the_host():
+    """export.prepare_export rejects mismatched tapped layers and pools that are
+    not on a CUDA device before any native call."""
+    from longspark_b200.export import ExportDestination, prepare_export
+    dest = ExportDestination(kv_k=256, kv_v=512, pool_pages=4, heads=8, tap_layers=2, ring_pages=0,
+                             page_table=torch.zeros(1, 4, dtype=torch.int32), seq_lens=torch.ones(1, dtype=torch.int32),
+                             slots=torch.zeros(1, dtype=torch.int32))
+    pool = torch.zeros(10, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="tapped layers"):
+        prepare_export(dest, src_k=[pool], src_v=[pool], locations=[0], counts=[1])
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        prepare_export(dest, src_k=[pool, pool], src_v=[pool, pool], locations=[0], counts=[1])
