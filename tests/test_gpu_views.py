@@ -154,6 +154,47 @@ def test_reference_api_scores_and_merge():
     np.testing.assert_allclose(to_np(lse)[[4, 0, 2]], exp_lse, rtol=3e-5, atol=3e-5)
 
 
+@pytest.mark.parametrize("batch", [1, 3, 64])
+def test_reference_protocol_gqa5_sixteen_steps(batch):
+    """The reference's own refresh test protocol (tests/gpu/test_gqa5_attention.py:
+    20-50): seed 980426, GQA-5 queries [1, 40, 16, 128] expanded over the
+    batch, keys/values [B, 8, 8, 128], pool capacity batch + 3 with permuted
+    slots, accept lengths ((arange(B) + step) % 8) + 1, 16 chained steps;
+    scores within 2e-5, the merged (out, lse) within 3e-5."""
+    g = torch.Generator().manual_seed(980426)
+    hq, hkv, s, rows = 40, 8, 16, 8
+    dev = "cuda"
+    query = torch.randn(1, hq, s, 128, generator=g).to(torch.bfloat16).to(dev).expand(batch, -1, -1, -1)
+    capacity = batch + 3
+    out = torch.randn(capacity, hq, s, 128, generator=g).to(dev)
+    lse = torch.randn(capacity, hq, s, generator=g).to(dev)
+    perm = torch.randperm(capacity, generator=g)[:batch]
+    slots = perm.to(torch.int32).to(dev)
+    out0 = to_np(out)
+    exp_out, exp_lse = out0[perm.numpy()], to_np(lse)[perm.numpy()]
+    qn = np.broadcast_to(to_np(query[:1]), (batch, hq, s, 128))
+    for step in range(16):
+        keys = torch.randn(batch, rows, hkv, 128, generator=g).to(torch.bfloat16).to(dev)
+        values = torch.randn(batch, rows, hkv, 128, generator=g).to(torch.bfloat16).to(dev)
+        sc = torch.empty(batch, hq, s, rows, device=dev)
+        ops.cache_position_scores(layer_id=0, global_query=query, new_keys=keys, output=sc,
+                                  softmax_scale=128 ** -0.5)
+        ref_sc = O.position_scores(qn, to_np(keys), 128 ** -0.5)
+        np.testing.assert_allclose(to_np(sc), ref_sc, rtol=2e-5, atol=2e-5)
+        lens = ((torch.arange(batch) + step) % rows + 1).to(torch.int32).to(dev)
+        locs = torch.arange(batch * rows, device=dev).reshape(batch, rows)
+        ops.merge_accepted_positions_(state_output=out, state_lse=lse, position_scores=sc,
+                                      value_cache=values.reshape(batch * rows, 1, hkv, 128),
+                                      accepted_cache_locs=locs, accept_lens=lens, accept_offsets=None,
+                                      state_slots=slots)
+        exp_out, exp_lse = O.merge_accepted(exp_out, exp_lse, ref_sc, to_np(values), lens.cpu().numpy())
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(to_np(out)[perm.numpy()], exp_out, rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(to_np(lse)[perm.numpy()], exp_lse, rtol=3e-5, atol=3e-5)
+    others = np.setdiff1d(np.arange(capacity), perm.numpy())
+    np.testing.assert_array_equal(to_np(out)[others], out0[others])  # pool entries of no request: untouched
+
+
 # --------------------------------------------------------------------------
 # (b) attention
 # --------------------------------------------------------------------------
