@@ -27,15 +27,20 @@ __global__ void __launch_bounds__(128) export_rows_kernel(const ls_export_args a
   const int b = blockIdx.x, layer = blockIdx.z;
   const int cnt = a.counts[b];
   const int len = a.seq_lens[b];
+  const long long first = a.row_offsets[b];
+  if (cnt < 0 || first < 0 || first + cnt > a.total_rows) {  // the request's rows are not all in `locations`
+    if (threadIdx.x == 0 && blockIdx.y == 0) record_status(a.status, LS_DEV_BAD_INDEX);
+    return;
+  }
   const int n16 = a.src_heads * 16;  // 16-byte pieces of one source row
   const uint4* sk = reinterpret_cast<const uint4*>(a.src_k[layer]);
   const uint4* sv = reinterpret_cast<const uint4*>(a.src_v[layer]);
   uint4* dk = reinterpret_cast<uint4*>(a.dst_k);
   uint4* dv = reinterpret_cast<uint4*>(a.dst_v);
   for (int i = blockIdx.y; i < cnt; i += gridDim.y) {
-    const long long e = (long long)a.row_offsets[b] + i;
+    const long long e = first + i;
     const int pos = len - cnt + i;
-    bool ok = e >= 0 && e < a.total_rows && pos >= 0;
+    bool ok = pos >= 0;
     const long long src = ok ? a.locations[e] : -1;
     ok = ok && src >= 0 && src < a.src_rows;
     int page = -1;

@@ -15,7 +15,7 @@ import torch.multiprocessing as mp
 import oracle as O
 import tp_workers
 from longspark_b200.draft import LongSparkDraft
-from longspark_b200.export import ExportDestination, export_rows
+from longspark_b200.export import ExportDestination, export_rows, prepare_export
 from longspark_b200.synthetic import make_weights
 
 pytestmark = pytest.mark.gpu
@@ -111,6 +111,30 @@ def test_export_rows_bad_location_skips_the_row():
     assert (gk[:, page, r] == _bits(fill)[:, page, r]).all()
     ref_k[:, page, r] = _bits(fill)[:, page, r]
     np.testing.assert_array_equal(gk, ref_k)
+
+
+def test_export_rows_bad_count_skips_the_request():
+    """A count that runs past the end of the locations: that request is
+    skipped whole (status LS_DEV_BAD_INDEX), the other request lands."""
+    dev = torch.device("cuda")
+    counts = [4, 6]
+    src_k, src_v, loc, table, lens, _, slots, pages = _case(5, 0, counts)
+    L, R, H, D = src_k.shape
+    fill = torch.full((L, pages, 16, H, D), -3.0).to(torch.bfloat16)
+    pool_k, pool_v = fill.clone().to(dev), fill.clone().to(dev)
+    dest = ExportDestination(kv_k=pool_k.data_ptr(), kv_v=pool_v.data_ptr(), pool_pages=pages, heads=H, tap_layers=L,
+                             ring_pages=0, page_table=table.to(dev), seq_lens=lens.to(dev), slots=slots.to(dev))
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    prep = prepare_export(dest, src_k=[src_k[l].to(dev) for l in range(L)], src_v=[src_v[l].to(dev) for l in range(L)],
+                          locations=loc, counts=counts, status=status)
+    bad = torch.tensor([4, 1 << 30], dtype=torch.int32, device=dev)  # request 1 claims far more rows than exist
+    prep.args.counts = bad.data_ptr()
+    prep.launch()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 110
+    ref_k, _ = O.export_rows(_bits(fill), _bits(fill), _bits(src_k), _bits(src_v), loc.numpy()[:4], [4],
+                             lens.numpy()[:1], table.numpy()[:1])
+    np.testing.assert_array_equal(_bits(pool_k), ref_k)
 
 
 def test_longspark_draft_in_place_export_matches_packets():
