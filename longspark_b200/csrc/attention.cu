@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(MANY ? 160 : 256, MANY ? 2 : 1) attention_clus
     for (int i = threadIdx.x; i < n_pages; i += blockDim.x) {
       int lp = first_lp + i;
       if (a.ring_pages > 0) lp %= a.ring_pages;
-      int page = a.page_table[(long long)b * a.table_stride + lp];
+      int page = lp < a.table_stride ? a.page_table[(long long)b * a.table_stride + lp] : -1;  // past the row: bad
       if (page < 0 || page >= a.pool_pages) {
         record_status(a.status, LS_DEV_BAD_INDEX);
         page = -1;

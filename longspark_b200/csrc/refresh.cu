@@ -42,7 +42,7 @@ __device__ __forceinline__ long long paged_row(const int* table, int table_strid
                                                long long pool_pages, int* status, bool* ok) {
   int lp = pos >> 4;
   if (ring_pages > 0) lp %= ring_pages;
-  const int page = table[(long long)b * table_stride + lp];
+  const int page = lp < table_stride ? table[(long long)b * table_stride + lp] : -1;  // past the row: bad
   if (page < 0 || page >= pool_pages) {
     record_status(status, LS_DEV_BAD_INDEX);
     *ok = false;

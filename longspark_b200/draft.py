@@ -30,7 +30,7 @@ import torch
 
 from . import ops
 from .config import DraftShape
-from .engine import DraftEngine, DraftWeights, GraphedDraft, ViewPools
+from .engine import DraftEngine, DraftWeights, GraphedDraft, ViewPools, capture_guard
 from .requests import RequestTable, unpack_packets
 
 GIB = 1 << 30
@@ -432,7 +432,7 @@ class StepGraph:
         torch.cuda.current_stream(d.device).wait_stream(s)
         torch.cuda.synchronize(d.device)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=s):
+        with capture_guard(), torch.cuda.graph(self.graph, stream=s):
             self._run()
         torch.cuda.current_stream(d.device).wait_stream(s)
 

@@ -11,6 +11,8 @@ global16_native_draft_executor.py:548-645``), plus the Markov greedy chain
 
 from __future__ import annotations
 
+import contextlib
+import gc
 import math
 from dataclasses import dataclass, field
 
@@ -341,6 +343,22 @@ class DraftEngine:
         self.buf["status"].zero_()
 
 
+@contextlib.contextmanager
+def capture_guard():
+    """Keep Python's cyclic garbage collector off while a CUDA graph is being
+    captured (``torch.cuda.graph`` collects just before capture begins): an
+    unreachable object collected mid-capture — say an earlier drafter that
+    owns CUDA graphs and events — would destroy them inside the capture,
+    which CUDA rejects and which invalidates the capture."""
+    was = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was:
+            gc.enable()
+
+
 class GraphedDraft:
     """CUDA graph of one drafter pass (optionally preceded by the refresh) for a
     fixed batch size.  Inputs are copied into static buffers before replay; the
@@ -390,7 +408,7 @@ class GraphedDraft:
         torch.cuda.current_stream(self.engine.device).wait_stream(s)
         torch.cuda.synchronize(self.engine.device)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=s):
+        with capture_guard(), torch.cuda.graph(self.graph, stream=s):
             self._run()
         return self
 
