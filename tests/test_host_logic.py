@@ -165,3 +165,24 @@ def test_export_arguments_are_checked_on_the_host():
         prepare_export(dest, src_k=[pool], src_v=[pool], locations=[0], counts=[1])
     with pytest.raises(ValueError, match="CUDA tensors"):
         prepare_export(dest, src_k=[pool, pool], src_v=[pool, pool], locations=[0], counts=[1])
+
+
+def test_capture_guard_pauses_and_restores_the_collector():
+    import gc
+    from longspark_b200.engine import capture_guard
+    assert gc.isenabled()
+    with capture_guard():
+        assert not gc.isenabled()
+        assert gc.collect() >= 0  # an explicit collection still runs
+    assert gc.isenabled()
+    gc.disable()
+    try:
+        with capture_guard():
+            pass
+        assert not gc.isenabled()  # a collector that was off stays off
+    finally:
+        gc.enable()
+    with pytest.raises(RuntimeError):
+        with capture_guard():
+            raise RuntimeError("capture failed")
+    assert gc.isenabled()
