@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--tp", action="store_true",
                     help="BASELINE config 5: the 14B drafter tensor-parallel over the torchrun ranks (batch 32, 64K "
                          "context), fused peer-store allreduce vs NCCL allreduce")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="at N > 1, skip the config-5 tensor-parallel section of the request-sharded line")
     ap.add_argument("--tp-batch", type=int, default=32)
     ap.add_argument("--tp-ctx", type=int, default=65536)
     ap.add_argument("--calls", action="store_true",
@@ -163,10 +165,30 @@ class ClockSampler:
 # CPU oracle baseline (bounded sample of the same workload)
 # ---------------------------------------------------------------------------
 
-def cpu_round_sample(shape, ctx, rounds, seed=0):
+def host_cores():
+    """Cores this process may run on (its affinity mask)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_round_sample(shape, ctx, rounds, seed=0, warmup=0, threads=None):
     """Time the numpy oracle (fp32, the reference drafter's CPU path restated)
-    on ``rounds`` drafting rounds of the workload.  Returns (seconds per round,
-    threads)."""
+    on ``rounds`` drafting rounds of the workload, after ``warmup`` untimed
+    rounds, with the BLAS pool set to ``threads`` (default: every core of the
+    affinity mask) whatever the launcher set OMP_NUM_THREADS to.  Returns
+    (median seconds per round, BLAS threads in use)."""
+    import numpy  # noqa: F401  (the BLAS pool must be loaded for the limit to reach it)
+    from threadpoolctl import threadpool_info, threadpool_limits
+    threads = threads or host_cores()
+    with threadpool_limits(limits=threads, user_api="blas"):
+        used = [d["num_threads"] for d in threadpool_info() if d.get("user_api") == "blas"]
+        sec = _cpu_rounds(shape, ctx, rounds, seed, warmup)
+    return sec, (max(used) if used else 1)
+
+
+def _cpu_rounds(shape, ctx, rounds, seed, warmup):
     import numpy as np
     import oracle as O
 
@@ -206,7 +228,7 @@ def cpu_round_sample(shape, ctx, rounds, seed=0):
     osh = O.DraftShapeOracle(H, Hq, Hkv, 128, shape.block, shape.mask_token_id)
     target = rng.integers(0, V, (1, shape.block + 1))
     times = []
-    for _ in range(rounds):
+    for i in range(warmup + rounds):
         t0 = time.perf_counter()
         out, lse = O.refresh_views(out, lse, np.array([0]), qg, new_k, new_v, np.array([shape.max_commit]),
                                    128 ** -0.5)
@@ -215,9 +237,22 @@ def cpu_round_sample(shape, ctx, rounds, seed=0):
         base, _ = O.draft_pass(W, osh, np.array([7]), np.array([ctx]), hidden, views, inv, "fp32")
         toks, _ = O.markov_sample(base, np.array([7]), W, "fp32")
         O.accept_lengths(target, toks)
-        times.append(time.perf_counter() - t0)
-    threads = os.cpu_count() or 1
-    return statistics.median(times), threads
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def cpu_cfg1_row():
+    """BASELINE config 1, the primary CPU row: one fp32 round of the oracle
+    at the Qwen3-4B shape (H=2560, 4K context, W=512, S=64, 16-token verify
+    block, one tapped and one drafter layer), median of 5 rounds after 2
+    warm-up rounds, on every host core."""
+    from longspark_b200.config import CFG1
+    sec, threads = cpu_round_sample(CFG1.shape, 4096, rounds=5, warmup=2)
+    return {"value": round(CFG1.shape.block / sec, 2), "unit": "draft tokens/s", "ms_per_round": round(sec * 1e3, 1),
+            "cores": threads, "kind": "port",
+            "sample": "BASELINE config 1 (Qwen3-4B shape, 4K context, W=512, S=64, B=16, batch 1): median of 5 fp32 "
+                      "rounds of the numpy restatement after 2 warm-ups"}
 
 
 # ---------------------------------------------------------------------------
@@ -244,9 +279,10 @@ def build_round(shape, ctx, batch, dev, seed):
     return eng, g, v
 
 
-def concurrency_round(shape, batch, dev, seed, steps=30):
+def concurrency_round(shape, batch, dev, seed, steps=30, view_peak=None):
     """one graph-replayed round for ``batch`` requests with
-    per-request contexts uniform in [2K, 32K]; returns (ms per round, status)."""
+    per-request contexts uniform in [2K, 32K]; returns (ms per round, status,
+    view-kernel timings when ``view_peak`` is given, else None)."""
     import torch
     from longspark_b200.engine import DraftEngine, DraftWeights, GraphedDraft, ViewPools
     from longspark_b200.synthetic import make_views, make_weights
@@ -268,9 +304,89 @@ def concurrency_round(shape, batch, dev, seed, steps=30):
     g.capture()
     ms = time_graph(g, steps, 3, 1)
     status = eng.device_status()
+    views = time_view_kernels(eng, g, view_peak) if view_peak else None
     del g, eng, pools, v, weights
     torch.cuda.empty_cache()
-    return ms, status
+    return ms, status, views
+
+
+def view_kernel_bytes(shape, eng, g):
+    """Algorithmic HBM bytes of one refresh launch and one attention launch
+    for the graph's batch: what each must read or write at least once.
+    Refresh, per request and tapped layer: the committed K/V rows, the fp32
+    state (output + lse) read and written; plus the bf16 state copy of the
+    drafter layers; the learned queries once per launch.  Attention, per
+    request (drafter layer 0): the window K/V rows (up to W), the bf16
+    summary values, q/k/v of the block in and its output out, the window's
+    page ids; the learned queries (the summary keys) once per launch."""
+    s = shape
+    B = g.batch
+    lens = g.seq_lens[:B].tolist()
+    commits = g.commit_lens[:B].tolist()
+    D = s.head_dim
+    qg_layer = s.q_heads * s.slots * D * 2
+    refresh = s.tap_layers * qg_layer
+    attn = qg_layer
+    for n, c in zip(lens, commits):
+        refresh += s.tap_layers * (2 * c * s.kv_heads * D * 2 + 2 * s.q_heads * s.slots * (D + 1) * 4)
+        refresh += s.draft_layers * s.q_heads * s.slots * D * 2
+        w = min(n, s.window)
+        attn += (2 * w * s.kv_heads * D * 2 + s.q_heads * s.slots * D * 2 + (w + 15) // 16 * 4
+                 + s.block * (s.q_heads + 2 * s.kv_heads) * D * 2 + s.block * s.q_heads * D * 2)
+    return refresh, attn
+
+
+def time_view_kernels(eng, g, hbm_peak, reps=20):
+    """The refresh (every tapped layer) and the drafter attention (layer 0)
+    launched alone on the round's live buffers, each launch after a 256 MiB
+    write (twice the L2) and bracketed by its own CUDA events; median ms per
+    launch, achieved GB/s of the algorithmic bytes and the fraction of the
+    measured HBM copy peak."""
+    import torch
+    from longspark_b200 import ops
+    s, p, b = eng.shape, eng.pools, eng.buf
+    B = g.batch
+    v = s.view_layer(0)
+
+    def refresh():
+        eng.refresh(slots=g.slots, seq_lens=g.seq_lens, commit_lens=g.commit_lens, page_table=g.page_table, batch=B)
+
+    def attention():
+        ops.draft_attention(qkv=b["qkv"], block=s.block, kv_k=p.kv_k[v], kv_v=p.kv_v[v], page_table=g.page_table,
+                            seq_lens=g.seq_lens, window=s.window, learned_query=eng.w.learned_query[v],
+                            state_out=p.summary_out[:, v], slots=g.slots, out=b["attn"], workspace=eng.attn_ws,
+                            q_heads=s.q_heads, kv_heads=s.kv_heads, ring_pages=p.ring_pages,
+                            softmax_scale=s.head_dim ** -0.5, status=b["status"], batch=B,
+                            state_bf16=p.summary_bf16[:, v])
+
+    # the refresh folds the same rows again at every launch: keep the state
+    saved = (p.summary_out.clone(), p.summary_lse.clone(), p.summary_bf16.clone())
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=eng.device)
+    st = torch.cuda.current_stream()
+    rb, ab = view_kernel_bytes(s, eng, g)
+    out = {}
+    for name, fn, nbytes in (("refresh", refresh, rb), ("attention", attention, ab)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for e0, e1 in ev:
+            flush.fill_(1)
+            e0.record(st)
+            fn()
+            e1.record(st)
+        torch.cuda.synchronize()
+        ts = sorted(e0.elapsed_time(e1) for e0, e1 in ev)
+        ms = ts[len(ts) // 2]
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "algorithmic_bytes": int(nbytes), "gbs": round(gbs, 1),
+                     "frac": round(gbs / hbm_peak, 3)}
+    p.summary_out.copy_(saved[0])
+    p.summary_lse.copy_(saved[1])
+    p.summary_bf16.copy_(saved[2])
+    out["status"] = eng.device_status()
+    del flush
+    return out
 
 
 def algorithmic_bytes(shape, eng, batch):
@@ -482,7 +598,7 @@ def e2e_api(shape, batch, steps, warmup, dev, world):
     W = make_weights(shape, device=dev, gen=gen)
     cfg = dict(draft_device=dev.index or 0, max_running_requests=batch, draft_state_gib=16.0, cuda_graph=True,
                graph_batch_sizes=(batch,))
-    d = LongSparkDraft(cfg, weights=W, shape=shape, materialize_logits=False)
+    d = LongSparkDraft(cfg, weights=W, shape=shape, materialize_logits=True)
     del W
     L, Hkv, Hq, S, Wn = shape.tap_layers, shape.kv_heads, shape.q_heads, shape.slots, shape.window
     ids = [f"r{i}" for i in range(batch)]
@@ -506,7 +622,7 @@ def e2e_api(shape, batch, steps, warmup, dev, world):
         length += c
         d.update(dict(format="longspark_state_batch_v1", ids=ids, lengths=[length] * batch, commit_lens=[c] * batch,
                       export_counts=[c] * batch, keys=keys, values=vals, last_hidden=hid))
-        toks, _, _ = d.propose(ids, anchors, 0.0)
+        toks, logits, _ = d.propose(ids, anchors, 0.0)  # logits [B, P, V] bf16 stay on the device
         return toks.cpu()
 
     for _ in range(warmup):
@@ -565,7 +681,8 @@ def run_b200(args):
             pf_ms, pf_flops, pf_status = time_prefill_summary(eng, v, batch)
             sr_ms, sr_bytes, sr_status = time_sampled_round(eng, g)
             ex_ms, ex_bytes, ex_status = time_export(shape, dev)
-            headline = dict(ms=ms_max, clocks=clk.summary(), launches=launches, status=status, dom_ms=dom_ms,
+            views = time_view_kernels(eng, g, hbm_peak)
+            headline = dict(views=views, ms=ms_max, clocks=clk.summary(), launches=launches, status=status, dom_ms=dom_ms,
                             abytes=abytes, eng=eng, prefill=(pf_ms, pf_flops, pf_status),
                             sampled=(sr_ms, sr_bytes, sr_status), export=(ex_ms, ex_bytes, ex_status))
         else:
@@ -597,22 +714,39 @@ def run_b200(args):
         e_ms = dist_max(e_ms, world)
         e2e = {"value": round(tokens_per_round * world / (e_ms * 1e-3), 1), "unit": "draft tokens/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 4),
-               "path": "LongSparkDraft.update(batch packet from pinned host) + propose(T=0) + tokens.cpu()",
+               "path": "LongSparkDraft.update(batch packet from pinned host) + propose(T=0) returning tokens and "
+                       "the Markov-corrected logits [B, 15, V] (a device tensor, as the reference returns) + "
+                       "tokens.cpu()",
                "device_status": e_status}
 
     batch_sweep = []
+    views32 = None
     for bs in [int(x) for x in args.batch_sweep.split(",") if x.strip()]:
-        ms_b, st_b = concurrency_round(shape, bs, dev, seed=2000 + rank)
+        ms_b, st_b, vk = concurrency_round(shape, bs, dev, seed=2000 + rank, view_peak=hbm_peak if bs == 32 else None)
         ms_b = dist_max(ms_b, world)
+        views32 = vk or views32
         batch_sweep.append({"requests_per_gpu": bs, "round_us": round(ms_b * 1e3, 1),
                             "draft_tokens_per_s": round(bs * shape.block * world / (ms_b * 1e-3), 1),
                             "device_status": st_b})
 
-    cpu = None
+    tp = None
+    if world > 1 and not args.no_tp:
+        # BASELINE config 5 on the same ranks: the drafter split by KV-head
+        # group, the fused peer-store allreduce against GEMM + NCCL
+        results, roof, parity, meta = tp_bench(args, rank, world, dev)
+        tp = {"config": meta, "modes": results, "parity": parity, "projection_roofline": roof,
+              "projection_roofline_note": TP_ROOF_NOTE,
+              "what": "cfg5 (14B, batch 32, 64K context) tensor-parallel over these ranks: whole rounds in one CUDA "
+                      "graph with the fused exchange (fp32 / bf16 partials) and with GEMM + NCCL allreduce, the two "
+                      "row-parallel projections alone (us per launch, max over ranks)"}
+
+    cpu = cpu1 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, threads = cpu_round_sample(shape, HEADLINE_CTX, rounds=3)
+        sec, threads = cpu_round_sample(shape, HEADLINE_CTX, rounds=3, warmup=1)
         cpu = {"value": round(tokens_per_round / sec, 2), "unit": "draft tokens/s", "cores": threads, "kind": "port",
-               "sample": f"3 fp32 rounds of the numpy oracle at the cfg2 shapes (median {sec:.2f} s/round)"}
+               "sample": f"median of 3 fp32 rounds (after 1 warm-up) of the numpy oracle at the cfg2 shapes, "
+                         f"{sec:.3f} s/round"}
+        cpu1 = cpu_cfg1_row()
 
     if rank == 0:
         line = {
@@ -640,7 +774,16 @@ def run_b200(args):
                          "frac": round(dom_gbs / hbm_peak, 3), "peak_source": peak_src,
                          "traffic": traffic, "algorithmic_bytes_per_launch": lm_bytes,
                          "launch_ms": round(headline["dom_ms"], 4)},
+            "view_kernels": {
+                "what": "refresh (5 tapped layers) and drafter attention (1 layer) launched alone on the round's "
+                        "buffers, median of 20 launches, each after a 256 MiB L2 flush; algorithmic bytes: state "
+                        "read+write, committed rows, bf16 state copy, window K/V, summary values, q/k/v/out, "
+                        "learned queries once per launch; frac of the measured HBM copy peak",
+                "cfg2_batch1_ctx": head_ctx, "cfg2_batch1": headline["views"],
+                "cfg4_32_requests": views32},
+            "tensor_parallel": tp,
             "cpu_baseline": cpu,
+            "cpu_baseline_cfg1": cpu1,
             "prefill_summary": {
                 "what": "ls_prefill_summary: fp32 (output, lse) of the 5 x 32 x 256 learned queries over the whole "
                         f"{head_ctx}-token prefix (replaces the target's FA3 summary pass)",
@@ -683,12 +826,106 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def tp_parity(rank, world, dev, all_gather, bar, batch=2, contexts=(3000, 700)):
+    """A short check before the TP timings: one round (refresh of a 16-row
+    commit + pass + chain) of the config-5 drafter on ``batch`` small requests,
+    tensor-parallel with the fused fp32 exchange, against the one-GPU engine
+    on the same weights and views (run on rank 0).  Returns tokens equal, the
+    largest logit difference in bf16 steps, and both device statuses."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from longspark_b200 import _native as N
+    from longspark_b200.config import CFG3
+    from longspark_b200.engine import DraftEngine, DraftWeights, ViewPools
+    from longspark_b200.synthetic import make_views, make_weights
+    from longspark_b200.tp import TPDraftEngine, shard_state_dict, shard_views
+
+    shape = CFG3.shape
+    gen = torch.Generator(device=dev).manual_seed(77)  # identical on every rank
+    W = make_weights(shape, device=dev, gen=gen, norm_jitter=0.05)
+    v = make_views(shape, batch, list(contexts), device=dev, gen=gen, extra_rows=shape.max_commit)
+    commit = torch.full((batch,), shape.max_commit, dtype=torch.int32, device=dev)
+    lens = v["seq_lens"] + commit
+    slots = torch.arange(batch, dtype=torch.int32, device=dev)
+    M = batch * shape.block
+    vl = shard_views(v, shape, rank, world)
+    pools = ViewPools(kv_k=vl["kv_k"], kv_v=vl["kv_v"], page_table=v["page_table"], summary_out=vl["summary_out"],
+                      summary_lse=vl["summary_lse"], hidden=v["hidden"])
+    eng = TPDraftEngine(shape, {k: t.clone() for k, t in shard_state_dict(W, shape, rank, world).items()}, pools,
+                        batch, rank=rank, world=world, device=dev, all_gather=all_gather, barrier=bar,
+                        allreduce="fused", wire=N.TP_WIRE_F32, pg=dist.group.WORLD)
+    eng.round(slots=slots, seq_lens=lens, commit_lens=commit, anchors=v["anchors"], page_table=v["page_table"],
+              batch=batch)
+    torch.cuda.synchronize()
+    tp_status = eng.device_status()
+    tp_tokens = eng.buf["tokens"][:batch].cpu().numpy()
+    shards = [None] * world
+    dist.all_gather_object(shards, eng.buf["logits"][:M].float().cpu().numpy())
+    eng.close()
+    del eng, pools
+    result = None
+    if rank == 0:
+        one = DraftEngine(shape, DraftWeights(shape, W, dev),
+                          ViewPools(kv_k=v["kv_k"], kv_v=v["kv_v"], page_table=v["page_table"],
+                                    summary_out=v["summary_out"], summary_lse=v["summary_lse"], hidden=v["hidden"]),
+                          max_batch=batch, device=dev)
+        one.round(slots=slots, seq_lens=lens, commit_lens=commit, anchors=v["anchors"], page_table=v["page_table"],
+                  batch=batch)
+        torch.cuda.synchronize()
+        ref = one.buf["logits"][:M].float().cpu().numpy()
+        got = np.concatenate(shards, axis=1)
+        step = 2.0 ** (np.floor(np.log2(np.abs(ref).max())) - 7)
+        steps = float(np.abs(got - ref).max() / step)
+        equal = bool(np.array_equal(tp_tokens, one.buf["tokens"][:batch].cpu().numpy()))
+        result = {"what": f"config-5 drafter, {batch} requests (contexts {list(contexts)}), one round with a "
+                          "16-row refresh: fused fp32 TP against the one-GPU engine",
+                  "tokens_equal": equal, "logits_max_diff_bf16_steps": round(steps, 2),
+                  "parity": equal and steps <= 4.0, "device_status": [tp_status, one.device_status()]}
+        del one
+    del W, v
+    torch.cuda.empty_cache()
+    bar()
+    return result
+
+
 def run_tp(args):
+    """BASELINE config 5 as its own bench line (``--tp``): see ``tp_bench``."""
+    import torch
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    results, roof, parity, meta = tp_bench(args, rank, world, dev)
+    if rank == 0:
+        line = {
+            "metric": "cfg5 TP drafter round: draft tokens/s per box (fused peer-store allreduce vs NCCL)",
+            "value": results["fused_f32"]["draft_tokens_per_s"], "unit": "draft tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": round(results["fused_f32"]["round_us"] / 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) paged K/V of this rank's heads)",
+            "config": meta, "modes": results, "parity": parity, "projection_roofline": roof,
+            "projection_roofline_note": TP_ROOF_NOTE,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+TP_ROOF_NOTE = ("target = max(weight bytes / measured HBM copy GB/s, bytes this rank sends over NVLink / 770 GB/s "
+                "measured peer copy); fp32 partials + bf16 results")
+
+
+def tp_bench(args, rank, world, dev):
     """one rank per GPU, the 14B-shaped drafter split by
     KV-head group.  Times the whole round (refresh + pass + sharded Markov chain
     + accept, one CUDA graph) with the row-parallel projections fused with the
     peer-store allreduce (fp32 and bf16 partials) and with a plain GEMM followed
-    by an NCCL allreduce, plus the two decoder-layer projections alone."""
+    by an NCCL allreduce, plus the two decoder-layer projections alone, after a
+    short parity check against the one-GPU engine (N > 1).  Returns (mode
+    results, projection roofline, parity, config); every rank takes the same
+    steps."""
     import torch
     import torch.distributed as dist
     from longspark_b200 import _native as N
@@ -698,9 +935,6 @@ def run_tp(args):
     from longspark_b200.synthetic import make_views, make_weights
     from longspark_b200.tp import TPDraftEngine, dist_helpers, local_shape, shard_state_dict
 
-    rank, world, local = dist_setup(args.gpus)
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
     shape = CFG3.shape
     batch, ctx = args.tp_batch, args.tp_ctx
     loc = local_shape(shape, world)
@@ -711,6 +945,7 @@ def run_tp(args):
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     nvlink_gbs = 770.0  # measured peer copy per direction on this pool
+    parity = tp_parity(rank, world, dev, all_gather, bar) if world > 1 else None
 
     gen = torch.Generator(device=dev).manual_seed(5)  # the same on every rank: replicated inputs agree
     W = make_weights(shape, device=dev, gen=gen)
@@ -839,27 +1074,15 @@ def run_tp(args):
         got = head["projection_us"][name]
         roof[name] = {"target_us": round(t_us, 2), "achieved_us": got, "frac": round(t_us / got, 3),
                       "weight_bytes": wbytes, "nvlink_bytes_sent": int(link)}
-    if rank == 0:
-        line = {
-            "metric": "cfg5 TP drafter round: draft tokens/s per box (fused peer-store allreduce vs NCCL)",
-            "value": head["draft_tokens_per_s"], "unit": "draft tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(head["round_us"] / 1e3, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) paged K/V of this rank's heads)",
-            "config": {"workload": "cfg5-qwen3-14b drafter, tensor-parallel by KV-head group (BASELINE configs[4])",
-                       "batch": batch, "ctx": ctx, "tp": world, "hidden": shape.hidden, "q_heads": shape.q_heads,
-                       "kv_heads": shape.kv_heads, "inter": shape.inter, "vocab": shape.vocab,
-                       "window": shape.window, "slots": shape.slots, "verify_block": shape.block + 1,
-                       "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights and K/V of every round)",
-                       "nccl_nvls": os.environ.get("NCCL_NVLS_ENABLE", "default")},
-            "modes": results,
-            "projection_roofline": roof,
-            "projection_roofline_note": ("target = max(weight bytes / measured HBM copy GB/s, bytes this rank sends "
-                                         "over NVLink / 770 GB/s measured peer copy); fp32 partials + bf16 results"),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    meta = {"workload": "cfg5-qwen3-14b drafter, tensor-parallel by KV-head group (BASELINE configs[4])",
+            "batch": batch, "ctx": ctx, "tp": world, "hidden": shape.hidden, "q_heads": shape.q_heads,
+            "kv_heads": shape.kv_heads, "inter": shape.inter, "vocab": shape.vocab,
+            "window": shape.window, "slots": shape.slots, "verify_block": shape.block + 1,
+            "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights and K/V of every round)",
+            "nccl_nvls": os.environ.get("NCCL_NVLS_ENABLE", "default")}
+    del Wl, v, pools
+    torch.cuda.empty_cache()
+    return results, roof, parity, meta
 
 
 def run_calls(args):
@@ -917,26 +1140,32 @@ def run_calls(args):
 
 def run_reference(args):
     """The reference arm: the reference drafter's CPU path (numpy restatement,
-    fp32) on the host cores, same metric/unit/config; rank 0 only."""
+    fp32) on the host cores, same metric/unit/config; rank 0 only.  One
+    process with its BLAS pool on every core of its affinity mask at every N
+    (torchrun sets OMP_NUM_THREADS=1 for its ranks; the pool is set here
+    explicitly, and the line reports the threads the pool actually used)."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     from longspark_b200.config import CFG2
     shape = CFG2.shape
-    for _ in range(min(args.warmup, 1)):
-        cpu_round_sample(shape, HEADLINE_CTX, rounds=1)
-    sec, threads = cpu_round_sample(shape, HEADLINE_CTX, rounds=max(1, min(args.steps, 5)))
+    steps = max(1, min(args.steps, 5))
+    warm = min(args.warmup, 1)
+    sec, threads = cpu_round_sample(shape, HEADLINE_CTX, rounds=steps, warmup=warm)
     value = shape.block / sec
     line = {"metric": METRIC, "value": round(value, 2), "unit": "draft tokens/s", "impl": "reference",
-            "n_gpus": world, "steps": max(1, min(args.steps, 5)), "warmup": min(args.warmup, 1),
+            "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
             "config": {"workload": "cfg2-qwen3-8b drafter round (BASELINE configs[1])", "batch_per_gpu": 1,
-                       "headline_ctx": HEADLINE_CTX},
+                       "headline_ctx": HEADLINE_CTX,
+                       "host": f"one process on {host_cores()} host cores at every N (rank 0 of {world})"},
             "cpu_baseline": {"value": round(value, 2), "unit": "draft tokens/s", "cores": threads, "kind": "port",
-                             "sample": "fp32 rounds of the numpy restatement of the reference drafter "
-                                       "(refresh + pass + Markov chain + accept) at the cfg2 shapes"},
+                             "sample": f"median of {steps} fp32 rounds (after {warm} warm-up) of the numpy "
+                                       "restatement of the reference drafter (refresh + pass + Markov chain + "
+                                       "accept) at the cfg2 shapes"},
+            "cpu_baseline_cfg1": cpu_cfg1_row(),
             "e2e": {"value": round(value, 2), "unit": "draft tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

@@ -37,7 +37,11 @@ __global__ void __launch_bounds__(128) export_rows_kernel(const ls_export_args a
   const uint4* sv = reinterpret_cast<const uint4*>(a.src_v[layer]);
   uint4* dk = reinterpret_cast<uint4*>(a.dst_k);
   uint4* dv = reinterpret_cast<uint4*>(a.dst_v);
-  for (int i = blockIdx.y; i < cnt; i += gridDim.y) {
+  // A ring keeps the last ring_pages * 16 positions: rows before those would
+  // land on the same slots as later rows (possibly from another CTA, in no
+  // fixed order), and the reference's ring ends holding the later ones.
+  const int skip = a.ring_pages > 0 ? max(0, cnt - a.ring_pages * 16) : 0;
+  for (int i = skip + blockIdx.y; i < cnt; i += gridDim.y) {
     const long long e = first + i;
     const int pos = len - cnt + i;
     bool ok = pos >= 0;

@@ -631,8 +631,10 @@ extern "C" size_t ls_markov_workspace_bytes(int batch, int block) {
 
 namespace ls {
 
-static int markov_launch(void* stream, const ls_markov_args* a, const VocabShards* shards, void* workspace,
-                         size_t workspace_bytes) {
+// Argument checks of every entry point of the chain kernel (the workspace
+// checks aside); an entry point enqueues nothing before they pass.  An empty
+// batch passes: there is nothing to launch.
+static int markov_check_args(const ls_markov_args* a) {
   if (a == nullptr || a->base == nullptr || a->tile_max == nullptr || a->tile_arg == nullptr || a->anchors == nullptr ||
       a->tokens == nullptr)
     return set_error(LS_ERR_INVALID, "ls_markov_argmax: null pointer argument");
@@ -644,6 +646,13 @@ static int markov_launch(void* stream, const ls_markov_args* a, const VocabShard
                            a->rank < 64 || a->rank > MK_MAXRANK || a->rank % 64))
     return set_error(LS_ERR_INVALID,
                      "ls_markov_argmax: Markov head needs w2, both row bounds and a rank in [64, 512], multiple of 64");
+  return LS_OK;
+}
+
+static int markov_launch(void* stream, const ls_markov_args* a, const VocabShards* shards, void* workspace,
+                         size_t workspace_bytes) {
+  const int rc = markov_check_args(a);
+  if (rc != LS_OK || a->batch <= 0) return rc;
   const size_t need = ls_markov_workspace_bytes(a->batch, a->block);
   if (workspace == nullptr || workspace_bytes < need)
     return set_error(LS_ERR_WORKSPACE, "ls_markov_argmax: workspace %zu < %zu", workspace_bytes, need);
@@ -752,8 +761,11 @@ static void* mk_static_ptr[MK_STATIC_MAX_DEVICES];  // device address of the arr
 
 extern "C" int ls_markov_argmax_static(void* stream, const ls_markov_args* a) {
   if (a == nullptr) return set_error(LS_ERR_INVALID, "ls_markov_argmax_static: null argument struct");
-  // empty batches and bad block sizes get the workspace entry point's own checks and errors
-  if (a->batch <= 0 || a->block < 1) return ls_markov_argmax(stream, a, nullptr, 0);
+  // the workspace entry point's own checks and errors, all before anything is
+  // enqueued: a rejected call must not touch the shared scratch, which a call
+  // still running on another stream may be using
+  const int rc = markov_check_args(a);
+  if (rc != LS_OK || a->batch <= 0) return rc;
   const long long rows = static_cast<long long>(a->batch) * a->block;
   if (rows > LS_MARKOV_STATIC_MAX_ROWS)
     return set_error(LS_ERR_WORKSPACE,

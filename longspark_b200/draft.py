@@ -315,14 +315,21 @@ class LongSparkDraft:
         return torch.ones(size, dtype=torch.int32, device=self.device)
 
     @torch.inference_mode()
-    def _step_graph(self, B):
+    def _step_graph(self, B, with_logits):
         """Graph of one full step for exactly B requests: page-table gather,
-        window scatter of the staged rows, drafter pass with the refresh."""
-        g = self._step_graphs.get(B)
+        window scatter of the staged rows, drafter pass with the refresh, and
+        with ``with_logits`` the corrected logits of the greedy chain."""
+        g = self._step_graphs.get((B, with_logits))
         if g is None:
-            g = StepGraph(self, B)
-            self._step_graphs[B] = g
+            g = StepGraph(self, B, with_logits=with_logits)
+            self._step_graphs[(B, with_logits)] = g
         return g
+
+    def _logits_buffer(self):
+        if self._logits is None:
+            s = self.shape
+            self._logits = torch.empty(self.capacity * s.block, s.vocab, dtype=torch.bfloat16, device=self.device)
+        return self._logits
 
     def propose(self, ids, anchors, temperature):
         if temperature < 0:
@@ -340,10 +347,12 @@ class LongSparkDraft:
             self._push_meta()
             if on_device:  # device anchors (e.g. the target's bonus tokens): no host round trip
                 self._meta_views(self._meta_dev)[4][:B].copy_(anchors.reshape(-1))
-            g = self._step_graph(B)
+            # at T = 0 the corrected logits of the greedy chain are part of the step graph
+            with_logits = self.materialize_logits and self._temperature == 0
+            g = self._step_graph(B, with_logits)
             g.replay()
             self.engine.graph_replays += 1
-            return self._propose_outputs(B, self._meta_views(self._meta_dev)[4][:B], B)
+            return self._propose_outputs(B, self._meta_views(self._meta_dev)[4][:B], B, logits_ready=with_logits)
         self._flush()
         slot_list, len_list = self.table.lookup(ids)
         slots = torch.tensor(slot_list, dtype=torch.int32, device=dev)
@@ -367,17 +376,15 @@ class LongSparkDraft:
             run_batch, run_anchors = B, anchor_t
         return self._propose_outputs(B, run_anchors, run_batch)
 
-    def _propose_outputs(self, B, run_anchors, run_batch):
+    def _propose_outputs(self, B, run_anchors, run_batch, logits_ready=False):
         if self._temperature > 0:
             return self._sampled_outputs(B, run_anchors, run_batch)
         tokens = self.engine.buf["tokens"][:B].clone()
         logits = None
         if self.materialize_logits:
             s = self.shape
-            if self._logits is None:
-                self._logits = torch.empty(self.capacity * s.block, s.vocab, dtype=torch.bfloat16,
-                                           device=self.device)
-            self.engine.corrected_logits(run_anchors, self._logits, batch=run_batch)
+            if not logits_ready:
+                self.engine.corrected_logits(run_anchors, self._logits_buffer(), batch=run_batch)
             logits = self._logits[:B * s.block].view(B, s.block, s.vocab).clone()
         return tokens, logits, None
 
@@ -388,10 +395,9 @@ class LongSparkDraft:
         s = self.shape
         self._sample_round += 1
         seed = (self._sample_seed * 0x9E3779B97F4A7C15 + self._sample_round) & (2 ** 64 - 1)
-        if self.materialize_logits and self._logits is None:
-            self._logits = torch.empty(self.capacity * s.block, s.vocab, dtype=torch.bfloat16, device=self.device)
         corr = self.engine.sample(run_anchors[:run_batch], temperature=self._temperature, seed=seed,
-                                  corrected=self._logits, batch=run_batch)
+                                  corrected=self._logits_buffer() if self.materialize_logits else None,
+                                  batch=run_batch)
         tokens = self.engine.buf["tokens"][:B].clone()
         q = self.engine.buf["q"][:B].clone()
         logits = corr[:B].clone() if self.materialize_logits else None
@@ -414,10 +420,14 @@ class StepGraph:
     """CUDA graph of one full drafting step for a fixed batch B, reading the
     drafter's staged rows and metadata block: gather of the requests' page-table
     rows, window scatter of the committed K/V rows and boundary hidden states,
-    then the drafter pass with the view refresh (``DraftEngine.draft``)."""
+    then the drafter pass with the view refresh (``DraftEngine.draft``), and
+    with ``with_logits`` the Markov-corrected logits of the greedy chain into
+    the drafter's logits buffer (``DraftEngine.corrected_logits``)."""
 
-    def __init__(self, d: "LongSparkDraft", B: int):
-        self.d, self.B = d, B
+    def __init__(self, d: "LongSparkDraft", B: int, with_logits: bool = False):
+        self.d, self.B, self.with_logits = d, B, with_logits
+        if with_logits:
+            d._logits_buffer()
         slot_t, lens_t, cnt_t, off_t, anc_t = (v[:B] for v in d._meta_views(d._meta_dev))
         self.args = (slot_t, lens_t, cnt_t, off_t, anc_t)
         self.table = torch.zeros(B, d.pools.page_table.shape[1], dtype=torch.int32, device=d.device)
@@ -429,6 +439,8 @@ class StepGraph:
             torch.index_select(d.pools.page_table, 0, self.args[0], out=self.table)
             d.engine.draft(slots=self.args[0], seq_lens=self.args[1], anchors=self.args[4], page_table=self.table,
                            batch=B)
+            if with_logits:
+                d.engine.corrected_logits(self.args[4], d._logits, batch=B)
         torch.cuda.current_stream(d.device).wait_stream(s)
         torch.cuda.synchronize(d.device)
         self.graph = torch.cuda.CUDAGraph()
@@ -446,6 +458,8 @@ class StepGraph:
                            slots=slot_t, status=d.engine.buf["status"], batch=B)
         d.engine.draft(slots=slot_t, seq_lens=lens_t, anchors=anc_t, page_table=self.table, batch=B,
                        commit_lens=cnt_t)
+        if self.with_logits:
+            d.engine.corrected_logits(anc_t, d._logits, batch=B)
 
     def replay(self):
         self.graph.replay()

@@ -166,11 +166,10 @@ class PagedViews:
         return merged.to(dtype=query.dtype)
 
 
-def draft_fixture(name, shape: DraftShape, *, contexts, seed, dtype, store_weights=True,
-                  norm_jitter=0.05, store_logits=True):
-    assert shape.block == 7, "the reference drafter pass is fixed to Local7"
-    batch = len(contexts)
-    W = make_weights(shape, seed=seed, norm_jitter=norm_jitter)
+def reference_model(shape: DraftShape, W, dtype):
+    """The reference drafter (``DraftFreeKVModel``, parallel_shifted_qwen +
+    Global16/Raw256) loaded with the reference-named weights ``W``, plus the
+    three target modules the pass uses (embedding, LM head, final norm)."""
     cfg = DraftFreeKVConfig(
         target_layer_ids=list(range(shape.tap_layers)), num_target_layers=max(8, shape.tap_layers + 1),
         block_size=7, hidden_size=shape.hidden, num_key_value_heads=shape.kv_heads, head_dim=128,
@@ -192,6 +191,15 @@ def draft_fixture(name, shape: DraftShape, *, contexts, seed, dtype, store_weigh
     head = nn.Linear(shape.hidden, shape.vocab, bias=False)
     head.weight = nn.Parameter(W["lm_head.weight"].to(dtype), requires_grad=False)
     fnorm = FinalNorm(W["model.norm.weight"].to(dtype), shape.final_eps)
+    return model, emb, head, fnorm
+
+
+def draft_fixture(name, shape: DraftShape, *, contexts, seed, dtype, store_weights=True,
+                  norm_jitter=0.05, store_logits=True):
+    assert shape.block == 7, "the reference drafter pass is fixed to Local7"
+    batch = len(contexts)
+    W = make_weights(shape, seed=seed, norm_jitter=norm_jitter)
+    model, emb, head, fnorm = reference_model(shape, W, dtype)
 
     v = make_views(shape, batch, list(contexts), seed=seed + 1, pool_pages=None, extra_rows=0)
     kv_k, kv_v, table, seq_lens = v["kv_k"], v["kv_v"], v["page_table"], v["seq_lens"]
@@ -243,14 +251,112 @@ def draft_fixture(name, shape: DraftShape, *, contexts, seed, dtype, store_weigh
     print("wrote", name, "tokens", tokens.tolist())
 
 
-def main():
+def chain_fixture(name, shape: DraftShape, *, ctx0, rounds, seed, topk=4):
+    """A chained run of the reference: every round folds that round's committed
+    rows into the fp32 summary (``reference_position_scores`` +
+    ``reference_merge_accepted_positions`` per tapped layer), then runs the
+    drafter pass on the refreshed views in bf16 and in fp32 and the greedy
+    Markov chain of the bf16 pass.  Inputs come from ``chain_inputs`` (seeds
+    ``seed`` and ``seed + 1``); the fixture keeps per round the bf16 tokens,
+    the top-``topk`` (value, id) pairs of the bf16 corrected and base logits
+    and of the fp32 base logits, and the summary lse after the first and the
+    last round."""
+    from chain_inputs import chain_views, chain_weights, committed_rows
+
+    assert shape.block == 7, "the reference drafter pass is fixed to Local7"
+    inc = load_incremental()
+    inc.GLOBAL_ROWS = shape.slots
+    inc.VERIFY_ROWS = shape.max_commit
+    W = chain_weights(shape, seed)
+    v = chain_views(shape, ctx0, rounds, seed + 1)
+    m16 = reference_model(shape, W, torch.bfloat16)
+    m32 = reference_model(shape, W, torch.float32)
+    qg = W["global16_raw256_reference.global_query_generator.learned_query"]  # [L, Hq, S, D] bf16
+    out, lse = v["summary_out"].clone(), v["summary_lse"].clone()
+    L = shape.tap_layers
+    rec = {k: [] for k in ("tokens", "corr_vals", "corr_ids", "base_vals", "base_ids", "base32_vals",
+                           "base32_ids")}
+    lse_first = None
+    for t in range(rounds):
+        c, n = int(v["commits"][t]), int(v["lengths"][t])
+        nk = committed_rows(v["kv_k"], v["page_table"], n, c, shape.max_commit)
+        nv = committed_rows(v["kv_v"], v["page_table"], n, c, shape.max_commit)
+        for layer in range(L):
+            sc = inc.reference_position_scores(global_query=qg[layer][None], new_keys=nk[layer],
+                                               softmax_scale=128 ** -0.5)
+            o, s_ = inc.reference_merge_accepted_positions(
+                state_output=out[:, layer].contiguous(), state_lse=lse[:, layer].contiguous(), position_scores=sc,
+                accepted_values=nv[layer], accept_lens=torch.tensor([c], dtype=torch.int32))
+            out[:, layer], lse[:, layer] = o, s_
+        if lse_first is None:
+            lse_first = lse.clone()
+        lens = torch.tensor([n], dtype=torch.int32)
+        anchors = v["anchors"][t:t + 1]
+        for dtype, (model, emb, head, fnorm) in ((torch.bfloat16, m16), (torch.float32, m32)):
+            views = PagedViews(qg.to(dtype), out, v["kv_k"].to(dtype), v["kv_v"].to(dtype), v["page_table"], lens,
+                               shape.window, 1)
+            with torch.no_grad():
+                base = model._forward_global16_raw256(
+                    keys=None, values=None, attention_mask=None, kv_source_indices=None,
+                    anchor_attention_mask=None, current_hidden_states=v["hidden"][t].to(dtype),
+                    current_token_ids=anchors, current_position_ids=lens.long(),
+                    teacher_forcing_token_ids=None, target_final_norm=fnorm, target_embed_tokens=emb,
+                    target_lm_head=head, candidate_token_ids=None, apply_markov_correction=False,
+                    global16_paged_context=views).to(dtype)
+                if dtype == torch.bfloat16:
+                    tokens, corrected = model.sample_parallel_tokens(base, first_previous_token_ids=anchors,
+                                                                     temperature=0.0)
+                    ct = torch.topk(corrected.float(), topk, dim=-1)
+                    bt = torch.topk(base.float(), topk, dim=-1)
+                    rec["tokens"].append(tokens[0].numpy())
+                    rec["corr_vals"].append(ct.values[0].numpy())
+                    rec["corr_ids"].append(ct.indices[0].numpy())
+                    rec["base_vals"].append(bt.values[0].numpy())
+                    rec["base_ids"].append(bt.indices[0].numpy())
+                else:
+                    bt = torch.topk(base.float(), topk, dim=-1)
+                    rec["base32_vals"].append(bt.values[0].numpy())
+                    rec["base32_ids"].append(bt.indices[0].numpy())
+        if t % 20 == 0:
+            print(name, "round", t, "tokens", rec["tokens"][-1].tolist(), flush=True)
+    fix = {k: np.stack(x) for k, x in rec.items()}
+    fix.update(seed=np.array(seed), ctx0=np.array(ctx0), rounds=np.array(rounds),
+               shape=np.array([shape.hidden, shape.q_heads, shape.kv_heads, shape.inter, shape.vocab,
+                               shape.tap_layers, shape.draft_layers, shape.slots, shape.window,
+                               shape.block, shape.markov_rank, shape.mask_token_id]),
+               lse_first=lse_first.numpy(), lse_last=lse.numpy())
+    np.savez_compressed(HERE / f"{name}.npz", **fix)
+    print("wrote", name)
+
+
+def main(which=("refresh", "draft", "chain")):
     torch.set_num_threads(os.cpu_count() or 1)
+    if "chain" in which:
+        sys.path.insert(0, str(HERE))
+        base = dict(tap_layers=1, draft_layers=1, slots=256, block=7, max_commit=8)
+        # Qwen3-14B dimensions (BASELINE config 3: 1 drafter layer, W=2048, S=256,
+        # 128K context, 200 chained rounds) at the reference's Local7 block
+        chain_fixture("chain_cfg3_p7", DraftShape(hidden=5120, q_heads=40, kv_heads=8, inter=17408, window=2048,
+                                                  **base), ctx0=131072, rounds=200, seed=300)
+        # Qwen3-8B dimensions (BASELINE config 2: W=1024, S=256, 128K context)
+        chain_fixture("chain_cfg2_p7", DraftShape(hidden=4096, q_heads=32, kv_heads=8, inter=12288, window=1024,
+                                                  **base), ctx0=131072, rounds=8, seed=200)
+    if "refresh" in which:
+        refresh_fixtures()
+    if "draft" in which:
+        draft_fixtures()
+
+
+def refresh_fixtures():
     refresh_fixture("refresh_gqa4_ref", q_heads=32, kv_heads=8, slots=16, verify_rows=8,
                     batches=(1, 2), steps=8)
     refresh_fixture("refresh_gqa5_ref", q_heads=40, kv_heads=8, slots=16, verify_rows=8,
                     batches=(1, 2), steps=8)
     refresh_fixture("refresh_gqa4_s64_v16", q_heads=16, kv_heads=4, slots=64, verify_rows=16,
                     batches=(1,), steps=6)
+
+
+def draft_fixtures():
     small = DraftShape(hidden=256, q_heads=8, kv_heads=2, inter=512, vocab=1024, tap_layers=2,
                        draft_layers=2, slots=16, window=256, block=7, max_commit=8, markov_rank=64,
                        mask_token_id=1000)
@@ -267,4 +373,4 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]) or ("refresh", "draft", "chain"))

@@ -55,3 +55,41 @@ def tokens_exact_or_tied(gpu_tokens, step_logits, what=""):
         assert not bad.any(), f"{what}: {int(bad.sum())} tokens differ beyond a near-tie"
         ties = int(mism.sum())
     return ties
+
+
+def bf16_ulp(v):
+    """One bf16 step at |v| (elementwise): 2^(floor(log2 |v|) - 7)."""
+    a = np.maximum(np.abs(np.asarray(v, dtype=np.float32)), np.float32(1e-30))
+    return 2.0 ** (np.floor(np.log2(a)) - 7)
+
+
+def compare_chain_with_reference(gpu_tokens, ref_tokens, ref_top_vals, ref_top_ids, what=""):
+    """GPU greedy tokens ``[B, P]`` against the reference's own tokens.
+
+    Rows must agree token for token.  The one difference accepted is a tie in
+    the reference's own bf16 logits: at the first step where a row differs,
+    the GPU's token must be among the reference's top-k at that step with a
+    value at most one bf16 step below the reference's maximum (0 steps is an
+    exact tie).  From that step on the row conditions on a different previous
+    token, so its later steps are not compared with the reference.
+    ``ref_top_vals`` / ``ref_top_ids``: ``[B, P, k]`` of the reference's
+    corrected step logits, largest first.  Returns a list of (row, step, gap
+    in bf16 steps) for those ties; raises on any other difference."""
+    gt = np.asarray(gpu_tokens)
+    rt = np.asarray(ref_tokens)
+    ties = []
+    for b in range(gt.shape[0]):
+        diff = np.nonzero(gt[b] != rt[b])[0]
+        if diff.size == 0:
+            continue
+        t = int(diff[0])
+        ids = list(np.asarray(ref_top_ids[b, t]))
+        vals = np.asarray(ref_top_vals[b, t], dtype=np.float32)
+        assert gt[b, t] in ids, (f"{what}: row {b} step {t}: token {gt[b, t]} is not in the reference's top "
+                                 f"{len(ids)} ({ids}, reference token {rt[b, t]})")
+        gap = float(vals[0] - vals[ids.index(gt[b, t])])
+        steps = gap / float(bf16_ulp(vals[0]))
+        assert steps <= 1.0, (f"{what}: row {b} step {t}: token {gt[b, t]} is {steps:.2f} bf16 steps below the "
+                              f"reference maximum (token {rt[b, t]}); not a tie")
+        ties.append((b, t, steps))
+    return ties

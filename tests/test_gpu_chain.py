@@ -1,9 +1,12 @@
 """a Qwen3-14B-shaped drafter (H=5120, 40 query / 8 KV heads,
 so GQA 5, SwiGLU 17408) at 128K context with W=2048, S=256 and a 16-token
 verify block, driven through 200 consecutive rounds of incremental refresh and
-drafting.  Every round the summary state (out, lse) must follow the oracle's
-incremental refresh chain, and at rounds 0, 99 and 199 the drafter pass (logits
-and Markov-greedy tokens) must match the oracle run on the oracle's own chain.
+drafting over 5 tapped layers.  Every round the summary state (out, lse) must
+follow the oracle's incremental refresh chain, the bf16 logits must lie within
+a few bf16 steps of the oracle's pass on the oracle's own state, and the
+Markov-greedy tokens must equal the oracle's own (un-forced) chain, a tie in
+the oracle's bf16 logits being the one accepted difference (counted and
+printed).
 """
 
 import numpy as np
@@ -11,7 +14,7 @@ import pytest
 import torch
 
 import oracle as O
-from gpu_util import assert_bf16_close, to_np, tokens_exact_or_tied
+from gpu_util import assert_bf16_close, compare_chain_with_reference, to_np
 from longspark_b200.config import CFG3
 from longspark_b200.engine import DraftEngine, DraftWeights, ViewPools
 from longspark_b200.synthetic import make_views, make_weights, rope_inv_freq
@@ -58,6 +61,7 @@ def test_chain_config3_200_rounds():
     anchors_all = torch.randint(0, shape.vocab, (rounds,), generator=torch.Generator().manual_seed(4))
     length = ctx0
     checked = 0
+    ties = []
     for t, c in enumerate(commits):
         length += c
         anchors = anchors_all[t:t + 1]
@@ -71,31 +75,30 @@ def test_chain_config3_200_rounds():
         nk[:, 0, :c] = _rows(v["kv_k"], table, new)
         nv[:, 0, :c] = _rows(v["kv_v"], table, new)
         ro, rl = O.refresh_views(ro, rl, np.array([0]), qg, nk, nv, np.array([c]), 128 ** -0.5)
-        if t % 10 == 9 or t in (0, 99, rounds - 1):
-            torch.cuda.synchronize()
-            assert eng.device_status() == 0, f"round {t}"
-            np.testing.assert_allclose(to_np(pools.summary_out), ro, rtol=1e-4, atol=1e-4,
-                                       err_msg=f"summary out after round {t}")
-            np.testing.assert_allclose(to_np(pools.summary_lse), rl, rtol=1e-4, atol=1e-4,
-                                       err_msg=f"summary lse after round {t}")
-        if t in (0, 99, rounds - 1):
-            win = np.arange(length - shape.window, length)
-            view_layer = shape.view_layer(0)
-            wk = _rows(v["kv_k"], table, win)[view_layer].transpose(1, 0, 2)[None]  # [1, Hkv, W, 128]
-            wv = _rows(v["kv_v"], table, win)[view_layer].transpose(1, 0, 2)[None]
-            views = [dict(qg=qg[view_layer], summary_out=ro[:, view_layer], win_k=wk, win_v=wv,
-                          win_len=np.array([shape.window]))]
-            ref16, _ = O.draft_pass(Wn, osh, anchors.numpy(), np.array([length]), hidden, views, inv_freq, "bf16")
-            gl = to_np(eng.buf["logits"][:shape.block]).reshape(1, shape.block, shape.vocab)
-            gt = eng.buf["tokens"][:1].cpu().numpy()
-            # every logit within 4 bf16 steps of the bf16 reference; with H = 5120 and
-            # I = 17408 the longer fp32 reductions leave fewer bit-identical values
-            # than at the 4B shape (measured 23% at round 0), hence the lower floor
-            assert_bf16_close(gl, ref16, steps=4.0, exact_frac=0.15, what=f"config 3 logits, round {t}")
-            _, corrected = O.markov_sample(ref16, anchors.numpy(), Wn, "bf16", forced=gt)
-            # every token is the oracle's choice or within one bf16 step of its maximum
-            # (checked inside); the synthetic 14B weights give near-flat top-2 logits, so
-            # such near-ties are common here (3 of 15 measured at round 0)
-            assert tokens_exact_or_tied(gt, corrected, what=f"config 3 tokens, round {t}") <= 5
-            checked += 1
-    assert checked == 3
+        torch.cuda.synchronize()
+        assert eng.device_status() == 0, f"round {t}"
+        np.testing.assert_allclose(to_np(pools.summary_out), ro, rtol=1e-4, atol=1e-4,
+                                   err_msg=f"summary out after round {t}")
+        np.testing.assert_allclose(to_np(pools.summary_lse), rl, rtol=1e-4, atol=1e-4,
+                                   err_msg=f"summary lse after round {t}")
+        win = np.arange(length - shape.window, length)
+        view_layer = shape.view_layer(0)
+        wk = _rows(v["kv_k"], table, win)[view_layer].transpose(1, 0, 2)[None]  # [1, Hkv, W, 128]
+        wv = _rows(v["kv_v"], table, win)[view_layer].transpose(1, 0, 2)[None]
+        views = [dict(qg=qg[view_layer], summary_out=ro[:, view_layer], win_k=wk, win_v=wv,
+                      win_len=np.array([shape.window]))]
+        ref16, _ = O.draft_pass(Wn, osh, anchors.numpy(), np.array([length]), hidden, views, inv_freq, "bf16")
+        gl = to_np(eng.buf["logits"][:shape.block]).reshape(1, shape.block, shape.vocab)
+        gt = eng.buf["tokens"][:1].cpu().numpy()
+        # every logit within 4 bf16 steps of the bf16 oracle; with H = 5120 and
+        # I = 17408 the longer fp32 reductions leave fewer bit-identical values
+        # than at the 4B shape (measured 23% at round 0), hence the lower floor
+        assert_bf16_close(gl, ref16, steps=4.0, exact_frac=0.15, what=f"config 3 logits, round {t}")
+        ref_tokens, corrected = O.markov_sample(ref16, anchors.numpy(), Wn, "bf16")
+        top = np.argsort(-corrected, axis=-1, kind="stable")[..., :4]
+        ties += [(t,) + x[1:] for x in compare_chain_with_reference(
+            gt, ref_tokens, np.take_along_axis(corrected, top, axis=-1), top, what=f"config 3 tokens, round {t}")]
+        checked += 1
+    print(f"config 3: {rounds} rounds x {shape.block} tokens against the oracle's own chain; rounds whose chain "
+          f"took a tie of the oracle's bf16 logits: {len(ties)} {ties}")
+    assert checked == rounds

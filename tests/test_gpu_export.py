@@ -54,6 +54,7 @@ def _case(seed, ring_pages, counts, L=3, H=8, R=5000, hidden=256):
 @pytest.mark.parametrize("ring_pages,counts,heads_split", [
     (0, [1, 16, 7, 3, 12], 1),
     (8, [5, 16, 128, 2], 1),       # ring pages; a prefill-sized request (the whole 128-row ring)
+    (2, [50, 5, 33, 32], 1),        # counts above the 32-row ring: only the last 32 rows of a request land
     (0, [9, 16, 1, 300], 2),        # two head slices, as two target TP ranks store them
 ])
 def test_export_rows_matches_oracle(ring_pages, counts, heads_split):

@@ -15,6 +15,10 @@ from longspark_b200.synthetic import make_views, make_weights, rope_inv_freq
 
 pytestmark = pytest.mark.gpu
 
+# the unmodified reference's bf16-vs-fp32 distance on the config-1 logits (max
+# over all 151,936 logits of the drafter pass, measured with the reference)
+CFG1_REFERENCE_DRIFT = 0.042
+
 SMALL = DraftShape(hidden=512, q_heads=8, kv_heads=2, inter=1024, vocab=4096, tap_layers=2, draft_layers=2,
                    slots=64, window=512, block=15, max_commit=16, markov_rank=64, mask_token_id=4000)
 
@@ -72,10 +76,9 @@ def _run_and_compare(shape, contexts, seed, *, fp32_tol=None):
     ties = tokens_exact_or_tied(gpu_tokens, corrected, what="draft tokens")
     if fp32_tol is not None:
         ref32 = _oracle_pass(shape, Wn, v, "fp32")
-        own = float(np.abs(ref16 - ref32).max())  # the reference's own bf16-vs-fp32 drift
+        own = float(np.abs(ref16 - ref32).max())  # the reference's own bf16-vs-fp32 drift, for the message
         err = float(np.abs(gpu_logits - ref32).max())
-        bound = max(fp32_tol, 1.5 * own + bf16_step(ref32))
-        assert err <= bound, f"logits vs fp32 reference: {err:.4f} > {bound:.4f} (reference bf16 drift {own:.4f})"
+        assert err <= fp32_tol, f"logits vs fp32 reference: {err:.4f} > {fp32_tol} (reference bf16 drift {own:.4f})"
     return ties
 
 
@@ -109,6 +112,15 @@ def test_round_config1_matches_oracle():
     assert_bf16_close(gl, ref16, steps=4.0, exact_frac=0.3, what="cfg1 logits vs bf16 reference")
     _, corrected = O.markov_sample(ref16, v["anchors"].numpy(), Wn, "bf16", forced=gt)
     assert tokens_exact_or_tied(gt, corrected, what="cfg1 tokens") <= 2
+    # Against fp32: the unmodified reference's own bf16 run is 0.042 (max over
+    # every logit) from its fp32 run at these dimensions, above the 3e-2 of the
+    # bf16-vs-fp32 bound; a path that rounds where the reference rounds cannot be
+    # closer, so config 1 is held to the reference's own measured distance.
+    ref32 = _oracle_pass(shape, Wn, v, "fp32")
+    err = float(np.abs(gl - ref32).max())
+    assert err <= max(3e-2, CFG1_REFERENCE_DRIFT), f"cfg1 logits vs fp32 reference: {err:.4f}"
+    print(f"cfg1 (P=15): logits vs the fp32 restatement {err:.4f}, its own bf16 run "
+          f"{float(np.abs(ref16 - ref32).max()):.4f}")
 
 
 def test_round_with_refresh_and_graph_replay():
@@ -245,3 +257,50 @@ def test_longspark_draft_api_prefill_update_propose():
     assert not torch.equal(t2, t3)
     d.release(["a"])
     assert 1 in d.free_slots or 0 in d.free_slots
+
+
+def test_step_graph_capture_with_collector_pressure():
+    """A drafter whose captured graphs sit in a reference cycle is dropped;
+    then, with Python's cyclic collector set to run at every allocation, a
+    second drafter captures its step graph (``capture_guard`` keeps automatic
+    collection out of the capture) and proposes the same tokens as a drafter
+    that runs eagerly on the same inputs."""
+    import gc
+
+    shape = SMALL.with_(window=256)
+    W = make_weights(shape, seed=41, norm_jitter=0.05)
+    g = torch.Generator().manual_seed(42)
+    L, Hkv, Hq, S = shape.tap_layers, shape.kv_heads, shape.q_heads, shape.slots
+    ids, n = ["x", "y"], 200
+    hist = torch.randn(L, 2 * (n + 16), Hkv, 128, generator=g).to(torch.bfloat16)
+
+    def drive(use_graph):
+        cfg = dict(draft_device=0, max_running_requests=2, draft_state_gib=0.5, cuda_graph=use_graph)
+        d = LongSparkDraft(cfg, weights=W, shape=shape)
+        d.update(dict(format="longspark_state_batch_v1", ids=ids, lengths=[n, n], commit_lens=[n, n],
+                      export_counts=[n, n], keys=hist[:, :2 * n], values=hist[:, :2 * n],
+                      last_hidden=torch.ones(2, L, shape.hidden, dtype=torch.bfloat16),
+                      global_output=torch.zeros(2, L, Hq, S, 128), global_lse=torch.full((2, L, Hq, S), 3.0)),
+                 prefill=True)
+        d.update(dict(format="longspark_state_batch_v1", ids=ids, lengths=[n + 16, n + 16], commit_lens=[16, 16],
+                      export_counts=[16, 16], keys=hist[:, 2 * n:], values=hist[:, 2 * n:],
+                      last_hidden=torch.ones(2, L, shape.hidden, dtype=torch.bfloat16)))
+        tokens, logits, _ = d.propose(ids, [5, 9], 0.0)
+        torch.cuda.synchronize()
+        assert d.device_status() == 0
+        return d, tokens, logits
+
+    d1, _, _ = drive(True)
+    d1.cycle = d1  # unreachable after the del below, collectable only by the cyclic collector
+    del d1
+    old = gc.get_threshold()
+    gc.set_threshold(1, 1, 1)
+    try:
+        d2, t2, l2 = drive(True)
+        assert d2.graph_stats()["replays"] >= 1
+    finally:
+        gc.set_threshold(*old)
+        gc.collect()
+    _, t3, l3 = drive(False)
+    assert torch.equal(t2, t3)
+    assert torch.equal(l2, l3)

@@ -102,3 +102,23 @@ def test_static_scratch_rejects_more_rows_than_its_maximum():
         N.call("ls_markov_argmax_static", C.c_void_p(torch.cuda.current_stream().cuda_stream), C.byref(a))
     torch.cuda.synchronize()
     assert (tokens == -1).all()  # nothing launched
+    assert int(status.item()) == 0  # and no device status recorded
+
+
+def test_static_scratch_empty_batch_and_bad_block():
+    """An empty batch returns LS_OK with nothing launched; a block of 0 is
+    rejected with LS_ERR_UNSUPPORTED like the workspace entry point does,
+    before anything is enqueued."""
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    lib = N.lib()
+    c = _case(seed=8, batch=2, block=4, vocab=1024, rank=0)
+    tokens, accept, status = _outputs(c)
+    a = _args(c, tokens, accept, status)
+    a.batch = 0
+    assert lib.ls_markov_argmax_static(stream, C.byref(a)) == N.LS_OK
+    a.batch, a.block = 2, 0
+    assert lib.ls_markov_argmax_static(stream, C.byref(a)) == 3  # LS_ERR_UNSUPPORTED
+    assert b"block <= 16" in lib.ls_last_error()
+    torch.cuda.synchronize()
+    assert (tokens == -1).all() and (accept == -1).all()
+    assert int(status.item()) == 0
