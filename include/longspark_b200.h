@@ -412,6 +412,39 @@ typedef struct ls_sample_step_args {
 LS_API size_t ls_sample_step_workspace_bytes(int batch);
 LS_API int ls_sample_step(void* stream, const ls_sample_step_args* a, void* workspace, size_t workspace_bytes);
 
+/* Temperature > 0 verification: the reference's two-phase exact rejection
+ * sampling (decide_acceptance + finish_sampling, LS engine/sampling.py:19-57,
+ * as the target drives it at LS engine/target.py:478-491 with the drafter's q
+ * rows of :613-614), both phases in one launch, one CTA per request.
+ *   p = softmax(target / T) over the block + 1 verify rows of request b;
+ *   lengths[b] = number of leading t with uniforms[b, t] * sampled_q[b, t]
+ *                < p[t, candidates[b, t]];
+ *   bonus[b] = count(final_uniforms[b] >= cumsum(probs)), at most vocab - 1,
+ *   probs = max(p[L] - softmax(draft[L] / T), 0) / mass at a rejection
+ *   (L = lengths[b] < block) when mass > 1e-8, else p[L].
+ * target_logits: bf16, row t of request b at (b * (block + 1) + t) *
+ * target_ld; draft_logits: the drafter's corrected bf16 logits, row t of
+ * request b at (b * block + t) * draft_ld.  vocab and both strides multiples
+ * of 8, logits 16-byte aligned.  A candidate outside [0, vocab) records
+ * LS_DEV_BAD_TOKEN and is read as token 0. */
+typedef struct ls_rejection_args {
+  const void* target_logits;
+  long long target_ld;
+  const void* draft_logits;
+  long long draft_ld;
+  const long long* candidates;  /* [batch, block] */
+  const float* sampled_q;       /* [batch, block]: q of each candidate */
+  const float* uniforms;        /* [batch, block] */
+  const float* final_uniforms;  /* [batch] */
+  float temperature;            /* > 0 */
+  int batch, block, vocab;
+  long long* lengths;           /* out [batch] */
+  long long* bonus;             /* out [batch] */
+  int* status;                  /* optional device status word */
+} ls_rejection_args;
+
+LS_API int ls_rejection_sample(void* stream, const ls_rejection_args* a);
+
 /* Greedy accept check: accept[b] = number of leading i < block with
  * target[b, i] == draft[b, i] (LS engine/target.py:472-477). */
 LS_API int ls_accept(void* stream, const long long* target, int target_ld, const long long* draft, long long* accept,

@@ -66,6 +66,13 @@ class SampleStepArgs(C.Structure):
                 ("status", vp)]
 
 
+class RejectionArgs(C.Structure):
+    _fields_ = [("target_logits", vp), ("target_ld", i64), ("draft_logits", vp), ("draft_ld", i64),
+                ("candidates", vp), ("sampled_q", vp), ("uniforms", vp), ("final_uniforms", vp),
+                ("temperature", f32), ("batch", i32), ("block", i32), ("vocab", i32), ("lengths", vp),
+                ("bonus", vp), ("status", vp)]
+
+
 class PrefillArgs(C.Structure):
     _fields_ = [("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("page_table", vp), ("table_stride", i32),
                 ("seq_lens", vp), ("slots", vp), ("learned_query", vp), ("state_out", vp), ("state_lse", vp),
@@ -114,6 +121,7 @@ SIGNATURES = {
     "ls_prefill_summary": (i32, [vp, C.POINTER(PrefillArgs)]),
     "ls_sample_step_workspace_bytes": (sz, [i32]),
     "ls_sample_step": (i32, [vp, C.POINTER(SampleStepArgs), vp, sz]),
+    "ls_rejection_sample": (i32, [vp, C.POINTER(RejectionArgs)]),
     "ls_ipc_alloc": (i32, [sz, C.POINTER(vp), vp]),
     "ls_ipc_open": (i32, [vp, C.POINTER(vp)]),
     "ls_ipc_close": (i32, [vp]),

@@ -379,6 +379,49 @@ def sample_step(*, logits, step, block, temperature, seed, tokens, workspace, q=
            workspace.numel() * workspace.element_size())
 
 
+def rejection_sample(*, candidates, sampled_q, target_logits, draft_logits, temperature, uniforms, final_uniforms,
+                     lengths=None, bonus=None, status=None):
+    """T > 0 verification of a drafted block (``ls_rejection_sample``): the
+    reference's ``decide_acceptance`` + ``finish_sampling``
+    (``src/longspark/engine/sampling.py:19-57``) in one launch.
+
+    candidates [B, P] int64 (the drafted tokens), sampled_q [B, P] fp32 (their
+    proposal probabilities), target_logits [B, P + 1, V] bf16 (the verify
+    pass), draft_logits [B, P, V] bf16 (the drafter's corrected logits, whose
+    softmax at the rejection position is the q row of phase two), uniforms
+    [B, P] and final_uniforms [B] fp32.  Returns (lengths [B], bonus [B])
+    int64 device tensors.  Shape errors raise ``ValueError`` with the
+    reference's messages."""
+    b, p = candidates.shape
+    if sampled_q.shape != (b, p) or uniforms.shape != (b, p):
+        raise ValueError("sampled q and uniforms must match the seven proposal positions")
+    if tuple(target_logits.shape[:2]) != (b, p + 1):
+        raise ValueError("target must verify proposal width plus one bonus row")
+    if final_uniforms.shape != (b,):
+        raise ValueError("one final uniform is required per request")
+    if tuple(draft_logits.shape[:2]) != (b, p) or draft_logits.shape[-1] != target_logits.shape[-1]:
+        raise ValueError("draft logits must cover the proposal positions over the target's vocabulary")
+    for t, dt in ((target_logits, torch.bfloat16), (draft_logits, torch.bfloat16), (candidates, torch.int64),
+                  (sampled_q, torch.float32), (uniforms, torch.float32), (final_uniforms, torch.float32)):
+        if t.dtype != dt:
+            raise ValueError(f"expected {dt} inputs, got {t.dtype}")
+    _require_cuda(candidates, sampled_q, target_logits, draft_logits, uniforms, final_uniforms)
+    tl = target_logits if target_logits.stride(-1) == 1 and target_logits.stride(1) * (p + 1) == \
+        target_logits.stride(0) else target_logits.contiguous()
+    dl = draft_logits if draft_logits.stride(-1) == 1 and draft_logits.stride(1) * p == draft_logits.stride(0) \
+        else draft_logits.contiguous()
+    dev = candidates.device
+    lengths = torch.empty(b, dtype=torch.int64, device=dev) if lengths is None else lengths
+    bonus = torch.empty(b, dtype=torch.int64, device=dev) if bonus is None else bonus
+    a = N.RejectionArgs(target_logits=_p(tl), target_ld=tl.stride(1), draft_logits=_p(dl), draft_ld=dl.stride(1),
+                        candidates=_p(candidates.contiguous()), sampled_q=_p(sampled_q.contiguous()),
+                        uniforms=_p(uniforms.contiguous()), final_uniforms=_p(final_uniforms.contiguous()),
+                        temperature=float(temperature), batch=b, block=p, vocab=tl.shape[-1], lengths=_p(lengths),
+                        bonus=_p(bonus), status=_p(status))
+    N.call("ls_rejection_sample", _stream(dev), C.byref(a))
+    return lengths, bonus
+
+
 def accept_lengths(target, draft, out):
     """Greedy accepted-prefix length (``src/longspark/engine/target.py:472-477``)."""
     _require_cuda(target, draft, out)

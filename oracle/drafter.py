@@ -33,7 +33,8 @@ __all__ = [
     "state_encoder", "shifted_input", "rope_tables", "apply_rotary",
     "attention_statistics", "statistics_as_normalized", "merge_normalized_attention",
     "window_positions", "gather_window", "export_rows", "attend", "decoder_layer", "project_logits",
-    "markov_sample", "markov_sample_gumbel", "gumbel_hash_uniform", "greedy_argmax", "accept_lengths", "position_scores", "merge_accepted",
+    "markov_sample", "markov_sample_gumbel", "gumbel_hash_uniform", "greedy_argmax", "accept_lengths",
+    "softmax_t", "rejection_sample", "position_scores", "merge_accepted",
     "full_prefix_state", "refresh_views", "draft_pass", "build_views", "DraftShapeOracle",
 ]
 
@@ -486,6 +487,59 @@ def accept_lengths(target_tokens, draft_tokens):
     acc = np.cumprod(t[:, :p] == d, axis=1).sum(axis=1).astype(np.int64)
     bonus = t[np.arange(t.shape[0]), acc] if t.shape[1] > p else None
     return acc, bonus
+
+
+def softmax_t(logits, temperature):
+    """``torch.softmax(logits.float() / T, -1)`` in float32 as torch computes it
+    on the CPU: the scaled logits by IEEE division, their maximum subtracted,
+    exponentials multiplied by the reciprocal of their sum."""
+    z = np.asarray(logits, dtype=np.float32) / np.float32(temperature)
+    e = np.exp(z - z.max(axis=-1, keepdims=True))
+    return (e * (np.float32(1) / e.sum(axis=-1, keepdims=True, dtype=np.float32))).astype(np.float32)
+
+
+def rejection_sample(target_logits, draft_logits, candidates, sampled_q, temperature, uniforms, final_uniforms):
+    """Two-phase exact rejection sampling of a verified block at T > 0 (LS
+    engine/sampling.py:19-57, driven from LS engine/target.py:478-491 and
+    :613-614).
+
+    Phase one, ``decide_acceptance``: with ``p = softmax(target / T)`` over the
+    P + 1 verify rows, proposal t is accepted when ``u[t] * q[t] < p[t,
+    cand[t]]``; the accept length is the number of leading accepted
+    proposals.  Phase two, ``finish_sampling``: a request that rejected at
+    position L draws its bonus token from the residual ``max(p[L] - q_row, 0)``
+    renormalised (``q_row = softmax(draft[L] / T)``, the drafter's corrected
+    logits; the target row itself when the residual mass is at most 1e-8); a
+    request that accepted all P draws from ``p[P]``.  The draw is the
+    reference's inverse CDF with the given final uniform:
+    ``count(u >= cumsum(probs))`` clamped to V - 1, the cumulative sum taken in
+    float64 and rounded to float32 as ``torch.cumsum`` does on the CPU.
+
+    target_logits [B, P + 1, V], draft_logits [B, P, V] (any float dtype
+    values), candidates [B, P] int, sampled_q, uniforms [B, P] float32,
+    final_uniforms [B] float32.  Returns (lengths [B] int64, bonus [B] int64)."""
+    tl = np.asarray(target_logits, dtype=np.float32)
+    dl = np.asarray(draft_logits, dtype=np.float32)
+    cand = np.asarray(candidates, dtype=np.int64)
+    b_n, p_n = cand.shape
+    vocab = tl.shape[-1]
+    probs = softmax_t(tl, temperature)
+    sel = np.take_along_axis(probs[:, :p_n], cand[..., None], axis=-1)[..., 0]
+    accept = (np.asarray(uniforms, np.float32) * np.asarray(sampled_q, np.float32)) < sel
+    lengths = np.cumprod(accept.astype(np.int64), axis=1).sum(axis=1)
+    bonus = np.zeros(b_n, dtype=np.int64)
+    for b in range(b_n):
+        L = int(lengths[b])
+        row = probs[b, L]
+        if L < p_n:
+            q_row = softmax_t(dl[b, L], temperature)
+            residual = np.maximum(row - q_row, np.float32(0))
+            mass = residual.sum(dtype=np.float32)
+            if mass > np.float32(1e-8):
+                row = residual / np.maximum(mass, np.float32(1e-30))
+        cdf = np.cumsum(row.astype(np.float64)).astype(np.float32)
+        bonus[b] = min(int((np.float32(final_uniforms[b]) >= cdf).sum()), vocab - 1)
+    return lengths.astype(np.int64), bonus
 
 
 # ----------------------------------------------------------------------------

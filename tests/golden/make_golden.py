@@ -329,10 +329,57 @@ def chain_fixture(name, shape: DraftShape, *, ctx0, rounds, seed, topk=4):
     print("wrote", name)
 
 
-def main(which=("refresh", "draft", "chain")):
+def load_sampling():
+    """``src/longspark/engine/sampling.py`` by file path (it imports torch only)."""
+    path = REF / "src/longspark/engine/sampling.py"
+    spec = importlib.util.spec_from_file_location("ls_ref_sampling", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def sampling_fixture(name="rejection_sampling"):
+    """Two-phase rejection sampling of the reference (``decide_acceptance`` then
+    ``finish_sampling`` with given uniforms, ``src/longspark/engine/
+    sampling.py:19-57``) driven as the target does (``engine/target.py:478-491``,
+    q rows from the drafter's corrected logits as at :613-614), on the inputs
+    of ``sampling_inputs.CASES``; the proposal probabilities q are the
+    reference drafter's (``engine/draft.py:284-286``).  Stores per case the
+    candidates, q, uniforms, accept lengths and bonus tokens."""
+    from sampling_inputs import CASES, sampling_draws, sampling_logits
+
+    smp = load_sampling()
+    out = {}
+    for case, (batch, block, vocab, temp, seed, sd, sn, same) in CASES.items():
+        target, draft = sampling_logits(batch, block, vocab, seed, sd, sn, same)
+        cand, uniforms, final = sampling_draws(draft, temp, seed)
+        cand_t = torch.from_numpy(cand)
+        q = torch.softmax(draft.float() / temp, -1).gather(-1, cand_t[..., None]).squeeze(-1)
+        # the requests whose target rows equal the drafter's claim q = 1: they
+        # reject where u >= p, and the residual there has zero mass (the
+        # reference's fallback to the target row)
+        q[:same] = 1.0
+        decision = smp.decide_acceptance(candidates=cand_t, sampled_q=q,
+                                         target_probs=torch.softmax(target.float() / temp, -1),
+                                         uniforms=torch.from_numpy(uniforms))
+        rows = decision.rejected_rows
+        q_rows = torch.softmax(draft[rows, decision.rejection_positions].float() / temp, -1)
+        bonus = smp.finish_sampling(decision, q_rows, uniforms=torch.from_numpy(final))
+        p = case + "_"
+        out.update({p + "candidates": cand, p + "q": q.numpy(), p + "uniforms": uniforms, p + "final": final,
+                    p + "lengths": decision.lengths.numpy(), p + "bonus": bonus.numpy()})
+        print(case, "lengths", decision.lengths.tolist(), "bonus", bonus.tolist())
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print("wrote", name)
+
+
+def main(which=("refresh", "draft", "chain", "sampling")):
     torch.set_num_threads(os.cpu_count() or 1)
+    sys.path.insert(0, str(HERE))
+    if "sampling" in which:
+        sampling_fixture()
     if "chain" in which:
-        sys.path.insert(0, str(HERE))
         base = dict(tap_layers=1, draft_layers=1, slots=256, block=7, max_commit=8)
         # Qwen3-14B dimensions (BASELINE config 3: 1 drafter layer, W=2048, S=256,
         # 128K context, 200 chained rounds) at the reference's Local7 block
@@ -373,4 +420,4 @@ def draft_fixtures():
 
 
 if __name__ == "__main__":
-    main(tuple(sys.argv[1:]) or ("refresh", "draft", "chain"))
+    main(tuple(sys.argv[1:]) or ("refresh", "draft", "chain", "sampling"))

@@ -39,6 +39,11 @@ FP32_TOL = 3e-2
 # their top 32, all 7 steps); no implementation that rounds where the
 # reference rounds can be closer, so this config is held to that distance.
 CFG1_REFERENCE_DRIFT = 0.0370
+# The chained fixtures' larger dimensions put the top logits at 6-8, where one
+# bf16 step is 0.031-0.062: the reference's own bf16 run is up to this far from
+# its own fp32 run on the logits both rank in their top 4 (max over every round
+# and step of the fixture), so these configs are held to that distance.
+CHAIN_REFERENCE_DRIFT = {"chain_cfg2_p7": 0.0435, "chain_cfg3_p7": 0.0594}
 # bf16 logits against the reference's bf16 run: the rounding points are the
 # reference's, only the fp32 accumulation order differs, and a one-step
 # difference in an intermediate propagates; at most this many bf16 steps (at
@@ -210,8 +215,9 @@ def test_chain_matches_reference_every_round(golden_dir, name):
         assert e16 <= BF16_STEPS * bf16_step(g["base_vals"][t]), f"{name} round {t}: {e16:.4g} from bf16 run"
         at32 = np.take_along_axis(base[0], g["base32_ids"][t], axis=-1)
         e32 = float(np.abs(at32 - g["base32_vals"][t]).max())
-        assert e32 <= FP32_TOL, f"{name} round {t}: {e32:.4g} from the reference's fp32 run"
+        assert e32 <= max(FP32_TOL, CHAIN_REFERENCE_DRIFT[name]), \
+            f"{name} round {t}: {e32:.4g} from the reference's fp32 run"
         worst16, worst32 = max(worst16, e16), max(worst32, e32)
     print(f"{name}: {rounds} rounds x {P} tokens; rounds whose chain took a tie of the reference: {len(all_ties)} "
-          f"{all_ties}; top-4 logits vs bf16 run <= {worst16:.4g}, vs fp32 run <= {worst32:.4g}; "
-          f"summary lse vs oracle <= {worst_state:.3g}")
+          f"{all_ties}; top-4 logits vs bf16 run <= {worst16:.4g}, vs fp32 run <= {worst32:.4g} (the reference's "
+          f"own bf16 run: {CHAIN_REFERENCE_DRIFT[name]}); summary lse vs oracle <= {worst_state:.3g}")

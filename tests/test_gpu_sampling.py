@@ -112,3 +112,92 @@ def test_engine_sample_matches_oracle_chain():
     assert (gt[sure] == toks[sure]).all()
     assert sure.mean() > 0.9
     np.testing.assert_allclose(gq[gt == toks], q[gt == toks], rtol=1e-3)
+
+
+# ----------------------------------------------------------------------------
+# T > 0 verification: two-phase rejection sampling (ls_rejection_sample)
+# ----------------------------------------------------------------------------
+
+def test_rejection_sampling_matches_reference(golden_dir):
+    """Accept lengths and bonus tokens equal to the reference's
+    ``decide_acceptance`` + ``finish_sampling`` run with the same uniforms
+    (fixtures from the unmodified reference): 64 requests at V=4096 and 8 at
+    V=151936 with 7 and 15 proposals, including requests that reject where the
+    residual has zero mass (the fallback to the target row)."""
+    import sys
+    sys.path.insert(0, str(golden_dir))
+    from sampling_inputs import CASES, sampling_logits
+
+    z = np.load(golden_dir / "rejection_sampling.npz")
+    dev = torch.device("cuda")
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    for case, (batch, block, vocab, temp, seed, sd, sn, same) in CASES.items():
+        target, draft = sampling_logits(batch, block, vocab, seed, sd, sn, same)
+        p = case + "_"
+        lengths, bonus = ops.rejection_sample(
+            candidates=torch.from_numpy(z[p + "candidates"]).to(dev), sampled_q=torch.from_numpy(z[p + "q"]).to(dev),
+            target_logits=target.to(dev), draft_logits=draft.to(dev), temperature=temp,
+            uniforms=torch.from_numpy(z[p + "uniforms"]).to(dev), final_uniforms=torch.from_numpy(z[p + "final"]).to(dev),
+            status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        np.testing.assert_array_equal(lengths.cpu().numpy(), z[p + "lengths"], err_msg=case)
+        np.testing.assert_array_equal(bonus.cpu().numpy(), z[p + "bonus"], err_msg=case)
+
+
+@pytest.mark.parametrize("batch,block,vocab,temp", [(33, 16, 8192, 0.3), (5, 1, 151936, 2.0), (3, 15, 151936, 0.8)])
+def test_rejection_sampling_matches_oracle(batch, block, vocab, temp):
+    """Random drafts and verify passes with consistent q (from the drafter's
+    own distribution), against the oracle restatement; strided views of
+    larger logit buffers, as the engine hands them over."""
+    g = torch.Generator().manual_seed(batch * 131 + block)
+    draft = (2.0 * torch.randn(batch, block, vocab, generator=g)).to(torch.bfloat16)
+    target = (draft.float()[:, list(range(block)) + [block - 1]] +
+              0.4 * torch.randn(batch, block + 1, vocab, generator=g)).to(torch.bfloat16)
+    probs = torch.softmax(draft.float() / temp, -1)
+    cand = torch.multinomial(probs.view(-1, vocab), 1, generator=g).view(batch, block)
+    q = probs.gather(-1, cand[..., None]).squeeze(-1)
+    u = torch.rand(batch, block, generator=g)
+    uf = torch.rand(batch, generator=g)
+    dev = torch.device("cuda")
+    pad = torch.zeros(batch, block + 1, vocab + 64, dtype=torch.bfloat16)
+    pad[..., :vocab] = target
+    lengths, bonus = ops.rejection_sample(candidates=cand.to(dev), sampled_q=q.to(dev),
+                                          target_logits=pad.to(dev)[..., :vocab], draft_logits=draft.to(dev),
+                                          temperature=temp, uniforms=u.to(dev), final_uniforms=uf.to(dev))
+    want_l, want_b = O.rejection_sample(target.float().numpy(), draft.float().numpy(), cand.numpy(), q.numpy(), temp,
+                                        u.numpy(), uf.numpy())
+    np.testing.assert_array_equal(lengths.cpu().numpy(), want_l)
+    np.testing.assert_array_equal(bonus.cpu().numpy(), want_b)
+
+
+def test_rejection_sampling_argument_errors():
+    """The reference's shape errors (LS engine/sampling.py:21-25, 41-43) and a
+    candidate outside the vocabulary (device status LS_DEV_BAD_TOKEN)."""
+    dev = torch.device("cuda")
+    b, p, v = 2, 3, 256
+    t = torch.zeros(b, p + 1, v, dtype=torch.bfloat16, device=dev)
+    d = torch.zeros(b, p, v, dtype=torch.bfloat16, device=dev)
+    c = torch.zeros(b, p, dtype=torch.int64, device=dev)
+    q = torch.full((b, p), 0.5, device=dev)
+    u = torch.full((b, p), 0.5, device=dev)
+    uf = torch.full((b,), 0.5, device=dev)
+    with pytest.raises(ValueError, match="proposal positions"):
+        ops.rejection_sample(candidates=c, sampled_q=q[:, :2], target_logits=t, draft_logits=d, temperature=1.0,
+                             uniforms=u, final_uniforms=uf)
+    with pytest.raises(ValueError, match="plus one bonus row"):
+        ops.rejection_sample(candidates=c, sampled_q=q, target_logits=t[:, :p], draft_logits=d, temperature=1.0,
+                             uniforms=u, final_uniforms=uf)
+    with pytest.raises(ValueError, match="one final uniform"):
+        ops.rejection_sample(candidates=c, sampled_q=q, target_logits=t, draft_logits=d, temperature=1.0,
+                             uniforms=u, final_uniforms=uf[:1])
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    c[1, 0] = v + 5
+    lengths, bonus = ops.rejection_sample(candidates=c, sampled_q=q, target_logits=t, draft_logits=d, temperature=1.0,
+                                          uniforms=u, final_uniforms=uf, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 111
+    # flat logits: p = 1/256 for every token, u * q = 0.25 >= p rejects at 0;
+    # the residual p - q_row is zero, so the draw falls back to the target row
+    assert lengths.tolist() == [0, 0]
+    assert bonus.tolist() == [128, 128]  # cumsum reaches 0.5 at index 127: 128 prefixes <= u

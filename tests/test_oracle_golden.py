@@ -152,3 +152,62 @@ def test_prefill_plus_increments_equals_full_prefix():
     ref_out, ref_lse = O.full_prefix_state(q, K, V, pos)
     np.testing.assert_allclose(out, ref_out, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(lse, ref_lse, rtol=1e-5, atol=1e-5)
+
+
+def test_rejection_sampling_matches_reference(golden_dir):
+    """The two-phase T > 0 accept rule and bonus draw (LS engine/sampling.py:
+    19-57) restated, against the reference run with the same uniforms: accept
+    lengths and bonus tokens equal."""
+    import sys
+    sys.path.insert(0, str(golden_dir))
+    from sampling_inputs import CASES, sampling_logits
+
+    z = _load(golden_dir, "rejection_sampling")
+    for case, (batch, block, vocab, temp, seed, sd, sn, same) in CASES.items():
+        target, draft = sampling_logits(batch, block, vocab, seed, sd, sn, same)
+        p = case + "_"
+        lengths, bonus = O.rejection_sample(target.float().numpy(), draft.float().numpy(), z[p + "candidates"],
+                                            z[p + "q"], temp, z[p + "uniforms"], z[p + "final"])
+        np.testing.assert_array_equal(lengths, z[p + "lengths"], err_msg=case)
+        np.testing.assert_array_equal(bonus, z[p + "bonus"], err_msg=case)
+
+
+def test_oracle_chain_cfg2_dimensions_matches_reference(golden_dir):
+    """The oracle's refresh chain and bf16 pass against the reference's own
+    chained run at config-2 dimensions (H=4096, 32/8 heads, I=12288,
+    V=151936, W=1024, S=256, 128K context, P=7, 8 rounds): tokens equal every
+    round but where the reference's own bf16 logits tie (top two at most one
+    bf16 step apart; 3 of the 8 rounds measured), and the summary lse after
+    the first and last round within 2e-5."""
+    from gpu_util import compare_chain_with_reference
+    import sys
+    sys.path.insert(0, str(golden_dir))
+    from chain_inputs import chain_views, chain_weights, committed_rows
+
+    g = _load(golden_dir, "chain_cfg2_p7")
+    shape = _shape_from(g["shape"])
+    rounds, ctx0, seed = int(g["rounds"]), int(g["ctx0"]), int(g["seed"])
+    Wt = chain_weights(shape, seed)
+    W = {k: v.float().numpy() for k, v in Wt.items()}
+    del Wt
+    v = chain_views(shape, ctx0, rounds, seed + 1)
+    qg = W["global16_raw256_reference.global_query_generator.learned_query"]
+    out, lse = v["summary_out"].numpy().copy(), v["summary_lse"].numpy().copy()
+    kk, vv = v["kv_k"].float().numpy(), v["kv_v"].float().numpy()
+    table = v["page_table"].numpy()
+    ties = []
+    for t in range(rounds):
+        c, n = int(v["commits"][t]), int(v["lengths"][t])
+        nk = committed_rows(v["kv_k"], v["page_table"], n, c, shape.max_commit).float().numpy()
+        nv = committed_rows(v["kv_v"], v["page_table"], n, c, shape.max_commit).float().numpy()
+        out, lse = O.refresh_views(out, lse, np.array([0]), qg, nk, nv, np.array([c]), 128 ** -0.5)
+        if t == 0:
+            np.testing.assert_allclose(lse, g["lse_first"], rtol=2e-5, atol=2e-5)
+        inp = dict(kv_k=kk, kv_v=vv, table=table, seq_lens=np.array([n], np.int32), summary_out=out,
+                   hidden=v["hidden"][t].float().numpy(), anchors=v["anchors"][t:t + 1].numpy())
+        base = _run_oracle(shape, W, inp, "bf16")
+        toks, _ = O.markov_sample(base, inp["anchors"], W, "bf16")
+        ties += compare_chain_with_reference(toks, g["tokens"][t][None], g["corr_vals"][t][None],
+                                             g["corr_ids"][t][None], what=f"round {t}")
+    np.testing.assert_allclose(lse, g["lse_last"], rtol=2e-5, atol=2e-5)
+    print(f"oracle vs reference, config-2 dimensions: {rounds} rounds, ties taken {ties}")
