@@ -569,6 +569,365 @@ __global__ void __launch_bounds__(MANY ? 160 : 256, MANY ? 2 : 1) attention_clus
   cluster_sync_all();  // keep the parked states alive until every CTA has read them
 }
 
+// ---------------------------------------------------------------------------
+// Streaming instantiation: one CTA per (request, KV head), for batches with
+// enough (request, KV head) units to fill the GPU.  The cluster kernel above
+// splits every unit over 8 CTAs, each holding a short burst of loads; with
+// many units that makes thousands of short CTAs, each mostly waiting on its
+// own staging (ncu at 32 requests: 11% of the warp slots occupied, 15% of
+// DRAM bandwidth).  Here one producer warp streams the unit's keys and values
+// into a ring of shared-memory stages with bulk copies (one per 256-byte
+// row: a window row of one KV head is contiguous, consecutive rows of a page
+// are not), each stage completing on an mbarrier, while 2 consumer warps per
+// query head run the same online-softmax tiles as the cluster kernel:
+//   window stages: 64 rows; warp `part` of a head takes rows [32 part, +32);
+//   summary stages: 16 slots of every head of the group; warp `part` takes
+//   the stages of its parity (each query head has its own summary keys);
+//   local rows: the part-1 warp of each head.
+// The two warps' states of a source are folded through shared memory and the
+// three sources merged exactly as the cluster kernel merges them (per-source
+// bf16 rounding of the weighted sum, then the log-sum-exp merge in the order
+// summary, window, local).  Window rows and learned queries are issued
+// before griddepcontrol.wait, the bf16 summary values (the view refresh may
+// be the preceding kernel) after it.
+// ---------------------------------------------------------------------------
+constexpr int AS_WROWS = 64;       // window rows per stage
+constexpr int AS_SSLOTS = 16;      // summary slots of each head per stage
+constexpr int AS_MAX_G = 5;
+constexpr int AS_MIN_UNITS = 64;   // (request, KV head) units from which the streaming kernel is used
+constexpr int AS_MAXPAGES = 264;   // window pages (W <= 4096 spans at most 257)
+constexpr int AS_HEAD_BYTES = 16 * AT_PITCH * 2;               // one 16-row bf16 tile
+constexpr int AS_PARK_BYTES = 16 * 128 * 4 + 16 * 2 * 4;       // fp32 state of one warp + (m, l) per row
+constexpr int AS_RES_BYTES = 16 * 128 * 2 + 16 * 2 * 4;        // bf16 weighted sum + (m, l) per row
+
+struct StreamLayout {
+  int G, stage_rows, stages;
+  size_t pg, q, loc, park, resw, stage0, total;
+};
+
+__host__ __device__ inline StreamLayout stream_layout(int G, int stages) {
+  StreamLayout L{};
+  L.G = G;
+  L.stage_rows = G * AS_SSLOTS > AS_WROWS ? G * AS_SSLOTS : AS_WROWS;
+  L.stages = stages;
+  L.pg = 128;                                   // [0, 128): mbarriers and the abort flag
+  L.q = L.pg + (size_t)AS_MAXPAGES * 4;         // 1184 (16-byte aligned)
+  L.loc = L.q + (size_t)G * AS_HEAD_BYTES;
+  L.park = L.loc + 2 * (size_t)AS_HEAD_BYTES;
+  L.resw = L.park + (size_t)G * AS_PARK_BYTES;
+  L.stage0 = L.resw + (size_t)G * AS_RES_BYTES;
+  L.total = L.stage0 + (size_t)stages * L.stage_rows * 2 * AT_PITCH * 2;
+  return L;
+}
+
+// Fold a state parked at offset 0 of (ml, acc) (park_state with one head and
+// slot 0) into this warp's state.
+__device__ __forceinline__ void fold_parked_at(const float2* ml, const float* acc, WarpState& st) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t2 = (lane & 3) * 2;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int row = g + hh * 8;
+    const float2 o = ml[row];
+    const float m = fmaxf(st.m[hh], o.x);
+    const float mu = m == -INFINITY ? 0.0f : m;
+    const float f0 = fast_exp(st.m[hh] - mu), f1 = fast_exp(o.x - mu);
+    st.m[hh] = m;
+    st.l[hh] = st.l[hh] * f0 + o.y * f1;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const float2 v = *reinterpret_cast<const float2*>(acc + row * 128 + nt * 8 + t2);
+      st.o[nt][hh * 2] = st.o[nt][hh * 2] * f0 + v.x * f1;
+      st.o[nt][hh * 2 + 1] = st.o[nt][hh * 2 + 1] * f0 + v.y * f1;
+    }
+  }
+}
+
+// A finished source of one head: the weighted sum rounded to bf16 ([16][128])
+// then (m, l) per row, as the merge reads it.
+__device__ __forceinline__ void store_result(uint8_t* res, const WarpState& st) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t2 = (lane & 3) * 2;
+  bf16* wv = reinterpret_cast<bf16*>(res);
+  float2* ml = reinterpret_cast<float2*>(res + 16 * 128 * 2);
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int row = g + hh * 8;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+      *reinterpret_cast<uint32_t*>(wv + row * 128 + nt * 8 + t2) = pack_bf16(st.o[nt][hh * 2], st.o[nt][hh * 2 + 1]);
+    if ((lane & 3) == 0) ml[row] = make_float2(st.m[hh], st.l[hh]);
+  }
+}
+
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Per-row normalised output of one source from a parked (bf16 weighted sum,
+// m, l) record: bf16(wv) / l (the rounded weighted sum is stored), and lse.
+__device__ __forceinline__ float src_lse(float m, float l) { return l > 0.0f ? m + __logf(fmaxf(l, 1.17549435e-38f)) : -INFINITY; }
+
+template <int NS>
+__global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_kernel(const AttnParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  asm volatile("griddepcontrol.launch_dependents;");
+  const ls_attention_args& a = p.a;
+  const int G = p.G;
+  const int ncons = 2 * G;            // consumer warps
+  const StreamLayout Ly = stream_layout(G, NS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + NS;
+  volatile int* abort = reinterpret_cast<volatile int*>(smem_raw + 64);
+  int* pg = reinterpret_cast<int*>(smem_raw + Ly.pg);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x % a.kv_heads;
+  const int b = blockIdx.x / a.kv_heads;
+  const int P = a.block;
+  const int len = a.seq_lens[b];
+  const int wl = len < a.window ? (len > 0 ? len : 0) : a.window;
+  const int wstart = len - wl;
+  const int nwb = (wl + AS_WROWS - 1) / AS_WROWS;
+  const int nsb = (a.slots_per_head + AS_SSLOTS - 1) / AS_SSLOTS;
+  const int nblocks = nwb + nsb;
+  const int stage_rows = Ly.stage_rows;
+  int slot = a.slots[b];
+  if (slot < 0 || slot >= a.capacity) {
+    if (threadIdx.x == 0) record_status(a.status, LS_DEV_BAD_INDEX);
+    slot = 0;  // read a valid entry; the status word reports the bad index
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], ncons);
+    }
+    *abort = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == ncons) {
+    // ---------------- producer warp ----------------
+    const int first_lp = wstart >> 4;
+    const int n_pages = wl > 0 ? ((wstart + wl - 1) >> 4) - first_lp + 1 : 0;
+    for (int i = lane; i < n_pages; i += 32) {
+      int lp = first_lp + i;
+      if (a.ring_pages > 0) lp %= a.ring_pages;
+      int page = lp < a.table_stride ? a.page_table[(long long)b * a.table_stride + lp] : -1;
+      if (page < 0 || page >= a.pool_pages) {
+        record_status(a.status, LS_DEV_BAD_INDEX);
+        page = -1;
+      }
+      pg[i] = page;
+    }
+    __syncwarp();
+    const bf16* kk = reinterpret_cast<const bf16*>(a.kv_k);
+    const bf16* vv = reinterpret_cast<const bf16*>(a.kv_v);
+    const bf16* lq = reinterpret_cast<const bf16*>(a.learned_query);
+    const bf16* sv = reinterpret_cast<const bf16*>(a.state_bf16) + (long long)slot * a.state_bf16_stride;
+    const uint64_t stream_pol = policy_evict_first();
+    const uint64_t keep_pol = policy_evict_last();
+    int armed = 0;
+    for (int blk = 0; blk < nblocks; ++blk) {
+      const int stage = blk % NS;
+      if (blk >= NS && !mbar_wait(&empty[stage], ((blk / NS) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER))
+        break;
+      if (blk == nwb) asm volatile("griddepcontrol.wait;" ::: "memory");  // summary values: after the refresh
+      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw + Ly.stage0) + (size_t)stage * 2 * stage_rows;
+      bf16 (*vs)[AT_PITCH] = ks + stage_rows;
+      uint32_t bytes = 0;
+      if (blk < nwb) {
+        const int r0 = blk * AS_WROWS;
+        const int n = wl - r0 < AS_WROWS ? wl - r0 : AS_WROWS;
+        // rows past the window or on a bad page: zeros (a masked key must not
+        // bring a NaN into P.V through its value row)
+        for (int r = lane; r < AS_WROWS; r += 32) {
+          const int pos = wstart + r0 + r;
+          const bool ok = r < n && pg[(pos >> 4) - first_lp] >= 0;
+          if (ok) {
+            bytes += 512;
+          } else {
+            for (int c = 0; c < 16; ++c) {
+              *reinterpret_cast<uint4*>(&ks[r][c * 8]) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(&vs[r][c * 8]) = make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+        bytes = __reduce_add_sync(0xffffffffu, bytes);
+        // the zeros are generic-proxy stores into rows that bulk copies (async
+        // proxy) filled before and will fill again: order them
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&full[stage], bytes);
+        __syncwarp();
+        for (int r = lane; r < n; r += 32) {
+          const int pos = wstart + r0 + r;
+          const int page = pg[(pos >> 4) - first_lp];
+          if (page >= 0) {
+            const long long off = (((long long)page * 16 + (pos & 15)) * a.kv_heads + g) * 128;
+            bulk_load(&ks[r][0], kk + off, 256, &full[stage], stream_pol);
+            bulk_load(&vs[r][0], vv + off, 256, &full[stage], stream_pol);
+          }
+        }
+      } else {
+        const int s0 = (blk - nwb) * AS_SSLOTS;
+        const int n = a.slots_per_head - s0 < AS_SSLOTS ? a.slots_per_head - s0 : AS_SSLOTS;
+        if (n < AS_SSLOTS) {  // a last partial block: zeros past the slots
+          for (int i = lane; i < G * AS_SSLOTS; i += 32) {
+            if (i % AS_SSLOTS < n) continue;
+            for (int c = 0; c < 16; ++c) {
+              *reinterpret_cast<uint4*>(&ks[i][c * 8]) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(&vs[i][c * 8]) = make_uint4(0, 0, 0, 0);
+            }
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&full[stage], (uint32_t)(G * n * 512));
+        __syncwarp();
+        for (int i = lane; i < G * AS_SSLOTS; i += 32) {
+          const int hw = i / AS_SSLOTS, s = i % AS_SSLOTS;
+          if (s < n) {
+            const long long off = ((long long)(g * G + hw) * a.slots_per_head + s0 + s) * 128;
+            bulk_load(&ks[i][0], lq + off, 256, &full[stage], keep_pol);
+            bulk_load(&vs[i][0], sv + off, 256, &full[stage], stream_pol);
+          }
+        }
+      }
+      armed = blk + 1;
+    }
+    if (armed < nblocks || *abort) {
+      // gave up: let the copies already issued land before the CTA exits
+      for (int blk = armed > NS ? armed - NS : 0; blk < armed; ++blk)
+        (void)mbar_wait(&full[blk % NS], (blk / NS) & 1, nullptr, a.status, LS_DEV_TIMEOUT_PRODUCER);
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int hw = warp % G, part = warp / G;  // head of the group, which half of the work
+  const int h = g * G + hw;
+  const int nthreads = ncons * 32;
+  const int row_ld = (a.q_heads + 2 * a.kv_heads) * 128;
+  const bf16* qkv = reinterpret_cast<const bf16*>(a.qkv);
+  bf16 (*qs)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw + Ly.q) + hw * 16;
+  bf16 (*lk)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw + Ly.loc);
+  bf16 (*lv)[AT_PITCH] = lk + 16;
+  uint8_t* park = smem_raw + Ly.park + (size_t)hw * AS_PARK_BYTES;
+  float2* park_ml = reinterpret_cast<float2*>(park + 16 * 128 * 4);
+  float* park_acc = reinterpret_cast<float*>(park);
+  uint8_t* resw = smem_raw + Ly.resw + (size_t)hw * AS_RES_BYTES;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // q, local k/v: outputs of the projection
+  if (part == 0) load_q_tile(qs, qkv, row_ld, b * P, P, h);
+  for (int i = threadIdx.x; i < 16 * 16; i += nthreads) {
+    const int r = i >> 4, col = (i & 15) << 3;
+    uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
+    if (r < P) {
+      const bf16* rowp = qkv + (long long)(b * P + r) * row_ld;
+      kv4 = *reinterpret_cast<const uint4*>(rowp + (a.q_heads + g) * 128 + col);
+      vv4 = *reinterpret_cast<const uint4*>(rowp + (a.q_heads + a.kv_heads + g) * 128 + col);
+    }
+    *reinterpret_cast<uint4*>(&lk[r][col]) = kv4;
+    *reinterpret_cast<uint4*>(&lv[r][col]) = vv4;
+  }
+  consumer_sync(nthreads);
+  uint32_t qf[8][4];
+  load_q_frags(qf, qs);
+  const float scale = a.softmax_scale;
+  const int gl = lane >> 2, t2 = (lane & 3) * 2;
+
+  WarpState st;
+  ws_init(st);
+  for (int blk = 0; blk < nblocks; ++blk) {
+    const int stage = blk % NS;
+    const bool ok = !*abort && mbar_wait(&full[stage], (blk / NS) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+    if (ok) {
+      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw + Ly.stage0) + (size_t)stage * 2 * stage_rows;
+      bf16 (*vs)[AT_PITCH] = ks + stage_rows;
+      if (blk < nwb) {
+        const int n = wl - blk * AS_WROWS < AS_WROWS ? wl - blk * AS_WROWS : AS_WROWS;
+        if (n > part * 32) attend_block<4>(st, qf, ks, vs, part * 32, n - part * 32, scale);
+      } else if (((blk - nwb) & 1) == part) {
+        const int s0 = (blk - nwb) * AS_SSLOTS;
+        const int n = a.slots_per_head - s0 < AS_SSLOTS ? a.slots_per_head - s0 : AS_SSLOTS;
+        attend_block<2>(st, qf, ks + hw * AS_SSLOTS, vs + hw * AS_SSLOTS, 0, n, scale);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (blk == nwb - 1) {
+      // ---- window done: fold the two halves, keep (bf16 weighted sum, m, l) ----
+      if (part == 1) park_state(park_ml, park_acc, 1, 0, 0, st);
+      consumer_sync(nthreads);
+      if (part == 0) {
+        fold_parked_at(park_ml, park_acc, st);
+        store_result(resw, st);
+      }
+      consumer_sync(nthreads);
+      ws_init(st);
+    }
+  }
+  if (nwb == 0) {
+    // no window rows: an empty window source
+    if (part == 0) {
+      WarpState e;
+      ws_init(e);
+      store_result(resw, e);
+    }
+  }
+  // ---- summary done: fold the halves; part 1 computes the local rows ----
+  if (part == 1) park_state(park_ml, park_acc, 1, 0, 0, st);
+  consumer_sync(nthreads);
+  WarpState loc;
+  ws_init(loc);
+  if (part == 0) {
+    fold_parked_at(park_ml, park_acc, st);
+  } else {
+    attend_block<2>(loc, qf, lk, lv, 0, P, scale);
+  }
+  consumer_sync(nthreads);
+  if (part == 1) store_result(park, loc);
+  consumer_sync(nthreads);
+  if (part != 0) return;
+  // ---- merge (summary, window, local) and store ----
+  const float2* wml = reinterpret_cast<const float2*>(resw + 16 * 128 * 2);
+  const bf16* wvb = reinterpret_cast<const bf16*>(resw);
+  const float2* lml = reinterpret_cast<const float2*>(park + 16 * 128 * 2);
+  const bf16* lvb = reinterpret_cast<const bf16*>(park);
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int row = gl + hh * 8;
+    const float ls_ = src_lse(st.m[hh], st.l[hh]);
+    const float2 wmlr = wml[row], lmlr = lml[row];
+    const float lw = src_lse(wmlr.x, wmlr.y), ll = src_lse(lmlr.x, lmlr.y);
+    const float mx = fmaxf(fmaxf(ls_, lw), ll);
+    const float mxs = mx == -INFINITY ? 0.0f : mx;
+    const float tot = fast_exp(ls_ - mxs) + fast_exp(lw - mxs) + fast_exp(ll - mxs);
+    const float merged = mxs + __logf(tot);
+    const float safe_m = (merged == -INFINITY || merged != merged) ? 0.0f : merged;
+    const float cs = fast_exp(ls_ - safe_m), cw = fast_exp(lw - safe_m), cl = fast_exp(ll - safe_m);
+    const float is = fmaxf(st.l[hh], 1.17549435e-38f), iw = fmaxf(wmlr.y, 1.17549435e-38f),
+                il = fmaxf(lmlr.y, 1.17549435e-38f);
+    if (row < P) {
+      bf16* out = reinterpret_cast<bf16*>(a.out) + (long long)(b * P + row) * a.q_heads * 128 + h * 128;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int d = j * 8 + t2;
+        float o2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float os = __fdividef(bf16_round(st.o[j][hh * 2 + e]), is);
+          const float ow = __fdividef(__bfloat162float(wvb[row * 128 + d + e]), iw);
+          const float ol = __fdividef(__bfloat162float(lvb[row * 128 + d + e]), il);
+          o2[e] = cs * os + cw * ow + cl * ol;
+        }
+        *reinterpret_cast<uint32_t*>(out + d) = pack_bf16(o2[0], o2[1]);
+      }
+    }
+  }
+}
+
 struct AttnPlan {
   int G, nw, wrows, sslots, sc, threads;
   bool many;
@@ -635,6 +994,40 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
   p.wrows = pl.wrows;
   p.sslots = pl.sslots;
   p.sc = pl.sc;
+  // Streaming instantiation for batches with enough (request, KV head) units
+  // (LONGSPARK_B200_ATTN=cluster|stream overrides the choice, for A/B timing).
+  const int G = a->q_heads / a->kv_heads;
+  const long long units = (long long)a->batch * a->kv_heads;
+  static const int attn_mode = [] {
+    const char* e = getenv("LONGSPARK_B200_ATTN");
+    if (e == nullptr) return 0;
+    return e[0] == 's' ? 1 : (e[0] == 'c' ? 2 : 0);
+  }();
+  const bool can_stream = G <= AS_MAX_G && a->state_bf16 != nullptr && (a->state_bf16_stride % 8) == 0;
+  const bool use_stream =
+      can_stream && (attn_mode == 1 || (attn_mode == 0 && units >= AS_MIN_UNITS));
+  if (use_stream) {
+    static bool stream_configured = false;
+    if (!stream_configured) {
+      cudaError_t e = cudaFuncSetAttribute(attention_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(stream_layout(4, 4).total));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attention_stream_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(stream_layout(5, 3).total));
+      if (e != cudaSuccess) return set_cuda_error("ls_draft_attention: cudaFuncSetAttribute (stream)", e);
+      stream_configured = true;
+    }
+    const int ns = G <= 4 ? 4 : 3;
+    const StreamLayout L = stream_layout(G, ns);
+    AttnParams sp{};
+    sp.a = *a;
+    sp.G = G;
+    cudaError_t e = ns == 4 ? launch_pdl(attention_stream_kernel<4>, dim3(static_cast<unsigned>(units)),
+                                         dim3(32 * (2 * G + 1)), L.total, reinterpret_cast<cudaStream_t>(stream), sp)
+                            : launch_pdl(attention_stream_kernel<3>, dim3(static_cast<unsigned>(units)),
+                                         dim3(32 * (2 * G + 1)), L.total, reinterpret_cast<cudaStream_t>(stream), sp);
+    return e == cudaSuccess ? LS_OK : set_cuda_error("ls_draft_attention: launch (stream)", e);
+  }
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,

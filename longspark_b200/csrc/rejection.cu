@@ -147,8 +147,12 @@ __device__ __forceinline__ float2 row_stats(const bf16* row, int vocab, float te
   return make_float2(m, __frcp_rn(s));
 }
 
+// exp(x / T - max) times the reciprocal of the sum, the product rounded on its
+// own: two equal rows must give bitwise equal probabilities, so p - q cannot be
+// contracted into an fma that keeps the rounding error of one product (the
+// reference's zero-mass residual of two equal rows would become rounding noise)
 __device__ __forceinline__ float prob(float x, float temp, float2 st) {
-  return expf(__fdiv_rn(x, temp) - st.x) * st.y;
+  return __fmul_rn(expf(__fdiv_rn(x, temp) - st.x), st.y);
 }
 
 __global__ void __launch_bounds__(RS_THREADS) rejection_sample_kernel(const ls_rejection_args a) {
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(RS_THREADS) rejection_sample_kernel(const ls_r
       load8(trow, i, x);
       load8(drow, i, y);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m += fmaxf(prob(x[k], T, st) - prob(y[k], T, qs), 0.0f);
+      for (int k = 0; k < 8; ++k) m += fmaxf(__fsub_rn(prob(x[k], T, st), prob(y[k], T, qs)), 0.0f);
     }
     const float mass = block_sum(m, sh);
     residual = mass > 1e-8f;
@@ -215,7 +219,8 @@ __global__ void __launch_bounds__(RS_THREADS) rejection_sample_kernel(const ls_r
         float y[8];
         load8(drow, i, y);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) pr[k] = __fdiv_rn(fmaxf(prob(x[k], T, st) - prob(y[k], T, qs), 0.0f), mass_c);
+        for (int k = 0; k < 8; ++k)
+          pr[k] = __fdiv_rn(fmaxf(__fsub_rn(prob(x[k], T, st), prob(y[k], T, qs)), 0.0f), mass_c);
       } else {
 #pragma unroll
         for (int k = 0; k < 8; ++k) pr[k] = prob(x[k], T, st);

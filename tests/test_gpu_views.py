@@ -208,8 +208,20 @@ def test_reference_protocol_gqa5_sixteen_steps(batch):
     (32, 8, 256, 1024, 15, tuple(900 + 37 * i for i in range(40))),
     (40, 8, 256, 2048, 15, tuple(2100 + 301 * i for i in range(12))),
     (8, 2, 16, 256, 7, tuple(5 + 23 * i for i in range(30))),
+    # streaming instantiation (>= 64 request x KV-head units): short windows
+    # (a partial 64-row stage, an empty one), a 16-slot summary
+    (32, 8, 64, 512, 15, (0, 3, 64, 65, 511, 512, 513, 4000, 77)),
+    (40, 8, 256, 2048, 15, tuple(1 + 555 * i for i in range(9))),
+    (8, 2, 16, 256, 7, tuple(5 + 23 * i for i in range(33))),
 ])
 def test_attention_matches_oracle(q_heads, kv_heads, slots, window, block, contexts):
+    """Both instantiations against the oracle: the cluster kernel below 64
+    (request, KV head) units, the streaming kernel from 64 on (the engine's
+    bf16 summary copy is passed, as the engine does)."""
+    _attention_case(q_heads, kv_heads, slots, window, block, contexts)
+
+
+def _attention_case(q_heads, kv_heads, slots, window, block, contexts):
     g = torch.Generator().manual_seed(11)
     batch = len(contexts)
     shape = DraftShape(hidden=512, q_heads=q_heads, kv_heads=kv_heads, inter=512, vocab=1024, tap_layers=1,
@@ -224,10 +236,12 @@ def test_attention_matches_oracle(q_heads, kv_heads, slots, window, block, conte
                      device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     slots_t = torch.arange(batch, dtype=torch.int32, device=dev)
+    state = v["summary_out"][:, 0].to(dev)
     ops.draft_attention(qkv=qkv.to(dev), block=block, kv_k=v["kv_k"][0].to(dev), kv_v=v["kv_v"][0].to(dev),
                         page_table=v["page_table"].to(dev), seq_lens=v["seq_lens"].to(dev), window=window,
-                        learned_query=qg.to(dev), state_out=v["summary_out"][:, 0].to(dev), slots=slots_t, out=out,
-                        workspace=ws, q_heads=q_heads, kv_heads=kv_heads, status=status)
+                        learned_query=qg.to(dev), state_out=state, slots=slots_t, out=out,
+                        workspace=ws, q_heads=q_heads, kv_heads=kv_heads, status=status,
+                        state_bf16=state.to(torch.bfloat16).contiguous())
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     x = to_np(qkv).reshape(batch, block, -1, 128)
@@ -240,6 +254,21 @@ def test_attention_matches_oracle(q_heads, kv_heads, slots, window, block, conte
     ref = O.attend(q, k, vl, w0["qg"], w0["summary_out"], w0["win_k"], w0["win_v"], w0["win_len"], "bf16")
     ref = ref.transpose(0, 2, 1, 3).reshape(batch * block, q_heads * 128)
     assert_bf16_close(to_np(out), ref, steps=2.0, exact_frac=0.5, what="attention")
+
+
+def test_attention_stream_kernel_at_every_batch_size():
+    """The streaming instantiation forced for every case of the test above
+    (LONGSPARK_B200_ATTN=stream, read once per process: a child process)."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    here = Path(__file__).resolve().parent
+    env = dict(os.environ, LONGSPARK_B200_ATTN="stream")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider",
+                        f"{here / 'test_gpu_views.py'}::test_attention_matches_oracle"],
+                       env=env, cwd=str(here.parent), capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
 
 # --------------------------------------------------------------------------
