@@ -575,49 +575,181 @@ __global__ void __launch_bounds__(MANY ? 160 : 256, MANY ? 2 : 1) attention_clus
 // splits every unit over 8 CTAs, each holding a short burst of loads; with
 // many units that makes thousands of short CTAs, each mostly waiting on its
 // own staging (ncu at 32 requests: 11% of the warp slots occupied, 15% of
-// DRAM bandwidth).  Here one producer warp streams the unit's keys and values
-// into a ring of shared-memory stages with bulk copies (one per 256-byte
-// row: a window row of one KV head is contiguous, consecutive rows of a page
-// are not), each stage completing on an mbarrier, while 2 consumer warps per
-// query head run the same online-softmax tiles as the cluster kernel:
-//   window stages: 64 rows; warp `part` of a head takes rows [32 part, +32);
-//   summary stages: 16 slots of every head of the group; warp `part` takes
-//   the stages of its parity (each query head has its own summary keys);
+// DRAM bandwidth).  Here two producer warps stream the unit's keys and values
+// with TMA into a ring of four 32 KB shared-memory stages, each completing on
+// an mbarrier, while 2 consumer warps per query head run the online-softmax
+// tiles.  (Measured on this part: one issuing warp moves ~26 GB/s of 2 KB TMA
+// boxes whatever the bytes in flight; two reach ~32, two CTAs per SM ~38.)
+//   window stages: 4 pool pages (64 positions, page-aligned); one TMA per
+//     page and 64-dimension half (16 rows of one KV head: a 3-D box over the
+//     [rows, kv_heads, 128] pool); warp `part` of a head takes rows
+//     [32 part, +32);
+//   summary stages: 64 slots of one query head (its learned queries and the
+//     request's bf16 summary, 2-D boxes of 64 rows); stage j belongs to head
+//     j % G, whose two warps take 32 slots each;
 //   local rows: the part-1 warp of each head.
-// The two warps' states of a source are folded through shared memory and the
-// three sources merged exactly as the cluster kernel merges them (per-source
-// bf16 rounding of the weighted sum, then the log-sum-exp merge in the order
-// summary, window, local).  Window rows and learned queries are issued
-// before griddepcontrol.wait, the bf16 summary values (the view refresh may
-// be the preceding kernel) after it.
+// Tiles land in the 128-byte-swizzled layout (a row's 16-byte chunk c at
+// c ^ (row % 8) inside each 64-dimension half), which ldmatrix reads without
+// bank conflicts.  The two warps' states of a source are folded through
+// shared memory and the three sources merged exactly as the cluster kernel
+// merges them (per-source bf16 rounding of the weighted sum, then the
+// log-sum-exp merge in the order summary, window, local).  Window pages and
+// learned queries are loaded before griddepcontrol.wait, the bf16 summary
+// values (the view refresh may be the preceding kernel) after it.
 // ---------------------------------------------------------------------------
-constexpr int AS_WROWS = 64;       // window rows per stage
-constexpr int AS_SSLOTS = 16;      // summary slots of each head per stage
+constexpr int AS_PAGES = 4;        // pool pages per window stage
+constexpr int AS_WROWS = AS_PAGES * 16;
+constexpr int AS_SSLOTS = 64;      // summary slots of one head per stage
+constexpr int AS_PRODUCERS = 2;    // producer warps, one issuing lane each
+constexpr int AS_STAGES = 4;       // 4 x 32 KB in flight per CTA (one CTA per SM)
 constexpr int AS_MAX_G = 5;
 constexpr int AS_MIN_UNITS = 64;   // (request, KV head) units from which the streaming kernel is used
 constexpr int AS_MAXPAGES = 264;   // window pages (W <= 4096 spans at most 257)
-constexpr int AS_HEAD_BYTES = 16 * AT_PITCH * 2;               // one 16-row bf16 tile
+constexpr int AS_HEAD_BYTES = 16 * AT_PITCH * 2;               // one 16-row padded bf16 tile
 constexpr int AS_PARK_BYTES = 16 * 128 * 4 + 16 * 2 * 4;       // fp32 state of one warp + (m, l) per row
 constexpr int AS_RES_BYTES = 16 * 128 * 2 + 16 * 2 * 4;        // bf16 weighted sum + (m, l) per row
 
 struct StreamLayout {
-  int G, stage_rows, stages;
-  size_t pg, q, loc, park, resw, stage0, total;
+  int G, rows, stages;
+  size_t pg, q, loc, park, resw, stages_at, stage_bytes, total;
 };
 
 __host__ __device__ inline StreamLayout stream_layout(int G, int stages) {
   StreamLayout L{};
   L.G = G;
-  L.stage_rows = G * AS_SSLOTS > AS_WROWS ? G * AS_SSLOTS : AS_WROWS;
+  L.rows = AS_WROWS;                            // rows of a stage tile (4 pages, or 64 slots of one head)
   L.stages = stages;
   L.pg = 128;                                   // [0, 128): mbarriers and the abort flag
   L.q = L.pg + (size_t)AS_MAXPAGES * 4;         // 1184 (16-byte aligned)
   L.loc = L.q + (size_t)G * AS_HEAD_BYTES;
   L.park = L.loc + 2 * (size_t)AS_HEAD_BYTES;
   L.resw = L.park + (size_t)G * AS_PARK_BYTES;
-  L.stage0 = L.resw + (size_t)G * AS_RES_BYTES;
-  L.total = L.stage0 + (size_t)stages * L.stage_rows * 2 * AT_PITCH * 2;
+  L.stages_at = L.resw + (size_t)G * AS_RES_BYTES;  // rounded up to 1024 bytes in the kernel
+  L.stage_bytes = (size_t)L.rows * 4 * 128;     // K lo | K hi | V lo | V hi, 128-byte rows
+  L.total = L.stages_at + 1024 + (size_t)stages * L.stage_bytes;
   return L;
+}
+
+// Address of element (r, c) (c a multiple of 8) of a swizzled tile whose two
+// 64-dimension halves are regions of `rows` 128-byte rows.
+__device__ __forceinline__ uint32_t sw_addr(uint32_t base, int rows, int r, int c) {
+  return base + static_cast<uint32_t>(c >> 6) * static_cast<uint32_t>(rows * 128) + static_cast<uint32_t>(r) * 128u +
+         (static_cast<uint32_t>(((c & 63) >> 3) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
+                                            int32_t c1, int32_t c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_u32(uint32_t smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
+                                                int32_t c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
+// attend_block over a swizzled tile: keys k0 .. k0 + 8 NT - 1 of the tile, of
+// which those at k0 + j with lo <= j < hi are visible.
+template <int NT>
+__device__ __forceinline__ void attend_block_sw(WarpState& st, const uint32_t qf[8][4], uint32_t kbase, uint32_t vbase,
+                                                int rows, int k0, int lo, int hi, float scale) {
+  static_assert(NT % 2 == 0, "keys in pairs of 8-key tiles");
+  const int lane = threadIdx.x & 31;
+  const int t2 = (lane & 3) * 2;
+  float s[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s[nt][i] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 128; kk += 32) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      uint32_t b[4];
+      ldsm_x4(b, sw_addr(kbase, rows, k0 + nt * 8 + (lane & 7), kk + ((lane >> 3) << 3)));
+      mma_16816(s[nt], qf[kk / 16], b);
+      mma_16816(s[nt], qf[kk / 16 + 1], b + 2);
+    }
+  }
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int key = nt * 8 + t2 + (i & 1);
+      float v = bf16_round(s[nt][i]) * scale;
+      v = (key >= lo && key < hi) ? v : -INFINITY;
+      s[nt][i] = v;
+      mx[i >> 1] = fmaxf(mx[i >> 1], v);
+    }
+  float corr[2], muse[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    const float mnew = fmaxf(st.m[h], mx[h]);
+    muse[h] = mnew == -INFINITY ? 0.0f : mnew;
+    corr[h] = fast_exp(st.m[h] - muse[h]);
+    st.m[h] = mnew;
+  }
+  float psum[2] = {0.0f, 0.0f};
+  uint32_t pa[NT / 2][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      pr[i] = fast_exp(s[nt][i] - muse[i >> 1]);
+      psum[i >> 1] += pr[i];
+    }
+    const int kst = nt >> 1, hi2 = nt & 1;
+    pa[kst][hi2 * 2 + 0] = pack_bf16(pr[0], pr[1]);
+    pa[kst][hi2 * 2 + 1] = pack_bf16(pr[2], pr[3]);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    psum[h] += __shfl_xor_sync(0xffffffffu, psum[h], 1);
+    psum[h] += __shfl_xor_sync(0xffffffffu, psum[h], 2);
+    st.l[h] = st.l[h] * corr[h] + psum[h];
+  }
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    st.o[nt][0] *= corr[0];
+    st.o[nt][1] *= corr[0];
+    st.o[nt][2] *= corr[1];
+    st.o[nt][3] *= corr[1];
+  }
+#pragma unroll
+  for (int kst = 0; kst < NT / 2; ++kst) {
+#pragma unroll
+    for (int dp = 0; dp < 8; ++dp) {
+      uint32_t b[4];
+      const int key = k0 + kst * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int dim = dp * 16 + ((lane >> 4) << 3);
+      ldsm_x4_t(b, sw_addr(vbase, rows, key, dim));
+      mma_16816(st.o[dp * 2], pa[kst], b);
+      mma_16816(st.o[dp * 2 + 1], pa[kst], b + 2);
+    }
+  }
 }
 
 // Fold a state parked at offset 0 of (ml, acc) (park_state with one head and
@@ -664,12 +796,15 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
 
-// Per-row normalised output of one source from a parked (bf16 weighted sum,
-// m, l) record: bf16(wv) / l (the rounded weighted sum is stored), and lse.
-__device__ __forceinline__ float src_lse(float m, float l) { return l > 0.0f ? m + __logf(fmaxf(l, 1.17549435e-38f)) : -INFINITY; }
+__device__ __forceinline__ float src_lse(float m, float l) {
+  return l > 0.0f ? m + __logf(fmaxf(l, 1.17549435e-38f)) : -INFINITY;
+}
 
 template <int NS>
-__global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(32 * (2 * AS_MAX_G + AS_PRODUCERS), 1)
+    attention_stream_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                            const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_s,
+                            const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   asm volatile("griddepcontrol.launch_dependents;");
   const ls_attention_args& a = p.a;
@@ -680,17 +815,22 @@ __global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_k
   uint64_t* empty = full + NS;
   volatile int* abort = reinterpret_cast<volatile int*>(smem_raw + 64);
   int* pg = reinterpret_cast<int*>(smem_raw + Ly.pg);
+  const uint32_t stage0 = (smem_u32(smem_raw + Ly.stages_at) + 1023u) & ~1023u;
+  const uint32_t stage_bytes = static_cast<uint32_t>(Ly.stage_bytes);
+  const int R = Ly.rows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x % a.kv_heads;
   const int b = blockIdx.x / a.kv_heads;
   const int P = a.block;
+  const int S = a.slots_per_head;
   const int len = a.seq_lens[b];
   const int wl = len < a.window ? (len > 0 ? len : 0) : a.window;
   const int wstart = len - wl;
-  const int nwb = (wl + AS_WROWS - 1) / AS_WROWS;
-  const int nsb = (a.slots_per_head + AS_SSLOTS - 1) / AS_SSLOTS;
+  const int first_lp = wstart >> 4;
+  const int n_pages = wl > 0 ? ((wstart + wl - 1) >> 4) - first_lp + 1 : 0;
+  const int nwb = (n_pages + AS_PAGES - 1) / AS_PAGES;
+  const int nsb = G * ((S + AS_SSLOTS - 1) / AS_SSLOTS);  // summary stage j: head j % G, slots 64 (j / G) ..
   const int nblocks = nwb + nsb;
-  const int stage_rows = Ly.stage_rows;
   int slot = a.slots[b];
   if (slot < 0 || slot >= a.capacity) {
     if (threadIdx.x == 0) record_status(a.status, LS_DEV_BAD_INDEX);
@@ -698,7 +838,7 @@ __global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_k
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], AS_PRODUCERS);
       mbar_init(&empty[i], ncons);
     }
     *abort = 0;
@@ -706,11 +846,11 @@ __global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_k
   }
   __syncthreads();
 
-  if (warp == ncons) {
-    // ---------------- producer warp ----------------
-    const int first_lp = wstart >> 4;
-    const int n_pages = wl > 0 ? ((wstart + wl - 1) >> 4) - first_lp + 1 : 0;
-    for (int i = lane; i < n_pages; i += 32) {
+  if (warp >= ncons) {
+    // ---------------- producer warps ----------------
+    const int pw = warp - ncons;  // this producer's share: pages 2 pw, 2 pw + 1 of a window stage;
+                                  // the keys (pw 0) or the values (pw 1) of a summary stage
+    for (int i = pw * 32 + lane; i < n_pages; i += 32 * AS_PRODUCERS) {
       int lp = first_lp + i;
       if (a.ring_pages > 0) lp %= a.ring_pages;
       int page = lp < a.table_stride ? a.page_table[(long long)b * a.table_stride + lp] : -1;
@@ -720,80 +860,72 @@ __global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_k
       }
       pg[i] = page;
     }
-    __syncwarp();
-    const bf16* kk = reinterpret_cast<const bf16*>(a.kv_k);
-    const bf16* vv = reinterpret_cast<const bf16*>(a.kv_v);
-    const bf16* lq = reinterpret_cast<const bf16*>(a.learned_query);
-    const bf16* sv = reinterpret_cast<const bf16*>(a.state_bf16) + (long long)slot * a.state_bf16_stride;
+    asm volatile("bar.sync 2, %0;" ::"r"(32 * AS_PRODUCERS) : "memory");  // both producers' page ids
+    if (lane == 0) {
+      tma_prefetch_desc(pw == 0 ? &map_k : &map_v);
+      tma_prefetch_desc(pw == 0 ? &map_q : &map_s);
+    }
     const uint64_t stream_pol = policy_evict_first();
     const uint64_t keep_pol = policy_evict_last();
+    const long long srow0 = (long long)slot * (a.state_bf16_stride / 128);
     int armed = 0;
     for (int blk = 0; blk < nblocks; ++blk) {
       const int stage = blk % NS;
       if (blk >= NS && !mbar_wait(&empty[stage], ((blk / NS) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER))
         break;
       if (blk == nwb) asm volatile("griddepcontrol.wait;" ::: "memory");  // summary values: after the refresh
-      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw + Ly.stage0) + (size_t)stage * 2 * stage_rows;
-      bf16 (*vs)[AT_PITCH] = ks + stage_rows;
-      uint32_t bytes = 0;
+      const uint32_t kb = stage0 + stage * stage_bytes;  // K lo, K hi, V lo, V hi regions of R rows
+      const uint32_t vb = kb + 2u * R * 128u;
       if (blk < nwb) {
-        const int r0 = blk * AS_WROWS;
-        const int n = wl - r0 < AS_WROWS ? wl - r0 : AS_WROWS;
-        // rows past the window or on a bad page: zeros (a masked key must not
-        // bring a NaN into P.V through its value row)
-        for (int r = lane; r < AS_WROWS; r += 32) {
-          const int pos = wstart + r0 + r;
-          const bool ok = r < n && pg[(pos >> 4) - first_lp] >= 0;
-          if (ok) {
-            bytes += 512;
-          } else {
-            for (int c = 0; c < 16; ++c) {
-              *reinterpret_cast<uint4*>(&ks[r][c * 8]) = make_uint4(0, 0, 0, 0);
-              *reinterpret_cast<uint4*>(&vs[r][c * 8]) = make_uint4(0, 0, 0, 0);
+        // pages past the window or with a bad id: zeros, so that a masked key
+        // cannot bring a NaN into P.V through its value row
+        int ok_pages = 0;
+        for (int j = pw * 2; j < pw * 2 + 2; ++j) {
+          const int i = blk * AS_PAGES + j;
+          const bool ok = i < n_pages && pg[i] >= 0;
+          ok_pages += ok;
+          if (!ok) {
+            for (int q = lane; q < 4 * 16 * 8; q += 32) {  // 4 regions x 16 rows x 8 chunks
+              const int reg = q >> 7, rr = (q >> 3) & 15, ch = q & 7;
+              const uint32_t addr = kb + reg * (uint32_t)(R * 128) + (uint32_t)(j * 16 + rr) * 128u + ch * 16u;
+              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
             }
           }
         }
-        bytes = __reduce_add_sync(0xffffffffu, bytes);
-        // the zeros are generic-proxy stores into rows that bulk copies (async
-        // proxy) filled before and will fill again: order them
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&full[stage], bytes);
-        __syncwarp();
-        for (int r = lane; r < n; r += 32) {
-          const int pos = wstart + r0 + r;
-          const int page = pg[(pos >> 4) - first_lp];
-          if (page >= 0) {
-            const long long off = (((long long)page * 16 + (pos & 15)) * a.kv_heads + g) * 128;
-            bulk_load(&ks[r][0], kk + off, 256, &full[stage], stream_pol);
-            bulk_load(&vs[r][0], vv + off, 256, &full[stage], stream_pol);
-          }
-        }
-      } else {
-        const int s0 = (blk - nwb) * AS_SSLOTS;
-        const int n = a.slots_per_head - s0 < AS_SSLOTS ? a.slots_per_head - s0 : AS_SSLOTS;
-        if (n < AS_SSLOTS) {  // a last partial block: zeros past the slots
-          for (int i = lane; i < G * AS_SSLOTS; i += 32) {
-            if (i % AS_SSLOTS < n) continue;
-            for (int c = 0; c < 16; ++c) {
-              *reinterpret_cast<uint4*>(&ks[i][c * 8]) = make_uint4(0, 0, 0, 0);
-              *reinterpret_cast<uint4*>(&vs[i][c * 8]) = make_uint4(0, 0, 0, 0);
-            }
-          }
+        if (ok_pages < 2) {
+          // generic stores into rows the TMA (async proxy) fills at other times
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
+          __threadfence_block();
         }
-        if (lane == 0) mbar_arrive_expect_tx(&full[stage], (uint32_t)(G * n * 512));
         __syncwarp();
-        for (int i = lane; i < G * AS_SSLOTS; i += 32) {
-          const int hw = i / AS_SSLOTS, s = i % AS_SSLOTS;
-          if (s < n) {
-            const long long off = ((long long)(g * G + hw) * a.slots_per_head + s0 + s) * 128;
-            bulk_load(&ks[i][0], lq + off, 256, &full[stage], keep_pol);
-            bulk_load(&vs[i][0], sv + off, 256, &full[stage], stream_pol);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(ok_pages) * 8192u);
+          for (int j = pw * 2; j < pw * 2 + 2; ++j) {
+            const int i = blk * AS_PAGES + j;
+            if (i < n_pages && pg[i] >= 0) {
+              const int row = pg[i] * 16;
+              const uint32_t off = static_cast<uint32_t>(j) * 2048u;
+              tma_load_3d(kb + off, &map_k, &full[stage], 0, g, row, stream_pol);
+              tma_load_3d(kb + R * 128u + off, &map_k, &full[stage], 64, g, row, stream_pol);
+              tma_load_3d(vb + off, &map_v, &full[stage], 0, g, row, stream_pol);
+              tma_load_3d(vb + R * 128u + off, &map_v, &full[stage], 64, g, row, stream_pol);
+            }
           }
+        }
+      } else if (lane == 0) {
+        const int jj = blk - nwb;
+        const int hs = jj % G, s0 = (jj / G) * AS_SSLOTS;
+        const int qrow = (g * G + hs) * S + s0;
+        mbar_arrive_expect_tx(&full[stage], 16384u);
+        if (pw == 0) {  // keys: the head's learned queries
+          tma_load_2d_u32(kb, &map_q, &full[stage], 0, qrow, keep_pol);
+          tma_load_2d_u32(kb + R * 128u, &map_q, &full[stage], 64, qrow, keep_pol);
+        } else {        // values: the request's bf16 summary
+          tma_load_2d_u32(vb, &map_s, &full[stage], 0, static_cast<int>(srow0 + qrow), stream_pol);
+          tma_load_2d_u32(vb + R * 128u, &map_s, &full[stage], 64, static_cast<int>(srow0 + qrow), stream_pol);
         }
       }
+      __syncwarp();
       armed = blk + 1;
     }
     if (armed < nblocks || *abort) {
@@ -836,6 +968,7 @@ __global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_k
   load_q_frags(qf, qs);
   const float scale = a.softmax_scale;
   const int gl = lane >> 2, t2 = (lane & 3) * 2;
+  const int p0 = first_lp * 16;  // position of row 0 of the first window stage
 
   WarpState st;
   ws_init(st);
@@ -843,15 +976,17 @@ __global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_k
     const int stage = blk % NS;
     const bool ok = !*abort && mbar_wait(&full[stage], (blk / NS) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
     if (ok) {
-      bf16 (*ks)[AT_PITCH] = reinterpret_cast<bf16 (*)[AT_PITCH]>(smem_raw + Ly.stage0) + (size_t)stage * 2 * stage_rows;
-      bf16 (*vs)[AT_PITCH] = ks + stage_rows;
+      const uint32_t kb = stage0 + stage * stage_bytes;
+      const uint32_t vb = kb + 2u * R * 128u;
       if (blk < nwb) {
-        const int n = wl - blk * AS_WROWS < AS_WROWS ? wl - blk * AS_WROWS : AS_WROWS;
-        if (n > part * 32) attend_block<4>(st, qf, ks, vs, part * 32, n - part * 32, scale);
-      } else if (((blk - nwb) & 1) == part) {
-        const int s0 = (blk - nwb) * AS_SSLOTS;
-        const int n = a.slots_per_head - s0 < AS_SSLOTS ? a.slots_per_head - s0 : AS_SSLOTS;
-        attend_block<2>(st, qf, ks + hw * AS_SSLOTS, vs + hw * AS_SSLOTS, 0, n, scale);
+        const int base = p0 + blk * AS_WROWS;  // position of the stage's row 0
+        const int lo = wstart - base - part * 32, hi = wstart + wl - base - part * 32;
+        if (hi > 0 && lo < 32) attend_block_sw<4>(st, qf, kb, vb, R, part * 32, lo, hi, scale);
+      } else if ((blk - nwb) % G == hw) {
+        // a last partial stage reads past the head's slots (the next head's
+        // rows, or zeros past the tensor): those keys are masked
+        const int n = S - ((blk - nwb) / G) * AS_SSLOTS;
+        if (n > part * 32) attend_block_sw<4>(st, qf, kb, vb, R, part * 32, 0, n - part * 32, scale);
       }
     }
     __syncwarp();
@@ -868,13 +1003,10 @@ __global__ void __launch_bounds__(32 * (2 * AS_MAX_G + 1), 1) attention_stream_k
       ws_init(st);
     }
   }
-  if (nwb == 0) {
-    // no window rows: an empty window source
-    if (part == 0) {
-      WarpState e;
-      ws_init(e);
-      store_result(resw, e);
-    }
+  if (nwb == 0 && part == 0) {  // no window rows: an empty window source
+    WarpState e;
+    ws_init(e);
+    store_result(resw, e);
   }
   // ---- summary done: fold the halves; part 1 computes the local rows ----
   if (part == 1) park_state(park_ml, park_acc, 1, 0, 0, st);
@@ -1003,29 +1135,43 @@ extern "C" int ls_draft_attention(void* stream, const ls_attention_args* a, void
     if (e == nullptr) return 0;
     return e[0] == 's' ? 1 : (e[0] == 'c' ? 2 : 0);
   }();
-  const bool can_stream = G <= AS_MAX_G && a->state_bf16 != nullptr && (a->state_bf16_stride % 8) == 0;
-  const bool use_stream =
-      can_stream && (attn_mode == 1 || (attn_mode == 0 && units >= AS_MIN_UNITS));
+  const bool can_stream = G <= AS_MAX_G && a->state_bf16 != nullptr && (a->state_bf16_stride % 128) == 0 &&
+                          a->capacity > 0;
+  const bool use_stream = can_stream && (attn_mode == 1 || (attn_mode == 0 && units >= AS_MIN_UNITS));
   if (use_stream) {
     static bool stream_configured = false;
     if (!stream_configured) {
-      cudaError_t e = cudaFuncSetAttribute(attention_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(stream_layout(4, 4).total));
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attention_stream_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(stream_layout(5, 3).total));
+      cudaError_t e = cudaFuncSetAttribute(attention_stream_kernel<AS_STAGES>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(stream_layout(AS_MAX_G, AS_STAGES).total));
       if (e != cudaSuccess) return set_cuda_error("ls_draft_attention: cudaFuncSetAttribute (stream)", e);
       stream_configured = true;
     }
-    const int ns = G <= 4 ? 4 : 3;
-    const StreamLayout L = stream_layout(G, ns);
+    // tensor maps: the layer's K and V pools as [rows][kv_heads][128] (3-D,
+    // 16-row boxes of one head), the learned queries [q_heads * S][128] and the
+    // bf16 summary [rows][128] (2-D, 64-row boxes); 64-element halves, 128-byte swizzle
+    CUtensorMap mk, mv, mq, ms;
+    const long long rows_per_slot = a->state_bf16_stride / 128;
+    int rc = encode_tma_3d_bf16(&mk, a->kv_k, 128, a->kv_heads, a->pool_pages * 16, 256,
+                                (long long)a->kv_heads * 256, 64, 1, 16);
+    if (rc == LS_OK)
+      rc = encode_tma_3d_bf16(&mv, a->kv_v, 128, a->kv_heads, a->pool_pages * 16, 256,
+                              (long long)a->kv_heads * 256, 64, 1, 16);
+    if (rc == LS_OK)
+      rc = encode_tma_2d_bf16(&mq, a->learned_query, 128, (long long)a->q_heads * a->slots_per_head, 128, 64,
+                              AS_SSLOTS);
+    if (rc == LS_OK)
+      rc = encode_tma_2d_bf16(&ms, a->state_bf16, 128,
+                              (long long)(a->capacity - 1) * rows_per_slot + (long long)a->q_heads * a->slots_per_head,
+                              128, 64, AS_SSLOTS);
+    if (rc != LS_OK) return rc;
+    const StreamLayout L = stream_layout(G, AS_STAGES);
     AttnParams sp{};
     sp.a = *a;
     sp.G = G;
-    cudaError_t e = ns == 4 ? launch_pdl(attention_stream_kernel<4>, dim3(static_cast<unsigned>(units)),
-                                         dim3(32 * (2 * G + 1)), L.total, reinterpret_cast<cudaStream_t>(stream), sp)
-                            : launch_pdl(attention_stream_kernel<3>, dim3(static_cast<unsigned>(units)),
-                                         dim3(32 * (2 * G + 1)), L.total, reinterpret_cast<cudaStream_t>(stream), sp);
+    cudaError_t e = launch_pdl(attention_stream_kernel<AS_STAGES>, dim3(static_cast<unsigned>(units)),
+                               dim3(32 * (2 * G + AS_PRODUCERS)), L.total, reinterpret_cast<cudaStream_t>(stream), mk,
+                               mv, mq, ms, sp);
     return e == cudaSuccess ? LS_OK : set_cuda_error("ls_draft_attention: launch (stream)", e);
   }
   static bool configured = false;

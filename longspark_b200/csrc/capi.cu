@@ -63,6 +63,26 @@ int encode_tma_2d_bf16(CUtensorMap* map, const void* base, long long inner, long
   return LS_OK;
 }
 
+int encode_tma_3d_bf16(CUtensorMap* map, const void* base, long long d0, long long d1, long long d2,
+                       long long stride1_bytes, long long stride2_bytes, int box0, int box1, int box2) {
+  std::call_once(g_encode_once, load_encode);
+  if (g_encode == nullptr) return set_error(LS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (no CUDA driver?)");
+  if (box0 * 2 != 128) return set_error(LS_ERR_INVALID, "TMA box inner extent must be 64 bf16 (128 B)");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride1_bytes & 15) || (stride2_bytes & 15))
+    return set_error(LS_ERR_INVALID, "TMA base must be 16-byte aligned and the strides multiples of 16 bytes");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride1_bytes), static_cast<cuuint64_t>(stride2_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), static_cast<cuuint32_t>(box2)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(LS_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d): dims %lld x %lld x %lld",
+                     static_cast<int>(r), d0, d1, d2);
+  return LS_OK;
+}
+
 }  // namespace ls
 
 extern "C" int ls_version(void) { return 100; }

@@ -28,6 +28,12 @@ int host_sm_count();
 int encode_tma_2d_bf16(CUtensorMap* map, const void* base, long long inner, long long outer, long long pitch,
                        int box_inner, int box_outer);
 
+// 3-D bf16 tensor map over [d2][d1][d0] elements (d0 contiguous, the other
+// strides in bytes); box = [box2][box1][box0] with box0 * 2 = 128 bytes and
+// 128-byte swizzle.
+int encode_tma_3d_bf16(CUtensorMap* map, const void* base, long long d0, long long d1, long long d2,
+                       long long stride1_bytes, long long stride2_bytes, int box0, int box1, int box2);
+
 // Programmatic dependent launch: a kernel launched this way may start while
 // the previous kernel of the stream drains; it must execute
 // griddepcontrol.wait before touching anything that kernel writes.
