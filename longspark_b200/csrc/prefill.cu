@@ -240,6 +240,377 @@ __global__ void __launch_bounds__(128) prefill_summary_kernel(const ls_prefill_a
   }
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 instantiation (a KV head's G x S query rows a multiple of 128).
+//
+// One CTA per (request, tapped layer, KV head, 128 query rows).  The query
+// tile stays in shared memory for the whole prefix; keys and values stream in
+// 128-key blocks (8 pool pages) by TMA, double-buffered.  Per block:
+//   S = Q . K^T        one 128 x 128 tcgen05 MMA chain (K = 128 dims) into one
+//                      of two TMEM score buffers;
+//   softmax            4 warps, one query row per thread: the row's 128 scores
+//                      from TMEM, the online max and sum in fp32, the weights
+//                      p = exp(s - max) split into a bf16 high part and a bf16
+//                      residual, written to shared memory as the A operands of
+//                      the next product; when a row's max moves, its fp32
+//                      accumulator in TMEM is rescaled in place first;
+//   O += P . V         two 128 x 128 MMA chains (high and residual weights, K =
+//                      128 keys) into the TMEM accumulator, V read as an
+//                      MN-major operand straight from its row-major tile.
+// The score MMA of the next block runs while the softmax works on this one.
+// Warp roles: warp 0 loads the queries and the keys, warp 2 the values, warp
+// 1 allocates TMEM and one of its lanes issues the MMAs, warps 4-7 own the
+// rows (TMEM lane quarters 0-3).  Every wait is bounded.
+// ---------------------------------------------------------------------------
+constexpr int PT_ROWS = 128;                        // query rows per CTA (the MMA's M)
+constexpr int PT_KEYS = 128;                        // keys per block
+constexpr uint32_t PT_TILE = 128 * 128;             // 128 rows x 64 bf16, 128-byte swizzled: 16 KB
+constexpr uint32_t PT_Q = 0;                        // 2 tiles: dims 0-63, 64-127
+constexpr uint32_t PT_KV = 2 * PT_TILE;             // 2 stages x (K: 2 tiles, V: 2 tiles)
+constexpr uint32_t PT_STAGE = 4 * PT_TILE;
+constexpr uint32_t PT_P = PT_KV + 2 * PT_STAGE;     // P high (2 tiles: keys 0-63, 64-127), P residual (2 tiles)
+constexpr uint32_t PT_BAR = PT_P + 4 * PT_TILE;     // mbarriers, abort flag, TMEM address
+constexpr size_t PT_SMEM = PT_BAR + 256 + 1024;     // + slack for the 1024-byte alignment
+constexpr uint32_t PT_TMEM_COLS = 512;              // S0 [0,128), S1 [128,256), O [256,384)
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+// Shared-memory descriptor of an MN-major operand in 128-byte-swizzled tiles:
+// 64 elements of N per 128-byte row, 8-row atoms along K 1024 bytes apart
+// (stride byte offset), the next 64 elements of N one tile further (leading
+// byte offset).
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t tile_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((tile_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+__device__ __forceinline__ void pt_tma_3d(uint32_t smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
+                                          int32_t c1, int32_t c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void pt_tma_2d(uint32_t smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
+                                          int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// One producer warp's share of block k (keys or values of 8 pages): page
+// rows by TMA, pages past the prefix or with a bad id zero-filled.
+__device__ __forceinline__ void pt_load_block(const ls_prefill_args& a, const CUtensorMap* map, uint32_t dst,
+                                              uint64_t* bar, int b, int layer, int hk, int k, int len,
+                                              uint64_t policy) {
+  const int lane = threadIdx.x & 31;
+  int page = -1;
+  if (lane < 8) {
+    const int pos0 = k * PT_KEYS + lane * 16;
+    if (pos0 < len) {
+      page = a.page_table[(long long)b * a.table_stride + (pos0 >> 4)];
+      if (page < 0 || page >= a.pool_pages) {
+        record_status(a.status, LS_DEV_BAD_INDEX);
+        page = -1;
+      }
+    }
+  }
+  const unsigned okmask = __ballot_sync(0xffffffffu, lane < 8 && page >= 0);
+  if (okmask != 0xffu) {
+    for (int j = 0; j < 8; ++j) {
+      if (okmask & (1u << j)) continue;
+      for (int q = lane; q < 2 * 16 * 8; q += 32) {  // 2 tiles x 16 rows x 8 chunks of 16 B
+        const uint32_t addr = dst + (q >> 7) * PT_TILE + (uint32_t)(j * 16 + ((q >> 3) & 15)) * 128u + (q & 7) * 16u;
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic zeros before tensor-core reads
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(__popc(okmask)) * 4096u);
+  __syncwarp();
+  if (lane < 8 && page >= 0) {
+    const int row = (layer * (int)a.pool_pages + page) * 16;
+    pt_tma_3d(dst + lane * 2048u, map, bar, 0, hk, row, policy);
+    pt_tma_3d(dst + PT_TILE + lane * 2048u, map, bar, 64, hk, row, policy);
+  }
+}
+
+__global__ void __launch_bounds__(256, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ ls_prefill_args a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  asm volatile("griddepcontrol.launch_dependents;");
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + PT_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  volatile int* abort = reinterpret_cast<volatile int*>(gbase + PT_BAR + 128);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + PT_BAR + 136);
+
+  const int G = a.q_heads / a.kv_heads;
+  const int S = a.slots_per_head;
+  const int tiles = G * S / PT_ROWS;
+  int bid = blockIdx.x;
+  const int qt = bid % tiles;
+  bid /= tiles;
+  const int hk = bid % a.kv_heads;
+  bid /= a.kv_heads;
+  const int layer = bid % a.tap_layers;
+  const int b = bid / a.tap_layers;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 2);   // the key and the value producer
+      mbar_init(&kv_empty[i], 1);  // the MMA commit after the block's P.V
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);    // the four softmax warps
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    *abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, PT_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  // learned queries: weights, not written by the previous kernel
+  const int qrow0 = (layer * a.q_heads + hk * G) * S + qt * PT_ROWS;
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    mbar_arrive_expect_tx(q_full, 2 * PT_TILE);
+    pt_tma_2d(base + PT_Q, &map_q, q_full, 0, qrow0);
+    pt_tma_2d(base + PT_Q + PT_TILE, &map_q, q_full, 64, qrow0);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the pool and the lengths may come from the previous kernel
+  const int len = a.seq_lens[b];
+  const int slot = a.slots[b];
+  const bool bad = slot < 0 || slot >= a.capacity || len < 0 || len > a.table_stride * 16;
+  if (bad && threadIdx.x == 0) record_status(a.status, LS_DEV_BAD_INDEX);
+  const int nblk = bad ? 0 : (len + PT_KEYS - 1) / PT_KEYS;
+
+  if (warp == 0 || warp == 2) {
+    // ---------------- producers: keys (warp 0), values (warp 2) ----------------
+    const CUtensorMap* map = warp == 0 ? &map_k : &map_v;
+    const uint32_t off = warp == 0 ? 0u : 2u * PT_TILE;
+    const uint64_t pol = policy_evict_last();  // the other query tiles of this KV head read the same blocks
+    int armed = 0;
+    for (int k = 0; k < nblk; ++k) {
+      const int st = k & 1;
+      if (k >= 2 && !mbar_wait(&kv_empty[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER)) break;
+      pt_load_block(a, map, base + PT_KV + st * PT_STAGE + off, &kv_full[st], b, layer, hk, k, len, pol);
+      armed = k + 1;
+    }
+    if (armed < nblk) {  // gave up: let the copies already issued land
+      for (int k = armed > 2 ? armed - 2 : 0; k < armed; ++k)
+        (void)mbar_wait(&kv_full[k & 1], (k >> 1) & 1, nullptr, a.status, LS_DEV_TIMEOUT_PRODUCER);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && nblk > 0) {
+      const uint32_t idesc_qk = idesc_bf16_f32(PT_ROWS, PT_KEYS);
+      const uint32_t idesc_pv = idesc_bf16_f32(PT_ROWS, 128) | (1u << 16);  // B (values) MN-major
+      bool ok = mbar_wait(q_full, 0, abort, a.status, LS_DEV_TIMEOUT_MMA);
+      auto pv = [&](int j) -> bool {
+        if (!mbar_wait(p_full, j & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t vb = base + PT_KV + (j & 1) * PT_STAGE + 2 * PT_TILE;
+#pragma unroll
+        for (int src = 0; src < 2; ++src) {
+          const uint32_t pb = base + PT_P + src * 2 * PT_TILE;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = sdesc_kmajor_sw128(pb + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
+            const uint64_t bd = sdesc_mnmajor_sw128(vb + kk * 2048u, PT_TILE);
+            tc_mma_bf16(tmem + 256, ad, bd, idesc_pv, (j > 0 || src > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(o_done);
+        tc_commit(&kv_empty[j & 1]);
+        return true;
+      };
+      for (int k = 0; ok && k < nblk; ++k) {
+        const int st = k & 1;
+        ok = mbar_wait(&kv_full[st], (k >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        if (ok && k >= 2) ok = mbar_wait(&s_free[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t kb = base + PT_KV + st * PT_STAGE;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = sdesc_kmajor_sw128(base + PT_Q + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
+          const uint64_t bd = sdesc_kmajor_sw128(kb + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
+          tc_mma_bf16(tmem + st * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[st]);
+        if (k >= 1) ok = pv(k - 1);
+      }
+      if (ok) ok = pv(nblk - 1);
+      if (!ok) {
+        // let the issued MMAs finish before the CTA tears down TMEM
+        (void)mbar_wait(o_done, (nblk - 1) & 1, nullptr, a.status, LS_DEV_TIMEOUT_MMA);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax, correction and epilogue: one row per thread ----------------
+    const int q = warp - 4;           // TMEM lane quarter
+    const int r = q * 32 + lane;      // query row of the tile
+    const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+    const float scale = a.softmax_scale;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int k = 0; ok && k < nblk; ++k) {
+      const int st = k & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (k >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[PT_KEYS];
+#pragma unroll
+      for (int c = 0; c < PT_KEYS / 16; ++c) tmem_ld16(tmem + lanes + st * 128 + c * 16, sv + c * 16);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[st]);
+      const int valid = len - k * PT_KEYS;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < PT_KEYS; ++j) {
+        sv[j] = j < valid ? sv[j] * scale : -INFINITY;
+        mx = fmaxf(mx, sv[j]);
+      }
+      const float mnew = fmaxf(m, mx);
+      const float muse = mnew == -INFINITY ? 0.0f : mnew;
+      const float corr = fast_exp(m - muse);  // 0 while the row is empty
+      float psum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < PT_KEYS; ++j) {
+        sv[j] = fast_exp(sv[j] - muse);
+        psum += sv[j];
+      }
+      l = l * corr + psum;
+      if (k >= 1) {
+        // the previous block's P.V is done: its P buffers are free, O is final for it
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (k - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, corr != 1.0f)) {
+          const uint32_t oa = tmem + lanes + 256;
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            float ov[16];
+            tmem_ld16(oa + c * 16, ov);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] *= corr;
+            tmem_st16(oa + c * 16, ov);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+      }
+      // P high and residual, row r, 128-byte-swizzled K-major tiles (keys 0-63 | 64-127)
+#pragma unroll
+      for (int c = 0; c < PT_KEYS / 8; ++c) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = sv[c * 8 + 2 * e], p1 = sv[c * 8 + 2 * e + 1];
+          const float h0 = bf16_round(p0), h1 = bf16_round(p1);
+          hi[e] = pack_bf16(h0, h1);
+          lo[e] = pack_bf16(p0 - h0, p1 - h1);
+        }
+        const uint32_t at = (uint32_t)(c >> 3) * PT_TILE + (uint32_t)r * 128u + ((uint32_t)((c & 7) ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + at), "r"(hi[0]), "r"(hi[1]),
+                     "r"(hi[2]), "r"(hi[3])
+                     : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + 2 * PT_TILE + at), "r"(lo[0]),
+                     "r"(lo[1]), "r"(lo[2]), "r"(lo[3])
+                     : "memory");
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic P stores before the MMA reads them
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      m = mnew;
+    }
+    // ---------------- epilogue: out = O / l, lse = m + log l ----------------
+    if (ok && nblk > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
+      tc_fence_after();
+    }
+    if (ok && !bad) {
+      const int R = qt * PT_ROWS + r;  // among this KV head's G x S query rows
+      const int h = hk * G + R / S, s0 = R % S;
+      const long long st_base = ((long long)slot * a.tap_layers + layer) * a.q_heads + h;
+      float* out = a.state_out + (st_base * S + s0) * 128;
+      bf16* ob = (a.state_bf16 != nullptr && layer < a.bf16_layers)
+                     ? reinterpret_cast<bf16*>(a.state_bf16) +
+                           ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * S + s0) * 128
+                     : nullptr;
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        float ov[16];
+        if (nblk > 0) {
+          tmem_ld16(tmem + lanes + 256 + c * 16, ov);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) ov[e] = 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 16; e += 4) {
+          const float4 o4 = make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
+          *reinterpret_cast<float4*>(out + c * 16 + e) = o4;
+          if (ob != nullptr) {
+            uint2 pk;
+            pk.x = pack_bf16(o4.x, o4.y);
+            pk.y = pack_bf16(o4.z, o4.w);
+            *reinterpret_cast<uint2*>(ob + c * 16 + e) = pk;
+          }
+        }
+      }
+      a.state_lse[st_base * S + s0] = l > 0.0f ? m + logf(l) : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, PT_TMEM_COLS);
+  }
+}
+
 }  // namespace ls
 
 using namespace ls;
@@ -255,6 +626,37 @@ extern "C" int ls_prefill_summary(void* stream, const ls_prefill_args* a) {
     return set_error(LS_ERR_UNSUPPORTED,
                      "ls_prefill_summary: need q_heads %% kv_heads == 0, slots %% 16 == 0 and "
                      "(q_heads / kv_heads) * slots %% 64 == 0");
+  // tcgen05 instantiation when a KV head's query rows tile by 128
+  // (LONGSPARK_B200_PREFILL=legacy keeps the mma.sync kernel, for A/B timing)
+  static const bool legacy = [] {
+    const char* e = getenv("LONGSPARK_B200_PREFILL");
+    return e != nullptr && e[0] == 'l';
+  }();
+  const int G = a->q_heads / a->kv_heads;
+  if (!legacy && (G * a->slots_per_head) % PT_ROWS == 0) {
+    static bool tc_configured = false;
+    if (!tc_configured) {
+      cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(PT_SMEM));
+      if (e != cudaSuccess) return set_cuda_error("ls_prefill_summary: cudaFuncSetAttribute (tc)", e);
+      tc_configured = true;
+    }
+    CUtensorMap mq, mk, mv;
+    const long long rows = (long long)a->tap_layers * a->pool_pages * 16;
+    int rc = encode_tma_2d_bf16(&mq, a->learned_query, 128,
+                                (long long)a->tap_layers * a->q_heads * a->slots_per_head, 128, 64, PT_ROWS);
+    if (rc == LS_OK)
+      rc = encode_tma_3d_bf16(&mk, a->kv_k, 128, a->kv_heads, rows, 256, (long long)a->kv_heads * 256, 64, 1, 16);
+    if (rc == LS_OK)
+      rc = encode_tma_3d_bf16(&mv, a->kv_v, 128, a->kv_heads, rows, 256, (long long)a->kv_heads * 256, 64, 1, 16);
+    if (rc != LS_OK) return rc;
+    if (rows > 0x7fffffffLL) return set_error(LS_ERR_UNSUPPORTED, "ls_prefill_summary: pool too large for TMA rows");
+    const long long grid = (long long)a->batch * a->tap_layers * a->kv_heads * (G * a->slots_per_head / PT_ROWS);
+    if (grid > 0x7fffffffLL) return set_error(LS_ERR_UNSUPPORTED, "ls_prefill_summary: grid too large");
+    cudaError_t e = launch_pdl(prefill_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), PT_SMEM,
+                               reinterpret_cast<cudaStream_t>(stream), mq, mk, mv, *a);
+    return e == cudaSuccess ? LS_OK : set_cuda_error("ls_prefill_summary: launch (tc)", e);
+  }
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(prefill_summary_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -28,12 +28,16 @@ def _rows(pool, table_row, layer, n):
     return pool[layer, pages, pos % 16]  # [n, Hkv, 128]
 
 
-@pytest.mark.parametrize("q_heads,kv_heads,slots", [(8, 2, 64), (10, 2, 64), (8, 8, 256)])
+@pytest.mark.parametrize("q_heads,kv_heads,slots", [(8, 2, 64), (10, 2, 64), (8, 8, 256), (40, 8, 256)])
 def test_prefill_summary_matches_oracle(q_heads, kv_heads, slots):
+    """(8, 2, 64), (8, 8, 256) and (40, 8, 256) (config 3's group: 5 heads x 256
+    slots) run the tcgen05 kernel (a KV head's query rows a multiple of 128),
+    (10, 2, 64) the mma.sync one."""
     shape = DraftShape(hidden=512, q_heads=q_heads, kv_heads=kv_heads, inter=1024, vocab=4096, tap_layers=2,
                        draft_layers=1, slots=slots, window=512, block=15, max_commit=16, markov_rank=0,
                        mask_token_id=4000)
-    lens = [0, 1, 15, 16, 17, 63, 64, 65, 1000, 3001]
+    # page (16), mma.sync block (64) and tcgen05 block (128) edges
+    lens = [0, 1, 15, 16, 17, 63, 64, 65, 127, 128, 129, 257, 1000, 3001]
     B = len(lens)
     dev = torch.device("cuda")
     W = make_weights(shape, seed=5)
