@@ -792,9 +792,9 @@ def run_b200(args):
                 "roofline": {"bound": "tensor", "peak": tensor_peak, "unit": "TFLOP/s",
                              "frac": round(headline["prefill"][1] / (headline["prefill"][0] * 1e-3) / 1e12
                                            / tensor_peak, 3),
-                             "note": "mma.sync (legacy tensor path) with a bf16 high + residual split of the "
-                                     "softmax weights (P.V issued twice); algorithmic flops = 4 * 128 per "
-                                     "(query, key)"},
+                             "note": "tcgen05 with scores and accumulators in TMEM (128-query tiles), the "
+                                     "softmax weights as a bf16 high part + residual (P.V issued twice); "
+                                     "algorithmic flops = 4 * 128 per (query, key)"},
                 "device_status": headline["prefill"][2]},
             "sampled_round": {
                 "what": "temperature 0.8: drafter pass with the refresh, then the 15-step chain (per step one "

@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(128) prefill_summary_kernel(const ls_prefill_a
 // 128-key blocks (8 pool pages) by TMA, double-buffered.  Per block:
 //   S = Q . K^T        one 128 x 128 tcgen05 MMA chain (K = 128 dims) into one
 //                      of two TMEM score buffers;
-//   softmax            4 warps, one query row per thread: the row's 128 scores
+//   softmax            8 warps, two threads per query row: the row's 128 scores
 //                      from TMEM, the online max and sum in fp32, the weights
 //                      p = exp(s - max) split into a bf16 high part and a bf16
 //                      residual, written to shared memory as the A operands of
@@ -258,9 +258,12 @@ __global__ void __launch_bounds__(128) prefill_summary_kernel(const ls_prefill_a
 //                      128 keys) into the TMEM accumulator, V read as an
 //                      MN-major operand straight from its row-major tile.
 // The score MMA of the next block runs while the softmax works on this one.
-// Warp roles: warp 0 loads the queries and the keys, warp 2 the values, warp
-// 1 allocates TMEM and one of its lanes issues the MMAs, warps 4-7 own the
-// rows (TMEM lane quarters 0-3).  Every wait is bounded.
+// Warp roles: warp 0 loads the queries and the keys, warps 2 and 3 the values,
+// warp 1 allocates TMEM and one of its lanes issues the MMAs, warps 4-7 own
+// the rows: warps 4-7 and 8-11 each take one TMEM lane quarter and one half
+// of the 128 key columns (the row max is exchanged in shared memory every
+// block, the row sums at the end).  Key stages are released by the score
+// MMAs, value stages by the P.V MMAs.  Every wait is bounded.
 // ---------------------------------------------------------------------------
 constexpr int PT_ROWS = 128;                        // query rows per CTA (the MMA's M)
 constexpr int PT_KEYS = 128;                        // keys per block
@@ -270,7 +273,7 @@ constexpr uint32_t PT_KV = 2 * PT_TILE;             // 2 stages x (K: 2 tiles, V
 constexpr uint32_t PT_STAGE = 4 * PT_TILE;
 constexpr uint32_t PT_P = PT_KV + 2 * PT_STAGE;     // P high (2 tiles: keys 0-63, 64-127), P residual (2 tiles)
 constexpr uint32_t PT_BAR = PT_P + 4 * PT_TILE;     // mbarriers, abort flag, TMEM address
-constexpr size_t PT_SMEM = PT_BAR + 256 + 1024;     // + slack for the 1024-byte alignment
+constexpr size_t PT_SMEM = PT_BAR + 256 + 2 * 128 * 4 + 1024;  // + row exchange, + 1024-byte alignment slack
 constexpr uint32_t PT_TMEM_COLS = 512;              // S0 [0,128), S1 [128,256), O [256,384)
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
@@ -317,15 +320,17 @@ __device__ __forceinline__ void pt_tma_2d(uint32_t smem_dst, const CUtensorMap* 
       : "memory");
 }
 
-// One producer warp's share of block k (keys or values of 8 pages): page
-// rows by TMA, pages past the prefix or with a bad id zero-filled.
+// One producer warp's share of block k: pages [j0, j0 + np) of the block's 8
+// (keys or values), page rows by TMA, pages past the prefix or with a bad id
+// zero-filled.
 __device__ __forceinline__ void pt_load_block(const ls_prefill_args& a, const CUtensorMap* map, uint32_t dst,
-                                              uint64_t* bar, int b, int layer, int hk, int k, int len,
+                                              uint64_t* bar, int b, int layer, int hk, int k, int len, int j0, int np,
                                               uint64_t policy) {
   const int lane = threadIdx.x & 31;
   int page = -1;
-  if (lane < 8) {
-    const int pos0 = k * PT_KEYS + lane * 16;
+  const int j = j0 + lane;
+  if (lane < np) {
+    const int pos0 = k * PT_KEYS + j * 16;
     if (pos0 < len) {
       page = a.page_table[(long long)b * a.table_stride + (pos0 >> 4)];
       if (page < 0 || page >= a.pool_pages) {
@@ -334,12 +339,13 @@ __device__ __forceinline__ void pt_load_block(const ls_prefill_args& a, const CU
       }
     }
   }
-  const unsigned okmask = __ballot_sync(0xffffffffu, lane < 8 && page >= 0);
-  if (okmask != 0xffu) {
-    for (int j = 0; j < 8; ++j) {
-      if (okmask & (1u << j)) continue;
+  const unsigned okmask = __ballot_sync(0xffffffffu, lane < np && page >= 0);
+  if (okmask != (1u << np) - 1u) {
+    for (int i = 0; i < np; ++i) {
+      if (okmask & (1u << i)) continue;
       for (int q = lane; q < 2 * 16 * 8; q += 32) {  // 2 tiles x 16 rows x 8 chunks of 16 B
-        const uint32_t addr = dst + (q >> 7) * PT_TILE + (uint32_t)(j * 16 + ((q >> 3) & 15)) * 128u + (q & 7) * 16u;
+        const uint32_t addr =
+            dst + (q >> 7) * PT_TILE + (uint32_t)((j0 + i) * 16 + ((q >> 3) & 15)) * 128u + (q & 7) * 16u;
         asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
       }
     }
@@ -348,14 +354,14 @@ __device__ __forceinline__ void pt_load_block(const ls_prefill_args& a, const CU
   __syncwarp();
   if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(__popc(okmask)) * 4096u);
   __syncwarp();
-  if (lane < 8 && page >= 0) {
+  if (lane < np && page >= 0) {
     const int row = (layer * (int)a.pool_pages + page) * 16;
-    pt_tma_3d(dst + lane * 2048u, map, bar, 0, hk, row, policy);
-    pt_tma_3d(dst + PT_TILE + lane * 2048u, map, bar, 64, hk, row, policy);
+    pt_tma_3d(dst + j * 2048u, map, bar, 0, hk, row, policy);
+    pt_tma_3d(dst + PT_TILE + j * 2048u, map, bar, 64, hk, row, policy);
   }
 }
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ ls_prefill_args a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -364,12 +370,14 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + PT_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]: the score MMAs of the block are done
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]: the P.V MMAs of the block are done
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_free = bars + 11;   // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_done = bars + 14;
   volatile int* abort = reinterpret_cast<volatile int*>(gbase + PT_BAR + 128);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + PT_BAR + 136);
 
@@ -388,12 +396,14 @@ __global__ void __launch_bounds__(256, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 2);   // the key and the value producer
-      mbar_init(&kv_empty[i], 1);  // the MMA commit after the block's P.V
+      mbar_init(&k_full[i], 1);    // the key producer
+      mbar_init(&k_empty[i], 1);   // the MMA commit after the block's scores
+      mbar_init(&v_full[i], 2);    // the two value producers
+      mbar_init(&v_empty[i], 1);   // the MMA commit after the block's P.V
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);    // the four softmax warps
+      mbar_init(&s_free[i], 8);    // the eight softmax warps
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(o_done, 1);
     *abort = 0;
     mbar_fence_init();
@@ -423,21 +433,28 @@ __global__ void __launch_bounds__(256, 1)
   if (bad && threadIdx.x == 0) record_status(a.status, LS_DEV_BAD_INDEX);
   const int nblk = bad ? 0 : (len + PT_KEYS - 1) / PT_KEYS;
 
-  if (warp == 0 || warp == 2) {
-    // ---------------- producers: keys (warp 0), values (warp 2) ----------------
-    const CUtensorMap* map = warp == 0 ? &map_k : &map_v;
-    const uint32_t off = warp == 0 ? 0u : 2u * PT_TILE;
+  if (warp == 0 || warp == 2 || warp == 3) {
+    // ---------------- producers: keys (warp 0, 8 pages), values (warps 2, 3, 4 pages each) ----------------
+    // Key stages are released by the score MMAs, value stages by the P.V MMAs;
+    // one warp issues a block's keys, two split its values (TMA issue is
+    // per-warp limited, and the values are needed later than the keys).
+    const bool keys = warp == 0;
+    const CUtensorMap* map = keys ? &map_k : &map_v;
+    const uint32_t off = keys ? 0u : 2u * PT_TILE;
+    uint64_t* fullb = keys ? k_full : v_full;
+    uint64_t* emptyb = keys ? k_empty : v_empty;
+    const int j0 = keys ? 0 : (warp - 2) * 4, np = keys ? 8 : 4;
     const uint64_t pol = policy_evict_last();  // the other query tiles of this KV head read the same blocks
     int armed = 0;
     for (int k = 0; k < nblk; ++k) {
       const int st = k & 1;
-      if (k >= 2 && !mbar_wait(&kv_empty[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER)) break;
-      pt_load_block(a, map, base + PT_KV + st * PT_STAGE + off, &kv_full[st], b, layer, hk, k, len, pol);
+      if (k >= 2 && !mbar_wait(&emptyb[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER)) break;
+      pt_load_block(a, map, base + PT_KV + st * PT_STAGE + off, &fullb[st], b, layer, hk, k, len, j0, np, pol);
       armed = k + 1;
     }
     if (armed < nblk) {  // gave up: let the copies already issued land
       for (int k = armed > 2 ? armed - 2 : 0; k < armed; ++k)
-        (void)mbar_wait(&kv_full[k & 1], (k >> 1) & 1, nullptr, a.status, LS_DEV_TIMEOUT_PRODUCER);
+        (void)mbar_wait(&fullb[k & 1], (k >> 1) & 1, nullptr, a.status, LS_DEV_TIMEOUT_PRODUCER);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -447,6 +464,7 @@ __global__ void __launch_bounds__(256, 1)
       bool ok = mbar_wait(q_full, 0, abort, a.status, LS_DEV_TIMEOUT_MMA);
       auto pv = [&](int j) -> bool {
         if (!mbar_wait(p_full, j & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
         tc_fence_after();
         const uint32_t vb = base + PT_KV + (j & 1) * PT_STAGE + 2 * PT_TILE;
 #pragma unroll
@@ -460,12 +478,12 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
         tc_commit(o_done);
-        tc_commit(&kv_empty[j & 1]);
+        tc_commit(&v_empty[j & 1]);
         return true;
       };
       for (int k = 0; ok && k < nblk; ++k) {
         const int st = k & 1;
-        ok = mbar_wait(&kv_full[st], (k >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        ok = mbar_wait(&k_full[st], (k >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
         if (ok && k >= 2) ok = mbar_wait(&s_free[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
         if (!ok) break;
         tc_fence_after();
@@ -477,6 +495,7 @@ __global__ void __launch_bounds__(256, 1)
           tc_mma_bf16(tmem + st * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[st]);
+        tc_commit(&k_empty[st]);
         if (k >= 1) ok = pv(k - 1);
       }
       if (ok) ok = pv(nblk - 1);
@@ -486,50 +505,80 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   } else if (warp >= 4) {
-    // ---------------- softmax, correction and epilogue: one row per thread ----------------
-    const int q = warp - 4;           // TMEM lane quarter
+    // ---------------- softmax, correction and epilogue: two threads per row ----------------
+    // warp w: TMEM lane quarter w % 4, columns [64 hf, 64 hf + 64) of its rows
+    const int q = warp & 3, hf = (warp - 4) >> 2;
     const int r = q * 32 + lane;      // query row of the tile
     const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
-    const float scale = a.softmax_scale;
-    float m = -INFINITY, l = 0.0f;
+    const int c0 = hf * 64;
+    float* xchg = reinterpret_cast<float*>(gbase + PT_BAR + 256);  // [2 halves][128 rows]
+    const float sl2 = a.softmax_scale * 1.4426950408889634f;       // scale, in base 2
+    float m = -INFINITY, l = 0.0f;  // running max (base e) and this half's running sum
     bool ok = true;
-    for (int k = 0; ok && k < nblk; ++k) {
+    // Every softmax warp runs all nblk iterations and both row barriers of each,
+    // also after a wait gave up (ok false: the work is skipped), so that no warp
+    // is left at a barrier the others never reach.
+    for (int k = 0; k < nblk; ++k) {
       const int st = k & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (k >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
-      if (!ok) break;
-      tc_fence_after();
-      float sv[PT_KEYS];
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[st], (k >> 1) & 1, abort, a.status,
+                                                   LS_DEV_TIMEOUT_EPILOGUE));
+      float sv[64];
+      if (ok) {
+        tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < PT_KEYS / 16; ++c) tmem_ld16(tmem + lanes + st * 128 + c * 16, sv + c * 16);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[st]);
-      const int valid = len - k * PT_KEYS;
-      float mx = -INFINITY;
+        for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lanes + st * 128 + c0 + c * 16, sv + c * 16);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[st]);
+      } else {
 #pragma unroll
-      for (int j = 0; j < PT_KEYS; ++j) {
-        sv[j] = j < valid ? sv[j] * scale : -INFINITY;
-        mx = fmaxf(mx, sv[j]);
+        for (int j = 0; j < 64; ++j) sv[j] = -INFINITY;
       }
-      const float mnew = fmaxf(m, mx);
+      const int valid = len - k * PT_KEYS - c0;  // visible keys of this half
+      float mx = -INFINITY;
+      if (valid >= 64) {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) mx = fmaxf(mx, sv[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          sv[j] = j < valid ? sv[j] : -INFINITY;
+          mx = fmaxf(mx, sv[j]);
+        }
+      }
+      // the row max over both halves (raw scores; the scale is positive)
+      xchg[hf * 128 + r] = mx;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      mx = fmaxf(mx, xchg[(hf ^ 1) * 128 + r]);
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // both read before the next write
+      if (!ok) continue;
+      const float mnew = fmaxf(m, mx * a.softmax_scale);
       const float muse = mnew == -INFINITY ? 0.0f : mnew;
       const float corr = fast_exp(m - muse);  // 0 while the row is empty
+      const float off2 = muse * 1.4426950408889634f;
       float psum = 0.0f;
+      uint32_t phi[32], plo[32];
 #pragma unroll
-      for (int j = 0; j < PT_KEYS; ++j) {
-        sv[j] = fast_exp(sv[j] - muse);
-        psum += sv[j];
+      for (int e = 0; e < 32; ++e) {
+        float p0, p1;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p0) : "f"(fmaf(sv[2 * e], sl2, -off2)));
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p1) : "f"(fmaf(sv[2 * e + 1], sl2, -off2)));
+        psum += p0 + p1;
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+        const float2 hf2 = __bfloat1622float2(h2);
+        phi[e] = *reinterpret_cast<const uint32_t*>(&h2);
+        plo[e] = pack_bf16(p0 - hf2.x, p1 - hf2.y);
       }
       l = l * corr + psum;
       if (k >= 1) {
         // the previous block's P.V is done: its P buffers are free, O is final for it
         ok = __all_sync(0xffffffffu, mbar_wait(o_done, (k - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
-        if (!ok) break;
+        if (!ok) continue;
         tc_fence_after();
         if (__any_sync(0xffffffffu, corr != 1.0f)) {
-          const uint32_t oa = tmem + lanes + 256;
+          const uint32_t oa = tmem + lanes + 256 + c0;
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
+          for (int c = 0; c < 4; ++c) {
             float ov[16];
             tmem_ld16(oa + c * 16, ov);
 #pragma unroll
@@ -539,23 +588,15 @@ __global__ void __launch_bounds__(256, 1)
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
       }
-      // P high and residual, row r, 128-byte-swizzled K-major tiles (keys 0-63 | 64-127)
+      // P high and residual: this half's keys are tile hf of each, row r, 128-byte swizzled
 #pragma unroll
-      for (int c = 0; c < PT_KEYS / 8; ++c) {
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = sv[c * 8 + 2 * e], p1 = sv[c * 8 + 2 * e + 1];
-          const float h0 = bf16_round(p0), h1 = bf16_round(p1);
-          hi[e] = pack_bf16(h0, h1);
-          lo[e] = pack_bf16(p0 - h0, p1 - h1);
-        }
-        const uint32_t at = (uint32_t)(c >> 3) * PT_TILE + (uint32_t)r * 128u + ((uint32_t)((c & 7) ^ (r & 7)) << 4);
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + at), "r"(hi[0]), "r"(hi[1]),
-                     "r"(hi[2]), "r"(hi[3])
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t at = (uint32_t)hf * PT_TILE + (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + at), "r"(phi[4 * c]),
+                     "r"(phi[4 * c + 1]), "r"(phi[4 * c + 2]), "r"(phi[4 * c + 3])
                      : "memory");
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + 2 * PT_TILE + at), "r"(lo[0]),
-                     "r"(lo[1]), "r"(lo[2]), "r"(lo[3])
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + 2 * PT_TILE + at),
+                     "r"(plo[4 * c]), "r"(plo[4 * c + 1]), "r"(plo[4 * c + 2]), "r"(plo[4 * c + 3])
                      : "memory");
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic P stores before the MMA reads them
@@ -569,21 +610,25 @@ __global__ void __launch_bounds__(256, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
       tc_fence_after();
     }
+    // the row's sum over both halves (every softmax thread reaches this barrier)
+    xchg[hf * 128 + r] = l;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    l += xchg[(hf ^ 1) * 128 + r];
     if (ok && !bad) {
       const int R = qt * PT_ROWS + r;  // among this KV head's G x S query rows
       const int h = hk * G + R / S, s0 = R % S;
       const long long st_base = ((long long)slot * a.tap_layers + layer) * a.q_heads + h;
-      float* out = a.state_out + (st_base * S + s0) * 128;
+      float* out = a.state_out + (st_base * S + s0) * 128 + c0;
       bf16* ob = (a.state_bf16 != nullptr && layer < a.bf16_layers)
                      ? reinterpret_cast<bf16*>(a.state_bf16) +
-                           ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * S + s0) * 128
+                           ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * S + s0) * 128 + c0
                      : nullptr;
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float ov[16];
         if (nblk > 0) {
-          tmem_ld16(tmem + lanes + 256 + c * 16, ov);
+          tmem_ld16(tmem + lanes + 256 + c0 + c * 16, ov);
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) ov[e] = 0.0f;
@@ -600,7 +645,7 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
       }
-      a.state_lse[st_base * S + s0] = l > 0.0f ? m + logf(l) : -INFINITY;
+      if (hf == 0) a.state_lse[st_base * S + s0] = l > 0.0f ? m + logf(l) : -INFINITY;
     }
   }
   tc_fence_before();
@@ -653,7 +698,7 @@ extern "C" int ls_prefill_summary(void* stream, const ls_prefill_args* a) {
     if (rows > 0x7fffffffLL) return set_error(LS_ERR_UNSUPPORTED, "ls_prefill_summary: pool too large for TMA rows");
     const long long grid = (long long)a->batch * a->tap_layers * a->kv_heads * (G * a->slots_per_head / PT_ROWS);
     if (grid > 0x7fffffffLL) return set_error(LS_ERR_UNSUPPORTED, "ls_prefill_summary: grid too large");
-    cudaError_t e = launch_pdl(prefill_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), PT_SMEM,
+    cudaError_t e = launch_pdl(prefill_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(384), PT_SMEM,
                                reinterpret_cast<cudaStream_t>(stream), mq, mk, mv, *a);
     return e == cudaSuccess ? LS_OK : set_cuda_error("ls_prefill_summary: launch (tc)", e);
   }
