@@ -302,6 +302,23 @@ __device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t
   return d;
 }
 
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void dsmem_st_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void dsmem_st_f2(uint32_t addr, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
+
 __device__ __forceinline__ void pt_tma_3d(uint32_t smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
                                           int32_t c1, int32_t c2, uint64_t policy) {
   asm volatile(
@@ -384,7 +401,10 @@ __global__ void __launch_bounds__(384, 1)
   const int G = a.q_heads / a.kv_heads;
   const int S = a.slots_per_head;
   const int tiles = G * S / PT_ROWS;
-  int bid = blockIdx.x;
+  uint32_t crank, csize;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
+  int bid = blockIdx.x / static_cast<int>(csize);
   const int qt = bid % tiles;
   bid /= tiles;
   const int hk = bid % a.kv_heads;
@@ -431,7 +451,10 @@ __global__ void __launch_bounds__(384, 1)
   const int slot = a.slots[b];
   const bool bad = slot < 0 || slot >= a.capacity || len < 0 || len > a.table_stride * 16;
   if (bad && threadIdx.x == 0) record_status(a.status, LS_DEV_BAD_INDEX);
-  const int nblk = bad ? 0 : (len + PT_KEYS - 1) / PT_KEYS;
+  // the cluster's CTAs split the prefix's 128-key blocks into contiguous ranges
+  const int nblk_all = bad ? 0 : (len + PT_KEYS - 1) / PT_KEYS;
+  const int kb0 = static_cast<int>(crank) * nblk_all / static_cast<int>(csize);
+  const int nblk = (static_cast<int>(crank) + 1) * nblk_all / static_cast<int>(csize) - kb0;
 
   if (warp == 0 || warp == 2 || warp == 3) {
     // ---------------- producers: keys (warp 0, 8 pages), values (warps 2, 3, 4 pages each) ----------------
@@ -449,7 +472,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int k = 0; k < nblk; ++k) {
       const int st = k & 1;
       if (k >= 2 && !mbar_wait(&emptyb[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER)) break;
-      pt_load_block(a, map, base + PT_KV + st * PT_STAGE + off, &fullb[st], b, layer, hk, k, len, j0, np, pol);
+      pt_load_block(a, map, base + PT_KV + st * PT_STAGE + off, &fullb[st], b, layer, hk, kb0 + k, len, j0, np, pol);
       armed = k + 1;
     }
     if (armed < nblk) {  // gave up: let the copies already issued land
@@ -504,17 +527,19 @@ __global__ void __launch_bounds__(384, 1)
         (void)mbar_wait(o_done, (nblk - 1) & 1, nullptr, a.status, LS_DEV_TIMEOUT_MMA);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- softmax, correction and epilogue: two threads per row ----------------
-    // warp w: TMEM lane quarter w % 4, columns [64 hf, 64 hf + 64) of its rows
-    const int q = warp & 3, hf = (warp - 4) >> 2;
-    const int r = q * 32 + lane;      // query row of the tile
-    const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
-    const int c0 = hf * 64;
+  }
+  // softmax rows: warp w >= 4 takes TMEM lane quarter w % 4 and columns
+  // [64 hf, 64 hf + 64) of its rows
+  const int q = warp & 3, hf = (warp - 4) >> 2;
+  const int r = q * 32 + lane;      // query row of the tile
+  const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+  const int c0 = hf * 64;
+  float m = -INFINITY, l = 0.0f;    // running max (base e) and the running sum
+  bool ok = true;
+  if (warp >= 4) {
+    // ---------------- softmax and correction: two threads per row ----------------
     float* xchg = reinterpret_cast<float*>(gbase + PT_BAR + 256);  // [2 halves][128 rows]
     const float sl2 = a.softmax_scale * 1.4426950408889634f;       // scale, in base 2
-    float m = -INFINITY, l = 0.0f;  // running max (base e) and this half's running sum
-    bool ok = true;
     // Every softmax warp runs all nblk iterations and both row barriers of each,
     // also after a wait gave up (ok false: the work is skipped), so that no warp
     // is left at a barrier the others never reach.
@@ -534,7 +559,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int j = 0; j < 64; ++j) sv[j] = -INFINITY;
       }
-      const int valid = len - k * PT_KEYS - c0;  // visible keys of this half
+      const int valid = len - (kb0 + k) * PT_KEYS - c0;  // visible keys of this half
       float mx = -INFINITY;
       if (valid >= 64) {
 #pragma unroll
@@ -605,7 +630,6 @@ __global__ void __launch_bounds__(384, 1)
       if (lane == 0) mbar_arrive(p_full);
       m = mnew;
     }
-    // ---------------- epilogue: out = O / l, lse = m + log l ----------------
     if (ok && nblk > 0) {
       ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
       tc_fence_after();
@@ -614,39 +638,86 @@ __global__ void __launch_bounds__(384, 1)
     xchg[hf * 128 + r] = l;
     asm volatile("bar.sync 1, 256;" ::: "memory");
     l += xchg[(hf ^ 1) * 128 + r];
-    if (ok && !bad) {
-      const int R = qt * PT_ROWS + r;  // among this KV head's G x S query rows
-      const int h = hk * G + R / S, s0 = R % S;
-      const long long st_base = ((long long)slot * a.tap_layers + layer) * a.q_heads + h;
-      float* out = a.state_out + (st_base * S + s0) * 128 + c0;
-      bf16* ob = (a.state_bf16 != nullptr && layer < a.bf16_layers)
-                     ? reinterpret_cast<bf16*>(a.state_bf16) +
-                           ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * S + s0) * 128 + c0
-                     : nullptr;
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+  }
+  // ---------------- merge across the cluster, out = O / L, lse = M + log L ----------------
+  // Rank 0 of the cluster keeps its state in TMEM; every other rank stores
+  // (m, l) and its unnormalised O rows into a slot of rank 0's shared memory
+  // (its tiles are free once every rank's MMAs are done: the first cluster
+  // barrier), and rank 0 merges the ranks in order after the second.
+  constexpr uint32_t PT_SLOT = 128 * 512 + 128 * 8;  // O [128][128] fp32, then (m, l) [128]
+  cluster_barrier();
+  if (warp >= 4 && crank > 0) {
+    const uint32_t slot_addr = dsmem_map(base + (crank - 1) * PT_SLOT, 0);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float ov[16];
-        if (nblk > 0) {
-          tmem_ld16(tmem + lanes + 256 + c0 + c * 16, ov);
-        } else {
+    for (int c = 0; c < 4; ++c) {
+      float ov[16];
+      if (nblk > 0) {
+        tmem_ld16(tmem + lanes + 256 + c0 + c * 16, ov);
+      } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) ov[e] = 0.0f;
-        }
+        for (int e = 0; e < 16; ++e) ov[e] = 0.0f;
+      }
 #pragma unroll
-        for (int e = 0; e < 16; e += 4) {
-          const float4 o4 = make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
-          *reinterpret_cast<float4*>(out + c * 16 + e) = o4;
-          if (ob != nullptr) {
-            uint2 pk;
-            pk.x = pack_bf16(o4.x, o4.y);
-            pk.y = pack_bf16(o4.z, o4.w);
-            *reinterpret_cast<uint2*>(ob + c * 16 + e) = pk;
-          }
+      for (int e = 0; e < 16; e += 4)
+        dsmem_st_f4(slot_addr + (uint32_t)r * 512u + (uint32_t)(c0 + c * 16 + e) * 4u,
+                    make_float4(ov[e], ov[e + 1], ov[e + 2], ov[e + 3]));
+    }
+    if (hf == 0) dsmem_st_f2(slot_addr + 128 * 512 + (uint32_t)r * 8u, make_float2(m, l));
+  }
+  cluster_barrier();
+  if (warp >= 4 && crank == 0 && ok && !bad) {
+    float M = m;
+    for (uint32_t rk = 1; rk < csize; ++rk) {
+      const float2 ml = *reinterpret_cast<const float2*>(gbase + (rk - 1) * PT_SLOT + 128 * 512 + r * 8);
+      M = fmaxf(M, ml.x);
+    }
+    const float Mu = M == -INFINITY ? 0.0f : M;
+    const float f0 = fast_exp(m - Mu);
+    float L = l * f0;
+    for (uint32_t rk = 1; rk < csize; ++rk) {
+      const float2 ml = *reinterpret_cast<const float2*>(gbase + (rk - 1) * PT_SLOT + 128 * 512 + r * 8);
+      L += ml.y * fast_exp(ml.x - Mu);
+    }
+    const int R = qt * PT_ROWS + r;  // among this KV head's G x S query rows
+    const int h = hk * G + R / S, s0 = R % S;
+    const long long st_base = ((long long)slot * a.tap_layers + layer) * a.q_heads + h;
+    float* out = a.state_out + (st_base * S + s0) * 128 + c0;
+    bf16* ob = (a.state_bf16 != nullptr && layer < a.bf16_layers)
+                   ? reinterpret_cast<bf16*>(a.state_bf16) +
+                         ((((long long)slot * a.bf16_layers + layer) * a.q_heads + h) * S + s0) * 128 + c0
+                   : nullptr;
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float ov[16];
+      if (nblk > 0) {
+        tmem_ld16(tmem + lanes + 256 + c0 + c * 16, ov);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ov[e] = 0.0f;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) ov[e] *= f0;
+      for (uint32_t rk = 1; rk < csize; ++rk) {
+        const uint8_t* sl = gbase + (rk - 1) * PT_SLOT;
+        const float fr = fast_exp(reinterpret_cast<const float2*>(sl + 128 * 512 + r * 8)->x - Mu);
+        const float* orow = reinterpret_cast<const float*>(sl + r * 512) + c0 + c * 16;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ov[e] += orow[e] * fr;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; e += 4) {
+        const float4 o4 = make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
+        *reinterpret_cast<float4*>(out + c * 16 + e) = o4;
+        if (ob != nullptr) {
+          uint2 pk;
+          pk.x = pack_bf16(o4.x, o4.y);
+          pk.y = pack_bf16(o4.z, o4.w);
+          *reinterpret_cast<uint2*>(ob + c * 16 + e) = pk;
         }
       }
-      if (hf == 0) a.state_lse[st_base * S + s0] = l > 0.0f ? m + logf(l) : -INFINITY;
     }
+    if (hf == 0) a.state_lse[st_base * S + s0] = L > 0.0f ? M + logf(L) : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
@@ -696,10 +767,56 @@ extern "C" int ls_prefill_summary(void* stream, const ls_prefill_args* a) {
       rc = encode_tma_3d_bf16(&mv, a->kv_v, 128, a->kv_heads, rows, 256, (long long)a->kv_heads * 256, 64, 1, 16);
     if (rc != LS_OK) return rc;
     if (rows > 0x7fffffffLL) return set_error(LS_ERR_UNSUPPORTED, "ls_prefill_summary: pool too large for TMA rows");
-    const long long grid = (long long)a->batch * a->tap_layers * a->kv_heads * (G * a->slots_per_head / PT_ROWS);
+    const long long tiles = (long long)a->batch * a->tap_layers * a->kv_heads * (G * a->slots_per_head / PT_ROWS);
+    // Each query tile's key blocks are split over a cluster of C CTAs (merged
+    // through distributed shared memory), so that short batches still fill
+    // the SMs and long ones lose less to the last partial wave.
+    // C is picked by a wave model, ceil(tiles C / resident CTAs) x (blocks / C
+    // + 20): a CTA's fixed cost (pipeline fill, epilogue, merge) measured at
+    // about 20 key blocks, the blocks taken from the page table's width (the
+    // longest prefix it can hold).  LONGSPARK_B200_PREFILL_SPLIT=1..4 forces C.
+    static const int split_env = [] {
+      const char* e = getenv("LONGSPARK_B200_PREFILL_SPLIT");
+      return e == nullptr ? 0 : atoi(e);
+    }();
+    static int resident[5] = {0, 0, 0, 0, 0};  // CTAs in flight at once, per cluster size
+    if (resident[1] == 0) {
+      for (int c = 1; c <= 4; ++c) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(c * 1024));
+        cfg.blockDim = dim3(384);
+        cfg.dynamicSmemBytes = PT_SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(c);
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, prefill_tc_kernel, &cfg) != cudaSuccess || n <= 0) {
+          (void)cudaGetLastError();
+          n = host_sm_count() / c;
+        }
+        resident[c] = n * c;
+      }
+    }
+    unsigned C = 1;
+    if (split_env >= 1 && split_env <= 4) {
+      C = static_cast<unsigned>(split_env);
+    } else {
+      const double blocks = (static_cast<double>(a->table_stride) * 16 + PT_KEYS - 1) / PT_KEYS;
+      double best = 0.0;
+      for (int c = 1; c <= 4; ++c) {
+        const double waves = static_cast<double>((tiles * c + resident[c] - 1) / resident[c]);
+        const double cost = waves * (blocks / c + 20.0);
+        if (c == 1 || cost < best * 0.98) best = cost, C = static_cast<unsigned>(c);
+      }
+    }
+    const long long grid = tiles * C;
     if (grid > 0x7fffffffLL) return set_error(LS_ERR_UNSUPPORTED, "ls_prefill_summary: grid too large");
-    cudaError_t e = launch_pdl(prefill_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(384), PT_SMEM,
-                               reinterpret_cast<cudaStream_t>(stream), mq, mk, mv, *a);
+    cudaError_t e = launch_pdl_cluster(prefill_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(384), PT_SMEM,
+                                       reinterpret_cast<cudaStream_t>(stream), C, mq, mk, mv, *a);
     return e == cudaSuccess ? LS_OK : set_cuda_error("ls_prefill_summary: launch (tc)", e);
   }
   static bool configured = false;
