@@ -269,12 +269,40 @@ constexpr int PT_ROWS = 128;                        // query rows per CTA (the M
 constexpr int PT_KEYS = 128;                        // keys per block
 constexpr uint32_t PT_TILE = 128 * 128;             // 128 rows x 64 bf16, 128-byte swizzled: 16 KB
 constexpr uint32_t PT_Q = 0;                        // 2 tiles: dims 0-63, 64-127
-constexpr uint32_t PT_KV = 2 * PT_TILE;             // 2 stages x (K: 2 tiles, V: 2 tiles)
+constexpr int PT_NST = 3;                           // key/value stages
+constexpr uint32_t PT_KV = 2 * PT_TILE;             // PT_NST stages x (K: 2 tiles, V: 2 tiles)
 constexpr uint32_t PT_STAGE = 4 * PT_TILE;
-constexpr uint32_t PT_P = PT_KV + 2 * PT_STAGE;     // P high (2 tiles: keys 0-63, 64-127), P residual (2 tiles)
-constexpr uint32_t PT_BAR = PT_P + 4 * PT_TILE;     // mbarriers, abort flag, TMEM address
+constexpr uint32_t PT_BAR = PT_KV + PT_NST * PT_STAGE;  // mbarriers, abort flag, TMEM address
 constexpr size_t PT_SMEM = PT_BAR + 256 + 2 * 128 * 4 + 1024;  // + row exchange, + 1024-byte alignment slack
-constexpr uint32_t PT_TMEM_COLS = 512;              // S0 [0,128), S1 [128,256), O [256,384)
+// TMEM columns: scores S0 [0,128) and S1 [128,256), the output accumulator O
+// [256,384), the softmax weights P of one block as packed bf16 pairs, high
+// part [384,448) and residual [448,512) (key 2c and 2c+1 in column c)
+constexpr uint32_t PT_TMEM_COLS = 512;
+constexpr uint32_t PT_TM_O = 256, PT_TM_PHI = 384, PT_TM_PLO = 448;
+
+// D[tmem] (+)= A[tmem] * B[smem]: A (M rows on the TMEM lanes, K packed two
+// bf16 per column) read from tensor memory.
+__device__ __forceinline__ void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns from registers (no wait).
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
   asm volatile(
@@ -387,16 +415,17 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + PT_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* k_empty = bars + 3;   // [2]: the score MMAs of the block are done
-  uint64_t* v_full = bars + 5;    // [2]
-  uint64_t* v_empty = bars + 7;   // [2]: the P.V MMAs of the block are done
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* s_free = bars + 11;   // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_done = bars + 14;
-  volatile int* abort = reinterpret_cast<volatile int*>(gbase + PT_BAR + 128);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + PT_BAR + 136);
+  uint64_t* k_full = bars + 1;                 // [PT_NST]
+  uint64_t* k_empty = k_full + PT_NST;        // [PT_NST]: the score MMAs of the block are done
+  uint64_t* v_full = k_empty + PT_NST;        // [PT_NST]
+  uint64_t* v_empty = v_full + PT_NST;        // [PT_NST]: the P.V MMAs of the block are done
+  uint64_t* s_full = v_empty + PT_NST;        // [2]
+  uint64_t* s_free = s_full + 2;              // [2]
+  uint64_t* p_full = s_free + 2;
+  uint64_t* o_done = p_full + 1;
+  static_assert(8 * (1 + 4 * PT_NST + 6) <= 192, "mbarriers overlap the flags");
+  volatile int* abort = reinterpret_cast<volatile int*>(gbase + PT_BAR + 192);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + PT_BAR + 200);
 
   const int G = a.q_heads / a.kv_heads;
   const int S = a.slots_per_head;
@@ -415,11 +444,13 @@ __global__ void __launch_bounds__(384, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < PT_NST; ++i) {
       mbar_init(&k_full[i], 1);    // the key producer
       mbar_init(&k_empty[i], 1);   // the MMA commit after the block's scores
       mbar_init(&v_full[i], 2);    // the two value producers
       mbar_init(&v_empty[i], 1);   // the MMA commit after the block's P.V
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 8);    // the eight softmax warps
     }
@@ -470,14 +501,15 @@ __global__ void __launch_bounds__(384, 1)
     const uint64_t pol = policy_evict_last();  // the other query tiles of this KV head read the same blocks
     int armed = 0;
     for (int k = 0; k < nblk; ++k) {
-      const int st = k & 1;
-      if (k >= 2 && !mbar_wait(&emptyb[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER)) break;
+      const int st = k % PT_NST;
+      if (k >= PT_NST && !mbar_wait(&emptyb[st], (k / PT_NST - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER))
+        break;
       pt_load_block(a, map, base + PT_KV + st * PT_STAGE + off, &fullb[st], b, layer, hk, kb0 + k, len, j0, np, pol);
       armed = k + 1;
     }
     if (armed < nblk) {  // gave up: let the copies already issued land
-      for (int k = armed > 2 ? armed - 2 : 0; k < armed; ++k)
-        (void)mbar_wait(&fullb[k & 1], (k >> 1) & 1, nullptr, a.status, LS_DEV_TIMEOUT_PRODUCER);
+      for (int k = armed > PT_NST ? armed - PT_NST : 0; k < armed; ++k)
+        (void)mbar_wait(&fullb[k % PT_NST], (k / PT_NST) & 1, nullptr, a.status, LS_DEV_TIMEOUT_PRODUCER);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -487,27 +519,26 @@ __global__ void __launch_bounds__(384, 1)
       bool ok = mbar_wait(q_full, 0, abort, a.status, LS_DEV_TIMEOUT_MMA);
       auto pv = [&](int j) -> bool {
         if (!mbar_wait(p_full, j & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(&v_full[j % PT_NST], (j / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
         tc_fence_after();
-        const uint32_t vb = base + PT_KV + (j & 1) * PT_STAGE + 2 * PT_TILE;
+        const uint32_t vb = base + PT_KV + (j % PT_NST) * PT_STAGE + 2 * PT_TILE;
 #pragma unroll
         for (int src = 0; src < 2; ++src) {
-          const uint32_t pb = base + PT_P + src * 2 * PT_TILE;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = sdesc_kmajor_sw128(pb + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
             const uint64_t bd = sdesc_mnmajor_sw128(vb + kk * 2048u, PT_TILE);
-            tc_mma_bf16(tmem + 256, ad, bd, idesc_pv, (j > 0 || src > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_bf16_ts(tmem + PT_TM_O, tmem + (src ? PT_TM_PLO : PT_TM_PHI) + kk * 8, bd, idesc_pv,
+                           (j > 0 || src > 0 || kk > 0) ? 1u : 0u);
           }
         }
         tc_commit(o_done);
-        tc_commit(&v_empty[j & 1]);
+        tc_commit(&v_empty[j % PT_NST]);
         return true;
       };
       for (int k = 0; ok && k < nblk; ++k) {
-        const int st = k & 1;
-        ok = mbar_wait(&k_full[st], (k >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
-        if (ok && k >= 2) ok = mbar_wait(&s_free[st], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        const int st = k % PT_NST, sb = k & 1;  // key/value stage, score buffer
+        ok = mbar_wait(&k_full[st], (k / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        if (ok && k >= 2) ok = mbar_wait(&s_free[sb], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
         if (!ok) break;
         tc_fence_after();
         const uint32_t kb = base + PT_KV + st * PT_STAGE;
@@ -515,9 +546,9 @@ __global__ void __launch_bounds__(384, 1)
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t ad = sdesc_kmajor_sw128(base + PT_Q + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
           const uint64_t bd = sdesc_kmajor_sw128(kb + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
-          tc_mma_bf16(tmem + st * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          tc_mma_bf16(tmem + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[st]);
+        tc_commit(&s_full[sb]);
         tc_commit(&k_empty[st]);
         if (k >= 1) ok = pv(k - 1);
       }
@@ -601,7 +632,7 @@ __global__ void __launch_bounds__(384, 1)
         if (!ok) continue;
         tc_fence_after();
         if (__any_sync(0xffffffffu, corr != 1.0f)) {
-          const uint32_t oa = tmem + lanes + 256 + c0;
+          const uint32_t oa = tmem + lanes + PT_TM_O + c0;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             float ov[16];
@@ -613,18 +644,10 @@ __global__ void __launch_bounds__(384, 1)
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
       }
-      // P high and residual: this half's keys are tile hf of each, row r, 128-byte swizzled
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t at = (uint32_t)hf * PT_TILE + (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + at), "r"(phi[4 * c]),
-                     "r"(phi[4 * c + 1]), "r"(phi[4 * c + 2]), "r"(phi[4 * c + 3])
-                     : "memory");
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + PT_P + 2 * PT_TILE + at),
-                     "r"(plo[4 * c]), "r"(plo[4 * c + 1]), "r"(plo[4 * c + 2]), "r"(plo[4 * c + 3])
-                     : "memory");
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic P stores before the MMA reads them
+      // P high and residual of this half's 64 keys: 32 packed columns each
+      tmem_st32u(tmem + lanes + PT_TM_PHI + 32 * hf, phi);
+      tmem_st32u(tmem + lanes + PT_TM_PLO + 32 * hf, plo);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
@@ -652,7 +675,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int c = 0; c < 4; ++c) {
       float ov[16];
       if (nblk > 0) {
-        tmem_ld16(tmem + lanes + 256 + c0 + c * 16, ov);
+        tmem_ld16(tmem + lanes + PT_TM_O + c0 + c * 16, ov);
       } else {
 #pragma unroll
         for (int e = 0; e < 16; ++e) ov[e] = 0.0f;
@@ -691,7 +714,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int c = 0; c < 4; ++c) {
       float ov[16];
       if (nblk > 0) {
-        tmem_ld16(tmem + lanes + 256 + c0 + c * 16, ov);
+        tmem_ld16(tmem + lanes + PT_TM_O + c0 + c * 16, ov);
       } else {
 #pragma unroll
         for (int e = 0; e < 16; ++e) ov[e] = 0.0f;
