@@ -274,11 +274,17 @@ constexpr uint32_t PT_KV = 2 * PT_TILE;             // PT_NST stages x (K: 2 til
 constexpr uint32_t PT_STAGE = 4 * PT_TILE;
 constexpr uint32_t PT_BAR = PT_KV + PT_NST * PT_STAGE;  // mbarriers, abort flag, TMEM address
 constexpr size_t PT_SMEM = PT_BAR + 256 + 2 * 128 * 4 + 1024;  // + row exchange, + 1024-byte alignment slack
-// TMEM columns: scores S0 [0,128) and S1 [128,256), the output accumulator O
-// [256,384), the softmax weights P of one block as packed bf16 pairs, high
-// part [384,448) and residual [448,512) (key 2c and 2c+1 in column c)
+// TMEM columns: the scores S [0,128), the output accumulator O [128,256) and
+// two buffers of softmax weights P [256,384) and [384,512), each the high
+// part (64 columns) then the residual (64), packed bf16 pairs (keys 2c and
+// 2c + 1 in column c)
 constexpr uint32_t PT_TMEM_COLS = 512;
-constexpr uint32_t PT_TM_O = 256, PT_TM_PHI = 384, PT_TM_PLO = 448;
+constexpr uint32_t PT_TM_S = 0, PT_TM_O = 128, PT_TM_P = 256;
+// The exponent offset of a row (its running max) moves only when the block's
+// max exceeds it by more than this (natural log units, weights up to 2^8), so
+// that O is rarely rescaled and the softmax of block k need not wait for the
+// P.V of block k - 1.
+constexpr float PT_RESCALE_GAP = 8.0f * 0.69314718055994531f;
 
 // D[tmem] (+)= A[tmem] * B[smem]: A (M rows on the TMEM lanes, K packed two
 // bf16 per column) read from tensor memory.
@@ -292,6 +298,19 @@ __device__ __forceinline__ void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem,
       : "memory");
 }
 
+// 32 lanes x 32 consecutive 32-bit columns into registers (no wait: the
+// caller issues tcgen05.wait::ld before reading them).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
 // 32 lanes x 32 consecutive 32-bit columns from registers (no wait).
 __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
   asm volatile(
@@ -302,6 +321,11 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
       "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
       "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
+}
+
+// The two softmax warps of TMEM lane quarter q (warps 4 + q and 8 + q).
+__device__ __forceinline__ void pair_sync(int q) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
@@ -419,11 +443,12 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* k_empty = k_full + PT_NST;        // [PT_NST]: the score MMAs of the block are done
   uint64_t* v_full = k_empty + PT_NST;        // [PT_NST]
   uint64_t* v_empty = v_full + PT_NST;        // [PT_NST]: the P.V MMAs of the block are done
-  uint64_t* s_full = v_empty + PT_NST;        // [2]
-  uint64_t* s_free = s_full + 2;              // [2]
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + 1;
-  static_assert(8 * (1 + 4 * PT_NST + 6) <= 192, "mbarriers overlap the flags");
+  uint64_t* s_full = v_empty + PT_NST;        // the block's scores are in TMEM
+  uint64_t* s_free = s_full + 1;              // the softmax warps have read them
+  uint64_t* p_full = s_free + 1;              // [2] per P buffer
+  uint64_t* pv_done = p_full + 2;             // [2] per P buffer: its P.V MMAs are done
+  uint64_t* drain = pv_done + 2;              // every issued MMA is done (error path)
+  static_assert(8 * (1 + 4 * PT_NST + 7) <= 192, "mbarriers overlap the flags");
   volatile int* abort = reinterpret_cast<volatile int*>(gbase + PT_BAR + 192);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + PT_BAR + 200);
 
@@ -450,12 +475,13 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&v_full[i], 2);    // the two value producers
       mbar_init(&v_empty[i], 1);   // the MMA commit after the block's P.V
     }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);          // the eight softmax warps
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 8);    // the eight softmax warps
+      mbar_init(&p_full[i], 8);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(p_full, 8);
-    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
     *abort = 0;
     mbar_fence_init();
   }
@@ -518,7 +544,7 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t idesc_pv = idesc_bf16_f32(PT_ROWS, 128) | (1u << 16);  // B (values) MN-major
       bool ok = mbar_wait(q_full, 0, abort, a.status, LS_DEV_TIMEOUT_MMA);
       auto pv = [&](int j) -> bool {
-        if (!mbar_wait(p_full, j & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
         if (!mbar_wait(&v_full[j % PT_NST], (j / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
         tc_fence_after();
         const uint32_t vb = base + PT_KV + (j % PT_NST) * PT_STAGE + 2 * PT_TILE;
@@ -527,18 +553,18 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t bd = sdesc_mnmajor_sw128(vb + kk * 2048u, PT_TILE);
-            tc_mma_bf16_ts(tmem + PT_TM_O, tmem + (src ? PT_TM_PLO : PT_TM_PHI) + kk * 8, bd, idesc_pv,
+            tc_mma_bf16_ts(tmem + PT_TM_O, tmem + PT_TM_P + (j & 1) * 128 + src * 64 + kk * 8, bd, idesc_pv,
                            (j > 0 || src > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        tc_commit(o_done);
+        tc_commit(&pv_done[j & 1]);
         tc_commit(&v_empty[j % PT_NST]);
         return true;
       };
       for (int k = 0; ok && k < nblk; ++k) {
-        const int st = k % PT_NST, sb = k & 1;  // key/value stage, score buffer
+        const int st = k % PT_NST;
         ok = mbar_wait(&k_full[st], (k / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
-        if (ok && k >= 2) ok = mbar_wait(&s_free[sb], ((k >> 1) - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        if (ok && k >= 1) ok = mbar_wait(s_free, (k - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
         if (!ok) break;
         tc_fence_after();
         const uint32_t kb = base + PT_KV + st * PT_STAGE;
@@ -546,16 +572,17 @@ __global__ void __launch_bounds__(384, 1)
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t ad = sdesc_kmajor_sw128(base + PT_Q + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
           const uint64_t bd = sdesc_kmajor_sw128(kb + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
-          tc_mma_bf16(tmem + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          tc_mma_bf16(tmem + PT_TM_S, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[sb]);
+        tc_commit(s_full);
         tc_commit(&k_empty[st]);
         if (k >= 1) ok = pv(k - 1);
       }
       if (ok) ok = pv(nblk - 1);
       if (!ok) {
         // let the issued MMAs finish before the CTA tears down TMEM
-        (void)mbar_wait(o_done, (nblk - 1) & 1, nullptr, a.status, LS_DEV_TIMEOUT_MMA);
+        tc_commit(drain);
+        (void)mbar_wait(drain, 0, nullptr, a.status, LS_DEV_TIMEOUT_MMA);
       }
     }
   }
@@ -575,91 +602,102 @@ __global__ void __launch_bounds__(384, 1)
     // also after a wait gave up (ok false: the work is skipped), so that no warp
     // is left at a barrier the others never reach.
     for (int k = 0; k < nblk; ++k) {
-      const int st = k & 1;
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[st], (k >> 1) & 1, abort, a.status,
-                                                   LS_DEV_TIMEOUT_EPILOGUE));
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full, k & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
       float sv[64];
       if (ok) {
         tc_fence_after();
+        uint32_t raw[64];
+        tmem_ld32_nowait(tmem + lanes + PT_TM_S + c0, raw);
+        tmem_ld32_nowait(tmem + lanes + PT_TM_S + c0 + 32, raw + 32);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lanes + st * 128 + c0 + c * 16, sv + c * 16);
+        for (int j = 0; j < 64; ++j) sv[j] = __uint_as_float(raw[j]);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[st]);
+        if (lane == 0) mbar_arrive(s_free);
       } else {
 #pragma unroll
         for (int j = 0; j < 64; ++j) sv[j] = -INFINITY;
       }
       const int valid = len - (kb0 + k) * PT_KEYS - c0;  // visible keys of this half
-      float mx = -INFINITY;
-      if (valid >= 64) {
+      if (valid < 64) {
 #pragma unroll
-        for (int j = 0; j < 64; ++j) mx = fmaxf(mx, sv[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          sv[j] = j < valid ? sv[j] : -INFINITY;
-          mx = fmaxf(mx, sv[j]);
-        }
+        for (int j = 0; j < 64; ++j) sv[j] = j < valid ? sv[j] : -INFINITY;
       }
-      // the row max over both halves (raw scores; the scale is positive)
+      float mx8[8];  // eight independent chains
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx8[j] = sv[j];
+#pragma unroll
+      for (int j = 8; j < 64; ++j) mx8[j & 7] = fmaxf(mx8[j & 7], sv[j]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      // the row max over both halves (raw scores; the scale is positive),
+      // exchanged with the partner warp (same rows, other half) only
       xchg[hf * 128 + r] = mx;
-      asm volatile("bar.sync 1, 256;" ::: "memory");
+      pair_sync(q);
       mx = fmaxf(mx, xchg[(hf ^ 1) * 128 + r]);
-      asm volatile("bar.sync 1, 256;" ::: "memory");  // both read before the next write
+      pair_sync(q);  // both read before the next write
       if (!ok) continue;
-      const float mnew = fmaxf(m, mx * a.softmax_scale);
-      const float muse = mnew == -INFINITY ? 0.0f : mnew;
-      const float corr = fast_exp(m - muse);  // 0 while the row is empty
-      const float off2 = muse * 1.4426950408889634f;
-      float psum = 0.0f;
+      // Both warps of a row take the same decision (same m, same max).
+      const bool move = mx * a.softmax_scale > m + PT_RESCALE_GAP;
+      const float mnew = move ? mx * a.softmax_scale : m;
+      const float corr = move ? fast_exp(m - mnew) : 1.0f;  // 0 while the row is empty
+      const float off2 = (mnew == -INFINITY ? 0.0f : mnew) * 1.4426950408889634f;
+      float ps8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // eight independent sums
       uint32_t phi[32], plo[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         float p0, p1;
         asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p0) : "f"(fmaf(sv[2 * e], sl2, -off2)));
         asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p1) : "f"(fmaf(sv[2 * e + 1], sl2, -off2)));
-        psum += p0 + p1;
+        ps8[e & 7] += p0 + p1;
         const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
         const float2 hf2 = __bfloat1622float2(h2);
         phi[e] = *reinterpret_cast<const uint32_t*>(&h2);
         plo[e] = pack_bf16(p0 - hf2.x, p1 - hf2.y);
       }
+      const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l = l * corr + psum;
-      if (k >= 1) {
-        // the previous block's P.V is done: its P buffers are free, O is final for it
-        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (k - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
+      if (k >= 1 && __any_sync(0xffffffffu, move)) {
+        // O rescaled once the previous block's P.V is done (then also block k - 2's)
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(k - 1) & 1], ((k - 1) >> 1) & 1, abort, a.status,
+                                               LS_DEV_TIMEOUT_EPILOGUE));
         if (!ok) continue;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, corr != 1.0f)) {
-          const uint32_t oa = tmem + lanes + PT_TM_O + c0;
+        const uint32_t oa = tmem + lanes + PT_TM_O + c0;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float ov[16];
-            tmem_ld16(oa + c * 16, ov);
+        for (int c = 0; c < 4; ++c) {
+          float ov[16];
+          tmem_ld16(oa + c * 16, ov);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] *= corr;
-            tmem_st16(oa + c * 16, ov);
-          }
-          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          for (int e = 0; e < 16; ++e) ov[e] *= corr;
+          tmem_st16(oa + c * 16, ov);
         }
+      } else if (k >= 2) {
+        // P buffer k % 2 is free once block k - 2's P.V is done
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[k & 1], ((k >> 1) - 1) & 1, abort, a.status,
+                                               LS_DEV_TIMEOUT_EPILOGUE));
+        if (!ok) continue;
+        tc_fence_after();
       }
       // P high and residual of this half's 64 keys: 32 packed columns each
-      tmem_st32u(tmem + lanes + PT_TM_PHI + 32 * hf, phi);
-      tmem_st32u(tmem + lanes + PT_TM_PLO + 32 * hf, plo);
+      const uint32_t pa = tmem + lanes + PT_TM_P + (k & 1) * 128 + 32 * hf;
+      tmem_st32u(pa, phi);
+      tmem_st32u(pa + 64, plo);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[k & 1]);
       m = mnew;
     }
     if (ok && nblk > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
+      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, abort, a.status,
+                                             LS_DEV_TIMEOUT_EPILOGUE));
       tc_fence_after();
     }
     // the row's sum over both halves (every softmax thread reaches this barrier)
     xchg[hf * 128 + r] = l;
-    asm volatile("bar.sync 1, 256;" ::: "memory");
+    pair_sync(q);
     l += xchg[(hf ^ 1) * 128 + r];
   }
   // ---------------- merge across the cluster, out = O / L, lse = M + log L ----------------
