@@ -64,6 +64,8 @@ def parse():
                     help="diagnostic: device time of every native call of one eager round (one GPU), not a bench line")
     ap.add_argument("--calls-shape", default="cfg2", help="cfg2, or cfg5-tpN: the per-rank shapes of config 5 at TP N")
     ap.add_argument("--calls-ctx", type=int, default=4096)
+    ap.add_argument("--calls-prefill", action="store_true",
+                    help="with --calls: also one ls_prefill_summary over every request's whole prefix per round")
     ap.add_argument("--calls-temperature", type=float, default=0.0,
                     help="> 0: the round includes the sampled chain (DraftEngine.sample)")
     return ap.parse_args()
@@ -1121,6 +1123,9 @@ def run_calls(args):
         for _ in range(max(2, min(args.steps, 20))):
             records.clear()
             g._run()
+            if args.calls_prefill:
+                eng.prefill_summary(slots=torch.arange(args.batch, dtype=torch.int32, device=dev),
+                                    seq_lens=v["seq_lens"][:args.batch], page_table=v["page_table"], batch=args.batch)
             if args.calls_temperature > 0:
                 eng.sample(g.anchors, temperature=args.calls_temperature, seed=7, batch=args.batch)
             torch.cuda.synchronize()

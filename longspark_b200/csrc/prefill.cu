@@ -274,12 +274,17 @@ constexpr uint32_t PT_KV = 2 * PT_TILE;             // PT_NST stages x (K: 2 til
 constexpr uint32_t PT_STAGE = 4 * PT_TILE;
 constexpr uint32_t PT_BAR = PT_KV + PT_NST * PT_STAGE;  // mbarriers, abort flag, TMEM address
 constexpr size_t PT_SMEM = PT_BAR + 256 + 2 * 128 * 4 + 1024;  // + row exchange, + 1024-byte alignment slack
-// TMEM columns: the scores S [0,128), the output accumulator O [128,256) and
-// two buffers of softmax weights P [256,384) and [384,512), each the high
-// part (64 columns) then the residual (64), packed bf16 pairs (keys 2c and
-// 2c + 1 in column c)
+// TMEM columns: three score buffers [0,128), [128,256), [256,384) (block k
+// in buffer k % 3), each overwritten in place by the block's softmax weights
+// P, the high part (64 columns) then the residual (64), packed bf16 pairs
+// (keys 2c and 2c + 1 in column c); the output accumulator O [384,512).
 constexpr uint32_t PT_TMEM_COLS = 512;
-constexpr uint32_t PT_TM_S = 0, PT_TM_O = 128, PT_TM_P = 256;
+constexpr int PT_NSB = 3;  // score buffers
+constexpr uint32_t PT_TM_S = 0, PT_TM_O = 384;
+// 12 warps, one per role on each SM sub-partition (warp w runs on w % 4):
+// 0 keys, 1 score MMAs, 2 values, 3 P.V MMAs, 4-11 softmax (two per TMEM
+// lane quarter, the quarter is w % 4)
+constexpr int PT_THREADS = 384;
 // The exponent offset of a row (its running max) moves only when the block's
 // max exceeds it by more than this (natural log units, weights up to 2^8), so
 // that O is rarely rescaled and the softmax of block k need not wait for the
@@ -321,6 +326,27 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
       "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
       "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
+}
+
+// mbar_wait for roles with slack (the producers, the score MMAs, several
+// blocks ahead): sleeps between polls, leaving the issue slots of the SM
+// sub-partition to the softmax warps that share it.
+__device__ __forceinline__ bool pt_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                                int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(128);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (global_timer_ns() - t0 > LS_WAIT_NS) {
+        record_status(status, code);
+        if (abort != nullptr) *abort = 1;
+        return false;
+      }
+    }
+  }
 }
 
 // The two softmax warps of TMEM lane quarter q (warps 4 + q and 8 + q).
@@ -430,7 +456,7 @@ __device__ __forceinline__ void pt_load_block(const ls_prefill_args& a, const CU
   }
 }
 
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(PT_THREADS, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ ls_prefill_args a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -443,12 +469,11 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* k_empty = k_full + PT_NST;        // [PT_NST]: the score MMAs of the block are done
   uint64_t* v_full = k_empty + PT_NST;        // [PT_NST]
   uint64_t* v_empty = v_full + PT_NST;        // [PT_NST]: the P.V MMAs of the block are done
-  uint64_t* s_full = v_empty + PT_NST;        // the block's scores are in TMEM
-  uint64_t* s_free = s_full + 1;              // the softmax warps have read them
-  uint64_t* p_full = s_free + 1;              // [2] per P buffer
-  uint64_t* pv_done = p_full + 2;             // [2] per P buffer: its P.V MMAs are done
-  uint64_t* drain = pv_done + 2;              // every issued MMA is done (error path)
-  static_assert(8 * (1 + 4 * PT_NST + 7) <= 192, "mbarriers overlap the flags");
+  uint64_t* s_full = v_empty + PT_NST;        // [PT_NSB] per score buffer: the block's scores are in TMEM
+  uint64_t* p_full = s_full + PT_NSB;         // [PT_NSB] its weights are written over them
+  uint64_t* pv_done = p_full + PT_NSB;        // [PT_NSB] its P.V MMAs are done
+  uint64_t* drain = pv_done + PT_NSB;         // [2] every MMA of an issuer is done (error path)
+  static_assert(8 * (1 + 4 * PT_NST + 3 * PT_NSB + 2) <= 192, "mbarriers overlap the flags");
   volatile int* abort = reinterpret_cast<volatile int*>(gbase + PT_BAR + 192);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + PT_BAR + 200);
 
@@ -472,16 +497,16 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < PT_NST; ++i) {
       mbar_init(&k_full[i], 1);    // the key producer
       mbar_init(&k_empty[i], 1);   // the MMA commit after the block's scores
-      mbar_init(&v_full[i], 2);    // the two value producers
+      mbar_init(&v_full[i], 1);    // the value producer
       mbar_init(&v_empty[i], 1);   // the MMA commit after the block's P.V
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 8);          // the eight softmax warps
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], 8);
+    for (int i = 0; i < PT_NSB; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 8);    // the eight softmax warps
       mbar_init(&pv_done[i], 1);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort = 0;
     mbar_fence_init();
   }
@@ -513,22 +538,20 @@ __global__ void __launch_bounds__(384, 1)
   const int kb0 = static_cast<int>(crank) * nblk_all / static_cast<int>(csize);
   const int nblk = (static_cast<int>(crank) + 1) * nblk_all / static_cast<int>(csize) - kb0;
 
-  if (warp == 0 || warp == 2 || warp == 3) {
-    // ---------------- producers: keys (warp 0, 8 pages), values (warps 2, 3, 4 pages each) ----------------
-    // Key stages are released by the score MMAs, value stages by the P.V MMAs;
-    // one warp issues a block's keys, two split its values (TMA issue is
-    // per-warp limited, and the values are needed later than the keys).
+  if (warp == 0 || warp == 2) {
+    // ---------------- producers: keys (warp 0), values (warp 2), 8 pages a block ----------------
+    // Key stages are released by the score MMAs, value stages by the P.V MMAs.
     const bool keys = warp == 0;
     const CUtensorMap* map = keys ? &map_k : &map_v;
     const uint32_t off = keys ? 0u : 2u * PT_TILE;
     uint64_t* fullb = keys ? k_full : v_full;
     uint64_t* emptyb = keys ? k_empty : v_empty;
-    const int j0 = keys ? 0 : (warp - 2) * 4, np = keys ? 8 : 4;
+    const int j0 = 0, np = 8;
     const uint64_t pol = policy_evict_last();  // the other query tiles of this KV head read the same blocks
     int armed = 0;
     for (int k = 0; k < nblk; ++k) {
       const int st = k % PT_NST;
-      if (k >= PT_NST && !mbar_wait(&emptyb[st], (k / PT_NST - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER))
+      if (k >= PT_NST && !pt_wait_backoff(&emptyb[st], (k / PT_NST - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_PRODUCER))
         break;
       pt_load_block(a, map, base + PT_KV + st * PT_STAGE + off, &fullb[st], b, layer, hk, kb0 + k, len, j0, np, pol);
       armed = k + 1;
@@ -538,33 +561,16 @@ __global__ void __launch_bounds__(384, 1)
         (void)mbar_wait(&fullb[k % PT_NST], (k / PT_NST) & 1, nullptr, a.status, LS_DEV_TIMEOUT_PRODUCER);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- score MMAs: S(k) = Q K(k)^T into buffer k % 3 ----------------
+    // Buffer k % 3 holds the weights of block k - 3 until their P.V is done.
     if (lane == 0 && nblk > 0) {
       const uint32_t idesc_qk = idesc_bf16_f32(PT_ROWS, PT_KEYS);
-      const uint32_t idesc_pv = idesc_bf16_f32(PT_ROWS, 128) | (1u << 16);  // B (values) MN-major
       bool ok = mbar_wait(q_full, 0, abort, a.status, LS_DEV_TIMEOUT_MMA);
-      auto pv = [&](int j) -> bool {
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(&v_full[j % PT_NST], (j / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA)) return false;
-        tc_fence_after();
-        const uint32_t vb = base + PT_KV + (j % PT_NST) * PT_STAGE + 2 * PT_TILE;
-#pragma unroll
-        for (int src = 0; src < 2; ++src) {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t bd = sdesc_mnmajor_sw128(vb + kk * 2048u, PT_TILE);
-            tc_mma_bf16_ts(tmem + PT_TM_O, tmem + PT_TM_P + (j & 1) * 128 + src * 64 + kk * 8, bd, idesc_pv,
-                           (j > 0 || src > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
-        tc_commit(&pv_done[j & 1]);
-        tc_commit(&v_empty[j % PT_NST]);
-        return true;
-      };
       for (int k = 0; ok && k < nblk; ++k) {
-        const int st = k % PT_NST;
-        ok = mbar_wait(&k_full[st], (k / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
-        if (ok && k >= 1) ok = mbar_wait(s_free, (k - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        const int st = k % PT_NST, sb = k % PT_NSB;
+        ok = pt_wait_backoff(&k_full[st], (k / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        if (ok && k >= PT_NSB)
+          ok = pt_wait_backoff(&pv_done[sb], (k / PT_NSB - 1) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
         if (!ok) break;
         tc_fence_after();
         const uint32_t kb = base + PT_KV + st * PT_STAGE;
@@ -572,17 +578,45 @@ __global__ void __launch_bounds__(384, 1)
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t ad = sdesc_kmajor_sw128(base + PT_Q + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
           const uint64_t bd = sdesc_kmajor_sw128(kb + (kk >> 2) * PT_TILE) + 2 * (kk & 3);
-          tc_mma_bf16(tmem + PT_TM_S, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          tc_mma_bf16(tmem + PT_TM_S + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        tc_commit(s_full);
+        tc_commit(&s_full[sb]);
         tc_commit(&k_empty[st]);
-        if (k >= 1) ok = pv(k - 1);
       }
-      if (ok) ok = pv(nblk - 1);
+      if (!ok) {  // let this thread's MMAs finish before the CTA tears down TMEM
+        tc_commit(&drain[0]);
+        (void)mbar_wait(&drain[0], 0, nullptr, a.status, LS_DEV_TIMEOUT_MMA);
+      }
+    }
+  } else if (warp == 3) {
+    // ---------------- P.V MMAs: O += P(j) V(j), high part then residual ----------------
+    // A second issuing thread, so that P.V(j) starts as soon as its weights
+    // are written, not behind the score MMAs of a later block.
+    if (lane == 0 && nblk > 0) {
+      const uint32_t idesc_pv = idesc_bf16_f32(PT_ROWS, 128) | (1u << 16);  // B (values) MN-major
+      bool ok = true;
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int sb = j % PT_NSB;
+        ok = mbar_wait(&p_full[sb], (j / PT_NSB) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA) &&
+             mbar_wait(&v_full[j % PT_NST], (j / PT_NST) & 1, abort, a.status, LS_DEV_TIMEOUT_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t vb = base + PT_KV + (j % PT_NST) * PT_STAGE + 2 * PT_TILE;
+#pragma unroll
+        for (int src = 0; src < 2; ++src) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t bd = sdesc_mnmajor_sw128(vb + kk * 2048u, PT_TILE);
+            tc_mma_bf16_ts(tmem + PT_TM_O, tmem + PT_TM_S + sb * 128 + src * 64 + kk * 8, bd, idesc_pv,
+                           (j > 0 || src > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(&pv_done[sb]);
+        tc_commit(&v_empty[j % PT_NST]);
+      }
       if (!ok) {
-        // let the issued MMAs finish before the CTA tears down TMEM
-        tc_commit(drain);
-        (void)mbar_wait(drain, 0, nullptr, a.status, LS_DEV_TIMEOUT_MMA);
+        tc_commit(&drain[1]);
+        (void)mbar_wait(&drain[1], 0, nullptr, a.status, LS_DEV_TIMEOUT_MMA);
       }
     }
   }
@@ -594,7 +628,8 @@ __global__ void __launch_bounds__(384, 1)
   const int c0 = hf * 64;
   float m = -INFINITY, l = 0.0f;    // running max (base e) and the running sum
   bool ok = true;
-  if (warp >= 4) {
+  const bool softmax_warp = warp >= 4 && warp < 12;
+  if (softmax_warp) {
     // ---------------- softmax and correction: two threads per row ----------------
     float* xchg = reinterpret_cast<float*>(gbase + PT_BAR + 256);  // [2 halves][128 rows]
     const float sl2 = a.softmax_scale * 1.4426950408889634f;       // scale, in base 2
@@ -602,19 +637,19 @@ __global__ void __launch_bounds__(384, 1)
     // also after a wait gave up (ok false: the work is skipped), so that no warp
     // is left at a barrier the others never reach.
     for (int k = 0; k < nblk; ++k) {
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full, k & 1, abort, a.status, LS_DEV_TIMEOUT_EPILOGUE));
+      const int sb = k % PT_NSB;
+      const uint32_t sbuf = tmem + lanes + PT_TM_S + sb * 128;
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (k / PT_NSB) & 1, abort, a.status,
+                                                   LS_DEV_TIMEOUT_EPILOGUE));
       float sv[64];
       if (ok) {
         tc_fence_after();
         uint32_t raw[64];
-        tmem_ld32_nowait(tmem + lanes + PT_TM_S + c0, raw);
-        tmem_ld32_nowait(tmem + lanes + PT_TM_S + c0 + 32, raw + 32);
+        tmem_ld32_nowait(sbuf + c0, raw);
+        tmem_ld32_nowait(sbuf + c0 + 32, raw + 32);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
         for (int j = 0; j < 64; ++j) sv[j] = __uint_as_float(raw[j]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(s_free);
       } else {
 #pragma unroll
         for (int j = 0; j < 64; ++j) sv[j] = -INFINITY;
@@ -636,7 +671,7 @@ __global__ void __launch_bounds__(384, 1)
       xchg[hf * 128 + r] = mx;
       pair_sync(q);
       mx = fmaxf(mx, xchg[(hf ^ 1) * 128 + r]);
-      pair_sync(q);  // both read before the next write
+      pair_sync(q);  // both read before the next write; both halves' scores are loaded
       if (!ok) continue;
       // Both warps of a row take the same decision (same m, same max).
       const bool move = mx * a.softmax_scale > m + PT_RESCALE_GAP;
@@ -660,7 +695,7 @@ __global__ void __launch_bounds__(384, 1)
       l = l * corr + psum;
       if (k >= 1 && __any_sync(0xffffffffu, move)) {
         // O rescaled once the previous block's P.V is done (then also block k - 2's)
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(k - 1) & 1], ((k - 1) >> 1) & 1, abort, a.status,
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(k - 1) % PT_NSB], ((k - 1) / PT_NSB) & 1, abort, a.status,
                                                LS_DEV_TIMEOUT_EPILOGUE));
         if (!ok) continue;
         tc_fence_after();
@@ -673,26 +708,20 @@ __global__ void __launch_bounds__(384, 1)
           for (int e = 0; e < 16; ++e) ov[e] *= corr;
           tmem_st16(oa + c * 16, ov);
         }
-      } else if (k >= 2) {
-        // P buffer k % 2 is free once block k - 2's P.V is done
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[k & 1], ((k >> 1) - 1) & 1, abort, a.status,
-                                               LS_DEV_TIMEOUT_EPILOGUE));
-        if (!ok) continue;
-        tc_fence_after();
       }
-      // P high and residual of this half's 64 keys: 32 packed columns each
-      const uint32_t pa = tmem + lanes + PT_TM_P + (k & 1) * 128 + 32 * hf;
-      tmem_st32u(pa, phi);
-      tmem_st32u(pa + 64, plo);
+      // P high and residual of this half's 64 keys over the block's scores: 32
+      // packed columns each
+      tmem_st32u(sbuf + 32 * hf, phi);
+      tmem_st32u(sbuf + 64 + 32 * hf, plo);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[k & 1]);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
       m = mnew;
     }
     if (ok && nblk > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, abort, a.status,
-                                             LS_DEV_TIMEOUT_EPILOGUE));
+      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(nblk - 1) % PT_NSB], ((nblk - 1) / PT_NSB) & 1, abort,
+                                             a.status, LS_DEV_TIMEOUT_EPILOGUE));
       tc_fence_after();
     }
     // the row's sum over both halves (every softmax thread reaches this barrier)
@@ -707,7 +736,7 @@ __global__ void __launch_bounds__(384, 1)
   // barrier), and rank 0 merges the ranks in order after the second.
   constexpr uint32_t PT_SLOT = 128 * 512 + 128 * 8;  // O [128][128] fp32, then (m, l) [128]
   cluster_barrier();
-  if (warp >= 4 && crank > 0) {
+  if (softmax_warp && crank > 0) {
     const uint32_t slot_addr = dsmem_map(base + (crank - 1) * PT_SLOT, 0);
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
@@ -726,7 +755,7 @@ __global__ void __launch_bounds__(384, 1)
     if (hf == 0) dsmem_st_f2(slot_addr + 128 * 512 + (uint32_t)r * 8u, make_float2(m, l));
   }
   cluster_barrier();
-  if (warp >= 4 && crank == 0 && ok && !bad) {
+  if (softmax_warp && crank == 0 && ok && !bad) {
     float M = m;
     for (uint32_t rk = 1; rk < csize; ++rk) {
       const float2 ml = *reinterpret_cast<const float2*>(gbase + (rk - 1) * PT_SLOT + 128 * 512 + r * 8);
@@ -845,7 +874,7 @@ extern "C" int ls_prefill_summary(void* stream, const ls_prefill_args* a) {
       for (int c = 1; c <= 4; ++c) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(static_cast<unsigned>(c * 1024));
-        cfg.blockDim = dim3(384);
+        cfg.blockDim = dim3(PT_THREADS);
         cfg.dynamicSmemBytes = PT_SMEM;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -876,7 +905,7 @@ extern "C" int ls_prefill_summary(void* stream, const ls_prefill_args* a) {
     }
     const long long grid = tiles * C;
     if (grid > 0x7fffffffLL) return set_error(LS_ERR_UNSUPPORTED, "ls_prefill_summary: grid too large");
-    cudaError_t e = launch_pdl_cluster(prefill_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(384), PT_SMEM,
+    cudaError_t e = launch_pdl_cluster(prefill_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(PT_THREADS), PT_SMEM,
                                        reinterpret_cast<cudaStream_t>(stream), C, mq, mk, mv, *a);
     return e == cudaSuccess ? LS_OK : set_cuda_error("ls_prefill_summary: launch (tc)", e);
   }
