@@ -36,6 +36,8 @@ def _rand(*shape, std=1.0):
     (480, 256, 65664),     # many tokens over an odd count (513) of 128-row blocks
     (480, 2560, 5120),     # narrowed token tile (128)
     (480, 640, 5120),      # narrowed token tile (64), short k
+    (480, 4096, 24576),    # gate/up shape at 32 requests, stream-K partial tiles
+    (1920, 1024, 8192),    # eight token tiles
 ])
 def test_gemm_store_matches_fp32(rows, k, n):
     x = _rand(rows, k)
@@ -176,3 +178,4 @@ def test_tiled_weights_match_row_major(rows, k, n):
     ops.gemm(x, wt, b, workspace=ws)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
