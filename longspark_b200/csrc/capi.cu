@@ -63,26 +63,6 @@ int encode_tma_2d_bf16(CUtensorMap* map, const void* base, long long inner, long
   return LS_OK;
 }
 
-int encode_tma_2d_f32(CUtensorMap* map, const void* base, long long inner, long long outer, long long pitch,
-                      int box_inner, int box_outer) {
-  std::call_once(g_encode_once, load_encode);
-  if (g_encode == nullptr) return set_error(LS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (no CUDA driver?)");
-  if (box_inner * 4 != 128) return set_error(LS_ERR_INVALID, "TMA box inner extent must be 32 fp32 (128 B)");
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((pitch * 4) & 15))
-    return set_error(LS_ERR_INVALID, "TMA base must be 16-byte aligned and the row pitch a multiple of 16 bytes");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch * 4)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_error(LS_ERR_CUDA, "cuTensorMapEncodeTiled (fp32) failed (%d): inner=%lld outer=%lld",
-                     static_cast<int>(r), inner, outer);
-  return LS_OK;
-}
-
 int encode_tma_3d_bf16(CUtensorMap* map, const void* base, long long d0, long long d1, long long d2,
                        long long stride1_bytes, long long stride2_bytes, int box0, int box1, int box2) {
   std::call_once(g_encode_once, load_encode);

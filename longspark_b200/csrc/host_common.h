@@ -28,11 +28,6 @@ int host_sm_count();
 int encode_tma_2d_bf16(CUtensorMap* map, const void* base, long long inner, long long outer, long long pitch,
                        int box_inner, int box_outer);
 
-// 2-D fp32 tensor map: [outer][inner] floats, row pitch in floats; box =
-// [box_outer][box_inner] with box_inner * 4 = 128 bytes and 128-byte swizzle.
-int encode_tma_2d_f32(CUtensorMap* map, const void* base, long long inner, long long outer, long long pitch,
-                      int box_inner, int box_outer);
-
 // 3-D bf16 tensor map over [d2][d1][d0] elements (d0 contiguous, the other
 // strides in bytes); box = [box2][box1][box0] with box0 * 2 = 128 bytes and
 // 128-byte swizzle.
