@@ -492,6 +492,95 @@ typedef struct ls_prefill_args {
 LS_API int ls_prefill_summary(void* stream, const ls_prefill_args* a);
 
 /* ------------------------------------------------------------------------- */
+/* One whole greedy drafting round in one call                               */
+/* ------------------------------------------------------------------------- */
+
+/* The launch sequence of a round for hosts that are not Python: the calls the
+ * Python engine (DraftEngine.draft) makes, in the same order and with the same
+ * arguments, so a C, C++, Go or Java host binds one function instead of
+ * replaying sixteen.  Replaces, on the reference side, the drafter forward of
+ * one proposal (Global16NativeDraftExecutor, global16_native_draft_executor.py:
+ * 548-645: state encoder, shifted input, decoder layers, LM head) plus the
+ * summary update of LongSparkDraft._update_delta (src/longspark/engine/draft.py:
+ * 215-260), the Markov chain (draftfreekv.py:2366-2407) and the accept check
+ * (src/longspark/engine/target.py:472-477).  All pointers are device pointers;
+ * "tiled" weights are in the ls_tile_weight layout. */
+typedef struct ls_round_layer {
+  const void* in_norm;   /* [hidden] bf16                                                  */
+  const void* qkv;       /* tiled [(q_heads + 2 kv_heads) * 128, hidden]: q | k | v rows  */
+  const void* q_norm;    /* [128] bf16                                                    */
+  const void* k_norm;    /* [128] bf16                                                    */
+  const void* o;         /* tiled [hidden, q_heads * 128]                                 */
+  const void* post_norm; /* [hidden] bf16                                                  */
+  const void* gate_up;   /* tiled [2 inter, hidden]: per 128-row tile 64 gate rows, then the
+                            64 up rows of the same outputs                                 */
+  const void* down;      /* tiled [hidden, inter]                                         */
+  int view;              /* the tapped layer this layer attends to (its pool, learned
+                            queries and summary entries); < bf16_layers when summary_bf16 */
+} ls_round_layer;
+
+typedef struct ls_round_args {
+  /* shape */
+  int hidden, q_heads, kv_heads, inter, vocab;
+  int tap_layers, slots_per_head, window, block, max_commit;
+  int markov_rank;       /* 0: no Markov head                                             */
+  int mask_token_id;
+  float rms_eps, final_eps;
+  int n_layers;
+  const ls_round_layer* layers;  /* host array of n_layers                                */
+  /* weights */
+  const void* enc_w1;    /* tiled [hidden, tap_layers * hidden]                           */
+  const void* enc_w2;    /* tiled [hidden, hidden]                                        */
+  const void* enc_norm;  /* [hidden] bf16                                                  */
+  const void* embed;     /* [vocab, hidden] bf16                                          */
+  const void* pos_emb;   /* [block, hidden] bf16                                          */
+  const void* sh_w1;     /* tiled [hidden, 2 hidden]                                      */
+  const void* sh_w2;     /* tiled [hidden, hidden]                                        */
+  const void* sh_norm;   /* [hidden] bf16                                                  */
+  const void* final_norm;/* [hidden] bf16                                                  */
+  const void* lm_head;   /* tiled [vocab, hidden]                                         */
+  const void* markov_w1; /* [vocab, markov_rank] bf16 or NULL                             */
+  const void* markov_w2;
+  const float* w1_bound; /* ls_row_norm_bound of markov_w1 / markov_w2                    */
+  const float* w2_bound;
+  const float* inv_freq; /* [64] fp32 RoPE inverse frequencies                            */
+  /* views, by pool slot */
+  const void* kv_k;      /* [tap_layers, pool_pages, 16, kv_heads, 128] bf16               */
+  const void* kv_v;
+  long long pool_pages;
+  int ring_pages;
+  const void* learned_query; /* [tap_layers, q_heads, slots, 128] bf16                    */
+  float* summary_out;    /* [capacity, tap_layers, q_heads, slots, 128] fp32              */
+  float* summary_lse;    /* [capacity, tap_layers, q_heads, slots] fp32                    */
+  void* summary_bf16;    /* [capacity, bf16_layers, q_heads, slots, 128] bf16 or NULL      */
+  int bf16_layers;
+  const void* hidden_pool; /* [capacity, tap_layers * hidden] bf16 boundary hidden states  */
+  int capacity;
+  /* this round, batch order */
+  int batch;
+  const int* slots;      /* [batch] pool slots                                            */
+  const int* seq_lens;   /* [batch] committed length                                      */
+  const int* commit_lens;/* [batch] rows committed since the last round; NULL: no refresh */
+  const int* page_table; /* [batch, table_stride]                                         */
+  int table_stride;
+  const long long* anchors;  /* [batch]                                                   */
+  const long long* target;   /* [batch, target_ld] or NULL (no accept check)              */
+  int target_ld;
+  int slots_are_rows;    /* 1: slots[b] == b, the hidden states are read in place         */
+  /* outputs */
+  long long* tokens;     /* [batch, block]                                                */
+  long long* accept;     /* [batch], with target                                          */
+  void* logits;          /* [batch * block, vocab] bf16 base logits                       */
+  int* status;           /* device status word                                            */
+  /* scratch, ls_round_workspace_bytes(this) bytes, 256-byte aligned */
+  void* workspace;
+  size_t workspace_bytes;
+} ls_round_args;
+
+LS_API size_t ls_round_workspace_bytes(const ls_round_args* a);
+LS_API int ls_draft_round(void* stream, const ls_round_args* a);
+
+/* ------------------------------------------------------------------------- */
 /* Tensor parallelism of the drafter over NVLink (one process per GPU).       */
 /* No counterpart in the reference, which forces the drafter to one GPU       */
 /* (SP global16_native_draft_executor.py:1101-1105); the design precedent is  */

@@ -93,6 +93,28 @@ class ExportArgs(C.Structure):
                 ("batch", i32), ("tap_layers", i32), ("status", vp)]
 
 
+class RoundLayer(C.Structure):
+    _fields_ = [("in_norm", vp), ("qkv", vp), ("q_norm", vp), ("k_norm", vp), ("o", vp), ("post_norm", vp),
+                ("gate_up", vp), ("down", vp), ("view", i32)]
+
+
+class RoundArgs(C.Structure):
+    _fields_ = [("hidden", i32), ("q_heads", i32), ("kv_heads", i32), ("inter", i32), ("vocab", i32),
+                ("tap_layers", i32), ("slots_per_head", i32), ("window", i32), ("block", i32), ("max_commit", i32),
+                ("markov_rank", i32), ("mask_token_id", i32), ("rms_eps", f32), ("final_eps", f32),
+                ("n_layers", i32), ("layers", C.POINTER(RoundLayer)),
+                ("enc_w1", vp), ("enc_w2", vp), ("enc_norm", vp), ("embed", vp), ("pos_emb", vp), ("sh_w1", vp),
+                ("sh_w2", vp), ("sh_norm", vp), ("final_norm", vp), ("lm_head", vp), ("markov_w1", vp),
+                ("markov_w2", vp), ("w1_bound", vp), ("w2_bound", vp), ("inv_freq", vp),
+                ("kv_k", vp), ("kv_v", vp), ("pool_pages", i64), ("ring_pages", i32), ("learned_query", vp),
+                ("summary_out", vp), ("summary_lse", vp), ("summary_bf16", vp), ("bf16_layers", i32),
+                ("hidden_pool", vp), ("capacity", i32),
+                ("batch", i32), ("slots", vp), ("seq_lens", vp), ("commit_lens", vp), ("page_table", vp),
+                ("table_stride", i32), ("anchors", vp), ("target", vp), ("target_ld", i32), ("slots_are_rows", i32),
+                ("tokens", vp), ("accept", vp), ("logits", vp), ("status", vp),
+                ("workspace", vp), ("workspace_bytes", sz)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "ls_version": (i32, []),
@@ -119,6 +141,8 @@ SIGNATURES = {
     "ls_accept": (i32, [vp, vp, i32, vp, vp, i32, i32]),
     "ls_row_norm_bound": (i32, [vp, vp, i32, i32, vp]),
     "ls_prefill_summary": (i32, [vp, C.POINTER(PrefillArgs)]),
+    "ls_round_workspace_bytes": (sz, [C.POINTER(RoundArgs)]),
+    "ls_draft_round": (i32, [vp, C.POINTER(RoundArgs)]),
     "ls_sample_step_workspace_bytes": (sz, [i32]),
     "ls_sample_step": (i32, [vp, C.POINTER(SampleStepArgs), vp, sz]),
     "ls_rejection_sample": (i32, [vp, C.POINTER(RejectionArgs)]),

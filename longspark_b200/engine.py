@@ -12,6 +12,7 @@ global16_native_draft_executor.py:548-645``), plus the Markov greedy chain
 from __future__ import annotations
 
 import contextlib
+import ctypes as C
 import gc
 import math
 from dataclasses import dataclass, field
@@ -268,6 +269,50 @@ class DraftEngine:
                           tokens=b["tokens"], block=P, workspace=self.markov_ws, w1=w.w1, w2=w.w2,
                           w1_bound=w.w1_bound, w2_bound=w.w2_bound, target=target,
                           accept_out=b["accept"] if target is not None else None, status=st, batch=B)
+
+    def draft_native(self, *, slots, seq_lens, anchors, page_table, target=None, batch=None, slots_are_rows=False,
+                     commit_lens=None):
+        """``draft`` as one C-ABI call (``ls_draft_round``): the same launches
+        issued from the library's C++ side, for hosts that bind the library
+        directly; writes the same buffers."""
+        s, w, p, b = self.shape, self.w, self.pools, self.buf
+        B = anchors.shape[0] if batch is None else batch
+        if not hasattr(self, "_round_layers"):
+            layers = (N.RoundLayer * len(w.layers))()
+            for j, L in enumerate(w.layers):
+                layers[j] = N.RoundLayer(in_norm=ops._p(L["in_norm"]), qkv=ops._p(L["qkv"].data),
+                                         q_norm=ops._p(L["q_norm"]), k_norm=ops._p(L["k_norm"]),
+                                         o=ops._p(L["o"].data), post_norm=ops._p(L["post_norm"]),
+                                         gate_up=ops._p(L["gate_up"].data), down=ops._p(L["down"].data),
+                                         view=s.view_layer(j))
+            self._round_layers = layers
+        a = N.RoundArgs(
+            hidden=s.hidden, q_heads=s.q_heads, kv_heads=s.kv_heads, inter=s.inter, vocab=s.vocab,
+            tap_layers=s.tap_layers, slots_per_head=s.slots, window=s.window, block=s.block,
+            max_commit=s.max_commit, markov_rank=s.markov_rank, mask_token_id=s.mask_token_id,
+            rms_eps=s.rms_eps, final_eps=s.final_eps, n_layers=len(w.layers),
+            layers=C.cast(self._round_layers, C.POINTER(N.RoundLayer)),
+            enc_w1=ops._p(w.enc_w1.data), enc_w2=ops._p(w.enc_w2.data), enc_norm=ops._p(w.enc_norm),
+            embed=ops._p(w.embed), pos_emb=ops._p(w.pos_emb), sh_w1=ops._p(w.sh_w1.data),
+            sh_w2=ops._p(w.sh_w2.data), sh_norm=ops._p(w.sh_norm), final_norm=ops._p(w.final_norm),
+            lm_head=ops._p(w.lm_head.data), markov_w1=ops._p(w.w1), markov_w2=ops._p(w.w2),
+            w1_bound=ops._p(w.w1_bound), w2_bound=ops._p(w.w2_bound), inv_freq=ops._p(w.inv_freq),
+            kv_k=ops._p(p.kv_k), kv_v=ops._p(p.kv_v), pool_pages=p.kv_k.shape[1], ring_pages=p.ring_pages,
+            learned_query=ops._p(w.learned_query), summary_out=ops._p(p.summary_out),
+            summary_lse=ops._p(p.summary_lse), summary_bf16=ops._p(p.summary_bf16),
+            bf16_layers=0 if p.summary_bf16 is None else p.summary_bf16.shape[1],
+            hidden_pool=ops._p(p.hidden), capacity=p.summary_out.shape[0],
+            batch=B, slots=ops._p(slots), seq_lens=ops._p(seq_lens), commit_lens=ops._p(commit_lens),
+            page_table=ops._p(page_table), table_stride=page_table.stride(0), anchors=ops._p(anchors),
+            target=ops._p(target), target_ld=0 if target is None else target.stride(0),
+            slots_are_rows=1 if slots_are_rows else 0, tokens=ops._p(b["tokens"]), accept=ops._p(b["accept"]),
+            logits=ops._p(b["logits"]), status=ops._p(b["status"]))
+        need = int(N.lib().ls_round_workspace_bytes(C.byref(a)))
+        if getattr(self, "round_ws", None) is None or self.round_ws.numel() < need:
+            self.round_ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        a.workspace = ops._p(self.round_ws)
+        a.workspace_bytes = self.round_ws.numel()
+        N.call("ls_draft_round", ops._stream(self.device), C.byref(a))
 
     def sample(self, anchors, *, temperature, seed, corrected=None, batch=None):
         """Sampled (T > 0) proposals from the base logits of the last pass, the

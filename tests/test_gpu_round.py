@@ -177,6 +177,43 @@ def test_round_with_refresh_and_graph_replay():
     np.testing.assert_array_equal(acc, O.accept_lengths(target.cpu().numpy(), e1.buf["tokens"][:batch].cpu().numpy())[0])
 
 
+@pytest.mark.parametrize("q_heads,kv_heads,slots_are_rows", [(8, 2, False), (10, 2, True)])
+def test_native_round_entry_matches_engine(q_heads, kv_heads, slots_are_rows):
+    """ls_draft_round (the whole round as one C-ABI call) against the Python
+    engine's launch sequence on the same buffers: refresh, two drafter layers
+    on different tapped layers, the Markov chain and the accept check; tokens,
+    accept lengths, base logits and the refreshed summary state bit for bit."""
+    shape = DraftShape(hidden=512, q_heads=q_heads, kv_heads=kv_heads, inter=1024, vocab=4096, tap_layers=2,
+                       draft_layers=2, slots=64, window=512, block=15, max_commit=16, markov_rank=64,
+                       mask_token_id=4000)
+    batch = 3
+    W = make_weights(shape, seed=21, norm_jitter=0.05)
+    v = make_views(shape, batch, [900, 333, 2000], seed=22, extra_rows=64)
+    dev = torch.device("cuda")
+    e1 = _engine(shape, W, v, batch)
+    e2 = _engine(shape, W, v, batch)
+    slots = (torch.arange(batch, dtype=torch.int32, device=dev) if slots_are_rows
+             else torch.tensor([2, 0, 1], dtype=torch.int32, device=dev))
+    commit = torch.tensor([16, 3, 9], dtype=torch.int32, device=dev)
+    lens = v["seq_lens"].to(dev) + commit
+    table = v["page_table"].to(dev)
+    anchors = v["anchors"].to(dev)
+    target = torch.randint(0, shape.vocab, (batch, shape.block + 1), device=dev)
+    kw = dict(slots=slots, seq_lens=lens, commit_lens=commit, anchors=anchors, page_table=table, target=target,
+              slots_are_rows=slots_are_rows)
+    e1.draft(**kw)
+    e2.draft_native(**kw)
+    torch.cuda.synchronize()
+    M = batch * shape.block
+    assert e1.device_status() == 0 and e2.device_status() == 0
+    assert torch.equal(e1.buf["tokens"][:batch], e2.buf["tokens"][:batch])
+    assert torch.equal(e1.buf["accept"][:batch], e2.buf["accept"][:batch])
+    assert torch.equal(e1.buf["logits"][:M], e2.buf["logits"][:M])
+    assert torch.equal(e1.pools.summary_out, e2.pools.summary_out)
+    assert torch.equal(e1.pools.summary_lse, e2.pools.summary_lse)
+    assert torch.equal(e1.pools.summary_bf16, e2.pools.summary_bf16)
+
+
 def test_longspark_draft_api_prefill_update_propose():
     """The drop-in API: prefill packets (window rows + summary), decode updates in
     the batch message format, proposals; checked against the oracle on the same

@@ -50,7 +50,8 @@ def test_struct_layouts_match_the_header(lib):
     for cname, py in (("ls_gemm_args", N.GemmArgs), ("ls_refresh_args", N.RefreshArgs),
                       ("ls_attention_args", N.AttentionArgs), ("ls_markov_args", N.MarkovArgs),
                       ("ls_prefill_args", N.PrefillArgs), ("ls_tp_group", N.TpGroup),
-                      ("ls_sample_step_args", N.SampleStepArgs), ("ls_export_args", N.ExportArgs)):
+                      ("ls_sample_step_args", N.SampleStepArgs), ("ls_export_args", N.ExportArgs),
+                      ("ls_round_layer", N.RoundLayer), ("ls_round_args", N.RoundArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         body = re.sub(r"\[[^\]]*\]", "", body)  # array declarators: the name is what precedes them
@@ -102,3 +103,25 @@ def test_export_rows_validates_on_the_host(lib):
     assert b"hidden % 8" in lib.ls_last_error()
     a.batch = 0
     assert lib.ls_export_rows(None, ctypes.byref(a)) == 0
+
+
+def test_round_entry_validates_before_any_launch(lib):
+    """ls_draft_round refuses a layer that views a tapped layer out of range,
+    and a workspace that is too small, before anything is enqueued."""
+    from longspark_b200 import _native as N
+    layers = (N.RoundLayer * 1)()
+    layers[0] = N.RoundLayer(view=5)
+    ptrs = {k: 256 for k in ("enc_w1", "enc_w2", "enc_norm", "embed", "pos_emb", "sh_w1", "sh_w2", "sh_norm",
+                             "final_norm", "lm_head", "inv_freq", "kv_k", "kv_v", "learned_query", "summary_out",
+                             "summary_lse", "hidden_pool", "slots", "seq_lens", "page_table", "anchors", "tokens",
+                             "logits", "workspace")}
+    a = N.RoundArgs(batch=1, n_layers=1, layers=ctypes.cast(layers, ctypes.POINTER(N.RoundLayer)), tap_layers=2,
+                    hidden=512, q_heads=8, kv_heads=2, inter=1024, vocab=4096, slots_per_head=64, window=512,
+                    block=15, max_commit=16, **ptrs)
+    assert lib.ls_draft_round(None, ctypes.byref(a)) == 1  # LS_ERR_INVALID
+    assert b"views tapped layer 5" in lib.ls_last_error()
+    layers[0] = N.RoundLayer(view=1)
+    a.workspace_bytes = 1024
+    assert lib.ls_draft_round(None, ctypes.byref(a)) == 4  # LS_ERR_WORKSPACE
+    assert b"workspace" in lib.ls_last_error()
+    assert lib.ls_round_workspace_bytes(ctypes.byref(a)) > 1024
