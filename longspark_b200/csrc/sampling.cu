@@ -76,7 +76,11 @@ constexpr int MK_MAXRANK = 512;
 constexpr int MK_MAXTILES = 1024;
 constexpr int MK_ROWCAND = 128;   // band candidates kept per row
 constexpr int MK_TPT = 8;         // tile maxima per thread held in registers (vocab <= 8 * 256 * 128)
-constexpr int MK_ROWPAIRS = 256;  // (previous candidate, candidate) pairs evaluated per row
+// (previous candidate, candidate) pairs evaluated per row; a row with more
+// sends its request to the step-by-step fallback, which takes the launch's
+// whole tail (one such row at 32 requests of random-weight data made the
+// kernel ~7x slower at 256)
+constexpr int MK_ROWPAIRS = 1024;
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
@@ -669,7 +673,7 @@ static int markov_launch(void* stream, const ls_markov_args* a, const VocabShard
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // within the default 48 KiB dynamic shared memory limit: no attribute needed
   static_assert(mk_table_bytes() <= 36 * 1024 && mk_stepwise_bytes() <= 36 * 1024 && MK_STAGE_BYTES <= 36 * 1024,
-                "Markov shared memory (with about 11 KiB of static shared memory, under the 48 KiB default)");
+                "Markov shared memory (with about 15 KiB of static shared memory, under the 48 KiB default)");
   size_t dsmem = 0;
   if (a->w1 != nullptr) {
     dsmem = mk_table_bytes();
