@@ -140,20 +140,39 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
             sn[j] = bf16_round(sinf(ang));
           }
         }
+        // Sums of squares of the 16 tokens over the warp's 32 features: a
+        // reduce-scatter (16 + 8 + 4 + 2 + 1 shuffles instead of 16 x 5) that
+        // adds the same pairs in the same tree as a butterfly sum, so the
+        // bits are the same; lane pairs (2t', 2t' + 1) end with one token each.
+        const int lane = threadIdx.x & 31;
         float ss[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ss[j] = warp_sum(y[j] * y[j]);
-        const int lane = threadIdx.x & 31;
-        if (lane == 0) {
+        for (int j = 0; j < 16; ++j) ss[j] = y[j] * y[j];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) sc->red_v[ew][j] = ss[j];
+        for (int lvl = 0; lvl < 4; ++lvl) {
+          const int half = 8 >> lvl, off = 16 >> lvl;
+          const bool upper = (lane & off) != 0;
+#pragma unroll
+          for (int i = 0; i < half; ++i) {
+            const float mine = upper ? ss[half + i] : ss[i];
+            const float other = upper ? ss[i] : ss[half + i];
+            ss[i] = mine + __shfl_xor_sync(0xffffffffu, other, off);
+          }
+        }
+        ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], 1);
+        const int tok = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+        if ((lane & 1) == 0) sc->red_v[ew][tok] = ss[0];
+        epi_bar();
+        // one thread per token: the inverse RMS, shared through the scratch
+        float* rstd_s = reinterpret_cast<float*>(&sc->red_i[0][0]);
+        if (r < 16) {
+          const float tot = sc->red_v[0][r] + sc->red_v[1][r] + sc->red_v[2][r] + sc->red_v[3][r];
+          rstd_s[r] = 1.0f / sqrtf(tot / 128.0f + a.norm_eps);
         }
         epi_bar();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const float tot = sc->red_v[0][j] + sc->red_v[1][j] + sc->red_v[2][j] + sc->red_v[3][j];
-          const float rstd = 1.0f / sqrtf(tot / 128.0f + a.norm_eps);
-          y[j] = bf16_round(bf16_round(y[j] * rstd) * wr);
+          y[j] = bf16_round(bf16_round(y[j] * rstd_s[j]) * wr);
           sc->xch[r][j] = y[j];
         }
         epi_bar();

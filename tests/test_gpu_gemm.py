@@ -94,8 +94,9 @@ def test_gemm_gate_up_interleaved():
     assert_bf16_close(to_np(out), ref, steps=1.0, exact_frac=0.95, what="gate_up")
 
 
-def test_gemm_qkv_norm_rope():
-    rows, hidden, hq, hkv = 15, 512, 4, 2
+@pytest.mark.parametrize("rows", [15, 300])
+def test_gemm_qkv_norm_rope(rows):
+    hidden, hq, hkv = 512, 4, 2
     x = _rand(rows, hidden)
     w = _rand((hq + 2 * hkv) * 128, hidden, std=0.05)
     qn = (1 + 0.1 * torch.randn(128, device="cuda")).to(torch.bfloat16)
