@@ -130,6 +130,12 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
             cs[j] = a.rope_table[(long long)tr * 128 + (r & 63)];
             sn[j] = a.rope_table[(long long)tr * 128 + 64 + (r & 63)];
           }
+          // the next chunk's table lines into L1 while this chunk computes: lane
+          // l fetches token l / 2's cos (even l) or sin (odd l) line of the warp
+          const int ln = threadIdx.x & 31, tn = n0 + 16 + (ln >> 1);
+          if (tn < rows)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(a.rope_table + (long long)tn * 128 + (ln & 1) * 64 +
+                                                           (r & 32)));
         } else {
           const float fr = a.inv_freq[r & 63];
 #pragma unroll
