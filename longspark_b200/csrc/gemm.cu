@@ -21,6 +21,7 @@
 #include "tp_common.cuh"
 
 #include <algorithm>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -42,14 +43,17 @@ struct GemmKernelParams {
   int bn;            // token tile (multiple of 16, <= 256)
   int n_tiles;       // token tiles
   int m_tiles;       // feature tiles (n_out / 128)
+  int mw;            // feature tiles per work tile (2: a 256-row work tile, both halves against the same
+                     // token tile, so the activations are read once for 256 features)
+  int nacc;          // accumulator buffers in TMEM (2: the epilogue of a tile overlaps the next tile)
   int kb;            // stream-K units per tile (each unit = kg k-blocks of 64)
   int kg;            // k-blocks per unit and per pipeline stage (1, 2 or 4)
   long long units;   // tiles * kb
   int grid;          // CTAs
   int stages;
   uint32_t tmem_cols;
-  float* partials;   // [grid * 2][bn][128]
-  int* counters;     // [tiles]
+  float* partials;   // [grid * 2][mw][bn][128]
+  int* counters;     // [work tiles]
   TpView tp;         // tp.world > 0: row-parallel GEMM fused with the allreduce (ls_gemm_allreduce)
   int tp_wire;       // LS_TP_WIRE_*
   int tp_oneshot;    // 1: every rank pushes its partials to every rank and reduces all tiles itself
@@ -64,6 +68,12 @@ __device__ __forceinline__ int cta_of_unit(long long u, long long units, long lo
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Feature tiles of work tile t (mw, or fewer for the last row of an odd tile count).
+__device__ __forceinline__ int work_halves(const GemmKernelParams& P, int t) {
+  const int left = P.m_tiles - (t / P.n_tiles) * P.mw;
+  return left < P.mw ? left : P.mw;
+}
+
 // ---------------------------------------------------------------------------
 // Final epilogue on a 16-token chunk: thread `r` owns feature row r of the
 // 128-row tile and v[j] = fp32 accumulator for token n0 + j.
@@ -75,12 +85,16 @@ struct EpiScratch {
   int flag;
 };
 
+// EPI (an LS_EPI_* value) is a template argument: each kernel instance holds
+// only its own epilogue, so no other epilogue's arithmetic is issued under a
+// false predicate.
+template <int EPI>
 __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_tile, int n0, const float (&v)[16],
                                                int r, int ew, EpiScratch* sc) {
   const ls_gemm_args& a = P.a;
   const int rows = a.rows;
   bf16* out = reinterpret_cast<bf16*>(a.out);
-  switch (a.epilogue) {
+  switch (EPI) {
     case LS_EPI_STORE:
     case LS_EPI_SILU:
     case LS_EPI_RESIDUAL:
@@ -89,22 +103,46 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
       // Every global load before the first store: the residual may alias the
       // output, so loads interleaved with stores would run one round trip each.
       float add[16];
-      const bool has_add = a.epilogue == LS_EPI_RESIDUAL || a.epilogue == LS_EPI_MARKOV_ADD;
+      constexpr bool has_add = EPI == LS_EPI_RESIDUAL || EPI == LS_EPI_MARKOV_ADD;
       if (has_add) {
-        const bf16* src = reinterpret_cast<const bf16*>(a.epilogue == LS_EPI_RESIDUAL ? a.residual : a.base);
-        const long long ld = a.epilogue == LS_EPI_RESIDUAL ? a.res_ld : a.base_ld;
+        const bf16* src = reinterpret_cast<const bf16*>(EPI == LS_EPI_RESIDUAL ? a.residual : a.base);
+        const long long ld = EPI == LS_EPI_RESIDUAL ? a.res_ld : a.base_ld;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int tok = n0 + j < rows ? n0 + j : rows - 1;
           add[j] = __bfloat162float(src[(long long)tok * ld + f]);
         }
       }
+      if (((reinterpret_cast<uintptr_t>(out) & 15) | (a.out_ld & 7)) == 0) {
+        // Through shared memory: the warp's 16 tokens x 32 features land in a
+        // 1 KB staging block, then leave as 16-byte rows of 8 features (two
+        // stores a lane instead of sixteen 2-byte stores).
+        bf16* st = reinterpret_cast<bf16*>(&sc->xch[0][0]) + ew * (16 * 32);
+        const int lane = r & 31;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float y = bf16_round(v[j]);
+          if (EPI == LS_EPI_SILU) y = silu_f(y);
+          if (has_add) y = y + add[j];
+          st[j * 32 + lane] = __float2bfloat16_rn(y);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q = lane; q < 64; q += 32) {
+          const int tok = n0 + (q >> 2);
+          if (tok < rows)
+            *reinterpret_cast<uint4*>(out + (long long)tok * a.out_ld + m_tile * BM + ew * 32 + (q & 3) * 8) =
+                *reinterpret_cast<const uint4*>(st + (q >> 2) * 32 + (q & 3) * 8);
+        }
+        __syncwarp();
+        break;
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int tok = n0 + j;
         if (tok >= rows) break;  // padded tokens of the last chunk: no work
         float y = bf16_round(v[j]);
-        if (a.epilogue == LS_EPI_SILU) y = silu_f(y);
+        if (EPI == LS_EPI_SILU) y = silu_f(y);
         if (has_add) y = y + add[j];
         out[(long long)tok * a.out_ld + f] = __float2bfloat16_rn(y);
       }
@@ -510,22 +548,27 @@ __device__ __noinline__ void tp_finish(const GemmKernelParams& P, int r, EpiScra
 
 // A finished 16-token chunk: the fused epilogue, or (row-parallel TP) the send
 // of the partial to the tile's owner.
+template <int EPI>
 __device__ __forceinline__ void emit_chunk(const GemmKernelParams& P, int t, int m_tile, int n0, int c,
                                            const float (&v)[16], int r, int ew, EpiScratch* sc, uint32_t tp_tgt) {
   if (P.tp.world > 0)
     tp_send_chunk(P, t, n0, c, v, r, sc, tp_tgt);
   else
-    final_epilogue(P, m_tile, n0 + c, v, r, ew, sc);
+    final_epilogue<EPI>(P, m_tile, n0 + c, v, r, ew, sc);
 }
 
 // Reduction of a stream-K tile by its last contributor: the fp32 partials of
 // CTAs first..last summed in that order, then the fused epilogue.
+template <int EPI>
 __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, int first, int last, int first_slot,
                                             int r, int ew, EpiScratch* sc, uint32_t tp_tgt) {
   const int bn = P.bn;
-  const int m_tile = t / P.n_tiles;
-  const int n0 = (t - m_tile * P.n_tiles) * bn;
-  for (int c = 0; c < bn; c += 16) {
+  const int m_work = t / P.n_tiles;
+  const int n0 = (t - m_work * P.n_tiles) * bn;
+  for (int hc = 0; hc < P.mw * bn; hc += 16) {
+    const int h = hc / bn, c = hc - h * bn;  // feature tile of the work tile, chunk
+    const int m_tile = m_work * P.mw + h;
+    if (m_tile >= P.m_tiles) break;
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = 0.0f;
@@ -536,7 +579,8 @@ __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, in
       for (int i = 0; i < 4; ++i) {
         const int q = q0 + i;
         const int q_slot = q == first ? first_slot : 0;
-        const float* qp = P.partials + (static_cast<long long>(q) * 2 + q_slot) * (static_cast<long long>(bn) * BM);
+        const float* qp = P.partials + ((static_cast<long long>(q) * 2 + q_slot) * P.mw + h) *
+                                           (static_cast<long long>(bn) * BM);
         if (q <= last) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) pv[i][j] = __ldcg(&qp[(c + j) * BM + r]);
@@ -550,7 +594,7 @@ __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, in
         }
       }
     }
-    if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc, tp_tgt);
+    if (n0 + c < P.a.rows) emit_chunk<EPI>(P, t, m_tile, n0, c, v, r, ew, sc, tp_tgt);
   }
 }
 
@@ -562,14 +606,19 @@ __device__ __forceinline__ void gemm_load_a(const GemmKernelParams& P, const CUt
                                             long long u, uint64_t pol) {
   const int t = static_cast<int>(u / P.kb);
   const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
-  const int m_tile = t / P.n_tiles;
-  if (tiled_w) {
-    // KG consecutive tiles of one row block are contiguous in the tiled layout
-    bulk_load(a_buf + st * a_stage_bytes,
-              w_tiles + (static_cast<long long>(m_tile) * P.kb * P.kg + kb0) * (BM * BK), a_stage_bytes, &full[st], pol);
-  } else {
-    for (int j = 0; j < P.kg; ++j)
-      tma_load_2d(a_buf + st * a_stage_bytes + j * A_STAGE_BYTES, map_w, &full[st], (kb0 + j) * BK, m_tile * BM, pol);
+  const int half_bytes = P.kg * A_STAGE_BYTES;  // one feature tile's KG k-blocks
+  for (int h = 0; h < P.mw; ++h) {
+    const int m_tile = (t / P.n_tiles) * P.mw + h;
+    if (m_tile >= P.m_tiles) break;  // the last work tile of an odd count: one half
+    uint8_t* dst = a_buf + st * a_stage_bytes + h * half_bytes;
+    if (tiled_w) {
+      // KG consecutive tiles of one row block are contiguous in the tiled layout
+      bulk_load(dst, w_tiles + (static_cast<long long>(m_tile) * P.kb * P.kg + kb0) * (BM * BK), half_bytes,
+                &full[st], pol);
+    } else {
+      for (int j = 0; j < P.kg; ++j)
+        tma_load_2d(dst + j * A_STAGE_BYTES, map_w, &full[st], (kb0 + j) * BK, m_tile * BM, pol);
+    }
   }
 }
 
@@ -583,6 +632,7 @@ __device__ __forceinline__ void gemm_load_b(const GemmKernelParams& P, const CUt
     tma_load_2d(b_buf + st * b_stage_bytes + j * b_blk_bytes, map_x, &full[st], (kb0 + j) * BK, n_tile * P.bn, pol);
 }
 
+template <int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ GemmKernelParams P) {
@@ -592,7 +642,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int bn = P.bn;
   const int KG = P.kg;
   const int b_blk_bytes = bn * BK * 2;          // one k-block of activations
-  const int a_stage_bytes = KG * A_STAGE_BYTES;  // one stage = KG k-blocks
+  const int a_half_bytes = KG * A_STAGE_BYTES;     // one feature tile's KG k-blocks
+  const int a_stage_bytes = P.mw * a_half_bytes;  // one stage = KG k-blocks of mw feature tiles
   const int b_stage_bytes = KG * b_blk_bytes;
   uint8_t* a_buf = smem;
   uint8_t* b_buf = a_buf + S * a_stage_bytes;
@@ -658,7 +709,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // weight tiles before waiting for it, then add the activation tiles.
       const int pre = static_cast<int>((u1 - u0) < S ? (u1 - u0) : S);
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], a_stage_bytes + b_stage_bytes);
+        mbar_arrive_expect_tx(&full[i], work_halves(P, static_cast<int>((u0 + i) / KB)) * a_half_bytes + b_stage_bytes);
         gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, i, u0 + i, pol_w);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -668,7 +719,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       long long issued = pre;
       for (long long u = u0 + pre; u < u1; ++u) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full[stage], a_stage_bytes + b_stage_bytes);
+        mbar_arrive_expect_tx(&full[stage], work_halves(P, static_cast<int>(u / KB)) * a_half_bytes + b_stage_bytes);
         gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, stage, u, pol_w);
         gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, u, pol_x);
         ++issued;
@@ -710,7 +761,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * bn);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P.mw * bn);
+        const int halves = work_halves(P, t);
         for (int kb = k0; kb < k1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, status, LS_DEV_TIMEOUT_MMA)) {
             ok = false;
@@ -718,14 +770,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           tc_fence_after();
           for (int j = 0; j < KG; ++j) {
-            const uint32_t a_addr = smem_u32(a_buf + stage * a_stage_bytes + j * A_STAGE_BYTES);
             const uint32_t b_addr = smem_u32(b_buf + stage * b_stage_bytes + j * b_blk_bytes);
-            const uint64_t a_desc = sdesc_kmajor_sw128(a_addr);
             const uint64_t b_desc = sdesc_kmajor_sw128(b_addr);
+            for (int h = 0; h < halves; ++h) {
+              const uint32_t a_addr = smem_u32(a_buf + stage * a_stage_bytes + h * a_half_bytes + j * A_STAGE_BYTES);
+              const uint64_t a_desc = sdesc_kmajor_sw128(a_addr);
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              // +32 bytes along K inside the 128-byte swizzled row (encoded >> 4).
-              tc_mma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb > k0 || j > 0 || kk > 0) ? 1u : 0u);
+              for (int kk = 0; kk < BK / 16; ++kk) {
+                // +32 bytes along K inside the 128-byte swizzled row (encoded >> 4).
+                tc_mma_bf16(d_tmem + static_cast<uint32_t>(h * bn), a_desc + 2 * kk, b_desc + 2 * kk, idesc,
+                            (kb > k0 || j > 0 || kk > 0) ? 1u : 0u);
+              }
             }
           }
           tc_commit(&empty[stage]);
@@ -737,7 +792,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!ok) break;
         tc_commit(&acc_full[acc]);
         acc_phase ^= 1u << acc;
-        acc ^= 1;
+        if (P.nacc == 2) acc ^= 1;
         u += k1 - k0;
       }
       // Drain: wait until every MMA issued by this thread has completed.
@@ -773,16 +828,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       epi_bar();
       if (!go) break;
       tc_fence_after();
-      const int m_tile = t / P.n_tiles;
-      const int n_tile = t - m_tile * P.n_tiles;
+      const int m_work = t / P.n_tiles;
+      const int n_tile = t - m_work * P.n_tiles;
       const int n0 = n_tile * P.bn;
+      const int halves = work_halves(P, t);
       const bool full_tile = (k0 == 0 && k1 == KB);
-      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * bn);
+      const uint32_t t_addr =
+          tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * P.mw * bn);
       if (full_tile) {
-        for (int c = 0; c < bn; c += 16) {
-          float v[16];
-          tmem_ld16(t_addr + c, v);
-          if (n0 + c < P.a.rows) emit_chunk(P, t, m_tile, n0, c, v, r, ew, sc, tp_tgt);
+        for (int h = 0; h < halves; ++h) {
+          for (int c = 0; c < bn; c += 16) {
+            float v[16];
+            tmem_ld16(t_addr + h * bn + c, v);
+            if (n0 + c < P.a.rows) emit_chunk<EPI>(P, t, m_work * P.mw + h, n0, c, v, r, ew, sc, tp_tgt);
+          }
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
@@ -790,8 +849,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       } else {
         // Partial tile: park the fp32 partial, the last contributor reduces.
         const int slot = (t == t_first) ? 0 : 1;
-        float* part = P.partials + (static_cast<long long>(blockIdx.x) * 2 + slot) * (static_cast<long long>(bn) * BM);
-        for (int c = 0; c < bn; c += 16) {
+        float* part =
+            P.partials + (static_cast<long long>(blockIdx.x) * 2 + slot) * P.mw * (static_cast<long long>(bn) * BM);
+        for (int c = 0; c < halves * bn; c += 16) {
           float v[16];
           tmem_ld16(t_addr + c, v);
 #pragma unroll
@@ -814,13 +874,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           // Tile t is the first tile of every contributor after `first`, and of
           // `first` itself only when its range starts exactly at the tile.
           const int first_slot = unit_begin(first, U, G) == tu0 ? 0 : 1;
-          reduce_tile(P, t, first, last, first_slot, r, ew, sc, tp_tgt);
+          reduce_tile<EPI>(P, t, first, last, first_slot, r, ew, sc, tp_tgt);
           if (r == 0) atomicExch(&P.counters[t], 0);
           if (P.tp.world > 0) tp_publish(P, t, r, tp_tgt);
         }
       }
       acc_phase ^= 1u << acc;
-      acc ^= 1;
+      if (P.nacc == 2) acc ^= 1;
       u += k1 - k0;
     }
     if (P.tp.world > 0) {
@@ -853,22 +913,47 @@ static int pick_bn(int rows) {
   return r16 > 256 ? 256 : r16;
 }
 
-static int pick_stages(int bn, int kg) {
+static int pick_stages(int bn, int kg, int mw) {
   const int budget = 227 * 1024 - 1024 - 256 - EPI_SCRATCH_BYTES - 512;
-  int s = budget / (kg * (A_STAGE_BYTES + bn * BK * 2));
+  int s = budget / (kg * (mw * A_STAGE_BYTES + bn * BK * 2));
   return s > 12 ? 12 : s;
 }
 
-static size_t gemm_smem_bytes(int bn, int kg, int stages) {
-  return 1024 + static_cast<size_t>(stages) * kg * (A_STAGE_BYTES + bn * BK * 2) + (2 * stages + 5) * 8 + 64 +
+static size_t gemm_smem_bytes(int bn, int kg, int mw, int stages) {
+  return 1024 + static_cast<size_t>(stages) * kg * (mw * A_STAGE_BYTES + bn * BK * 2) + (2 * stages + 5) * 8 + 64 +
          EPI_SCRATCH_BYTES;
 }
 
 struct GemmPlan {
-  int bn, n_tiles, m_tiles, kb, kg, grid, stages;
+  int bn, n_tiles, m_tiles, mw, nacc, kb, kg, grid, stages;
   long long units;
   size_t partial_bytes, counter_bytes;
 };
+
+// Work tiles of two feature tiles (256 weight rows against one token tile of
+// up to 256: the tile's operand bytes per MAC are two thirds of a 128-row
+// tile's).  LONGSPARK_B200_GEMM_WIDE: 0 never; 1 always, with the widest token
+// tile; 2 always, with the token tile plan_bn picks; unset: the measured rule
+// in wide_auto.
+static int wide_env() {
+  static int mode = -2;
+  if (mode == -2) {
+    const char* e = getenv("LONGSPARK_B200_GEMM_WIDE");
+    mode = (e != nullptr && e[0] >= '0' && e[0] <= '2') ? e[0] - '0' : -1;
+  }
+  return mode;
+}
+
+// Wide tiles pay off where there are enough of them to keep every SM on whole
+// tiles, or where long reductions make the split tiles' partials cheap
+// against the operand bytes saved.  Measured (B200, L2 flushed, wide / plain):
+// vocabulary 480 x 4096 x 151936 876 / 964 us, 1920 x 4096 x 24576 607 / 645,
+// 1920 x 12288 x 4096 275 / 344; slower with few tiles: 480 x 4096 x 6144
+// 115 / 76, 480 x 12288 x 4096 159 / 108, 480 x 4096 x 24576 211 / 203.
+static bool wide_auto(int rows, int k, int n_out, int sms) {
+  const long long tiles = static_cast<long long>(n_out / BM / 2) * ((rows + pick_bn(rows) - 1) / pick_bn(rows));
+  return tiles >= 4LL * sms || (k >= 8192 && 2 * tiles >= sms);
+}
 
 // Next narrower token tile: half, rounded up to a multiple of 16 (the MMA N
 // step and the epilogue's 16-token chunk), never below 64.
@@ -895,29 +980,45 @@ static int plan_bn(int rows, int k, int n_out, int sms) {
   return bn;
 }
 
-static GemmPlan plan_gemm(int rows, int k, int n_out) {
+static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide) {
   GemmPlan p{};
   const int sms = host_sm_count();
-  p.bn = plan_bn(rows, k, n_out, sms);
+  int wide = 0;
+  if (allow_wide && rows > 128 && n_out >= 2 * BM) {
+    wide = wide_env();
+    if (wide < 0) wide = wide_auto(rows, k, n_out, sms) ? 1 : 0;
+  }
+  p.bn = wide == 1 ? pick_bn(rows) : plan_bn(rows, k, n_out, sms);
+  p.mw = wide ? 2 : 1;
+  // Tuning override, LONGSPARK_B200_GEMM_PLAN="bn,kg,mw,grid" (0 keeps the
+  // planned value; read at every call so one process can sweep plans).
+  int o_bn = 0, o_kg = 0, o_mw = 0, o_grid = 0;
+  if (const char* e = getenv("LONGSPARK_B200_GEMM_PLAN")) {
+    if (sscanf(e, "%d,%d,%d,%d", &o_bn, &o_kg, &o_mw, &o_grid) != 4) o_bn = o_kg = o_mw = o_grid = 0;
+    if (o_bn > 0 && o_bn <= 256 && o_bn % 16 == 0) p.bn = o_bn;
+    if (allow_wide && (o_mw == 1 || o_mw == 2)) p.mw = o_mw;
+  }
+  p.nacc = 2 * p.mw * p.bn <= 512 ? 2 : 1;
   p.n_tiles = (rows + p.bn - 1) / p.bn;
   p.m_tiles = n_out / BM;
   // Pipeline stages of up to 4 k-blocks (64 KiB of weights): HBM streams best
   // with a few large requests in flight per SM.  Smaller stages when the tile
   // count is low (stream-K balance) or the token tile is wide (shared memory).
-  const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  const long long tiles = static_cast<long long>((p.m_tiles + p.mw - 1) / p.mw) * p.n_tiles;
   p.kg = 1;
   for (int kg = 4; kg > 1; kg >>= 1) {
     if (k % (BK * kg)) continue;
-    if (pick_stages(p.bn, kg) < 3) continue;
+    if (pick_stages(p.bn, kg, p.mw) < 3) continue;
     if (tiles * (k / (BK * kg)) < 4LL * sms) continue;
     p.kg = kg;
     break;
   }
+  if ((o_kg == 1 || o_kg == 2 || o_kg == 4) && k % (BK * o_kg) == 0 && pick_stages(p.bn, o_kg, p.mw) >= 2) p.kg = o_kg;
   p.kb = k / (BK * p.kg);
   p.units = tiles * p.kb;
-  p.grid = static_cast<int>(std::min<long long>(sms, p.units));
-  p.stages = pick_stages(p.bn, p.kg);
-  p.partial_bytes = static_cast<size_t>(p.grid) * 2 * p.bn * BM * sizeof(float);
+  p.grid = static_cast<int>(std::min<long long>(o_grid > 0 && o_grid <= sms ? o_grid : sms, p.units));
+  p.stages = pick_stages(p.bn, p.kg, p.mw);
+  p.partial_bytes = static_cast<size_t>(p.grid) * 2 * p.mw * p.bn * BM * sizeof(float);
   p.counter_bytes = COUNTER_BYTES;
   return p;
 }
@@ -928,8 +1029,8 @@ using namespace ls;
 
 extern "C" size_t ls_gemm_workspace_bytes(int rows, int k, int n_out) {
   if (rows <= 0 || k <= 0 || n_out <= 0) return 0;
-  const GemmPlan p = plan_gemm(rows, k, n_out);
-  return p.counter_bytes + p.partial_bytes;
+  const GemmPlan p = plan_gemm(rows, k, n_out, true), q = plan_gemm(rows, k, n_out, false);
+  return std::max(p.counter_bytes + p.partial_bytes, q.counter_bytes + q.partial_bytes);
 }
 
 namespace ls {
@@ -978,7 +1079,7 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
     default:
       return set_error(LS_ERR_INVALID, "ls_gemm: unknown epilogue %d", a->epilogue);
   }
-  GemmPlan p = plan_gemm(a->rows, a->k, a->n_out);
+  GemmPlan p = plan_gemm(a->rows, a->k, a->n_out, tp == nullptr);
   if (static_cast<long long>(p.m_tiles) * p.n_tiles > MAX_TILES)
     return set_error(LS_ERR_UNSUPPORTED, "ls_gemm: %d x %d tiles exceed the %d tile counters", p.m_tiles, p.n_tiles,
                      MAX_TILES);
@@ -1005,13 +1106,15 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
   kp.bn = p.bn;
   kp.n_tiles = p.n_tiles;
   kp.m_tiles = p.m_tiles;
+  kp.mw = p.mw;
+  kp.nacc = p.nacc;
   kp.kb = p.kb;
   kp.kg = p.kg;
   kp.units = p.units;
   kp.grid = p.grid;
   kp.stages = p.stages;
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(2 * p.bn)) cols <<= 1;
+  while (cols < static_cast<uint32_t>(p.nacc * p.mw * p.bn)) cols <<= 1;
   kp.tmem_cols = cols;
   kp.counters = reinterpret_cast<int*>(workspace);
   kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + p.counter_bytes);
@@ -1021,16 +1124,24 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
     kp.tp_oneshot = tp_oneshot(tp->world) ? 1 : 0;
   }
 
-  const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.stages);
-  static int configured_smem = 0;
-  if (configured_smem < static_cast<int>(smem)) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.mw, p.stages);
+  using GemmKernel = void (*)(CUtensorMap, CUtensorMap, GemmKernelParams);
+  static const GemmKernel kernels[] = {
+      gemm_tc_kernel<LS_EPI_STORE>,  gemm_tc_kernel<LS_EPI_SILU>,   gemm_tc_kernel<LS_EPI_RESIDUAL>,
+      gemm_tc_kernel<LS_EPI_QKV>,    gemm_tc_kernel<LS_EPI_GATEUP>, gemm_tc_kernel<LS_EPI_LMHEAD>,
+      gemm_tc_kernel<LS_EPI_MARKOV_ADD>};
+  static_assert(LS_EPI_STORE == 0 && LS_EPI_SILU == 1 && LS_EPI_RESIDUAL == 2 && LS_EPI_QKV == 3 &&
+                    LS_EPI_GATEUP == 4 && LS_EPI_LMHEAD == 5 && LS_EPI_MARKOV_ADD == 6,
+                "kernel table order");
+  const GemmKernel kernel = kernels[a->epilogue];
+  static bool configured[7] = {};
+  if (!configured[a->epilogue]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(227 * 1024));
     if (e != cudaSuccess) return set_cuda_error("ls_gemm: cudaFuncSetAttribute", e);
-    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return set_cuda_error("ls_gemm: carveout", e);
-    configured_smem = 227 * 1024;
+    configured[a->epilogue] = true;
   }
   // Programmatic dependent launch: the GEMM may start while the previous
   // kernel of the stream finishes; it prefetches weights, then waits for it.
@@ -1044,7 +1155,7 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map_w, map_x, kp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, map_w, map_x, kp);
   if (e != cudaSuccess) return set_cuda_error("ls_gemm: launch", e);
   return LS_OK;
 }
@@ -1089,7 +1200,7 @@ extern "C" int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_t
       (reinterpret_cast<uintptr_t>(a->out) & 15))
     return set_error(LS_ERR_INVALID,
                      "ls_gemm_allreduce: bad rows/n_out/out_ld (out 16-byte aligned, out_ld a multiple of 8)");
-  const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out);
+  const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out, false);
   if (static_cast<long long>(p.m_tiles) * p.n_tiles > TP_MAX_TILES)
     return set_error(LS_ERR_UNSUPPORTED, "ls_gemm_allreduce: %d x %d output tiles exceed %d", p.m_tiles, p.n_tiles,
                      TP_MAX_TILES);
