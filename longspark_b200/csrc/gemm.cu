@@ -244,6 +244,28 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
 #pragma unroll
       for (int j = 0; j < 16; ++j) sc->xch[r][j] = bf16_round(v[j]);
       epi_bar();
+      if (((reinterpret_cast<uintptr_t>(out) & 15) | (a.out_ld & 7)) == 0) {
+        // 16 tokens x 64 outputs staged as bf16 [16][64] over the scratch,
+        // then one 16-byte store a thread
+        float o[16];
+        if (r < 64) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = bf16_round(silu_f(sc->xch[r][j])) * sc->xch[r + 64][j];
+        }
+        epi_bar();
+        bf16* st = reinterpret_cast<bf16*>(&sc->xch[0][0]);
+        if (r < 64) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) st[j * 64 + r] = __float2bfloat16_rn(o[j]);
+        }
+        epi_bar();
+        const int tok = n0 + (r >> 3);
+        if (tok < rows)
+          *reinterpret_cast<uint4*>(out + (long long)tok * a.out_ld + m_tile * 64 + (r & 7) * 8) =
+              *reinterpret_cast<const uint4*>(st + (r >> 3) * 64 + (r & 7) * 8);
+        epi_bar();
+        break;
+      }
       if (r < 64) {
         const int f = m_tile * 64 + r;
 #pragma unroll
@@ -261,6 +283,51 @@ __device__ __forceinline__ void final_epilogue(const GemmKernelParams& P, int m_
     case LS_EPI_LMHEAD: {
       const int f = m_tile * BM + r;
       const int lane = threadIdx.x & 31;
+      if (((reinterpret_cast<uintptr_t>(out) & 15) | (a.out_ld & 7)) == 0) {
+        // bf16 logits staged as [16 tokens][128 features]: two 16-byte stores a
+        // thread, and each token's (max, lowest index) from 8 threads that scan
+        // 16 features each in order, then combine by shuffles
+        bf16* st = reinterpret_cast<bf16*>(&sc->xch[0][0]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) st[j * 128 + r] = __float2bfloat16_rn(v[j]);
+        epi_bar();
+#pragma unroll
+        for (int q = r; q < 256; q += 128) {
+          const int tok = n0 + (q >> 4);
+          if (tok < rows)
+            *reinterpret_cast<uint4*>(out + (long long)tok * a.out_ld + m_tile * BM + (q & 15) * 8) =
+                *reinterpret_cast<const uint4*>(st + (q >> 4) * 128 + (q & 15) * 8);
+        }
+        const int j = r >> 3, part = r & 7;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(st + j * 128 + part * 16);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(st + j * 128 + part * 16 + 8);
+        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float bv = __uint_as_float(wv[0] << 16);
+        int bi = part * 16;
+#pragma unroll
+        for (int i = 1; i < 16; ++i) {
+          const float x = __uint_as_float(i & 1 ? (wv[i >> 1] & 0xffff0000u) : (wv[i >> 1] << 16));
+          if (x > bv) {
+            bv = x;
+            bi = part * 16 + i;
+          }
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (part == 0 && n0 + j < rows) {
+          a.tile_max[(long long)(n0 + j) * P.m_tiles + m_tile] = bv;
+          a.tile_arg[(long long)(n0 + j) * P.m_tiles + m_tile] = m_tile * BM + bi;
+        }
+        epi_bar();
+        break;
+      }
       float y[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -598,18 +665,49 @@ __device__ __forceinline__ void reduce_tile(const GemmKernelParams& P, int t, in
   }
 }
 
-// Producer helpers: stage `st` receives unit u's KG k-blocks of weights (one
-// contiguous bulk copy from the tiled layout, or KG tensor-map boxes) and of
-// activations (KG tensor-map boxes).  The tensor maps stay in parameter space.
+// Position of a stream-K unit, advanced one unit at a time: the producer
+// thread issues a stage every few hundred cycles, and 64-bit divisions per
+// unit on that one thread were measurable (vocabulary projection at 480
+// tokens 667 -> 921 us with three of them per unit).
+struct UnitPos {
+  int kbi;     // unit within its work tile (k-blocks kbi * kg ...)
+  int n_tile;  // token tile
+  int m_work;  // work tile row (feature tiles m_work * mw ...)
+  int halves;  // feature tiles of this work tile
+  __device__ __forceinline__ void init(const GemmKernelParams& P, long long u) {
+    const int t = static_cast<int>(u / P.kb);
+    kbi = static_cast<int>(u - static_cast<long long>(t) * P.kb);
+    m_work = t / P.n_tiles;
+    n_tile = t - m_work * P.n_tiles;
+    set_halves(P);
+  }
+  __device__ __forceinline__ void set_halves(const GemmKernelParams& P) {
+    const int left = P.m_tiles - m_work * P.mw;
+    halves = left < P.mw ? left : P.mw;
+  }
+  __device__ __forceinline__ void next(const GemmKernelParams& P) {
+    if (++kbi == P.kb) {
+      kbi = 0;
+      if (++n_tile == P.n_tiles) {
+        n_tile = 0;
+        ++m_work;
+        set_halves(P);
+      }
+    }
+  }
+};
+
+// Producer helpers: stage `st` receives a unit's KG k-blocks of weights (one
+// contiguous bulk copy per feature tile from the tiled layout, or KG
+// tensor-map boxes) and of activations (KG tensor-map boxes).  The tensor
+// maps stay in parameter space.
 __device__ __forceinline__ void gemm_load_a(const GemmKernelParams& P, const CUtensorMap* map_w, const bf16* w_tiles,
                                             bool tiled_w, uint8_t* a_buf, int a_stage_bytes, uint64_t* full, int st,
-                                            long long u, uint64_t pol) {
-  const int t = static_cast<int>(u / P.kb);
-  const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
+                                            const UnitPos& q, uint64_t pol) {
+  const int kb0 = q.kbi * P.kg;
   const int half_bytes = P.kg * A_STAGE_BYTES;  // one feature tile's KG k-blocks
-  for (int h = 0; h < P.mw; ++h) {
-    const int m_tile = (t / P.n_tiles) * P.mw + h;
-    if (m_tile >= P.m_tiles) break;  // the last work tile of an odd count: one half
+  for (int h = 0; h < q.halves; ++h) {
+    const int m_tile = q.m_work * P.mw + h;
     uint8_t* dst = a_buf + st * a_stage_bytes + h * half_bytes;
     if (tiled_w) {
       // KG consecutive tiles of one row block are contiguous in the tiled layout
@@ -623,13 +721,12 @@ __device__ __forceinline__ void gemm_load_a(const GemmKernelParams& P, const CUt
 }
 
 __device__ __forceinline__ void gemm_load_b(const GemmKernelParams& P, const CUtensorMap* map_x, uint8_t* b_buf,
-                                            int b_stage_bytes, int b_blk_bytes, uint64_t* full, int st, long long u,
-                                            uint64_t pol) {
-  const int t = static_cast<int>(u / P.kb);
-  const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
-  const int n_tile = t % P.n_tiles;
+                                            int b_stage_bytes, int b_blk_bytes, uint64_t* full, int st,
+                                            const UnitPos& q, uint64_t pol) {
+  const int kb0 = q.kbi * P.kg;
   for (int j = 0; j < P.kg; ++j)
-    tma_load_2d(b_buf + st * b_stage_bytes + j * b_blk_bytes, map_x, &full[st], (kb0 + j) * BK, n_tile * P.bn, pol);
+    tma_load_2d(b_buf + st * b_stage_bytes + j * b_blk_bytes, map_x, &full[st], (kb0 + j) * BK, q.n_tile * P.bn,
+                pol);
 }
 
 template <int EPI>
@@ -708,20 +805,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // Weights do not depend on the previous kernel: fill the first stages with
       // weight tiles before waiting for it, then add the activation tiles.
       const int pre = static_cast<int>((u1 - u0) < S ? (u1 - u0) : S);
+      UnitPos q;
+      q.init(P, u0);
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], work_halves(P, static_cast<int>((u0 + i) / KB)) * a_half_bytes + b_stage_bytes);
-        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, i, u0 + i, pol_w);
+        mbar_arrive_expect_tx(&full[i], q.halves * a_half_bytes + b_stage_bytes);
+        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, i, q, pol_w);
+        q.next(P);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int i = 0; i < pre; ++i) gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, i, u0 + i, pol_x);
+      q.init(P, u0);
+      for (int i = 0; i < pre; ++i) {
+        gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, i, q, pol_x);
+        q.next(P);
+      }
       int stage = pre % S;
       uint32_t phase = pre == S ? 1u : 0u;
       long long issued = pre;
       for (long long u = u0 + pre; u < u1; ++u) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full[stage], work_halves(P, static_cast<int>(u / KB)) * a_half_bytes + b_stage_bytes);
-        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, stage, u, pol_w);
-        gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, u, pol_x);
+        mbar_arrive_expect_tx(&full[stage], q.halves * a_half_bytes + b_stage_bytes);
+        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, stage, q, pol_w);
+        gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, q, pol_x);
+        q.next(P);
         ++issued;
         if (++stage == S) {
           stage = 0;
@@ -930,29 +1035,14 @@ struct GemmPlan {
   size_t partial_bytes, counter_bytes;
 };
 
-// Work tiles of two feature tiles (256 weight rows against one token tile of
-// up to 256: the tile's operand bytes per MAC are two thirds of a 128-row
-// tile's).  LONGSPARK_B200_GEMM_WIDE: 0 never; 1 always, with the widest token
-// tile; 2 always, with the token tile plan_bn picks; unset: the measured rule
-// in wide_auto.
-static int wide_env() {
-  static int mode = -2;
-  if (mode == -2) {
-    const char* e = getenv("LONGSPARK_B200_GEMM_WIDE");
-    mode = (e != nullptr && e[0] >= '0' && e[0] <= '2') ? e[0] - '0' : -1;
-  }
-  return mode;
-}
-
-// Wide tiles pay off where there are enough of them to keep every SM on whole
-// tiles, or where long reductions make the split tiles' partials cheap
-// against the operand bytes saved.  Measured (B200, L2 flushed, wide / plain):
-// vocabulary 480 x 4096 x 151936 876 / 964 us, 1920 x 4096 x 24576 607 / 645,
-// 1920 x 12288 x 4096 275 / 344; slower with few tiles: 480 x 4096 x 6144
-// 115 / 76, 480 x 12288 x 4096 159 / 108, 480 x 4096 x 24576 211 / 203.
-static bool wide_auto(int rows, int k, int n_out, int sms) {
-  const long long tiles = static_cast<long long>(n_out / BM / 2) * ((rows + pick_bn(rows) - 1) / pick_bn(rows));
-  return tiles >= 4LL * sms || (k >= 8192 && 2 * tiles >= sms);
+// LONGSPARK_B200_GEMM_PLANNER=legacy: the token-tile rule of plan_bn for
+// every token count (one feature tile per work tile), for comparisons.
+static bool legacy_planner() {
+  static const bool v = [] {
+    const char* e = getenv("LONGSPARK_B200_GEMM_PLANNER");
+    return e != nullptr && strcmp(e, "legacy") == 0;
+  }();
+  return v;
 }
 
 // Next narrower token tile: half, rounded up to a multiple of 16 (the MMA N
@@ -962,7 +1052,8 @@ static int narrower_bn(int bn) {
   return h < 64 ? 64 : h;
 }
 
-// Token tile: as wide as the tokens (up to 256), narrowed while the grid would
+// Token tile of the fused-allreduce GEMMs, of GEMMs of up to 64 tokens and of
+// the legacy planner: as wide as the tokens (up to 256), narrowed while the grid would
 // have fewer output tiles than SMs (twice the SMs for k <= 1024): with few
 // tiles every tile is split along k, and the fp32 partial round trips of the
 // split tiles cost more than the extra weight re-reads of a narrower tile.
@@ -980,16 +1071,77 @@ static int plan_bn(int rows, int k, int n_out, int sms) {
   return bn;
 }
 
+// More than 64 tokens (up to 64 the GEMMs stream weights and keep the plan
+// above, and so do the fused-allreduce GEMMs): the plan with the lowest
+// modelled time among balanced token tiles (rows split into nt tiles of equal
+// width, rounded up to 16), one or two feature tiles per work tile, and
+// either one work tile per CTA (grid = tiles, no split tile) or stream-K over
+// every SM.  Model, fitted to 900 timed plans of the 8B drafter's GEMMs at
+// 120 / 480 / 1920 tokens on a B200 with L2 flushed (rms error 8.6%): a CTA
+// streams its k-blocks at 70.1 GB/s of operands, or at 0.66 MMA cycles per
+// token column of each feature tile plus 1577 / kg cycles per k-block,
+// whichever is longer; a launch with split tiles pays 127 ns per token
+// column of each feature tile for the fp32 partials; the last tile's
+// epilogue 199 ns per 16-token chunk of each feature tile, and with a single
+// accumulator buffer (two 128-row feature tiles of more than 128 tokens)
+// every earlier tile's epilogue 616 ns per chunk; 9.1 us fixed.
+struct ManyTokenPlan {
+  int bn, mw, kg, grid;
+};
+
+static double model_us(int rows, int k, int n_out, int sms, int bn, int mw, int kg, int grid) {
+  const long long tiles = static_cast<long long>((n_out / BM + mw - 1) / mw) * ((rows + bn - 1) / bn);
+  const long long units = tiles * (k / BK);  // k-blocks
+  const long long g = grid > 0 ? grid : std::min<long long>(sms, units / kg);
+  const long long nkb = (units / kg + g - 1) / g * kg;  // k-blocks of the busiest CTA
+  const bool split = grid > 0 ? false : !(tiles >= sms && tiles % sms == 0);
+  const double t_load = (mw * 16384.0 + bn * 128.0) / (70.08e3);  // us per k-block
+  const double t_mma = (0.6582 * mw * bn + 1576.9 / kg) / 1900.0;
+  const int chunks = (std::min(bn, rows) + 15) / 16;
+  const double tiles_per_cta = static_cast<double>(nkb) / (k / BK);
+  const double exposed = 2 * mw * bn > 512 ? 0.6155 * mw * chunks * std::max(0.0, tiles_per_cta - 1.0) : 0.0;
+  return 9.054 + nkb * std::max(t_load, t_mma) + 0.1988 * mw * chunks + (split ? 0.12706 * mw * bn : 0.0) + exposed;
+}
+
+static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms) {
+  ManyTokenPlan best{pick_bn(rows), 1, 1, 0};
+  double best_t = 1e30;
+  int prev_bn = 0;
+  for (int nt = (rows + 255) / 256; nt <= (rows + 63) / 64; ++nt) {
+    const int bn = ((rows + nt - 1) / nt + 15) / 16 * 16;
+    if (bn > 256 || bn == prev_bn) continue;
+    prev_bn = bn;
+    for (int mw = 1; mw <= (n_out >= 2 * BM ? 2 : 1); ++mw) {
+      const int kg = (k % (2 * BK) == 0 && pick_stages(bn, 2, mw) >= 2) ? 2 : 1;
+      const long long tiles = static_cast<long long>((n_out / BM + mw - 1) / mw) * ((rows + bn - 1) / bn);
+      if (tiles > MAX_TILES) continue;
+      for (int dp = 0; dp < 2; ++dp) {
+        if (dp && tiles > sms) continue;
+        const int grid = dp ? static_cast<int>(tiles) : 0;
+        const double t = model_us(rows, k, n_out, sms, bn, mw, kg, grid);
+        if (t < best_t) {
+          best_t = t;
+          best = {bn, mw, kg, grid};
+        }
+      }
+    }
+  }
+  return best;
+}
+
 static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide) {
   GemmPlan p{};
   const int sms = host_sm_count();
-  int wide = 0;
-  if (allow_wide && rows > 128 && n_out >= 2 * BM) {
-    wide = wide_env();
-    if (wide < 0) wide = wide_auto(rows, k, n_out, sms) ? 1 : 0;
+  int model_kg = 0, model_grid = 0;
+  p.bn = plan_bn(rows, k, n_out, sms);
+  p.mw = 1;
+  if (allow_wide && rows > 64 && !legacy_planner()) {
+    const ManyTokenPlan m = plan_many_tokens(rows, k, n_out, sms);
+    p.bn = m.bn;
+    p.mw = m.mw;
+    model_kg = m.kg;
+    model_grid = m.grid;
   }
-  p.bn = wide == 1 ? pick_bn(rows) : plan_bn(rows, k, n_out, sms);
-  p.mw = wide ? 2 : 1;
   // Tuning override, LONGSPARK_B200_GEMM_PLAN="bn,kg,mw,grid" (0 keeps the
   // planned value; read at every call so one process can sweep plans).
   int o_bn = 0, o_kg = 0, o_mw = 0, o_grid = 0;
@@ -1012,6 +1164,10 @@ static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide) {
     if (tiles * (k / (BK * kg)) < 4LL * sms) continue;
     p.kg = kg;
     break;
+  }
+  if (model_kg > 0 && o_bn == 0 && o_mw == 0) {
+    p.kg = model_kg;
+    if (o_grid == 0) o_grid = model_grid;
   }
   if ((o_kg == 1 || o_kg == 2 || o_kg == 4) && k % (BK * o_kg) == 0 && pick_stages(p.bn, o_kg, p.mw) >= 2) p.kg = o_kg;
   p.kb = k / (BK * p.kg);
@@ -1080,9 +1236,9 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
       return set_error(LS_ERR_INVALID, "ls_gemm: unknown epilogue %d", a->epilogue);
   }
   GemmPlan p = plan_gemm(a->rows, a->k, a->n_out, tp == nullptr);
-  if (static_cast<long long>(p.m_tiles) * p.n_tiles > MAX_TILES)
-    return set_error(LS_ERR_UNSUPPORTED, "ls_gemm: %d x %d tiles exceed the %d tile counters", p.m_tiles, p.n_tiles,
-                     MAX_TILES);
+  if (static_cast<long long>((p.m_tiles + p.mw - 1) / p.mw) * p.n_tiles > MAX_TILES)
+    return set_error(LS_ERR_UNSUPPORTED, "ls_gemm: %d x %d work tiles exceed the %d tile counters",
+                     (p.m_tiles + p.mw - 1) / p.mw, p.n_tiles, MAX_TILES);
   if (workspace == nullptr || workspace_bytes < p.counter_bytes + p.partial_bytes)
     return set_error(LS_ERR_WORKSPACE, "ls_gemm: workspace %zu < %zu bytes", workspace_bytes,
                      p.counter_bytes + p.partial_bytes);
