@@ -729,7 +729,38 @@ __device__ __forceinline__ void gemm_load_b(const GemmKernelParams& P, const CUt
                 pol);
 }
 
-template <int EPI>
+// The same copies addressed from the unit index, for the kernel instances
+// that stream weights (tiled weights, token tiles of at most 32).  Measured in
+// the batch-1 round (CUDA graph, programmatic launches): ~9 us faster for the
+// vocabulary projection (15 tokens) with the producer in exactly this form --
+// per-unit divisions, the feature-tile loop and the expected bytes from
+// work_halves -- than with UnitPos or with this form without those steps
+// (427 us against 420 us per round); in isolation within 2%.  The cause was
+// not found: a plain delay between the wait and the copies, the order of the
+// copies, a non-inlined producer and 32-bit divisions did not reproduce it.
+__device__ __forceinline__ void gemm_load_a_u(const GemmKernelParams& P, const bf16* w_tiles, uint8_t* a_buf,
+                                              int a_stage_bytes, uint64_t* full, int st, long long u, uint64_t pol) {
+  const int t = static_cast<int>(u / P.kb);
+  const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
+  const int half_bytes = P.kg * A_STAGE_BYTES;
+  for (int h = 0; h < P.mw; ++h) {
+    const int m_tile = (t / P.n_tiles) * P.mw + h;
+    if (m_tile >= P.m_tiles) break;
+    bulk_load(a_buf + st * a_stage_bytes + h * half_bytes,
+              w_tiles + (static_cast<long long>(m_tile) * P.kb * P.kg + kb0) * (BM * BK), half_bytes, &full[st], pol);
+  }
+}
+__device__ __forceinline__ void gemm_load_b_u(const GemmKernelParams& P, const CUtensorMap* map_x, uint8_t* b_buf,
+                                              int b_stage_bytes, int b_blk_bytes, uint64_t* full, int st, long long u,
+                                              uint64_t pol) {
+  const int t = static_cast<int>(u / P.kb);
+  const int kb0 = static_cast<int>(u - static_cast<long long>(t) * P.kb) * P.kg;
+  const int n_tile = t % P.n_tiles;
+  for (int j = 0; j < P.kg; ++j)
+    tma_load_2d(b_buf + st * b_stage_bytes + j * b_blk_bytes, map_x, &full[st], (kb0 + j) * BK, n_tile * P.bn, pol);
+}
+
+template <int EPI, bool BY_INDEX>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ GemmKernelParams P) {
@@ -805,32 +836,53 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // Weights do not depend on the previous kernel: fill the first stages with
       // weight tiles before waiting for it, then add the activation tiles.
       const int pre = static_cast<int>((u1 - u0) < S ? (u1 - u0) : S);
-      UnitPos q;
-      q.init(P, u0);
-      for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], q.halves * a_half_bytes + b_stage_bytes);
-        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, i, q, pol_w);
-        q.next(P);
-      }
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      q.init(P, u0);
-      for (int i = 0; i < pre; ++i) {
-        gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, i, q, pol_x);
-        q.next(P);
-      }
       int stage = pre % S;
       uint32_t phase = pre == S ? 1u : 0u;
       long long issued = pre;
-      for (long long u = u0 + pre; u < u1; ++u) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&full[stage], q.halves * a_half_bytes + b_stage_bytes);
-        gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, stage, q, pol_w);
-        gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, q, pol_x);
-        q.next(P);
-        ++issued;
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+      if constexpr (BY_INDEX) {
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], work_halves(P, static_cast<int>((u0 + i) / KB)) * a_half_bytes + b_stage_bytes);
+          gemm_load_a_u(P, w_tiles, a_buf, a_stage_bytes, full, i, u0 + i, pol_w);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int i = 0; i < pre; ++i)
+          gemm_load_b_u(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, i, u0 + i, pol_x);
+        for (long long u = u0 + pre; u < u1; ++u) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full[stage], work_halves(P, static_cast<int>(u / KB)) * a_half_bytes + b_stage_bytes);
+          gemm_load_a_u(P, w_tiles, a_buf, a_stage_bytes, full, stage, u, pol_w);
+          gemm_load_b_u(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, u, pol_x);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      } else {
+        UnitPos q;
+        q.init(P, u0);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], q.halves * a_half_bytes + b_stage_bytes);
+          gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, i, q, pol_w);
+          q.next(P);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        q.init(P, u0);
+        for (int i = 0; i < pre; ++i) {
+          gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, i, q, pol_x);
+          q.next(P);
+        }
+        for (long long u = u0 + pre; u < u1; ++u) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, LS_DEV_TIMEOUT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full[stage], q.halves * a_half_bytes + b_stage_bytes);
+          gemm_load_a(P, &map_w, w_tiles, tiled_w, a_buf, a_stage_bytes, full, stage, q, pol_w);
+          gemm_load_b(P, &map_x, b_buf, b_stage_bytes, b_blk_bytes, full, stage, q, pol_x);
+          q.next(P);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
       if (*abort_flag) {
@@ -1282,22 +1334,28 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
 
   const size_t smem = gemm_smem_bytes(p.bn, p.kg, p.mw, p.stages);
   using GemmKernel = void (*)(CUtensorMap, CUtensorMap, GemmKernelParams);
-  static const GemmKernel kernels[] = {
-      gemm_tc_kernel<LS_EPI_STORE>,  gemm_tc_kernel<LS_EPI_SILU>,   gemm_tc_kernel<LS_EPI_RESIDUAL>,
-      gemm_tc_kernel<LS_EPI_QKV>,    gemm_tc_kernel<LS_EPI_GATEUP>, gemm_tc_kernel<LS_EPI_LMHEAD>,
-      gemm_tc_kernel<LS_EPI_MARKOV_ADD>};
+  static const GemmKernel kernels[2][7] = {
+      {gemm_tc_kernel<LS_EPI_STORE, false>, gemm_tc_kernel<LS_EPI_SILU, false>,
+       gemm_tc_kernel<LS_EPI_RESIDUAL, false>, gemm_tc_kernel<LS_EPI_QKV, false>,
+       gemm_tc_kernel<LS_EPI_GATEUP, false>, gemm_tc_kernel<LS_EPI_LMHEAD, false>,
+       gemm_tc_kernel<LS_EPI_MARKOV_ADD, false>},
+      {gemm_tc_kernel<LS_EPI_STORE, true>, gemm_tc_kernel<LS_EPI_SILU, true>, gemm_tc_kernel<LS_EPI_RESIDUAL, true>,
+       gemm_tc_kernel<LS_EPI_QKV, true>, gemm_tc_kernel<LS_EPI_GATEUP, true>, gemm_tc_kernel<LS_EPI_LMHEAD, true>,
+       gemm_tc_kernel<LS_EPI_MARKOV_ADD, true>}};
   static_assert(LS_EPI_STORE == 0 && LS_EPI_SILU == 1 && LS_EPI_RESIDUAL == 2 && LS_EPI_QKV == 3 &&
                     LS_EPI_GATEUP == 4 && LS_EPI_LMHEAD == 5 && LS_EPI_MARKOV_ADD == 6,
                 "kernel table order");
-  const GemmKernel kernel = kernels[a->epilogue];
-  static bool configured[7] = {};
-  if (!configured[a->epilogue]) {
+  // weight streaming: tiled weights, one feature tile per work tile, token tiles of at most 32
+  const int by_index = (a->w_layout == LS_W_TILED && p.mw == 1 && p.bn <= 32) ? 1 : 0;
+  const GemmKernel kernel = kernels[by_index][a->epilogue];
+  static bool configured[2][7] = {};
+  if (!configured[by_index][a->epilogue]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(227 * 1024));
     if (e != cudaSuccess) return set_cuda_error("ls_gemm: cudaFuncSetAttribute", e);
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return set_cuda_error("ls_gemm: carveout", e);
-    configured[a->epilogue] = true;
+    configured[by_index][a->epilogue] = true;
   }
   // Programmatic dependent launch: the GEMM may start while the previous
   // kernel of the stream finishes; it prefetches weights, then waits for it.
