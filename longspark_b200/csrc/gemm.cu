@@ -1126,17 +1126,23 @@ static int plan_bn(int rows, int k, int n_out, int sms) {
 // More than 64 tokens (up to 64 the GEMMs stream weights and keep the plan
 // above, and so do the fused-allreduce GEMMs): the plan with the lowest
 // modelled time among balanced token tiles (rows split into nt tiles of equal
-// width, rounded up to 16), one or two feature tiles per work tile, and
-// either one work tile per CTA (grid = tiles, no split tile) or stream-K over
-// every SM.  Model, fitted to 900 timed plans of the 8B drafter's GEMMs at
-// 120 / 480 / 1920 tokens on a B200 with L2 flushed (rms error 8.6%): a CTA
-// streams its k-blocks at 70.1 GB/s of operands, or at 0.66 MMA cycles per
-// token column of each feature tile plus 1577 / kg cycles per k-block,
-// whichever is longer; a launch with split tiles pays 127 ns per token
-// column of each feature tile for the fp32 partials; the last tile's
-// epilogue 199 ns per 16-token chunk of each feature tile, and with a single
-// accumulator buffer (two 128-row feature tiles of more than 128 tokens)
-// every earlier tile's epilogue 616 ns per chunk; 9.1 us fixed.
+// width, rounded up to 16), one or two feature tiles per work tile, 1, 2 or 4
+// k-blocks per stage, and either one work tile per CTA (grid = tiles, no
+// split tile) or stream-K over every SM.  Model, fitted to ~1,400 timed plans
+// of the 8B drafter's GEMMs (STORE epilogue) at 120 / 480 / 1920 tokens on a
+// B200 with L2 flushed (rms error 14%; the picks are within 1% of the best
+// timed plan summed over the 18 shapes): a CTA streams its k-blocks at
+// 75.4 GB/s of operands, or at 0.21 MMA cycles per token column of each
+// feature tile plus 854 / kg cycles per k-block, whichever is longer; a launch
+// with split tiles pays 142 ns per token column of each feature tile for the
+// fp32 partials; with a single accumulator buffer (two feature tiles of more
+// than 128 tokens) every tile's epilogue but the last is exposed, 487 ns per
+// 16-token chunk of each feature tile; 7.3 us fixed.  The QKV and SwiGLU
+// epilogues cost several times the STORE one and do not fit this model with
+// two feature tiles per work tile (measured at 1920 tokens, gate/up with the
+// SwiGLU epilogue: 601 us for 240 tokens x 2 feature tiles, 544 us for 128 x
+// 2, 442 us for 240 x 1; the STORE epilogue 390 / 504 / 405 us), so for them
+// only one feature tile per work tile is considered.
 struct ManyTokenPlan {
   int bn, mw, kg, grid;
 };
@@ -1147,15 +1153,15 @@ static double model_us(int rows, int k, int n_out, int sms, int bn, int mw, int 
   const long long g = grid > 0 ? grid : std::min<long long>(sms, units / kg);
   const long long nkb = (units / kg + g - 1) / g * kg;  // k-blocks of the busiest CTA
   const bool split = grid > 0 ? false : !(tiles >= sms && tiles % sms == 0);
-  const double t_load = (mw * 16384.0 + bn * 128.0) / (70.08e3);  // us per k-block
-  const double t_mma = (0.6582 * mw * bn + 1576.9 / kg) / 1900.0;
+  const double t_load = (mw * 16384.0 + bn * 128.0) / (75.35e3);  // us per k-block
+  const double t_mma = (0.2112 * mw * bn + 854.3 / kg) / 1900.0;
   const int chunks = (std::min(bn, rows) + 15) / 16;
   const double tiles_per_cta = static_cast<double>(nkb) / (k / BK);
-  const double exposed = 2 * mw * bn > 512 ? 0.6155 * mw * chunks * std::max(0.0, tiles_per_cta - 1.0) : 0.0;
-  return 9.054 + nkb * std::max(t_load, t_mma) + 0.1988 * mw * chunks + (split ? 0.12706 * mw * bn : 0.0) + exposed;
+  const double exposed = 2 * mw * bn > 512 ? 0.4869 * mw * chunks * std::max(0.0, tiles_per_cta - 1.0) : 0.0;
+  return 7.282 + nkb * std::max(t_load, t_mma) + (split ? 0.14188 * mw * bn : 0.0) + exposed;
 }
 
-static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms) {
+static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms, bool heavy_epilogue) {
   ManyTokenPlan best{pick_bn(rows), 1, 1, 0};
   double best_t = 1e30;
   int prev_bn = 0;
@@ -1164,16 +1170,19 @@ static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms) {
     if (bn > 256 || bn == prev_bn) continue;
     prev_bn = bn;
     for (int mw = 1; mw <= (n_out >= 2 * BM ? 2 : 1); ++mw) {
-      const int kg = (k % (2 * BK) == 0 && pick_stages(bn, 2, mw) >= 2) ? 2 : 1;
+      if (heavy_epilogue && mw == 2) continue;
       const long long tiles = static_cast<long long>((n_out / BM + mw - 1) / mw) * ((rows + bn - 1) / bn);
       if (tiles > MAX_TILES) continue;
-      for (int dp = 0; dp < 2; ++dp) {
-        if (dp && tiles > sms) continue;
-        const int grid = dp ? static_cast<int>(tiles) : 0;
-        const double t = model_us(rows, k, n_out, sms, bn, mw, kg, grid);
-        if (t < best_t) {
-          best_t = t;
-          best = {bn, mw, kg, grid};
+      for (int kg = 1; kg <= 4; kg <<= 1) {
+        if (k % (kg * BK) || pick_stages(bn, kg, mw) < 2) continue;
+        for (int dp = 0; dp < 2; ++dp) {
+          if (dp && tiles > sms) continue;
+          const int grid = dp ? static_cast<int>(tiles) : 0;
+          const double t = model_us(rows, k, n_out, sms, bn, mw, kg, grid);
+          if (t < best_t) {
+            best_t = t;
+            best = {bn, mw, kg, grid};
+          }
         }
       }
     }
@@ -1181,14 +1190,15 @@ static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms) {
   return best;
 }
 
-static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide) {
+// heavy_epilogue: LS_EPI_QKV or LS_EPI_GATEUP (see plan_many_tokens).
+static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide, bool heavy_epilogue) {
   GemmPlan p{};
   const int sms = host_sm_count();
   int model_kg = 0, model_grid = 0;
   p.bn = plan_bn(rows, k, n_out, sms);
   p.mw = 1;
   if (allow_wide && rows > 64 && !legacy_planner()) {
-    const ManyTokenPlan m = plan_many_tokens(rows, k, n_out, sms);
+    const ManyTokenPlan m = plan_many_tokens(rows, k, n_out, sms, heavy_epilogue);
     p.bn = m.bn;
     p.mw = m.mw;
     model_kg = m.kg;
@@ -1237,8 +1247,12 @@ using namespace ls;
 
 extern "C" size_t ls_gemm_workspace_bytes(int rows, int k, int n_out) {
   if (rows <= 0 || k <= 0 || n_out <= 0) return 0;
-  const GemmPlan p = plan_gemm(rows, k, n_out, true), q = plan_gemm(rows, k, n_out, false);
-  return std::max(p.counter_bytes + p.partial_bytes, q.counter_bytes + q.partial_bytes);
+  // the largest of the plans an epilogue or the fused allreduce can pick
+  size_t need = 0;
+  for (const GemmPlan& p : {plan_gemm(rows, k, n_out, true, false), plan_gemm(rows, k, n_out, true, true),
+                            plan_gemm(rows, k, n_out, false, false)})
+    need = std::max(need, p.counter_bytes + p.partial_bytes);
+  return need;
 }
 
 namespace ls {
@@ -1287,7 +1301,8 @@ static int gemm_launch(void* stream, const ls_gemm_args* a, void* workspace, siz
     default:
       return set_error(LS_ERR_INVALID, "ls_gemm: unknown epilogue %d", a->epilogue);
   }
-  GemmPlan p = plan_gemm(a->rows, a->k, a->n_out, tp == nullptr);
+  GemmPlan p = plan_gemm(a->rows, a->k, a->n_out, tp == nullptr,
+                         a->epilogue == LS_EPI_QKV || a->epilogue == LS_EPI_GATEUP);
   if (static_cast<long long>((p.m_tiles + p.mw - 1) / p.mw) * p.n_tiles > MAX_TILES)
     return set_error(LS_ERR_UNSUPPORTED, "ls_gemm: %d x %d work tiles exceed the %d tile counters",
                      (p.m_tiles + p.mw - 1) / p.mw, p.n_tiles, MAX_TILES);
@@ -1414,7 +1429,7 @@ extern "C" int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_t
       (reinterpret_cast<uintptr_t>(a->out) & 15))
     return set_error(LS_ERR_INVALID,
                      "ls_gemm_allreduce: bad rows/n_out/out_ld (out 16-byte aligned, out_ld a multiple of 8)");
-  const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out, false);
+  const GemmPlan p = plan_gemm(a->rows, a->k > 0 ? a->k : BK, a->n_out, false, false);
   if (static_cast<long long>(p.m_tiles) * p.n_tiles > TP_MAX_TILES)
     return set_error(LS_ERR_UNSUPPORTED, "ls_gemm_allreduce: %d x %d output tiles exceed %d", p.m_tiles, p.n_tiles,
                      TP_MAX_TILES);
