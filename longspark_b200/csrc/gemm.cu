@@ -1104,8 +1104,7 @@ static int narrower_bn(int bn) {
   return h < 64 ? 64 : h;
 }
 
-// Token tile of the fused-allreduce GEMMs, of GEMMs of up to 64 tokens and of
-// the legacy planner: as wide as the tokens (up to 256), narrowed while the grid would
+// Token tile of GEMMs of up to 64 tokens and of the legacy planner: as wide as the tokens (up to 256), narrowed while the grid would
 // have fewer output tiles than SMs (twice the SMs for k <= 1024): with few
 // tiles every tile is split along k, and the fp32 partial round trips of the
 // split tiles cost more than the extra weight re-reads of a narrower tile.
@@ -1124,7 +1123,7 @@ static int plan_bn(int rows, int k, int n_out, int sms) {
 }
 
 // More than 64 tokens (up to 64 the GEMMs stream weights and keep the plan
-// above, and so do the fused-allreduce GEMMs): the plan with the lowest
+// above): the plan with the lowest
 // modelled time among balanced token tiles (rows split into nt tiles of equal
 // width, rounded up to 16), one or two feature tiles per work tile, 1, 2 or 4
 // k-blocks per stage, and either one work tile per CTA (grid = tiles, no
@@ -1197,8 +1196,10 @@ static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide, bool heav
   int model_kg = 0, model_grid = 0;
   p.bn = plan_bn(rows, k, n_out, sms);
   p.mw = 1;
-  if (allow_wide && rows > 64 && !legacy_planner()) {
-    const ManyTokenPlan m = plan_many_tokens(rows, k, n_out, sms, heavy_epilogue);
+  if (rows > 64 && !legacy_planner()) {
+    // the fused-allreduce GEMMs (allow_wide false) keep one feature tile per
+    // work tile: their exchange is per 128-row tile
+    const ManyTokenPlan m = plan_many_tokens(rows, k, n_out, sms, heavy_epilogue || !allow_wide);
     p.bn = m.bn;
     p.mw = m.mw;
     model_kg = m.kg;
@@ -1399,17 +1400,17 @@ extern "C" size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire) {
   if (world < 1 || world > LS_TP_MAX_RANKS || rows <= 0 || n_out <= 0 || n_out % BM ||
       (wire != LS_TP_WIRE_F32 && wire != LS_TP_WIRE_BF16))
     return 0;
-  // the exchange slots of any token tile the plan can pick for these rows
-  // (plan_bn narrows pick_bn down to 64 depending on k)
+  // the exchange slots of any token tile a plan can pick for these rows (every
+  // multiple of 16 up to pick_bn: the token-tile rule narrows down to 64, the
+  // many-token planner splits the rows into equal tiles)
   size_t need = 0;
-  for (int bn = pick_bn(rows);; bn = narrower_bn(bn)) {
+  for (int bn = 16; bn <= pick_bn(rows); bn += 16) {
     const long long tiles = static_cast<long long>(n_out / BM) * ((rows + bn - 1) / bn);
     const long long owned = (tiles + world - 1) / world;
     const size_t tile_bytes = static_cast<size_t>(bn) * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);
     const size_t b = tp_oneshot(world) ? 2 * static_cast<size_t>(tiles) * world * tile_bytes
                                        : static_cast<size_t>(owned) * world * tile_bytes;
     need = b > need ? b : need;
-    if (bn <= 64) break;
   }
   return TP_XCH_OFF + need;
 }

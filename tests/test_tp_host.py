@@ -165,10 +165,11 @@ def test_tp_entry_points_validate_without_gpu():
     assert lib.ls_tp_sync_bytes(9, 480, 5120, 0) == 0
     assert lib.ls_tp_sync_bytes(2, 480, 5000, 0) == 0  # n_out not a multiple of 128
     assert lib.ls_tp_sync_bytes(2, 480, 5120, 7) == 0  # unknown wire format
-    # exchange slots: ceil(tiles / world) * world slots of one 256-token tile each
-    tiles = 40 * 2
-    assert lib.ls_tp_sync_bytes(8, 480, 5120, 0) - lib.ls_tp_sync_bytes(8, 480, 5120, 1) == \
-        (tiles + 7) // 8 * 8 * 256 * 128 * 2
+    # exchange slots: ceil(tiles / world) * world slots of one token tile each,
+    # for the widest need over every token tile a plan can pick (multiples of 16
+    # up to 256 for 480 rows)
+    need = max(-(-(40 * -(-480 // bn)) // 8) * 8 * bn * 128 for bn in range(16, 257, 16))
+    assert lib.ls_tp_sync_bytes(8, 480, 5120, 0) - lib.ls_tp_sync_bytes(8, 480, 5120, 1) == need * 2
     g = N.TpGroup(world=0, rank=0, heap=(C.c_void_p * 8)(), heap_bytes=1 << 20, sync_offset=0)
     a = N.GemmArgs()
     assert lib.ls_gemm_allreduce(None, C.byref(a), C.byref(g), 0, None, 0) == 1
