@@ -106,6 +106,30 @@ typedef struct ls_gemm_args {
  * all GEMMs issued on the same stream. */
 LS_API size_t ls_gemm_workspace_bytes(int rows, int k, int n_out);
 
+/* The plan ls_gemm (fused_allreduce = 0) or ls_gemm_allreduce
+ * (fused_allreduce = 1, `world` ranks, LS_TP_WIRE_* `wire` partials) picks
+ * for a shape and epilogue on the current device (148 SMs assumed without
+ * one), and what it needs: shared memory per CTA, TMEM columns, the GEMM
+ * workspace, the exchange region.  kernel_weight_streaming: the instance with
+ * the indexed producer runs (with tiled weights).  No counterpart in the
+ * reference: it exists to inspect and test the planner without a GPU. */
+typedef struct ls_gemm_plan {
+  int bn;                      /* token tile                                    */
+  int mw;                      /* 128-row feature tiles per work tile (1 or 2)  */
+  int kg;                      /* k-blocks of 64 per pipeline stage             */
+  int stages;
+  int grid;                    /* CTAs                                          */
+  int n_tiles, m_tiles;        /* token tiles, feature tiles                    */
+  int kernel_weight_streaming;
+  long long units;             /* stream-K units (work tiles x k-steps)         */
+  size_t smem_bytes;           /* dynamic shared memory per CTA                 */
+  size_t tmem_cols;
+  size_t workspace_bytes;      /* counters + fp32 partials this plan uses       */
+  size_t tp_sync_bytes;        /* fused: exchange region this plan uses, else 0 */
+} ls_gemm_plan;
+LS_API int ls_gemm_plan_info(int rows, int k, int n_out, int epilogue, int fused_allreduce, int world, int wire,
+                             ls_gemm_plan* out);
+
 /* Re-lay a row-major [n_out, k] bf16 weight matrix (n_out % 128 == 0,
  * k % 64 == 0) into the LS_W_TILED layout: 128 x 64 tiles stored
  * contiguously in (row tile, k tile) order, each already in the 128-byte

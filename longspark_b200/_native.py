@@ -80,6 +80,12 @@ class PrefillArgs(C.Structure):
                 ("q_heads", i32), ("kv_heads", i32), ("slots_per_head", i32), ("softmax_scale", f32), ("status", vp)]
 
 
+class GemmPlan(C.Structure):
+    _fields_ = [("bn", i32), ("mw", i32), ("kg", i32), ("stages", i32), ("grid", i32), ("n_tiles", i32),
+                ("m_tiles", i32), ("kernel_weight_streaming", i32), ("units", C.c_longlong), ("smem_bytes", sz),
+                ("tmem_cols", sz), ("workspace_bytes", sz), ("tp_sync_bytes", sz)]
+
+
 class TpGroup(C.Structure):
     _fields_ = [("world", i32), ("rank", i32), ("heap", vp * TP_MAX_RANKS), ("heap_bytes", sz), ("sync_offset", sz)]
 
@@ -121,6 +127,7 @@ SIGNATURES = {
     "ls_last_error": (C.c_char_p, []),
     "ls_device_sm_count": (i32, []),
     "ls_gemm_workspace_bytes": (sz, [i32, i32, i32]),
+    "ls_gemm_plan_info": (i32, [i32, i32, i32, i32, i32, i32, i32, C.POINTER(GemmPlan)]),
     "ls_gemm": (i32, [vp, C.POINTER(GemmArgs), vp, sz]),
     "ls_tile_weight": (i32, [vp, vp, vp, i32, i32]),
     "ls_position_scores": (i32, [vp, vp, i64, i64, vp, vp, i32, i32, i32, i32, i32, f32]),

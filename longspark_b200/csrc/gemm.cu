@@ -1415,6 +1415,41 @@ extern "C" size_t ls_tp_sync_bytes(int world, int rows, int n_out, int wire) {
   return TP_XCH_OFF + need;
 }
 
+extern "C" int ls_gemm_plan_info(int rows, int k, int n_out, int epilogue, int fused_allreduce, int world, int wire,
+                                 ls_gemm_plan* out) {
+  if (out == nullptr) return set_error(LS_ERR_INVALID, "ls_gemm_plan_info: null out");
+  if (rows <= 0 || k <= 0 || k % BK || n_out <= 0 || n_out % BM || epilogue < LS_EPI_STORE ||
+      epilogue > LS_EPI_MARKOV_ADD)
+    return set_error(LS_ERR_INVALID, "ls_gemm_plan_info: rows>0, k%%64==0, n_out%%128==0 and a known epilogue required");
+  if (fused_allreduce && (world < 1 || world > LS_TP_MAX_RANKS || (wire != LS_TP_WIRE_F32 && wire != LS_TP_WIRE_BF16)))
+    return set_error(LS_ERR_INVALID, "ls_gemm_plan_info: bad world or wire for a fused plan");
+  const bool fused = fused_allreduce != 0 && world > 1;
+  const GemmPlan p = plan_gemm(rows, k, n_out, !fused, epilogue == LS_EPI_QKV || epilogue == LS_EPI_GATEUP);
+  memset(out, 0, sizeof(*out));
+  out->bn = p.bn;
+  out->mw = p.mw;
+  out->kg = p.kg;
+  out->stages = p.stages;
+  out->grid = p.grid;
+  out->n_tiles = p.n_tiles;
+  out->m_tiles = p.m_tiles;
+  out->kernel_weight_streaming = (!fused && p.mw == 1 && p.bn <= 32) ? 1 : 0;
+  out->units = p.units;
+  out->smem_bytes = gemm_smem_bytes(p.bn, p.kg, p.mw, p.stages);
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(p.nacc * p.mw * p.bn)) cols <<= 1;
+  out->tmem_cols = cols;
+  out->workspace_bytes = p.counter_bytes + p.partial_bytes;
+  if (fused) {
+    const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+    const long long owned = (tiles + world - 1) / world;
+    const size_t tile_bytes = static_cast<size_t>(p.bn) * BM * (wire == LS_TP_WIRE_BF16 ? 2 : 4);
+    out->tp_sync_bytes = TP_XCH_OFF + (tp_oneshot(world) ? 2 * static_cast<size_t>(tiles) * world * tile_bytes
+                                                         : static_cast<size_t>(owned) * world * tile_bytes);
+  }
+  return LS_OK;
+}
+
 extern "C" int ls_gemm_allreduce(void* stream, const ls_gemm_args* a, const ls_tp_group* g, int wire, void* workspace,
                                  size_t workspace_bytes) {
   TpView v;

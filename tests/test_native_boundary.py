@@ -51,7 +51,8 @@ def test_struct_layouts_match_the_header(lib):
                       ("ls_attention_args", N.AttentionArgs), ("ls_markov_args", N.MarkovArgs),
                       ("ls_prefill_args", N.PrefillArgs), ("ls_tp_group", N.TpGroup),
                       ("ls_sample_step_args", N.SampleStepArgs), ("ls_export_args", N.ExportArgs),
-                      ("ls_round_layer", N.RoundLayer), ("ls_round_args", N.RoundArgs)):
+                      ("ls_round_layer", N.RoundLayer), ("ls_round_args", N.RoundArgs),
+                      ("ls_gemm_plan", N.GemmPlan)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         body = re.sub(r"\[[^\]]*\]", "", body)  # array declarators: the name is what precedes them
