@@ -1160,7 +1160,7 @@ static double model_us(int rows, int k, int n_out, int sms, int bn, int mw, int 
   return 7.282 + nkb * std::max(t_load, t_mma) + (split ? 0.14188 * mw * bn : 0.0) + exposed;
 }
 
-static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms, bool heavy_epilogue) {
+static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms, bool heavy_epilogue, long long max_tiles) {
   ManyTokenPlan best{pick_bn(rows), 1, 1, 0};
   double best_t = 1e30;
   int prev_bn = 0;
@@ -1171,7 +1171,7 @@ static ManyTokenPlan plan_many_tokens(int rows, int k, int n_out, int sms, bool 
     for (int mw = 1; mw <= (n_out >= 2 * BM ? 2 : 1); ++mw) {
       if (heavy_epilogue && mw == 2) continue;
       const long long tiles = static_cast<long long>((n_out / BM + mw - 1) / mw) * ((rows + bn - 1) / bn);
-      if (tiles > MAX_TILES) continue;
+      if (tiles > max_tiles) continue;
       for (int kg = 1; kg <= 4; kg <<= 1) {
         if (k % (kg * BK) || pick_stages(bn, kg, mw) < 2) continue;
         for (int dp = 0; dp < 2; ++dp) {
@@ -1199,7 +1199,8 @@ static GemmPlan plan_gemm(int rows, int k, int n_out, bool allow_wide, bool heav
   if (rows > 64 && !legacy_planner()) {
     // the fused-allreduce GEMMs (allow_wide false) keep one feature tile per
     // work tile: their exchange is per 128-row tile
-    const ManyTokenPlan m = plan_many_tokens(rows, k, n_out, sms, heavy_epilogue || !allow_wide);
+    const ManyTokenPlan m =
+        plan_many_tokens(rows, k, n_out, sms, heavy_epilogue || !allow_wide, allow_wide ? MAX_TILES : TP_MAX_TILES);
     p.bn = m.bn;
     p.mw = m.mw;
     model_kg = m.kg;

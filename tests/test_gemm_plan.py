@@ -60,6 +60,7 @@ def test_fused_allreduce_plans_fit_the_exchange_region(rows, k, n, world):
             p = _plan(rows, k, n, epi, fused=1, world=world, wire=wire)
             _check_fits(p, rows, k, n)
             assert p.mw == 1 and p.kernel_weight_streaming == 0
+            assert p.m_tiles * p.n_tiles <= 4096  # the exchange's per-tile flags
             assert p.workspace_bytes <= ws
             assert p.tp_sync_bytes <= N.lib().ls_tp_sync_bytes(world, rows, n, wire), (rows, k, n, world, wire)
 
